@@ -1,0 +1,280 @@
+// Decode attention with fused RoPE + KV-cache store, split over positions (flash-decode),
+// and causal prefill attention.
+//
+// Replaces, per layer of Model::layer_decode (src/model.cpp:125-129): apply_rope on q and k
+// (src/attention.cpp:31-47), KVCache::store (src/kvcache.cpp:31-36) and attn_decode
+// (src/attention.cpp:55-80); and attn_prefill (src/attention.cpp:82-111).
+//
+// Cache layout (HBM): per layer [slot][kv_head][cap][head_dim] (head-major: each head's
+// positions are one contiguous slab, the reference's KVLayout::HeadMajor) in fp32, fp16 or
+// bf16.  One CTA handles (kv head, position split, activation row): it rotates the n_rep
+// query heads of its group and the new key with the host-computed cos/sin table (the
+// reference's float cos/sin of pos*freq, so the rotation itself is bit-identical: the
+// products are contracted exactly as the reference's g++ build contracts them), split 0
+// stores the new k/v, then it forms scores scale*dot(q,k), a max-subtracted exp partial
+// and the V-weighted sum over its positions.  The last CTA of a (row, kv head) combines the
+// split partials (max, sum, acc) into the normalised output.  The new position's k/v are
+// taken from shared memory, never re-read from the cache slot being written.
+#include "attention.cuh"
+
+namespace tfb {
+
+__device__ __forceinline__ float kv_load(const void* base, long long idx, int t) {
+    if (t == KV_F32) return reinterpret_cast<const float*>(base)[idx];
+    if (t == KV_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+}
+__device__ __forceinline__ void kv_store(void* base, long long idx, int t, float v) {
+    if (t == KV_F32) reinterpret_cast<float*>(base)[idx] = v;
+    else if (t == KV_F16) reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+}
+
+// NeoX rotate-half with the reference's contraction (src/attention.cpp:31-41 built by g++:
+// x0*c - x1*s -> fma(x0, c, -(x1*s)); x0*s + x1*c -> fma(x0, s, x1*c)).
+__device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) {
+    const float x0 = a, x1 = b;
+    a = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+    b = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+}
+
+__global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
+    __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
+    __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
+    __shared__ float sc[AT_MAX_REP][AT_MAX_CHUNK];
+    __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP];
+    __shared__ int last_s;
+
+    pdl_trigger();
+    pdl_wait();
+    const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
+    const int slot = a.slots ? a.slots[m] : 0;
+    const int pos = a.fresh ? a.pos[slot] : a.n_pos_fixed - 1;
+    const int n_pos = pos + 1;
+    if (a.fresh && (pos < 0 || pos >= a.cap)) {
+        if (tid == 0) atomicCAS(a.err, 0, ERR_POS);
+        return;
+    }
+    const float* row = a.qkv + (size_t)m * a.ld_qkv;
+    const float* q = row + (size_t)kvh * n_rep * hd;
+    const size_t cache_off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd;
+
+    // query heads of this group (rotated when fresh), new key/value
+    for (int i = tid; i < n_rep * hd; i += AT_THREADS) qs[i / hd][i % hd] = q[i];
+    if (a.fresh) {
+        const float* kr = row + (size_t)a.n_head * hd + (size_t)kvh * hd;
+        const float* vr = row + (size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd;
+        for (int i = tid; i < hd; i += AT_THREADS) {
+            kn[i] = kr[i];
+            vn[i] = vr[i];
+        }
+    }
+    __syncthreads();
+    if (a.fresh) {
+        const float* cp = a.cosb + (size_t)pos * d2;
+        const float* sp = a.sinb + (size_t)pos * d2;
+        for (int i = tid; i < (n_rep + 1) * d2; i += AT_THREADS) {
+            const int h = i / d2, j = i % d2;
+            if (h < n_rep) rope_pair(qs[h][j], qs[h][j + d2], cp[j], sp[j]);
+            else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
+        }
+        __syncthreads();
+        if (split == 0)
+            for (int i = tid; i < hd; i += AT_THREADS) {
+                kv_store(a.kc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, kn[i]);
+                kv_store(a.vc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, vn[i]);
+            }
+    }
+
+    // positions of this split: [ws, n_pos) split evenly; ws > 0 only inside a prefill
+    // chunk, whose attention sees the chunk alone (attn_prefill, src/attention.cpp:82-111)
+    const int ws = (a.fresh && a.wstart) ? min(max(a.wstart[slot], 0), pos) : 0;
+    const int chunk = (n_pos - ws + a.n_split - 1) / a.n_split;
+    const int p0 = ws + split * chunk;
+    const int p1 = min(n_pos, p0 + chunk);
+    const int np = max(0, p1 - p0);
+    const float scale = 1.0f / sqrtf((float)hd);
+
+    // scores: warp per position, lanes over head_dim
+    for (int pi = warp; pi < np; pi += AT_THREADS / 32) {
+        const int p = p0 + pi;
+        float kv[AT_MAX_HD / 32];
+        const int nr = (hd + 31) / 32;
+        for (int r = 0; r < nr; ++r) {
+            const int d = lane + 32 * r;
+            kv[r] = d >= hd ? 0.f
+                    : (a.fresh && p == pos) ? kn[d]
+                                            : kv_load(a.kc, (long long)(cache_off + (size_t)p * hd + d), a.kv_type);
+        }
+        for (int h = 0; h < n_rep; ++h) {
+            float s = 0.f;
+            for (int r = 0; r < nr; ++r) s = fmaf(lane + 32 * r < hd ? qs[h][lane + 32 * r] : 0.f, kv[r], s);
+            s = warp_sum(s);
+            if (lane == 0) sc[h][pi] = scale * s;
+        }
+    }
+    __syncthreads();
+    // per-head max and exp-sum over the split (max-subtracted, as softmax, src/layers.cpp:25-35)
+    for (int h = warp; h < n_rep; h += AT_THREADS / 32) {
+        float mx = -INFINITY;
+        for (int i = lane; i < np; i += 32) mx = fmaxf(mx, sc[h][i]);
+        mx = warp_max(mx);
+        float l = 0.f;
+        for (int i = lane; i < np; i += 32) {
+            const float e = expf(sc[h][i] - mx);
+            sc[h][i] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            mx_s[h] = mx;
+            l_s[h] = l;
+        }
+    }
+    __syncthreads();
+    // weighted V: thread per (head, dim)
+    for (int i = tid; i < n_rep * hd; i += AT_THREADS) {
+        const int h = i / hd, d = i % hd;
+        float acc = 0.f;
+        for (int pi = 0; pi < np; ++pi) {
+            const int p = p0 + pi;
+            const float v = (a.fresh && p == pos) ? vn[d] : kv_load(a.vc, (long long)(cache_off + (size_t)p * hd + d), a.kv_type);
+            acc = fmaf(sc[h][pi], v, acc);
+        }
+        const int head = kvh * n_rep + h;
+        if (a.n_split == 1) {
+            a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = acc / l_s[h];
+        } else {
+            float* pp = a.part + (((size_t)m * a.n_head + head) * a.n_split + split) * (hd + 2);
+            pp[2 + d] = acc;
+            if (d == 0) {
+                pp[0] = np > 0 ? mx_s[h] : -INFINITY;
+                pp[1] = l_s[h];
+            }
+        }
+    }
+    if (a.n_split == 1) return;
+
+    // last CTA of (row, kv head) combines the splits
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned t = atomicAdd(&a.counters[(size_t)m * a.n_kv + kvh], 1u);
+        last_s = (t == (unsigned)a.n_split - 1);
+    }
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    for (int i = tid; i < n_rep * hd; i += AT_THREADS) {
+        const int h = i / hd, d = i % hd;
+        const int head = kvh * n_rep + h;
+        const float* pb = a.part + (((size_t)m * a.n_head + head) * a.n_split) * (hd + 2);
+        float M = -INFINITY;
+        for (int s = 0; s < a.n_split; ++s) M = fmaxf(M, __ldcg(pb + (size_t)s * (hd + 2)));
+        float num = 0.f, den = 0.f;
+        for (int s = 0; s < a.n_split; ++s) {
+            const float ms = __ldcg(pb + (size_t)s * (hd + 2));
+            if (ms == -INFINITY) continue;
+            const float w = expf(ms - M);
+            den = fmaf(w, __ldcg(pb + (size_t)s * (hd + 2) + 1), den);
+            num = fmaf(w, __ldcg(pb + (size_t)s * (hd + 2) + 2 + d), num);
+        }
+        a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = num / den;
+    }
+    if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
+}
+
+// ---- prefill attention (attn_prefill): one CTA per (query row i, head h) -----------------
+__global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillAttnArgs a) {
+    extern __shared__ float sbuf[];  // [seq] scores
+    __shared__ float qs[AT_MAX_HD];
+    __shared__ float red[AT_THREADS / 32];
+    __shared__ float stat[2];
+    const int i = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = a.hd, n_rep = a.n_head / a.n_kv, hv = h / n_rep;
+    const float* qi = a.q + ((size_t)i * a.n_head + h) * hd;
+    for (int d = tid; d < hd; d += AT_THREADS) qs[d] = qi[d];
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int j = warp; j <= i; j += AT_THREADS / 32) {
+        const float* kj = a.k + ((size_t)j * a.n_kv + hv) * hd;
+        float s = 0.f;
+        for (int d = lane; d < hd; d += 32) s = fmaf(qs[d], kj[d], s);
+        s = warp_sum(s);
+        if (lane == 0) sbuf[j] = scale * s;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = tid; j <= i; j += AT_THREADS) mx = fmaxf(mx, sbuf[j]);
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    if (tid == 0) {
+        float v = red[0];
+        for (int w = 1; w < AT_THREADS / 32; ++w) v = fmaxf(v, red[w]);
+        stat[0] = v;
+    }
+    __syncthreads();
+    mx = stat[0];
+    float l = 0.f;
+    for (int j = tid; j <= i; j += AT_THREADS) {
+        const float e = expf(sbuf[j] - mx);
+        sbuf[j] = e;
+        l += e;
+    }
+    l = warp_sum(l);
+    __syncthreads();
+    if (lane == 0) red[warp] = l;
+    __syncthreads();
+    if (tid == 0) {
+        float v = 0.f;
+        for (int w = 0; w < AT_THREADS / 32; ++w) v += red[w];
+        stat[1] = v;
+    }
+    __syncthreads();
+    const float inv = 1.0f / stat[1];
+    for (int d = tid; d < hd; d += AT_THREADS) {
+        float acc = 0.f;
+        for (int j = 0; j <= i; ++j) acc = fmaf(sbuf[j] * inv, a.v[((size_t)j * a.n_kv + hv) * hd + d], acc);
+        a.out[((size_t)i * a.n_head + h) * hd + d] = acc;
+    }
+}
+
+// ---- host ------------------------------------------------------------------------------
+int attn_pick_split(int cap) {
+    int s = (cap + AT_MAX_CHUNK - 1) / AT_MAX_CHUNK;
+    return s < 1 ? 1 : s;
+}
+
+cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
+    if (a.hd > AT_MAX_HD || a.hd % 2 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
+    const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;
+    if ((max_pos + a.n_split - 1) / a.n_split > AT_MAX_CHUNK) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_kv, a.n_split, M);
+    cfg.blockDim = dim3(AT_THREADS);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+}
+
+cudaError_t attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st) {
+    if (a.hd > AT_MAX_HD) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)a.seq * sizeof(float);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    attn_prefill_kernel<<<dim3(a.seq, a.n_head), AT_THREADS, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace tfb

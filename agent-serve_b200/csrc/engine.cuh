@@ -1,0 +1,29 @@
+// Host-side engine internals shared by model.cu and ops.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/tinferno_b200.h"
+#include "gemv.cuh"
+
+namespace tfb {
+
+// kernels (gemv.cu, attention.cu, misc.cu)
+void gemv_plan(GemvArgs& a);
+int gemv_grid(const GemvArgs& a, int num_sms);
+int gemv_max_rows(int K);
+cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl);
+cudaError_t gemv_init_attrs();
+
+struct AttnArgs;
+struct PrefillAttnArgs;
+int attn_pick_split(int cap);
+
+std::string& last_error_tls();
+int set_error(const std::string& msg);
+
+}  // namespace tfb

@@ -1,0 +1,72 @@
+// Dequant-GEMV: y[m][n] = sum_k x[m][k] * W[n][k] for M <= 8 activation rows, W in its
+// GGUF block layout (Q8_0, Q4_0, Q4_1, Q6_K, F16, F32), with fused prologues (RMSNorm,
+// embedding lookup) and epilogues (bias, residual add, SwiGLU, logits + greedy argmax,
+// end-of-step bookkeeping).  Replaces matmul()/dot_weight_row() (src/matmul.cpp:5-73)
+// together with the rmsnorm / apply_bias / add_inplace / silu_mul / sample_greedy calls
+// that Model::layer_decode (src/model.cpp:108-142) makes around each matmul.
+#pragma once
+
+#include "common.cuh"
+
+namespace tfb {
+
+constexpr int GV_WARPS = 8;                      // compute warps per CTA
+constexpr int GV_THREADS = (GV_WARPS + 1) * 32;  // + one producer warp issuing bulk copies
+constexpr int GV_STAGES = 4;                     // weight stages in flight per CTA
+constexpr int GV_MAXM = 8;                       // activation rows per launch
+constexpr int GV_STAGE_BUDGET = 18 * 1024;       // target bytes of weights per stage
+
+enum : int { PRO_COPY = 0, PRO_RMSNORM = 1, PRO_EMBED_RMSNORM = 2 };
+enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+enum : int { FIN_NONE = 0, FIN_ADVANCE = 1, FIN_ARGMAX = 2 };
+
+// Per-step control words in device memory (one set per engine).
+struct StepCtl {
+    unsigned int done;      // CTAs of the finishing kernel that have completed
+    int gen_step;           // steps taken since the last reset of this counter
+    int hist_cap;           // rows of `hist`
+    int pad_;
+};
+
+struct GemvArgs {
+    const uint8_t* W;   // first row of the weight block (rows contiguous, native layout)
+    int wtype;
+    int K;              // elements per row
+    long long rb;       // bytes per row
+    int n_items;        // output items: rows (P == 1) or row pairs (P == 2)
+    int P;              // rows per item
+    int KS;             // warps sharing one item along K
+    int M;              // activation rows (<= GV_MAXM)
+    int stage_bytes;    // bytes of one stage buffer (multiple of 16)
+    int fast;           // 1: Q8_0 64-element-unit path
+    // prologue
+    int pro;
+    const float* x;     // [M][ldx]
+    int ldx;
+    const float* norm_w;
+    float eps;
+    const uint8_t* embd; // embedding table (PRO_EMBED_RMSNORM)
+    int embd_type;
+    long long embd_rb;
+    int n_vocab;
+    const int* tokens;   // [M] token ids (device)
+    float* x_out;        // CTA 0 stores the embedded rows here, [M][ldx]
+    // epilogue
+    int epi;
+    float* y;
+    int ldy;
+    const float* bias;   // per row (EPI_STORE)
+    float* resid;        // EPI_RESID
+    int ldr;
+    unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
+    // end of step
+    int fin;
+    StepCtl* ctl;
+    int* tok_next;       // FIN_ARGMAX: next input token per row
+    int* pos;            // per slot
+    const int* slots;    // slot of activation row m
+    int* hist;           // FIN_ARGMAX: generated ids [hist_cap][M] (optional)
+    int* err;
+};
+
+}  // namespace tfb

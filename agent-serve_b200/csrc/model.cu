@@ -1,0 +1,799 @@
+// The engine behind the model-level C-ABI (include/tinferno_b200.h): weight upload, KV cache,
+// scratch, the per-step kernel sequence, CUDA-graph capture and the API entry points.
+//
+// HBM layout (one arena, 256-byte aligned regions, 256 bytes of slack at the end):
+//   per layer  attn_norm f32 | fused QKV rows [wq; wk; wv] (byte-exact concatenation of the
+//              three GGUF tensors, same block layout) | fused bias [bq; bk; bv] f32 |
+//              wo | ffn_norm f32 | gate/up rows interleaved (gate_i, up_i) | down
+//   token_embd | output (only when not tied) | output_norm
+// The concatenation / row interleave move whole rows and keep every row's bytes as they are
+// in the file; bytes per token equal GGUF::weight_bytes() (src/gguf.cpp:219-223).
+//
+// One decode step for M rows (src/model.cpp:197-208 per row) is 5 kernels per layer + 1:
+//   [embed+]rmsnorm+QKV GEMV+bias -> RoPE+KV store+flash-decode -> wo GEMV+residual ->
+//   rmsnorm+gate/up GEMV+SwiGLU -> down GEMV+residual ... -> rmsnorm+lm_head GEMV+argmax
+//   (+ end-of-step bookkeeping: next token, history, position), all launched with
+//   programmatic dependent launch and captured once per row count into a CUDA graph.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "engine.cuh"
+
+namespace tfb {
+
+cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, cudaStream_t st);
+cudaError_t launch_silu_mul(float* g, const float* u, int n, cudaStream_t st);
+cudaError_t launch_softmax(float* x, int n, int rows, cudaStream_t st);
+cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float* freq, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int n, int rows, int* out, cudaStream_t st);
+cudaError_t launch_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, cudaStream_t st);
+
+std::string& last_error_tls() {
+    static thread_local std::string s;
+    return s;
+}
+int set_error(const std::string& msg) {
+    last_error_tls() = msg;
+    return -1;
+}
+
+}  // namespace tfb
+
+using namespace tfb;
+
+namespace {
+
+struct WeightRef {
+    const uint8_t* p = nullptr;
+    int type = 0;
+    int K = 0;
+    long long rb = 0;
+    int rows = 0;
+};
+
+struct LayerDev {
+    const float* attn_norm;
+    WeightRef qkv;          // rows = H + 2*KV
+    const float* bqkv;      // nullptr when the model has no q/k/v bias
+    WeightRef wo;
+    const float* ffn_norm;
+    WeightRef gateup;       // rows = 2*FF, interleaved
+    WeightRef down;
+};
+
+const char* err_code_text(int c) {
+    switch (c) {
+        case ERR_WAIT_FULL: return "device wait for a weight stage timed out";
+        case ERR_WAIT_EMPTY: return "device wait for a free weight stage timed out";
+        case ERR_BAD_TOKEN: return "token id out of range";
+        case ERR_POS: return "position out of range";
+        default: return "device error";
+    }
+}
+
+}  // namespace
+
+struct tf_model {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int num_sms = 148;
+    tf_hparams hp{};
+    tf_options opt{};
+    int D = 0, H = 0, KV = 0, FF = 0, V = 0, hd = 0;
+    uint8_t* arena = nullptr;
+    std::vector<LayerDev> L;
+    WeightRef embd, outw;
+    const float* out_norm = nullptr;
+    unsigned long long weight_bytes = 0;
+    // KV cache
+    void* kc = nullptr;
+    void* vc = nullptr;
+    long long layer_elems = 0, slot_elems = 0;
+    float *cosb = nullptr, *sinb = nullptr;
+    // scratch for up to `tile` activation rows
+    int tile = 1;
+    float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
+    unsigned* counters = nullptr;
+    unsigned long long* keys = nullptr;
+    int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_wstart = nullptr, *d_hist = nullptr;
+    int *d_prompt = nullptr, *d_err = nullptr;
+    StepCtl* ctl = nullptr;
+    int n_split = 1;
+    // host staging (pinned)
+    int* hi = nullptr;      // small int staging
+    float* hlog = nullptr;  // logits staging [tile][V]
+    std::vector<int> hpos;  // host mirror of each slot's position
+    std::map<long long, cudaGraphExec_t> graphs;
+    int kernels_per_step = 0;
+    std::string err;
+};
+
+namespace {
+
+int fail(tf_model* m, const std::string& s) {
+    if (m) m->err = s;
+    return set_error(s);
+}
+
+#define CK(call)                                                                                   \
+    do {                                                                                           \
+        cudaError_t e_ = (call);                                                                   \
+        if (e_ != cudaSuccess) return fail(m, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// Host restatement of rope_freqs (src/attention.cpp:9-29), evaluated in float with the
+// reference build's contraction of the llama3 blend.
+void rope_freqs_host(std::vector<float>& f, const tf_hparams& hp) {
+    const int d2 = hp.head_dim / 2;
+    f.resize(d2);
+    for (int i = 0; i < d2; ++i) {
+        float v = 1.0f / std::pow(hp.rope_theta, (float)(2 * i) / (float)hp.head_dim);
+        if (hp.rope_llama3) {
+            const float wavelen = 2.0f * 3.14159265358979323846f / v;
+            const float lo_wl = hp.rope_orig_ctx / hp.rope_low_freq_f;
+            const float hi_wl = hp.rope_orig_ctx / hp.rope_high_freq_f;
+            if (wavelen < hi_wl) {
+            } else if (wavelen > lo_wl) {
+                v /= hp.rope_scale;
+            } else {
+                const float smooth = (hp.rope_orig_ctx / wavelen - hp.rope_low_freq_f) /
+                                     (hp.rope_high_freq_f - hp.rope_low_freq_f);
+                v = std::fma(smooth, v, (1.0f - smooth) * v / hp.rope_scale);
+            }
+        }
+        f[i] = v;
+    }
+}
+
+const tf_tensor_desc* find_desc(const tf_tensor_desc* t, int n, const std::string& name) {
+    for (int i = 0; i < n; ++i)
+        if (t[i].name && name == t[i].name) return &t[i];
+    return nullptr;
+}
+
+bool type_ok(int t) { return t == T_F32 || t == T_F16 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q6_K; }
+
+// Common GEMV argument skeleton for one weight block.
+GemvArgs gemv_base(tf_model* m, const WeightRef& w, int n_items, int P, int M) {
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.W = w.p;
+    a.wtype = w.type;
+    a.K = w.K;
+    a.rb = w.rb;
+    a.n_items = n_items;
+    a.P = P;
+    a.M = M;
+    a.err = m->d_err;
+    gemv_plan(a);
+    return a;
+}
+
+int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch) {
+    const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
+    const int ldq = H + 2 * KV;
+    int launches = 0;
+    for (int li = 0; li < m->hp.n_layer; ++li) {
+        const LayerDev& Ld = m->L[li];
+        {   // [embedding +] rmsnorm + fused QKV GEMV + bias
+            GemvArgs a = gemv_base(m, Ld.qkv, H + 2 * KV, 1, M);
+            a.pro = li == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM;
+            a.x = m->x;
+            a.ldx = D;
+            a.norm_w = Ld.attn_norm;
+            a.eps = m->hp.rms_eps;
+            a.embd = m->embd.p;
+            a.embd_type = m->embd.type;
+            a.embd_rb = m->embd.rb;
+            a.n_vocab = V;
+            a.tokens = m->d_tokens;
+            a.x_out = m->x;
+            a.epi = EPI_STORE;
+            a.y = m->qkv;
+            a.ldy = ldq;
+            a.bias = Ld.bqkv;
+            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            ++launches;
+        }
+        {   // RoPE + KV store + attention
+            AttnArgs a;
+            memset(&a, 0, sizeof(a));
+            a.qkv = m->qkv;
+            a.ld_qkv = ldq;
+            const size_t esz = m->opt.kv_type == TF_KV_F32 ? 4 : 2;
+            a.kc = static_cast<uint8_t*>(m->kc) + (size_t)li * m->layer_elems * esz;
+            a.vc = static_cast<uint8_t*>(m->vc) + (size_t)li * m->layer_elems * esz;
+            a.slot_stride = m->slot_elems;
+            a.cap = m->opt.max_seq;
+            a.kv_type = m->opt.kv_type;
+            a.pos = m->d_pos;
+            a.wstart = m->d_wstart;
+            a.slots = m->d_slots;
+            a.cosb = m->cosb;
+            a.sinb = m->sinb;
+            a.n_head = m->hp.n_head;
+            a.n_kv = m->hp.n_kv_head;
+            a.hd = m->hd;
+            a.n_split = m->n_split;
+            a.part = m->part;
+            a.counters = m->counters;
+            a.out = m->attn;
+            a.ld_out = H;
+            a.fresh = 1;
+            a.err = m->d_err;
+            CK(attn_decode_launch(a, M, m->stream, pdl));
+            ++launches;
+        }
+        {   // wo GEMV + residual
+            GemvArgs a = gemv_base(m, Ld.wo, D, 1, M);
+            a.pro = PRO_COPY;
+            a.x = m->attn;
+            a.ldx = H;
+            a.epi = EPI_RESID;
+            a.resid = m->x;
+            a.ldr = D;
+            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            ++launches;
+        }
+        {   // rmsnorm + gate/up GEMV + SwiGLU
+            GemvArgs a = gemv_base(m, Ld.gateup, FF, 2, M);
+            a.pro = PRO_RMSNORM;
+            a.x = m->x;
+            a.ldx = D;
+            a.norm_w = Ld.ffn_norm;
+            a.eps = m->hp.rms_eps;
+            a.epi = EPI_SWIGLU;
+            a.y = m->h;
+            a.ldy = FF;
+            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            ++launches;
+        }
+        {   // down GEMV + residual
+            GemvArgs a = gemv_base(m, Ld.down, D, 1, M);
+            a.pro = PRO_COPY;
+            a.x = m->h;
+            a.ldx = FF;
+            a.epi = EPI_RESID;
+            a.resid = m->x;
+            a.ldr = D;
+            if (!head && li == m->hp.n_layer - 1) {
+                a.fin = FIN_ADVANCE;
+                a.ctl = m->ctl;
+                a.pos = m->d_pos;
+                a.slots = m->d_slots;
+            }
+            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            ++launches;
+        }
+    }
+    if (head) {  // rmsnorm + lm_head GEMV + logits + greedy argmax + end of step
+        GemvArgs a = gemv_base(m, m->outw, V, 1, M);
+        a.pro = PRO_RMSNORM;
+        a.x = m->x;
+        a.ldx = D;
+        a.norm_w = m->out_norm;
+        a.eps = m->hp.rms_eps;
+        a.epi = EPI_ARGMAX;
+        a.y = m->logits;
+        a.ldy = V;
+        a.keys = m->keys;
+        a.fin = FIN_ARGMAX;
+        a.ctl = m->ctl;
+        a.tok_next = m->d_tokens;
+        a.pos = m->d_pos;
+        a.slots = m->d_slots;
+        a.hist = m->d_hist;
+        CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+        ++launches;
+    }
+    if (n_launch) *n_launch = launches;
+    return 0;
+}
+
+// Run one step for M rows (tokens in d_tokens[0..M), slots in d_slots[0..M)).
+int run_step(tf_model* m, int M, bool head) {
+    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr);
+    const long long key = (long long)M * 2 + (head ? 1 : 0);
+    auto it = m->graphs.find(key);
+    if (it == m->graphs.end()) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_step(m, M, head, true, nullptr);
+        cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rc) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) return fail(m, std::string("graph capture: ") + cudaGetErrorString(e));
+        cudaGraphExec_t ge = nullptr;
+        e = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) return fail(m, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        it = m->graphs.emplace(key, ge).first;
+    }
+    CK(cudaGraphLaunch(it->second, m->stream));
+    return 0;
+}
+
+// Synchronise and surface any device-side error word.
+int finish_call(tf_model* m) {
+    CK(cudaMemcpyAsync(m->hi + 60, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    if (m->hi[60] != 0) {
+        const int c = m->hi[60];
+        cudaMemsetAsync(m->d_err, 0, sizeof(int), m->stream);
+        cudaMemsetAsync(m->counters, 0, sizeof(unsigned) * (size_t)m->tile * m->hp.n_kv_head, m->stream);
+        cudaMemsetAsync(m->ctl, 0, sizeof(unsigned), m->stream);
+        cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * m->tile, m->stream);
+        cudaStreamSynchronize(m->stream);
+        return fail(m, err_code_text(c));
+    }
+    return 0;
+}
+
+int check_seq(tf_model* m, int seq) {
+    if (seq < 0 || seq >= m->opt.max_batch) return fail(m, "sequence slot out of range");
+    return 0;
+}
+
+int set_slot_row(tf_model* m, int row, int seq, int token) {
+    m->hi[0] = token;
+    m->hi[1] = seq;
+    CK(cudaMemcpyAsync(m->d_tokens + row, m->hi + 0, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    CK(cudaMemcpyAsync(m->d_slots + row, m->hi + 1, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    return 0;
+}
+
+int read_outputs(tf_model* m, int M, float* logits, int* argmax_out) {
+    if (logits)
+        CK(cudaMemcpyAsync(m->hlog, m->logits, sizeof(float) * (size_t)M * m->V, cudaMemcpyDeviceToHost, m->stream));
+    if (argmax_out) CK(cudaMemcpyAsync(m->hi + 8, m->d_tokens, sizeof(int) * M, cudaMemcpyDeviceToHost, m->stream));
+    int rc = finish_call(m);
+    if (rc) return rc;
+    if (logits) memcpy(logits, m->hlog, sizeof(float) * (size_t)M * m->V);
+    if (argmax_out) memcpy(argmax_out, m->hi + 8, sizeof(int) * M);
+    return 0;
+}
+
+}  // namespace
+
+// ============================== C-ABI ==============================================
+
+extern "C" {
+
+const char* tf_cuda_last_error(tf_model* m) { return m && !m->err.empty() ? m->err.c_str() : last_error_tls().c_str(); }
+
+int tf_cuda_destroy(tf_model* m) {
+    if (!m) return 0;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
+                   m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
+                   m->d_err, m->ctl};
+    for (void* p : dev)
+        if (p) cudaFree(p);
+    if (m->hi) cudaFreeHost(m->hi);
+    if (m->hlog) cudaFreeHost(m->hlog);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+    return 0;
+}
+
+int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, const tf_options* opt_in, tf_model** out) {
+    if (!out) return set_error("out is null");
+    *out = nullptr;
+    if (!t || !hp_in) return set_error("null tensors or hparams");
+    tf_model* m = new tf_model();
+    m->hp = *hp_in;
+    tf_options o;
+    o.max_seq = 4096;  // RunConfig::max_seq default (src/common.hpp:112)
+    o.max_batch = 1;
+    o.device = 0;
+    o.kv_type = TF_KV_F32;
+    o.use_graph = 1;
+    if (opt_in) o = *opt_in;
+    if (o.max_seq <= 0 || o.max_batch <= 0) {
+        delete m;
+        return set_error("max_seq and max_batch must be positive");
+    }
+    m->opt = o;
+    m->device = o.device;
+    const tf_hparams& hp = m->hp;
+    if (hp.n_head <= 0 || hp.n_kv_head <= 0 || hp.n_embd <= 0 || hp.n_layer <= 0 || hp.n_ff <= 0 || hp.n_vocab <= 0) {
+        delete m;
+        return set_error("invalid hyper-parameters");
+    }
+    m->hd = hp.n_embd / hp.n_head;  // head_dim = n_embd / n_head always wins (src/model.cpp:22-24)
+    if (hp.head_dim != m->hd) m->hp.head_dim = m->hd;
+    if (m->hd % 2 || m->hd > AT_MAX_HD || hp.n_head % hp.n_kv_head || hp.n_head / hp.n_kv_head > AT_MAX_REP) {
+        delete m;
+        return set_error("unsupported attention shape (head_dim must be even and <= 128, n_head/n_kv_head <= 8)");
+    }
+    m->D = hp.n_embd;
+    m->H = hp.n_head * m->hd;
+    m->KV = hp.n_kv_head * m->hd;
+    m->FF = hp.n_ff;
+    m->V = hp.n_vocab;
+
+    cudaError_t e = cudaSetDevice(o.device);
+    if (e != cudaSuccess) {
+        delete m;
+        return set_error(std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    }
+#define CKD(call)                                                                 \
+    do {                                                                          \
+        cudaError_t e_ = (call);                                                  \
+        if (e_ != cudaSuccess) {                                                  \
+            std::string s_ = std::string(#call) + ": " + cudaGetErrorString(e_); \
+            tf_cuda_destroy(m);                                                   \
+            return set_error(s_);                                                 \
+        }                                                                         \
+    } while (0)
+#define BAD(msg)                  \
+    do {                          \
+        std::string s_ = (msg);   \
+        tf_cuda_destroy(m);       \
+        return set_error(s_);     \
+    } while (0)
+    CKD(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+    CKD(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, o.device));
+    CKD(gemv_init_attrs());
+
+    for (int i = 0; i < nt; ++i) m->weight_bytes += t[i].nbytes;
+
+    // ---- bind tensors as the reference does (src/model.cpp:43-65) ----
+    auto need = [&](const std::string& n) -> const tf_tensor_desc* { return find_desc(t, nt, n); };
+    const tf_tensor_desc* te = need("token_embd.weight");
+    const tf_tensor_desc* on = need("output_norm.weight");
+    const tf_tensor_desc* ow = need("output.weight");
+    if (!te) BAD("missing tensor token_embd.weight");
+    if (!on) BAD("missing tensor output_norm.weight");
+    if (!ow) ow = te;
+    struct LDesc {
+        const tf_tensor_desc *an, *q, *k, *v, *o, *bq, *bk, *bv, *fn, *g, *u, *d;
+    };
+    std::vector<LDesc> ld(hp.n_layer);
+    for (int i = 0; i < hp.n_layer; ++i) {
+        const std::string p = "blk." + std::to_string(i) + ".";
+        LDesc& L = ld[i];
+        const char* must[] = {"attn_norm.weight", "attn_q.weight", "attn_k.weight", "attn_v.weight",
+                              "attn_output.weight", "ffn_norm.weight", "ffn_gate.weight", "ffn_up.weight",
+                              "ffn_down.weight"};
+        const tf_tensor_desc** dst[] = {&L.an, &L.q, &L.k, &L.v, &L.o, &L.fn, &L.g, &L.u, &L.d};
+        for (int j = 0; j < 9; ++j) {
+            *dst[j] = need(p + must[j]);
+            if (!*dst[j]) BAD("missing tensor " + p + must[j]);
+        }
+        L.bq = need(p + "attn_q.bias");
+        L.bk = need(p + "attn_k.bias");
+        L.bv = need(p + "attn_v.bias");
+    }
+    // ---- shape / type validation ----
+    auto check_w = [&](const tf_tensor_desc* d, int K, int N) -> std::string {
+        if (!type_ok(d->ggml_type)) return std::string("unsupported ggml type in ") + d->name;
+        if (d->ne[0] != K || (N > 0 && d->ne[1] != N)) return std::string("unexpected shape of ") + d->name;
+        const int be = blk_elems(d->ggml_type);
+        if (K % be || K % 32) return std::string("row length not divisible by block size in ") + d->name;
+        if ((long long)d->nbytes != row_bytes(d->ggml_type, K) * (N > 0 ? N : d->ne[1]))
+            return std::string("byte size mismatch in ") + d->name;
+        return "";
+    };
+    std::string s;
+    if (!(s = check_w(te, m->D, 0)).empty()) BAD(s);
+    if (te->ne[1] < m->V) BAD("token_embd has fewer rows than n_vocab");
+    if (!(s = check_w(ow, m->D, 0)).empty()) BAD(s);
+    if (ow->ne[1] < m->V) BAD("output has fewer rows than n_vocab");
+    if (on->ggml_type != T_F32 || on->ne[0] != m->D) BAD("output_norm.weight must be F32 [n_embd]");
+    for (int i = 0; i < hp.n_layer; ++i) {
+        LDesc& L = ld[i];
+        if (!(s = check_w(L.q, m->D, m->H)).empty()) BAD(s);
+        if (!(s = check_w(L.k, m->D, m->KV)).empty()) BAD(s);
+        if (!(s = check_w(L.v, m->D, m->KV)).empty()) BAD(s);
+        if (!(s = check_w(L.o, m->H, m->D)).empty()) BAD(s);
+        if (!(s = check_w(L.g, m->D, m->FF)).empty()) BAD(s);
+        if (!(s = check_w(L.u, m->D, m->FF)).empty()) BAD(s);
+        if (!(s = check_w(L.d, m->FF, m->D)).empty()) BAD(s);
+        if (L.q->ggml_type != L.k->ggml_type || L.q->ggml_type != L.v->ggml_type)
+            BAD("attn_q/k/v of one layer must share a type (they are streamed as one block)");
+        if (L.g->ggml_type != L.u->ggml_type) BAD("ffn_gate/ffn_up of one layer must share a type");
+        if (L.an->ggml_type != T_F32 || L.fn->ggml_type != T_F32) BAD("norm weights must be F32");
+        const bool any_b = L.bq || L.bk || L.bv;
+        if (any_b && !(L.bq && L.bk && L.bv)) BAD("q/k/v biases must be all present or all absent");
+        if (any_b && (L.bq->ggml_type != T_F32 || L.bk->ggml_type != T_F32 || L.bv->ggml_type != T_F32))
+            BAD("q/k/v biases must be F32 (read as raw floats, src/model.cpp:85-89)");
+    }
+
+    // ---- arena layout ----
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o2 = off;
+        off = (off + bytes + 255) & ~(size_t)255;
+        return o2;
+    };
+    struct Place {
+        size_t an, qkv, b, o, fn, gu, d;
+    };
+    std::vector<Place> pl(hp.n_layer);
+    for (int i = 0; i < hp.n_layer; ++i) {
+        LDesc& L = ld[i];
+        pl[i].an = take(L.an->nbytes);
+        pl[i].qkv = take(L.q->nbytes + L.k->nbytes + L.v->nbytes);
+        pl[i].b = L.bq ? take((size_t)(m->H + 2 * m->KV) * 4) : 0;
+        pl[i].o = take(L.o->nbytes);
+        pl[i].fn = take(L.fn->nbytes);
+        pl[i].gu = take(L.g->nbytes + L.u->nbytes);
+        pl[i].d = take(L.d->nbytes);
+    }
+    const size_t p_embd = take(te->nbytes);
+    const size_t p_out = (ow == te) ? p_embd : take(ow->nbytes);
+    const size_t p_onorm = take(on->nbytes);
+    const size_t arena_bytes = off + 256;
+    CKD(cudaMalloc(&m->arena, arena_bytes));
+    CKD(cudaMemset(m->arena + off, 0, 256));
+    uint8_t* A = m->arena;
+
+    auto wref = [&](const uint8_t* p, int type, int K, int rows) {
+        WeightRef w;
+        w.p = p;
+        w.type = type;
+        w.K = K;
+        w.rb = row_bytes(type, K);
+        w.rows = rows;
+        return w;
+    };
+    m->L.resize(hp.n_layer);
+    for (int i = 0; i < hp.n_layer; ++i) {
+        LDesc& L = ld[i];
+        LayerDev& Ld = m->L[i];
+        CKD(cudaMemcpy(A + pl[i].an, L.an->data, L.an->nbytes, cudaMemcpyHostToDevice));
+        Ld.attn_norm = reinterpret_cast<const float*>(A + pl[i].an);
+        CKD(cudaMemcpy(A + pl[i].qkv, L.q->data, L.q->nbytes, cudaMemcpyHostToDevice));
+        CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes, L.k->data, L.k->nbytes, cudaMemcpyHostToDevice));
+        CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes + L.k->nbytes, L.v->data, L.v->nbytes, cudaMemcpyHostToDevice));
+        Ld.qkv = wref(A + pl[i].qkv, L.q->ggml_type, m->D, m->H + 2 * m->KV);
+        Ld.bqkv = nullptr;
+        if (L.bq) {
+            float* b = reinterpret_cast<float*>(A + pl[i].b);
+            CKD(cudaMemcpy(b, L.bq->data, (size_t)m->H * 4, cudaMemcpyHostToDevice));
+            CKD(cudaMemcpy(b + m->H, L.bk->data, (size_t)m->KV * 4, cudaMemcpyHostToDevice));
+            CKD(cudaMemcpy(b + m->H + m->KV, L.bv->data, (size_t)m->KV * 4, cudaMemcpyHostToDevice));
+            Ld.bqkv = b;
+        }
+        CKD(cudaMemcpy(A + pl[i].o, L.o->data, L.o->nbytes, cudaMemcpyHostToDevice));
+        Ld.wo = wref(A + pl[i].o, L.o->ggml_type, m->H, m->D);
+        CKD(cudaMemcpy(A + pl[i].fn, L.fn->data, L.fn->nbytes, cudaMemcpyHostToDevice));
+        Ld.ffn_norm = reinterpret_cast<const float*>(A + pl[i].fn);
+        const size_t grb = (size_t)row_bytes(L.g->ggml_type, m->D);
+        CKD(cudaMemcpy2D(A + pl[i].gu, 2 * grb, L.g->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
+        CKD(cudaMemcpy2D(A + pl[i].gu + grb, 2 * grb, L.u->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
+        Ld.gateup = wref(A + pl[i].gu, L.g->ggml_type, m->D, 2 * m->FF);
+        CKD(cudaMemcpy(A + pl[i].d, L.d->data, L.d->nbytes, cudaMemcpyHostToDevice));
+        Ld.down = wref(A + pl[i].d, L.d->ggml_type, m->FF, m->D);
+    }
+    CKD(cudaMemcpy(A + p_embd, te->data, te->nbytes, cudaMemcpyHostToDevice));
+    m->embd = wref(A + p_embd, te->ggml_type, m->D, (int)te->ne[1]);
+    if (ow != te) CKD(cudaMemcpy(A + p_out, ow->data, ow->nbytes, cudaMemcpyHostToDevice));
+    m->outw = wref(A + p_out, ow->ggml_type, m->D, (int)ow->ne[1]);
+    CKD(cudaMemcpy(A + p_onorm, on->data, on->nbytes, cudaMemcpyHostToDevice));
+    m->out_norm = reinterpret_cast<const float*>(A + p_onorm);
+
+    // ---- KV cache: per layer [slot][kv_head][cap][hd] ----
+    const size_t esz = o.kv_type == TF_KV_F32 ? 4 : 2;
+    m->slot_elems = (long long)hp.n_kv_head * o.max_seq * m->hd;
+    m->layer_elems = m->slot_elems * o.max_batch;
+    const size_t kv_bytes = (size_t)m->layer_elems * hp.n_layer * esz;
+    CKD(cudaMalloc(&m->kc, kv_bytes));
+    CKD(cudaMalloc(&m->vc, kv_bytes));
+    CKD(cudaMemset(m->kc, 0, kv_bytes));
+    CKD(cudaMemset(m->vc, 0, kv_bytes));
+
+    // ---- RoPE table: cos/sin((float)pos * freq[i]) in float, as rope_one computes them ----
+    {
+        std::vector<float> f;
+        rope_freqs_host(f, m->hp);
+        const int d2 = m->hd / 2;
+        std::vector<float> c((size_t)o.max_seq * d2), sn((size_t)o.max_seq * d2);
+        for (int p = 0; p < o.max_seq; ++p)
+            for (int i = 0; i < d2; ++i) {
+                const float ang = (float)p * f[i];
+                c[(size_t)p * d2 + i] = std::cos(ang);
+                sn[(size_t)p * d2 + i] = std::sin(ang);
+            }
+        CKD(cudaMalloc(&m->cosb, c.size() * 4));
+        CKD(cudaMalloc(&m->sinb, sn.size() * 4));
+        CKD(cudaMemcpy(m->cosb, c.data(), c.size() * 4, cudaMemcpyHostToDevice));
+        CKD(cudaMemcpy(m->sinb, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    }
+
+    // ---- scratch ----
+    int tile = GV_MAXM;
+    for (int K : {m->D, m->H, m->FF}) tile = std::min(tile, gemv_max_rows(K));
+    m->tile = std::max(1, std::min(tile, o.max_batch));
+    m->n_split = attn_pick_split(o.max_seq);
+    const int T = m->tile;
+    CKD(cudaMalloc(&m->x, sizeof(float) * T * m->D));
+    CKD(cudaMalloc(&m->qkv, sizeof(float) * T * (m->H + 2 * m->KV)));
+    CKD(cudaMalloc(&m->attn, sizeof(float) * T * m->H));
+    CKD(cudaMalloc(&m->h, sizeof(float) * T * m->FF));
+    CKD(cudaMalloc(&m->logits, sizeof(float) * (size_t)T * m->V));
+    CKD(cudaMalloc(&m->part, sizeof(float) * (size_t)T * hp.n_head * m->n_split * (m->hd + 2)));
+    CKD(cudaMalloc(&m->counters, sizeof(unsigned) * T * hp.n_kv_head));
+    CKD(cudaMemset(m->counters, 0, sizeof(unsigned) * T * hp.n_kv_head));
+    CKD(cudaMalloc(&m->keys, sizeof(unsigned long long) * T));
+    CKD(cudaMemset(m->keys, 0, sizeof(unsigned long long) * T));
+    CKD(cudaMalloc(&m->d_tokens, sizeof(int) * T));
+    CKD(cudaMemset(m->d_tokens, 0, sizeof(int) * T));
+    CKD(cudaMalloc(&m->d_slots, sizeof(int) * T));
+    CKD(cudaMemset(m->d_slots, 0, sizeof(int) * T));
+    CKD(cudaMalloc(&m->d_pos, sizeof(int) * o.max_batch));
+    CKD(cudaMemset(m->d_pos, 0, sizeof(int) * o.max_batch));
+    CKD(cudaMalloc(&m->d_wstart, sizeof(int) * o.max_batch));
+    CKD(cudaMemset(m->d_wstart, 0, sizeof(int) * o.max_batch));
+    CKD(cudaMalloc(&m->d_hist, sizeof(int) * ((size_t)o.max_seq + 1) * T));
+    CKD(cudaMalloc(&m->d_prompt, sizeof(int) * ((size_t)o.max_seq + 1)));
+    CKD(cudaMalloc(&m->d_err, sizeof(int)));
+    CKD(cudaMemset(m->d_err, 0, sizeof(int)));
+    CKD(cudaMalloc(&m->ctl, sizeof(StepCtl)));
+    CKD(cudaMemset(m->ctl, 0, sizeof(StepCtl)));
+    CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
+    CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
+    m->hpos.assign(o.max_batch, 0);
+    CKD(cudaDeviceSynchronize());
+    {
+        int n = 0;
+        // count launches of one step (no device work: enqueue into a throwaway capture)
+        cudaGraph_t g = nullptr;
+        CKD(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_step(m, 1, true, true, &n);
+        cudaStreamEndCapture(m->stream, &g);
+        if (g) cudaGraphDestroy(g);
+        if (rc) BAD(m->err);
+        m->kernels_per_step = n;
+    }
+    *out = m;
+    return 0;
+#undef CKD
+#undef BAD
+}
+
+int tf_cuda_reset(tf_model* m, int seq) {
+    if (!m) return set_error("null model");
+    CK(cudaSetDevice(m->device));
+    const int s0 = seq < 0 ? 0 : seq, s1 = seq < 0 ? m->opt.max_batch : seq + 1;
+    if (seq >= m->opt.max_batch) return fail(m, "sequence slot out of range");
+    const size_t esz = m->opt.kv_type == TF_KV_F32 ? 4 : 2;
+    for (int s = s0; s < s1; ++s) {
+        m->hpos[s] = 0;
+        for (int li = 0; li < m->hp.n_layer; ++li) {  // KVCache::clear (src/kvcache.cpp:16-19)
+            const size_t o2 = ((size_t)li * m->layer_elems + (size_t)s * m->slot_elems) * esz;
+            CK(cudaMemsetAsync(static_cast<uint8_t*>(m->kc) + o2, 0, m->slot_elems * esz, m->stream));
+            CK(cudaMemsetAsync(static_cast<uint8_t*>(m->vc) + o2, 0, m->slot_elems * esz, m->stream));
+        }
+    }
+    CK(cudaMemsetAsync(m->d_pos + s0, 0, sizeof(int) * (s1 - s0), m->stream));
+    CK(cudaMemsetAsync(m->d_wstart + s0, 0, sizeof(int) * (s1 - s0), m->stream));
+    return finish_call(m);
+}
+
+int tf_cuda_decode(tf_model* m, int seq, int token, float* logits, int* argmax_out) {
+    if (!m) return set_error("null model");
+    CK(cudaSetDevice(m->device));
+    if (check_seq(m, seq)) return -1;
+    if (m->hpos[seq] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
+    if (token < 0 || token >= m->V) return fail(m, "token id out of range");
+    if (set_slot_row(m, 0, seq, token)) return -1;
+    if (run_step(m, 1, true)) return -1;
+    m->hpos[seq] += 1;
+    return read_outputs(m, 1, logits, argmax_out);
+}
+
+int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logits, int* argmax_out) {
+    if (!m) return set_error("null model");
+    if (n <= 0) return 0;  // Model::prefill returns immediately (src/model.cpp:184)
+    CK(cudaSetDevice(m->device));
+    if (check_seq(m, seq)) return -1;
+    if (!tokens) return fail(m, "tokens is null");
+    if (m->hpos[seq] + n > m->opt.max_seq) return fail(m, "prefill exceeds max_seq");
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= m->V) return fail(m, "token id out of range");
+    int* stage = m->hi + 64;
+    memcpy(stage, tokens, sizeof(int) * n);
+    CK(cudaMemcpyAsync(m->d_prompt, stage, sizeof(int) * n, cudaMemcpyHostToDevice, m->stream));
+    // attention inside the chunk sees the chunk alone, from its first position
+    m->hi[2] = m->hpos[seq];
+    m->hi[3] = 0;
+    CK(cudaMemcpyAsync(m->d_wstart + seq, m->hi + 2, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    if (set_slot_row(m, 0, seq, tokens[0])) return -1;
+    for (int i = 0; i < n; ++i) {
+        CK(cudaMemcpyAsync(m->d_tokens, m->d_prompt + i, sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
+        if (run_step(m, 1, i == n - 1)) return -1;
+    }
+    CK(cudaMemcpyAsync(m->d_wstart + seq, m->hi + 3, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    m->hpos[seq] += n;
+    return read_outputs(m, 1, logits, argmax_out);
+}
+
+int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eos, int* out_ids, int* n_out) {
+    if (!m) return set_error("null model");
+    if (n_out) *n_out = 0;
+    if (n <= 0) return 0;
+    CK(cudaSetDevice(m->device));
+    if (check_seq(m, seq)) return -1;
+    if (!out_ids) return fail(m, "out_ids is null");
+    if (m->hpos[seq] + n > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
+    if (first_token < 0 || first_token >= m->V) return fail(m, "token id out of range");
+    if (set_slot_row(m, 0, seq, first_token)) return -1;
+    StepCtl c = {0u, 0, n, 0};
+    memcpy(m->hi + 4, &c, sizeof(c));
+    CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
+    for (int i = 0; i < n; ++i)
+        if (run_step(m, 1, true)) return -1;
+    int* hist = m->hi + 64;
+    CK(cudaMemcpyAsync(hist, m->d_hist, sizeof(int) * n, cudaMemcpyDeviceToHost, m->stream));
+    int rc = finish_call(m);
+    if (rc) return rc;
+    // accepted ids: t0 = first_token, t_i = hist[i-1]; stop before t_j == eos, j > 0
+    // (src/main.cpp:113-121); j decodes were needed for the accepted tokens.
+    int j = n;
+    out_ids[0] = first_token;
+    for (int i = 1; i < n; ++i) {
+        if (eos >= 0 && hist[i - 1] == eos) {
+            j = i;
+            break;
+        }
+        out_ids[i] = hist[i - 1];
+    }
+    const int pos0 = m->hpos[seq];
+    m->hpos[seq] = pos0 + j;
+    if (j < n) {
+        m->hi[2] = pos0 + j;
+        CK(cudaMemcpyAsync(m->d_pos + seq, m->hi + 2, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        CK(cudaStreamSynchronize(m->stream));
+    }
+    if (n_out) *n_out = j;
+    return 0;
+}
+
+int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int B, int* argmax_out, float* logits) {
+    if (!m) return set_error("null model");
+    if (B <= 0) return 0;
+    CK(cudaSetDevice(m->device));
+    if (!seq_ids || !tokens) return fail(m, "null seq_ids or tokens");
+    std::vector<char> seen(m->opt.max_batch, 0);
+    for (int b = 0; b < B; ++b) {
+        if (check_seq(m, seq_ids[b])) return -1;
+        if (seen[seq_ids[b]]) return fail(m, "duplicate sequence slot in one batch");
+        seen[seq_ids[b]] = 1;
+        if (m->hpos[seq_ids[b]] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
+        if (tokens[b] < 0 || tokens[b] >= m->V) return fail(m, "token id out of range");
+    }
+    for (int b0 = 0; b0 < B; b0 += m->tile) {
+        const int T = std::min(m->tile, B - b0);
+        memcpy(m->hi + 8, tokens + b0, sizeof(int) * T);
+        memcpy(m->hi + 24, seq_ids + b0, sizeof(int) * T);
+        CK(cudaMemcpyAsync(m->d_tokens, m->hi + 8, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+        CK(cudaMemcpyAsync(m->d_slots, m->hi + 24, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+        if (run_step(m, T, true)) return -1;
+        for (int b = 0; b < T; ++b) m->hpos[seq_ids[b0 + b]] += 1;
+        int rc = read_outputs(m, T, logits ? logits + (size_t)b0 * m->V : nullptr, argmax_out ? argmax_out + b0 : nullptr);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int tf_cuda_n_pos(tf_model* m, int seq) {
+    if (!m || seq < 0 || seq >= m->opt.max_batch) return -1;
+    return m->hpos[seq];
+}
+int tf_cuda_n_vocab(tf_model* m) { return m ? m->V : -1; }
+unsigned long long tf_cuda_weight_bytes(tf_model* m) { return m ? m->weight_bytes : 0ull; }
+void* tf_cuda_stream(tf_model* m) { return m ? (void*)m->stream : nullptr; }
+int tf_cuda_kernels_per_step(tf_model* m) { return m ? m->kernels_per_step : -1; }
+
+}  // extern "C"

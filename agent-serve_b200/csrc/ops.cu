@@ -1,0 +1,158 @@
+// Op-level C-ABI (tf_op_*): each reference op on device pointers, for the cfg3 kernel sweep
+// and for op-by-op parity against the reference.
+#include <string>
+
+#include "attention.cuh"
+#include "engine.cuh"
+
+namespace tfb {
+cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, cudaStream_t st);
+cudaError_t launch_silu_mul(float* g, const float* u, int n, cudaStream_t st);
+cudaError_t launch_softmax(float* x, int n, int rows, cudaStream_t st);
+cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float* freq, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int n, int rows, int* out, cudaStream_t st);
+cudaError_t launch_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, cudaStream_t st);
+}  // namespace tfb
+
+using namespace tfb;
+
+namespace {
+int op_status(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) return set_error(std::string(what) + ": " + cudaGetErrorString(e));
+    return 0;
+}
+bool type_ok(int t) { return t == T_F32 || t == T_F16 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q6_K; }
+
+int* g_err_word = nullptr;  // device error word for op-level launches (one per process)
+int err_word(int** out) {
+    if (!g_err_word) {
+        cudaError_t e = cudaMalloc(&g_err_word, sizeof(int));
+        if (e != cudaSuccess) return op_status(e, "cudaMalloc");
+        e = cudaMemset(g_err_word, 0, sizeof(int));
+        if (e != cudaSuccess) return op_status(e, "cudaMemset");
+    }
+    *out = g_err_word;
+    return 0;
+}
+}  // namespace
+
+extern "C" {
+
+int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, int M, void* stream) {
+    if (!type_ok(t)) return set_error("unsupported ggml type");
+    if (N <= 0 || K <= 0 || M < 0) return set_error("bad matmul shape");
+    if (K % 32 || K % blk_elems(t)) return set_error("row length not divisible by block size");
+    if (M == 0) return 0;
+    if (t == T_F32 && (reinterpret_cast<uintptr_t>(W) & 3)) return set_error("F32 weights must be 4-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* err = nullptr;
+    if (err_word(&err)) return -1;
+    if (op_status(gemv_init_attrs(), "cudaFuncSetAttribute")) return -1;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tile = gemv_max_rows(K);
+    for (int m0 = 0; m0 < M; m0 += tile) {
+        GemvArgs a;
+        memset(&a, 0, sizeof(a));
+        a.W = static_cast<const uint8_t*>(W);
+        a.wtype = t;
+        a.K = K;
+        a.rb = row_bytes(t, K);
+        a.n_items = N;
+        a.P = 1;
+        a.M = M - m0 < tile ? M - m0 : tile;
+        a.err = err;
+        gemv_plan(a);
+        a.pro = PRO_COPY;
+        a.x = A + (size_t)m0 * K;
+        a.ldx = K;
+        a.epi = EPI_STORE;
+        a.y = C + (size_t)m0 * N;
+        a.ldy = N;
+        if (op_status(gemv_launch(a, gemv_grid(a, sms), st, false), "gemv")) return -1;
+    }
+    return 0;
+}
+
+int tf_op_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, void* stream) {
+    if (!type_ok(t)) return set_error("unsupported ggml type");
+    if (n_rows <= 0) return 0;
+    return op_status(launch_dequant_rows(out, t, W, K, rows, n_rows, static_cast<cudaStream_t>(stream)), "dequant_rows");
+}
+
+int tf_op_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, void* stream) {
+    if (rows <= 0) return 0;
+    return op_status(launch_rmsnorm(out, x, w, n, rows, eps, static_cast<cudaStream_t>(stream)), "rmsnorm");
+}
+
+int tf_op_silu_mul(float* gate, const float* up, int n, void* stream) {
+    if (n <= 0) return 0;
+    return op_status(launch_silu_mul(gate, up, n, static_cast<cudaStream_t>(stream)), "silu_mul");
+}
+
+int tf_op_softmax(float* x, int n, int rows, void* stream) {
+    if (rows <= 0 || n <= 0) return 0;
+    return op_status(launch_softmax(x, n, rows, static_cast<cudaStream_t>(stream)), "softmax");
+}
+
+int tf_op_rope(float* x, int seq, int n_heads, int head_dim, int pos0, const float* freq, void* stream) {
+    if (seq <= 0) return 0;
+    return op_status(launch_rope(x, seq, n_heads, head_dim, pos0, freq, static_cast<cudaStream_t>(stream)), "rope");
+}
+
+int tf_op_attn_decode(float* out, const float* q, const void* k_cache, const void* v_cache, int kv_type, int cap,
+                      int n_pos, int n_heads, int n_kv_heads, int head_dim, void* stream) {
+    if (n_pos <= 0 || n_pos > cap) return set_error("n_pos must be in [1, cap]");
+    if (n_heads % n_kv_heads) return set_error("n_heads must be a multiple of n_kv_heads");
+    int* err = nullptr;
+    if (err_word(&err)) return -1;
+    const int n_split = attn_pick_split(n_pos);
+    float* part = nullptr;
+    unsigned* counters = nullptr;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (n_split > 1) {
+        if (op_status(cudaMallocAsync((void**)&part, sizeof(float) * n_heads * n_split * (head_dim + 2), st), "alloc")) return -1;
+        if (op_status(cudaMallocAsync((void**)&counters, sizeof(unsigned) * n_kv_heads, st), "alloc")) return -1;
+        cudaMemsetAsync(counters, 0, sizeof(unsigned) * n_kv_heads, st);
+    }
+    AttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.qkv = q;
+    a.ld_qkv = n_heads * head_dim;
+    a.kc = const_cast<void*>(k_cache);
+    a.vc = const_cast<void*>(v_cache);
+    a.slot_stride = 0;
+    a.cap = cap;
+    a.kv_type = kv_type;
+    a.n_head = n_heads;
+    a.n_kv = n_kv_heads;
+    a.hd = head_dim;
+    a.n_split = n_split;
+    a.part = part;
+    a.counters = counters;
+    a.out = out;
+    a.ld_out = n_heads * head_dim;
+    a.fresh = 0;
+    a.n_pos_fixed = n_pos;
+    a.err = err;
+    int rc = op_status(attn_decode_launch(a, 1, st, false), "attn_decode");
+    if (part) cudaFreeAsync(part, st);
+    if (counters) cudaFreeAsync(counters, st);
+    return rc;
+}
+
+int tf_op_attn_prefill(float* out, const float* q, const float* k, const float* v, int seq, int n_heads, int n_kv_heads,
+                       int head_dim, void* stream) {
+    if (seq <= 0) return 0;
+    if (n_heads % n_kv_heads) return set_error("n_heads must be a multiple of n_kv_heads");
+    PrefillAttnArgs a{q, k, v, out, seq, n_heads, n_kv_heads, head_dim};
+    return op_status(attn_prefill_launch(a, static_cast<cudaStream_t>(stream)), "attn_prefill");
+}
+
+int tf_op_argmax(const float* logits, int n, int rows, int* out, void* stream) {
+    if (rows <= 0 || n <= 0) return 0;
+    return op_status(launch_argmax(logits, n, rows, out, static_cast<cudaStream_t>(stream)), "argmax");
+}
+
+}  // extern "C"

@@ -1,0 +1,319 @@
+"""Benchmark of the hot path: greedy decode of the BASELINE cfg0 model (Llama-3.2-1B
+architecture, Q8_0, synthetic seeded weights) at batch 1 on each GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one decoded token.  The timed region holds K steps after W warm-up steps, after a
+32-token prompt prefill, bracketed by a barrier and a device synchronise, timed with CUDA
+events on the engine's stream; the job value is the max over ranks.  With N > 1 every rank
+runs an independent replica of the batch-1 decode on its own GPU (the batch-1 path does not
+shard: replicas only) and the value is the aggregate tok/s.
+
+  value      tok/s with the token fed back on the device (graph replays, no host round trip)
+  e2e        tok/s through the reference-facing call tf_cuda_decode(token -> host logits),
+             one host->device token copy and one device->host logits copy per step
+  roofline   the Q8_0 dequant-GEMV kernel (every matmul of the step runs on it) timed alone
+             on the lm_head shape, algorithmic bytes / launch time vs MEASURED_PEAKS.json
+  cpu_baseline  the reference engine's stage-v2 path (oracle/_ref, built from the reference's
+             own sources) on this host's cores, on a bounded sample of the same decode
+
+--impl reference times only the reference's CPU decode of the same workload (rank 0).
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "agent-serve_b200"))
+
+from tinferno_b200 import synth  # noqa: E402
+
+CFG = synth.CFG0
+PROMPT = 32
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.idx)], stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                rows.append(f)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def model_file():
+    cache = os.environ.get("TFB200_CACHE", "/tmp/tfb200_models")
+    return synth.model_path(CFG, cache)
+
+
+def cpu_reference_decode(path, prompt, n_tokens, max_seconds=None):
+    """Reference (oracle/_ref, stage v2, all host threads) when built, else the oracle port.
+    Prefill untimed; times decode steps; returns (tok/s, tokens, threads, kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import pyoracle as po
+    if po.ref_available():
+        m = po.RefModel(path, 2048, stage="v2")
+        kind, threads = "reference", m.n_threads
+    else:
+        from tinferno_b200 import gguf
+        threads = os.cpu_count() or 1
+        m = po.OracleModel(gguf.GGUFReader(path), 2048, threads=threads)
+        kind = "port"
+    logits = m.prefill(prompt)
+    t = int(np.argmax(logits))
+    n = 0
+    t0 = time.perf_counter()
+    while n < n_tokens:
+        logits = m.decode(t)
+        t = int(np.argmax(logits))
+        n += 1
+        if max_seconds and time.perf_counter() - t0 > max_seconds:
+            break
+    dt = time.perf_counter() - t0
+    m.close()
+    return n / dt, n, threads, kind
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    path = model_file()
+    prompt = synth.prompt_tokens(CFG, PROMPT)
+    # warm-up steps then the timed steps, within one generation (positions 32 .. 32+W+K)
+    tps, n, threads, kind = cpu_reference_decode(path, prompt, args.warmup + args.steps)
+    line = {"metric": "decode tok/s (batch 1, cfg0 Llama-3.2-1B Q8_0)", "value": round(tps, 3), "unit": "tok/s",
+            "impl": "reference", "n_gpus": args.gpus, "steps": n, "warmup": 0, "ms_per_step": round(1e3 / tps, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "cfg0 batch-1 greedy decode after a 32-token prompt", "model": CFG.name,
+                       "global_batch": 1, "seq_len": PROMPT + n, "parallelism": "cpu threads"},
+            "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+                             "sample": f"1 sequence, {PROMPT}-token prompt (untimed prefill), {n} decode steps"},
+            "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local_rank, dist):
+    import torch
+    from tinferno_b200 import native
+    from tinferno_b200.model import Model, RunConfig
+
+    torch.cuda.set_device(local_rank)
+    if rank == 0:
+        path = model_file()
+    if dist:
+        dist.barrier()
+    path = model_file()
+    m = Model(path, RunConfig(max_seq=CFG.max_seq, device=local_rank))
+    stream = torch.cuda.ExternalStream(m.stream)
+    prompt = synth.prompt_tokens(CFG, PROMPT)
+    L = m.L
+
+    def prefill():
+        m.reset(0)
+        return int(np.argmax(m.prefill(prompt)))
+
+    # ---- value: device-resident decode (graph replays, argmax fed back on the device) ----
+    out = np.zeros(args.steps, np.int32)
+    n_out = C.c_int(0)
+    first = prefill()
+    ids = m.generate_greedy(first, args.warmup)  # W untimed steps (graph captured and warm)
+    nxt = ids[-1]  # the timed steps continue the stream at positions 32+W ..
+    clocks = ClockSampler(local_rank)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    native.check(L.tf_cuda_generate_greedy(m.h, 0, int(nxt), args.steps, -1, out.ctypes.data_as(native.i32p),
+                                           C.byref(n_out)), m.h)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    t = torch.tensor([ms], device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * args.steps / (ms_max / 1e3)
+
+    # ---- e2e: the reference-facing call with host token in and host logits out ----
+    first = prefill()
+    tok = first
+    logits = np.empty(m.n_vocab, np.float32)
+    for _ in range(args.warmup):
+        m.decode(tok, logits)
+        tok = m.last_argmax
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.decode(tok, logits)
+        tok = m.last_argmax
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e = world * args.steps / float(t.item())
+
+    # ---- roofline: the Q8_0 GEMV kernel alone on the lm_head shape ----
+    roof = None
+    if rank == 0:
+        roof = gemv_roofline(torch, native, m)
+    kps = m.kernels_per_step
+    m.close()
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu and world == 1:
+            tps, n, threads, kind = cpu_reference_decode(path, prompt, 512, max_seconds=15.0)
+            cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+                   "sample": f"1 sequence, {PROMPT}-token prompt (untimed prefill), {n} decode steps (~15 s)"}
+        wb = synth.weight_bytes(CFG)
+        line = {"metric": "decode tok/s (batch 1, cfg0 Llama-3.2-1B Q8_0)", "value": round(value, 2), "unit": "tok/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "config": {"workload": "cfg0 batch-1 greedy decode after a 32-token prompt (replicas per GPU)",
+                           "model": CFG.name, "global_batch": world, "seq_len": PROMPT + 2 * args.warmup + args.steps,
+                           "parallelism": f"replicas x{world}", "kv_cache": "f32",
+                           "l2": "weights 1.31 GB per step stream through the 126 MB L2 (inputs larger than L2)"},
+                "hbm_roofline": {"bytes_per_token": wb, "achieved_gbs": round(wb * value / world / 1e9, 1),
+                                 "frac_of_peak": round(wb * value / world / 1e9 / peaks()[0], 4),
+                                 "peak_gbs": peaks()[0], "peak_kind": peaks()[1]},
+                "roofline": roof, "cpu_baseline": cpu,
+                "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                        "d2h_bytes_per_step": 4 * CFG.n_vocab + 8},
+                "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk}
+        print(json.dumps(line), flush=True)
+
+
+def gemv_roofline(torch, native, m):
+    """Time tf_op_matmul (the engine's dequant-GEMV kernel) on the lm_head shape: 128256 x 2048
+    Q8_0 weights (279 MB, > L2) times one fp32 row."""
+    from tinferno_b200 import quants
+    N, K = CFG.n_vocab, CFG.n_embd
+    rb = K // 32 * 34
+    nbytes = N * rb
+    W = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    # fill with valid Q8_0 blocks: random int8 quants, scale 1/127
+    W.view(N, K // 32, 34)[:, :, 2:] = torch.randint(-127, 128, (N, K // 32, 32), device="cuda").to(torch.int8).view(torch.uint8)
+    d = np.float16(1.0 / 127).view(np.uint16)
+    W.view(N, K // 32, 34)[:, :, 0] = int(d & 0xFF)
+    W.view(N, K // 32, 34)[:, :, 1] = int(d >> 8)
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    st = torch.cuda.current_stream()
+    L = native.lib()
+    for _ in range(5):
+        native.check(L.tf_op_matmul(C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()), native.TF_Q8_0,
+                                    C.c_void_p(W.data_ptr()), N, K, 1, C.c_void_p(st.cuda_stream)))
+    reps = 50
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    for a, b in evs:
+        a.record(st)
+        native.check(L.tf_op_matmul(C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()), native.TF_Q8_0,
+                                    C.c_void_p(W.data_ptr()), N, K, 1, C.c_void_p(st.cuda_stream)))
+        b.record(st)
+    torch.cuda.synchronize()
+    ts = sorted(a.elapsed_time(b) for a, b in evs)
+    t = statistics.median(ts) / 1e3
+    alg = nbytes + K * 4 + N * 4
+    peak, kind = peaks()
+    ach = alg / t / 1e9
+    return {"bound": "hbm", "kernel": "gemv_kernel<1> (Q8_0, lm_head 128256x2048)", "achieved": round(ach, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": kind,
+            "traffic": None, "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as td
+        torch.cuda.set_device(local_rank)
+        td.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist = td
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

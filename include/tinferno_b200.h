@@ -1,0 +1,161 @@
+/* tinferno-b200: B200 (sm_100a) decode/prefill engine for Llama-style GGUF models.
+ *
+ * C-ABI of libtinferno_b200.so.  Plain pointers and sizes only; every entry point returns
+ * an int status (0 = ok) and never throws or exits.  The text of the last failure is
+ * available from tf_cuda_last_error().
+ *
+ * The model-level calls replace the reference engine's C++ Model class
+ * (RohanDisa/agent-serve src/model.hpp:24-90); the tf_op_* calls replace its op functions
+ * one for one and take DEVICE pointers (they exist for the cfg3 kernel sweep and for
+ * op-level parity tests).  Each declaration cites the reference interface it replaces.
+ */
+#ifndef TINFERNO_B200_H
+#define TINFERNO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TF_API __attribute__((visibility("default")))
+#else
+#define TF_API
+#endif
+
+/* ggml type ids (src/common.hpp:99 DType). */
+enum { TF_F32 = 0, TF_F16 = 1, TF_Q4_0 = 2, TF_Q4_1 = 3, TF_Q8_0 = 8, TF_Q6_K = 14 };
+
+/* KV cache element type.  F32 is the reference's own cache type (src/kvcache.hpp:26-27). */
+enum { TF_KV_F32 = 0, TF_KV_F16 = 1, TF_KV_BF16 = 2 };
+
+/* One GGUF tensor as the reference's Tensor describes it (src/tensor.hpp:7-23): ne[0] is
+ * the innermost dimension (K for 2-D weights), data points at the tensor's bytes in their
+ * GGUF block layout (host memory; the library copies them into HBM). */
+typedef struct tf_tensor_desc {
+    const char* name;
+    int ggml_type;
+    int ndim;
+    int64_t ne[4];
+    const void* data;
+    size_t nbytes;
+} tf_tensor_desc;
+
+/* Hyper-parameters as the reference derives them from GGUF keys (src/model.cpp:14-41). */
+typedef struct tf_hparams {
+    int n_vocab, n_embd, n_ff, n_layer, n_head, n_kv_head, head_dim;
+    float rms_eps;
+    int rope_llama3; /* 0 = standard RoPE, 1 = llama3 frequency scaling */
+    float rope_theta, rope_scale, rope_low_freq_f, rope_high_freq_f, rope_orig_ctx;
+    int bos, eos;
+} tf_hparams;
+
+/* Engine options.  max_seq replaces RunConfig::max_seq (src/common.hpp:112); max_batch is
+ * the number of independent sequence slots (the reference has one, src/model.hpp:29-31). */
+typedef struct tf_options {
+    int max_seq;
+    int max_batch;
+    int device;
+    int kv_type;   /* TF_KV_* */
+    int use_graph; /* 1: capture the decode step in a CUDA graph (default) */
+} tf_options;
+
+typedef struct tf_model tf_model;
+
+/* Model(const std::string& path, const RunConfig&)  src/model.hpp:26, src/model.cpp:9-78.
+ * Uploads every tensor once into HBM (native block layouts), sizes the KV cache and the
+ * scratch, and precomputes the RoPE cos/sin table with the reference's own formula. */
+TF_API int tf_cuda_create(const tf_tensor_desc* tensors, int n_tensors, const tf_hparams* hp,
+                   const tf_options* opt, tf_model** out);
+
+/* ~Model.  Releases every device allocation and the graph. */
+TF_API int tf_cuda_destroy(tf_model* m);
+
+/* Model::prefill(const int* tokens, int n, float* logits)  src/model.hpp:29, model.cpp:183-195.
+ * Consumes tokens[0..n) of sequence `seq` at positions n_pos..n_pos+n-1; writes the
+ * logits of the last token to `logits` (host, n_vocab floats) when non-null; when
+ * `argmax_out` is non-null writes the greedy id (sample_greedy, src/sampler.cpp:8-13). */
+TF_API int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logits,
+                    int* argmax_out);
+
+/* Model::decode(int token, float* logits)  src/model.hpp:31, model.cpp:197-208. */
+TF_API int tf_cuda_decode(tf_model* m, int seq, int token, float* logits, int* argmax_out);
+
+/* The CLI's greedy loop (src/main.cpp:112-122 at --temp 0): starting from `first_token`
+ * (the argmax of the prefill logits), n times { append token; stop if token == eos and
+ * i > 0 (eos < 0 disables the rule); decode(token) } with the argmax fed back on the
+ * device and no host round trip.  Writes the accepted ids to out_ids and their count to
+ * *n_out; the sequence's position then matches the reference after the same loop. */
+TF_API int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eos, int* out_ids,
+                            int* n_out);
+
+/* Batched decode: one step for B sequences (distinct slots), token[b] appended to
+ * seq_ids[b].  argmax_out[b] (host) receives each greedy id; logits (host, B*n_vocab) is
+ * optional.  No reference counterpart: the reference decodes one sequence per Model. */
+TF_API int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int B,
+                         int* argmax_out, float* logits);
+
+/* Model::reset()  src/model.cpp:80-83 (one slot; seq < 0 resets every slot). */
+TF_API int tf_cuda_reset(tf_model* m, int seq);
+
+/* Accessors: Model::n_pos / n_vocab / weight_bytes  src/model.hpp:35-43. */
+TF_API int tf_cuda_n_pos(tf_model* m, int seq);
+TF_API int tf_cuda_n_vocab(tf_model* m);
+TF_API unsigned long long tf_cuda_weight_bytes(tf_model* m);
+/* cudaStream_t the model runs on (for callers that time it with CUDA events). */
+TF_API void* tf_cuda_stream(tf_model* m);
+/* Kernels launched per decode step (for launch accounting). */
+TF_API int tf_cuda_kernels_per_step(tf_model* m);
+
+/* Message of the last failure on this thread (m may be NULL). */
+TF_API const char* tf_cuda_last_error(tf_model* m);
+
+/* ---- op level: DEVICE pointers, launched on `stream` (NULL = default stream) ----------- */
+
+/* matmul(float* C, const float* A, const Tensor& W, int M, const Exec&)  src/matmul.hpp:9:
+ * C[M][N] = A[M][K] . W[N][K]^T, W in its GGUF block layout (row-major, ne0 = K). */
+TF_API int tf_op_matmul(float* C, const float* A, int ggml_type, const void* W, int N, int K, int M,
+                 void* stream);
+
+/* dequant_row(float* out, const Tensor& t, int64_t row)  src/quant.hpp:42: out[i][K] is
+ * row rows[i] of W (embedding lookup). */
+TF_API int tf_op_dequant_rows(float* out, int ggml_type, const void* W, int K, const int* rows,
+                       int n_rows, void* stream);
+
+/* rmsnorm(out, x, weight, n, eps)  src/layers.hpp:7, applied to `rows` rows of length n. */
+TF_API int tf_op_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps,
+                  void* stream);
+
+/* silu_mul(gate, up, n)  src/layers.hpp:8 */
+TF_API int tf_op_silu_mul(float* gate, const float* up, int n, void* stream);
+
+/* softmax(x, n)  src/layers.hpp:10, applied to `rows` rows of length n. */
+TF_API int tf_op_softmax(float* x, int n, int rows, void* stream);
+
+/* apply_rope_many(x, seq, n_heads, head_dim, pos0, freq)  src/attention.hpp:25. */
+TF_API int tf_op_rope(float* x, int seq, int n_heads, int head_dim, int pos0, const float* freq,
+               void* stream);
+
+/* attn_decode(out, q, cache, layer, n_heads, n_kv_heads, head_dim, n_pos)
+ * src/attention.hpp:27-28, over one layer's cache in the engine's layout
+ * [n_kv_heads][cap][head_dim] of kv_type (TF_KV_*). */
+TF_API int tf_op_attn_decode(float* out, const float* q, const void* k_cache, const void* v_cache,
+                      int kv_type, int cap, int n_pos, int n_heads, int n_kv_heads, int head_dim,
+                      void* stream);
+
+/* attn_prefill(out, q, k, v, seq, n_heads, n_kv_heads, head_dim)  src/attention.hpp:29-30:
+ * causal attention within the chunk; q [seq][n_heads][hd], k/v [seq][n_kv][hd]. */
+TF_API int tf_op_attn_prefill(float* out, const float* q, const float* k, const float* v, int seq,
+                       int n_heads, int n_kv_heads, int head_dim, void* stream);
+
+/* sample_greedy(logits, n)  src/sampler.hpp:9: out[r] = first index of the maximum of row r. */
+TF_API int tf_op_argmax(const float* logits, int n, int rows, int* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
