@@ -24,6 +24,11 @@ __device__ __forceinline__ float kv_load(const void* base, long long idx, int t)
     if (t == KV_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);
     return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
 }
+__device__ __forceinline__ float kv_round(float v, int t) {
+    if (t == KV_F32) return v;
+    if (t == KV_F16) return __half2float(__float2half_rn(v));
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
 __device__ __forceinline__ void kv_store(void* base, long long idx, int t, float v) {
     if (t == KV_F32) reinterpret_cast<float*>(base)[idx] = v;
     else if (t == KV_F16) reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
@@ -38,11 +43,60 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) 
     b = __fmaf_rn(x0, s, __fmul_rn(x1, c));
 }
 
+// Shared memory of one CTA: the K tile (row stride hd+1, so threads reading consecutive
+// positions hit distinct banks) and the V tile of its <= AT_CHUNK positions, in fp32.
+static inline size_t attn_smem_bytes(int hd) { return (size_t)AT_CHUNK * (2 * hd + 1) * sizeof(float); }
+
+// Loads `n` consecutive cache elements starting at element `e0` into dst[] as floats, all
+// loads in flight before the stores (one memory round trip), 16-byte vectors.
+__device__ __forceinline__ void load_tile(float* dst, int dst_stride, int hd, const void* base, long long e0, int np,
+                                          int kv_type) {
+    const int tid = threadIdx.x;
+    const int per_vec = kv_type == KV_F32 ? 4 : 8;      // elements per 16-byte vector
+    const int nvec = np * hd / per_vec;
+    for (int v0 = tid; v0 < nvec; v0 += AT_THREADS * 4) {
+        uint4 r[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int v = v0 + u * AT_THREADS;
+            if (v < nvec) r[u] = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + (e0 * (kv_type == KV_F32 ? 4 : 2)))[v];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int v = v0 + u * AT_THREADS;
+            if (v >= nvec) continue;
+            const int e = v * per_vec;
+            const int p = e / hd, d = e % hd;
+            float* o = dst + (size_t)p * dst_stride + d;
+            if (kv_type == KV_F32) {
+                const float4 f = *reinterpret_cast<const float4*>(&r[u]);
+                o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
+            } else {
+                const uint32_t w4[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t lo = w4[j] & 0xFFFFu, hi = w4[j] >> 16;
+                    if (kv_type == KV_F16) {
+                        o[2 * j] = __half2float(__ushort_as_half((unsigned short)lo));
+                        o[2 * j + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+                    } else {
+                        o[2 * j] = __uint_as_float(lo << 16);
+                        o[2 * j + 1] = __uint_as_float(hi << 16);
+                    }
+                }
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
+    extern __shared__ float tile[];
     __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
     __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
-    __shared__ float sc[AT_MAX_REP][AT_MAX_CHUNK];
+    __shared__ float sc[AT_MAX_REP][AT_CHUNK];
     __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP];
+    __shared__ float cw[AT_MAX_REP][AT_MAX_SPLIT];
+    __shared__ float cden[AT_MAX_REP];
     __shared__ int last_s;
 
     pdl_trigger();
@@ -52,26 +106,41 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
     const int slot = a.slots ? a.slots[m] : 0;
     const int pos = a.fresh ? a.pos[slot] : a.n_pos_fixed - 1;
-    const int n_pos = pos + 1;
     if (a.fresh && (pos < 0 || pos >= a.cap)) {
-        if (tid == 0) atomicCAS(a.err, 0, ERR_POS);
+        if (tid == 0 && split == 0) atomicCAS(a.err, 0, ERR_POS);
         return;
     }
+    const int n_pos = pos + 1;
+    // positions [ws, n_pos); ws > 0 only inside a prefill chunk, whose attention sees the
+    // chunk alone (attn_prefill, src/attention.cpp:82-111)
+    const int ws = (a.fresh && a.wstart) ? min(max(a.wstart[slot], 0), pos) : 0;
+    const int n_att = n_pos - ws;
+    const int nsp = min((int)gridDim.y, (n_att + AT_CHUNK - 1) / AT_CHUNK);  // active splits
+    if (split >= nsp) return;
+    const int chunk = (n_att + nsp - 1) / nsp;
+    const int p0 = ws + split * chunk;
+    const int p1 = min(n_pos, p0 + chunk);
+    const int np = max(0, p1 - p0);
+    float* ks = tile;                                  // [AT_CHUNK][hd + 1]
+    float* vs = tile + (size_t)AT_CHUNK * (hd + 1);    // [AT_CHUNK][hd]
+
     const float* row = a.qkv + (size_t)m * a.ld_qkv;
     const float* q = row + (size_t)kvh * n_rep * hd;
     const size_t cache_off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd;
 
-    // query heads of this group (rotated when fresh), new key/value
+    // 1) query heads of the group, new k/v, cached K/V of this split: independent loads
     for (int i = tid; i < n_rep * hd; i += AT_THREADS) qs[i / hd][i % hd] = q[i];
-    if (a.fresh) {
-        const float* kr = row + (size_t)a.n_head * hd + (size_t)kvh * hd;
-        const float* vr = row + (size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd;
+    if (a.fresh)
         for (int i = tid; i < hd; i += AT_THREADS) {
-            kn[i] = kr[i];
-            vn[i] = vr[i];
+            kn[i] = row[(size_t)a.n_head * hd + (size_t)kvh * hd + i];
+            vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
         }
-    }
+    const int np_cached = (a.fresh && p1 == n_pos) ? np - 1 : np;  // the new position is not read
+    load_tile(ks, hd + 1, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type);
+    load_tile(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type);
     __syncthreads();
+
+    // 2) RoPE (fresh): the host table holds the reference's float cos/sin of pos*freq
     if (a.fresh) {
         const float* cp = a.cosb + (size_t)pos * d2;
         const float* sp = a.sinb + (size_t)pos * d2;
@@ -86,37 +155,29 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
                 kv_store(a.kc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, kn[i]);
                 kv_store(a.vc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, vn[i]);
             }
+        if (p1 == n_pos)
+            for (int i = tid; i < hd; i += AT_THREADS) {
+                // the new key/value enter at the stored precision, as later steps read them
+                ks[(size_t)(np - 1) * (hd + 1) + i] = kv_round(kn[i], a.kv_type);
+                vs[(size_t)(np - 1) * hd + i] = kv_round(vn[i], a.kv_type);
+            }
+        __syncthreads();
     }
 
-    // positions of this split: [ws, n_pos) split evenly; ws > 0 only inside a prefill
-    // chunk, whose attention sees the chunk alone (attn_prefill, src/attention.cpp:82-111)
-    const int ws = (a.fresh && a.wstart) ? min(max(a.wstart[slot], 0), pos) : 0;
-    const int chunk = (n_pos - ws + a.n_split - 1) / a.n_split;
-    const int p0 = ws + split * chunk;
-    const int p1 = min(n_pos, p0 + chunk);
-    const int np = max(0, p1 - p0);
+    // 3) scores: thread per (head, position), scale * dot(q, k) (attn_decode, src/attention.cpp:63-64)
     const float scale = 1.0f / sqrtf((float)hd);
-
-    // scores: warp per position, lanes over head_dim
-    for (int pi = warp; pi < np; pi += AT_THREADS / 32) {
-        const int p = p0 + pi;
-        float kv[AT_MAX_HD / 32];
-        const int nr = (hd + 31) / 32;
-        for (int r = 0; r < nr; ++r) {
-            const int d = lane + 32 * r;
-            kv[r] = d >= hd ? 0.f
-                    : (a.fresh && p == pos) ? kn[d]
-                                            : kv_load(a.kc, (long long)(cache_off + (size_t)p * hd + d), a.kv_type);
+    for (int i = tid; i < n_rep * np; i += AT_THREADS) {
+        const int h = i / np, p = i % np;
+        const float* kp = ks + (size_t)p * (hd + 1);
+        float s0 = 0.f, s1 = 0.f;
+        for (int d = 0; d < hd; d += 2) {
+            s0 = fmaf(qs[h][d], kp[d], s0);
+            s1 = fmaf(qs[h][d + 1], kp[d + 1], s1);
         }
-        for (int h = 0; h < n_rep; ++h) {
-            float s = 0.f;
-            for (int r = 0; r < nr; ++r) s = fmaf(lane + 32 * r < hd ? qs[h][lane + 32 * r] : 0.f, kv[r], s);
-            s = warp_sum(s);
-            if (lane == 0) sc[h][pi] = scale * s;
-        }
+        sc[h][p] = scale * (s0 + s1);
     }
     __syncthreads();
-    // per-head max and exp-sum over the split (max-subtracted, as softmax, src/layers.cpp:25-35)
+    // 4) max-subtracted exponentials per head (softmax, src/layers.cpp:25-35)
     for (int h = warp; h < n_rep; h += AT_THREADS / 32) {
         float mx = -INFINITY;
         for (int i = lane; i < np; i += 32) mx = fmaxf(mx, sc[h][i]);
@@ -134,54 +195,70 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
         }
     }
     __syncthreads();
-    // weighted V: thread per (head, dim)
+    // 5) weighted V: thread per (head, dim)
     for (int i = tid; i < n_rep * hd; i += AT_THREADS) {
         const int h = i / hd, d = i % hd;
-        float acc = 0.f;
-        for (int pi = 0; pi < np; ++pi) {
-            const int p = p0 + pi;
-            const float v = (a.fresh && p == pos) ? vn[d] : kv_load(a.vc, (long long)(cache_off + (size_t)p * hd + d), a.kv_type);
-            acc = fmaf(sc[h][pi], v, acc);
+        float acc0 = 0.f, acc1 = 0.f;
+        int p = 0;
+        for (; p + 1 < np; p += 2) {
+            acc0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], acc0);
+            acc1 = fmaf(sc[h][p + 1], vs[(size_t)(p + 1) * hd + d], acc1);
         }
+        if (p < np) acc0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], acc0);
+        const float acc = acc0 + acc1;
         const int head = kvh * n_rep + h;
-        if (a.n_split == 1) {
+        if (nsp == 1) {
             a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = acc / l_s[h];
         } else {
             float* pp = a.part + (((size_t)m * a.n_head + head) * a.n_split + split) * (hd + 2);
             pp[2 + d] = acc;
             if (d == 0) {
-                pp[0] = np > 0 ? mx_s[h] : -INFINITY;
+                pp[0] = mx_s[h];
                 pp[1] = l_s[h];
             }
         }
     }
-    if (a.n_split == 1) return;
+    if (nsp == 1) return;
 
-    // last CTA of (row, kv head) combines the splits
+    // 6) the last CTA of (row, kv head) combines the active splits
     __threadfence();
     __syncthreads();
     if (tid == 0) {
         const unsigned t = atomicAdd(&a.counters[(size_t)m * a.n_kv + kvh], 1u);
-        last_s = (t == (unsigned)a.n_split - 1);
+        last_s = (t == (unsigned)nsp - 1);
     }
     __syncthreads();
     if (!last_s) return;
     __threadfence();
+    const float* pbase = a.part + ((size_t)m * a.n_head + (size_t)kvh * n_rep) * a.n_split * (hd + 2);
+    for (int i = tid; i < n_rep * nsp; i += AT_THREADS) {
+        const int h = i / nsp, s = i % nsp;
+        cw[h][s] = __ldcg(pbase + ((size_t)h * a.n_split + s) * (hd + 2));
+    }
+    __syncthreads();
+    if (tid < n_rep) {
+        float M = -INFINITY;
+        for (int s = 0; s < nsp; ++s) M = fmaxf(M, cw[tid][s]);
+        float den = 0.f;
+        for (int s = 0; s < nsp; ++s) {
+            const float w = expf(cw[tid][s] - M);
+            den = fmaf(w, __ldcg(pbase + ((size_t)tid * a.n_split + s) * (hd + 2) + 1), den);
+            cw[tid][s] = w;
+        }
+        cden[tid] = den;
+    }
+    __syncthreads();
     for (int i = tid; i < n_rep * hd; i += AT_THREADS) {
         const int h = i / hd, d = i % hd;
-        const int head = kvh * n_rep + h;
-        const float* pb = a.part + (((size_t)m * a.n_head + head) * a.n_split) * (hd + 2);
-        float M = -INFINITY;
-        for (int s = 0; s < a.n_split; ++s) M = fmaxf(M, __ldcg(pb + (size_t)s * (hd + 2)));
-        float num = 0.f, den = 0.f;
-        for (int s = 0; s < a.n_split; ++s) {
-            const float ms = __ldcg(pb + (size_t)s * (hd + 2));
-            if (ms == -INFINITY) continue;
-            const float w = expf(ms - M);
-            den = fmaf(w, __ldcg(pb + (size_t)s * (hd + 2) + 1), den);
-            num = fmaf(w, __ldcg(pb + (size_t)s * (hd + 2) + 2 + d), num);
+        const float* pb = pbase + (size_t)h * a.n_split * (hd + 2) + 2 + d;
+        float num0 = 0.f, num1 = 0.f;
+        int s = 0;
+        for (; s + 1 < nsp; s += 2) {
+            num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
+            num1 = fmaf(cw[h][s + 1], __ldcg(pb + (size_t)(s + 1) * (hd + 2)), num1);
         }
-        a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = num / den;
+        if (s < nsp) num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
+        a.out[(size_t)m * a.ld_out + (size_t)(kvh * n_rep + h) * hd + d] = (num0 + num1) / cden[h];
     }
     if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
 }
@@ -245,18 +322,32 @@ __global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillA
 
 // ---- host ------------------------------------------------------------------------------
 int attn_pick_split(int cap) {
-    int s = (cap + AT_MAX_CHUNK - 1) / AT_MAX_CHUNK;
-    return s < 1 ? 1 : s;
+    const int s = (cap + AT_CHUNK - 1) / AT_CHUNK;
+    return s < 1 ? 1 : (s > AT_MAX_SPLIT ? AT_MAX_SPLIT : s);
 }
 
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
-    if (a.hd > AT_MAX_HD || a.hd % 2 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
+    if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
     const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;
-    if ((max_pos + a.n_split - 1) / a.n_split > AT_MAX_CHUNK) return cudaErrorInvalidValue;
+    if ((max_pos + a.n_split - 1) / a.n_split > AT_CHUNK || a.n_split > AT_MAX_SPLIT) return cudaErrorInvalidValue;
+    const size_t smem = attn_smem_bytes(a.hd);
+    static bool attrs[64] = {false};  // set once per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attrs[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)attn_smem_bytes(AT_MAX_HD));
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+        if (e != cudaSuccess) return e;
+        attrs[dev] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv, a.n_split, M);
     cfg.blockDim = dim3(AT_THREADS);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

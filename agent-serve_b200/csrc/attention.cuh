@@ -6,7 +6,8 @@
 namespace tfb {
 
 constexpr int AT_THREADS = 128;
-constexpr int AT_MAX_CHUNK = 256;  // positions per CTA
+constexpr int AT_CHUNK = 64;       // positions per CTA (decode)
+constexpr int AT_MAX_SPLIT = 256;  // position splits per (row, kv head): contexts up to 16384
 constexpr int AT_MAX_REP = 8;      // query heads per kv head
 constexpr int AT_MAX_HD = 128;
 

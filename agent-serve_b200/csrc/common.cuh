@@ -15,7 +15,7 @@ enum : int { T_F32 = 0, T_F16 = 1, T_Q4_0 = 2, T_Q4_1 = 3, T_Q8_0 = 8, T_Q6_K = 
 enum : int { KV_F32 = 0, KV_F16 = 1, KV_BF16 = 2 };
 
 // Error codes written into the device error word (first writer wins).
-enum : int { ERR_NONE = 0, ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_BAD_TOKEN = 3, ERR_POS = 4 };
+enum : int { ERR_NONE = 0, ERR_WAIT_FULL = 1, ERR_WAIT_EMPTY = 2, ERR_BAD_TOKEN = 3, ERR_POS = 4, ERR_GRID_SYNC = 5 };
 
 // Spin budget of every bounded wait: polls of mbarrier.try_wait with a nanosleep back-off,
 // on the order of a second in total.
@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     for (int i = 0; i < kWaitPolls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if (abort && *abort) return false;
-        if (i > 16) __nanosleep(256);
+        if (i > (1 << 14)) __nanosleep(256);  // only once the wait is clearly not a stall
     }
     if (err) atomicCAS(err, 0, code);
     if (abort) *abort = 1;

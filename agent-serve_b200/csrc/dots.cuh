@@ -1,0 +1,230 @@
+// Row-dot routines shared by the GEMV kernel (gemv.cu) and the decode megakernel
+// (decode_mk.cu): fp32 activations (shared memory, xpad layout) times GGUF block weights
+// (shared memory, native layout), fp32 accumulation.
+#pragma once
+
+#include "common.cuh"
+
+namespace tfb {
+
+__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
+
+// ---- Q8_0 unit dot with the activation held in registers --------------------------------
+// One 64-element unit (two 34-byte blocks, 17 aligned words at wp) of one row against the
+// lane's 64 activations xr[] (kept in registers for a whole phase, so shared-memory traffic
+// is the weights only).  int8 -> fp32 by the exact construction 0x4B0000xx - (2^23 + 128);
+// products on the packed fp32x2 pipe with four independent accumulators per block.
+// acc += dA * sum(x*qA) + dB * sum(x*qB)  (the block-scale form of src/quant.cpp:266-283).
+__device__ __forceinline__ void unit_dot_q8_reg(const uint32_t* wp, const float (&xr)[64], float& acc) {
+    const float2 kBias = make_float2(-8388736.0f, -8388736.0f);
+    uint32_t w[17];
+#pragma unroll
+    for (int i = 0; i < 17; ++i) w[i] = wp[i];
+    const float dA = h2f(w[0]);
+    const float dB = h2f(w[8] >> 16);
+#pragma unroll
+    for (int i = 0; i < 17; ++i) w[i] ^= 0x80808080u;
+    float2 sA[4], sB[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) sA[r] = sB[r] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+        float qa[4], qb[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int ja = 2 + 4 * g + e, jb = 36 + 4 * g + e;  // bytes of block A / B in the unit
+            qa[e] = __int_as_float((int)__byte_perm(w[ja >> 2], 0x4B000000u, 0x7650u | (uint32_t)(ja & 3)));
+            qb[e] = __int_as_float((int)__byte_perm(w[jb >> 2], 0x4B000000u, 0x7650u | (uint32_t)(jb & 3)));
+        }
+        const float2 qa0 = __fadd2_rn(make_float2(qa[0], qa[1]), kBias), qa1 = __fadd2_rn(make_float2(qa[2], qa[3]), kBias);
+        const float2 qb0 = __fadd2_rn(make_float2(qb[0], qb[1]), kBias), qb1 = __fadd2_rn(make_float2(qb[2], qb[3]), kBias);
+        const int r0 = (2 * g) & 3, r1 = (2 * g + 1) & 3;
+        sA[r0] = __ffma2_rn(make_float2(xr[4 * g], xr[4 * g + 1]), qa0, sA[r0]);
+        sA[r1] = __ffma2_rn(make_float2(xr[4 * g + 2], xr[4 * g + 3]), qa1, sA[r1]);
+        sB[r0] = __ffma2_rn(make_float2(xr[32 + 4 * g], xr[32 + 4 * g + 1]), qb0, sB[r0]);
+        sB[r1] = __ffma2_rn(make_float2(xr[32 + 4 * g + 2], xr[32 + 4 * g + 3]), qb1, sB[r1]);
+    }
+    const float2 a2 = __fadd2_rn(__fadd2_rn(sA[0], sA[1]), __fadd2_rn(sA[2], sA[3]));
+    const float2 b2 = __fadd2_rn(__fadd2_rn(sB[0], sB[1]), __fadd2_rn(sB[2], sB[3]));
+    acc = fmaf(dA, a2.x + a2.y, acc);
+    acc = fmaf(dB, b2.x + b2.y, acc);
+}
+
+// ---- Q8_0 fast path: one row segment of `units` 64-element units -----------------------
+// Products and partial sums use the packed fp32x2 pipe of sm_100 (__ffma2_rn / __fadd2_rn):
+// two weights per instruction, each lane still forming exact fp32 x*q products.
+template <int MAXM>
+__device__ __forceinline__ void dot_q8_fast(const uint8_t* seg, int units, const float* xseg, int xl, int M,
+                                            int lane, float (&acc)[MAXM]) {
+    const float2 kBias = make_float2(-8388736.0f, -8388736.0f);
+    for (int u = lane; u < units; u += 32) {
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(seg + (size_t)u * 68);
+        uint32_t w[17];
+#pragma unroll
+        for (int i = 0; i < 17; ++i) w[i] = wp[i];
+        const float dA = h2f(w[0]);
+        const float dB = h2f(w[8] >> 16);
+#pragma unroll
+        for (int i = 0; i < 17; ++i) w[i] ^= 0x80808080u;
+        const float* xu = xseg + (size_t)u * 68;
+        float2 sA[MAXM][2], sB[MAXM][2];
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) sA[m][r] = sB[m][r] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+            float qa[4], qb[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int ja = 2 + 4 * g + e;  // byte of block A within the unit
+                const int jb = 36 + 4 * g + e; // byte of block B
+                qa[e] = __int_as_float((int)__byte_perm(w[ja >> 2], 0x4B000000u, 0x7650u | (uint32_t)(ja & 3)));
+                qb[e] = __int_as_float((int)__byte_perm(w[jb >> 2], 0x4B000000u, 0x7650u | (uint32_t)(jb & 3)));
+            }
+            const float2 qa0 = __fadd2_rn(make_float2(qa[0], qa[1]), kBias);
+            const float2 qa1 = __fadd2_rn(make_float2(qa[2], qa[3]), kBias);
+            const float2 qb0 = __fadd2_rn(make_float2(qb[0], qb[1]), kBias);
+            const float2 qb1 = __fadd2_rn(make_float2(qb[2], qb[3]), kBias);
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m < M) {
+                    const float4 xa = *reinterpret_cast<const float4*>(xu + m * xl + 4 * g);
+                    const float4 xb = *reinterpret_cast<const float4*>(xu + m * xl + 32 + 4 * g);
+                    float2& a2 = sA[m][g & 1];
+                    float2& b2 = sB[m][g & 1];
+                    a2 = __ffma2_rn(make_float2(xa.x, xa.y), qa0, a2);
+                    a2 = __ffma2_rn(make_float2(xa.z, xa.w), qa1, a2);
+                    b2 = __ffma2_rn(make_float2(xb.x, xb.y), qb0, b2);
+                    b2 = __ffma2_rn(make_float2(xb.z, xb.w), qb1, b2);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            const float2 a2 = __fadd2_rn(sA[m][0], sA[m][1]);
+            const float2 b2 = __fadd2_rn(sB[m][0], sB[m][1]);
+            acc[m] = fmaf(dA, a2.x + a2.y, acc[m]);
+            acc[m] = fmaf(dB, b2.x + b2.y, acc[m]);
+        }
+    }
+}
+
+// ---- generic path: one lane per block (32 elements; 256 for Q6_K) ----------------------
+// Produces either (scale, q[32]) with the block scale applied to the block sum (Q8_0, Q4_0,
+// as src/quant.cpp:266-363 do) or dequantised w[32] (Q4_1, Q6_K, F16, F32, as
+// dequant_row + dot_f32 do).
+template <int MAXM>
+__device__ __forceinline__ void dot_generic(int t, const uint8_t* seg, int e0, int nelem, const float* xs, int xl,
+                                            int M, int lane, float (&acc)[MAXM]) {
+    const int be = (t == T_Q6_K) ? 256 : 32;
+    const int bb = (t == T_F32) ? 128 : (t == T_F16) ? 64 : blk_bytes(t);
+    const int nblk = nelem / be;
+    for (int b = lane; b < nblk; b += 32) {
+        const uint8_t* p = seg + (size_t)b * bb;
+        const int groups = be / 32;
+        for (int g = 0; g < groups; ++g) {
+            float w[32];
+            float scale = 1.f;
+            bool scaled = false;
+            if (t == T_Q8_0) {
+                scale = h2f(ld_u16(p));
+                scaled = true;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) w[j] = (float)(int8_t)p[2 + j];
+            } else if (t == T_Q4_0) {
+                scale = h2f(ld_u16(p));
+                scaled = true;
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t q = p[2 + j];
+                    w[j] = (float)((int)(q & 15u) - 8);
+                    w[j + 16] = (float)((int)(q >> 4) - 8);
+                }
+            } else if (t == T_Q4_1) {
+                const float d = h2f(ld_u16(p)), mn = h2f(ld_u16(p + 2));
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const uint32_t q = p[4 + j];
+                    w[j] = __fmaf_rn((float)(q & 15u), d, mn);
+                    w[j + 16] = __fmaf_rn((float)(q >> 4), d, mn);
+                }
+            } else if (t == T_Q6_K) {
+                const int h = g >> 2, tq = g & 3;
+                const float d = h2f(ld_u16(p + 208));
+                const uint8_t* ql = p + 64 * h + ((tq & 1) ? 32 : 0);
+                const uint8_t* qh = p + 128 + 32 * h;
+                const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + 8 * h + 2 * tq);
+                const float ds0 = __fmul_rn(d, (float)sc[0]);
+                const float ds1 = __fmul_rn(d, (float)sc[1]);
+#pragma unroll
+                for (int l = 0; l < 32; ++l) {
+                    const uint32_t lo = (tq >= 2) ? (ql[l] >> 4) : (ql[l] & 15u);
+                    const uint32_t hi = (qh[l] >> (2 * tq)) & 3u;
+                    const int q = (int)(lo | (hi << 4)) - 32;
+                    w[l] = __fmul_rn(l < 16 ? ds0 : ds1, (float)q);
+                }
+            } else if (t == T_F16) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) w[j] = h2f(ld_u16(p + 2 * j));
+            } else {  // F32: rows are 4-byte aligned
+                const float* fp = reinterpret_cast<const float*>(p);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) w[j] = fp[j];
+            }
+            const int ebase = e0 + b * be + 32 * g;
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m < M) {
+                    const float* xm = xs + m * xl;
+                    float s = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) s = fmaf(xm[xpad(ebase + j)], w[j], s);
+                    acc[m] = scaled ? fmaf(scale, s, acc[m]) : acc[m] + s;
+                }
+            }
+        }
+    }
+}
+
+// ---- embedding row dequantisation into shared memory (dequant_row, src/quant.cpp:133) ---
+static __device__ void embed_row(float* xm, const uint8_t* E, int t, long long rb, int K, long long tok, int nthreads) {
+    const uint8_t* row = E + tok * rb;
+    const int be = (t == T_Q6_K) ? 256 : 32;
+    const int bb = (t == T_F32) ? 128 : (t == T_F16) ? 64 : blk_bytes(t);
+    const int tid = threadIdx.x;
+    const int nb = K / be;
+    for (int b = tid; b < nb; b += nthreads) {
+        const uint8_t* p = row + (size_t)b * bb;
+        for (int g = 0; g < be / 32; ++g) {
+            const int e = b * be + 32 * g;
+            for (int j = 0; j < 32; ++j) {
+                float v;
+                if (t == T_Q8_0) {
+                    v = __fmul_rn(h2f(ld_u16(p)), (float)(int8_t)p[2 + j]);
+                } else if (t == T_Q4_0) {
+                    const uint32_t q = p[2 + (j & 15)];
+                    v = __fmul_rn(h2f(ld_u16(p)), (float)((int)((j < 16) ? (q & 15u) : (q >> 4)) - 8));
+                } else if (t == T_Q4_1) {
+                    const uint32_t q = p[4 + (j & 15)];
+                    v = __fmaf_rn((float)((j < 16) ? (q & 15u) : (q >> 4)), h2f(ld_u16(p)), h2f(ld_u16(p + 2)));
+                } else if (t == T_Q6_K) {
+                    const int h = g >> 2, tq = g & 3;
+                    const uint8_t* ql = p + 64 * h + ((tq & 1) ? 32 : 0);
+                    const uint8_t* qh = p + 128 + 32 * h;
+                    const int8_t sc = reinterpret_cast<const int8_t*>(p + 192 + 8 * h + 2 * tq)[j >> 4];
+                    const uint32_t lo = (tq >= 2) ? (ql[j] >> 4) : (ql[j] & 15u);
+                    const uint32_t hi = (qh[j] >> (2 * tq)) & 3u;
+                    v = __fmul_rn(__fmul_rn(h2f(ld_u16(p + 208)), (float)sc), (float)((int)(lo | (hi << 4)) - 32));
+                } else if (t == T_F16) {
+                    v = h2f(ld_u16(p + 2 * (32 * g + j)));
+                } else {
+                    v = reinterpret_cast<const float*>(p)[32 * g + j];
+                }
+                xm[xpad(e + j)] = v;
+            }
+        }
+    }
+}
+
+}  // namespace tfb

@@ -7,13 +7,14 @@
 #include <string>
 #include <vector>
 
-#include "../../include/tinferno_b200.h"
+#include "tinferno_b200.h"
 #include "gemv.cuh"
 
 namespace tfb {
 
 // kernels (gemv.cu, attention.cu, misc.cu)
 void gemv_plan(GemvArgs& a);
+void gemv_plan_w(GemvArgs& a, int warps, int budget);
 int gemv_grid(const GemvArgs& a, int num_sms);
 int gemv_max_rows(int K);
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl);

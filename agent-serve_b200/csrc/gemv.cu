@@ -17,187 +17,15 @@
 // conflict-free shared loads at a 17-word lane stride); int8 -> fp32 conversion uses the
 // exact magic-number construction 0x4B0000xx - (2^23 + 128) (one PRMT + one FADD), which
 // keeps the conversion off the 16/clk conversion pipe.
+#include <cstdlib>
+
+#include "dots.cuh"
 #include "gemv.cuh"
 
 namespace tfb {
 
 __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_u16(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8); }
-
-__device__ __forceinline__ float q8_magic(uint32_t wbiased, int byte) {
-    // wbiased holds four (q + 128) bytes; returns q of byte `byte` exactly.
-    return __int_as_float((int)__byte_perm(wbiased, 0x4B000000u, 0x7650u | (uint32_t)byte)) - 8388736.0f;
-}
-
-// ---- Q8_0 fast path: one row segment of `units` 64-element units -----------------------
-template <int MAXM>
-__device__ __forceinline__ void dot_q8_fast(const uint8_t* seg, int units, const float* xseg, int xl, int M,
-                                            int lane, float (&acc)[MAXM]) {
-    for (int u = lane; u < units; u += 32) {
-        const uint32_t* wp = reinterpret_cast<const uint32_t*>(seg + (size_t)u * 68);
-        uint32_t w[17];
-#pragma unroll
-        for (int i = 0; i < 17; ++i) w[i] = wp[i];
-        const float dA = h2f(w[0]);
-        const float dB = h2f(w[8] >> 16);
-#pragma unroll
-        for (int i = 0; i < 17; ++i) w[i] ^= 0x80808080u;
-        const float* xu = xseg + (size_t)u * 68;
-        float sA[MAXM], sB[MAXM];
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) sA[m] = sB[m] = 0.f;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-            float qa[4], qb[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int ja = 2 + 4 * g + e;        // byte of block A within the unit
-                qa[e] = q8_magic(w[ja >> 2], ja & 3);
-                const int jb = 36 + 4 * g + e;       // byte of block B
-                qb[e] = q8_magic(w[jb >> 2], jb & 3);
-            }
-#pragma unroll
-            for (int m = 0; m < MAXM; ++m) {
-                if (m < M) {
-                    const float4 xa = *reinterpret_cast<const float4*>(xu + m * xl + 4 * g);
-                    const float4 xb = *reinterpret_cast<const float4*>(xu + m * xl + 32 + 4 * g);
-                    sA[m] = fmaf(xa.x, qa[0], sA[m]);
-                    sA[m] = fmaf(xa.y, qa[1], sA[m]);
-                    sA[m] = fmaf(xa.z, qa[2], sA[m]);
-                    sA[m] = fmaf(xa.w, qa[3], sA[m]);
-                    sB[m] = fmaf(xb.x, qb[0], sB[m]);
-                    sB[m] = fmaf(xb.y, qb[1], sB[m]);
-                    sB[m] = fmaf(xb.z, qb[2], sB[m]);
-                    sB[m] = fmaf(xb.w, qb[3], sB[m]);
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
-            acc[m] = fmaf(dA, sA[m], acc[m]);
-            acc[m] = fmaf(dB, sB[m], acc[m]);
-        }
-    }
-}
-
-// ---- generic path: one lane per block (32 elements; 256 for Q6_K) ----------------------
-// Produces either (scale, q[32]) with the block scale applied to the block sum (Q8_0, Q4_0,
-// as src/quant.cpp:266-363 do) or dequantised w[32] (Q4_1, Q6_K, F16, F32, as
-// dequant_row + dot_f32 do).
-template <int MAXM>
-__device__ __forceinline__ void dot_generic(int t, const uint8_t* seg, int e0, int nelem, const float* xs, int xl,
-                                            int M, int lane, float (&acc)[MAXM]) {
-    const int be = (t == T_Q6_K) ? 256 : 32;
-    const int bb = (t == T_F32) ? 128 : (t == T_F16) ? 64 : blk_bytes(t);
-    const int nblk = nelem / be;
-    for (int b = lane; b < nblk; b += 32) {
-        const uint8_t* p = seg + (size_t)b * bb;
-        const int groups = be / 32;
-        for (int g = 0; g < groups; ++g) {
-            float w[32];
-            float scale = 1.f;
-            bool scaled = false;
-            if (t == T_Q8_0) {
-                scale = h2f(ld_u16(p));
-                scaled = true;
-#pragma unroll
-                for (int j = 0; j < 32; ++j) w[j] = (float)(int8_t)p[2 + j];
-            } else if (t == T_Q4_0) {
-                scale = h2f(ld_u16(p));
-                scaled = true;
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint32_t q = p[2 + j];
-                    w[j] = (float)((int)(q & 15u) - 8);
-                    w[j + 16] = (float)((int)(q >> 4) - 8);
-                }
-            } else if (t == T_Q4_1) {
-                const float d = h2f(ld_u16(p)), mn = h2f(ld_u16(p + 2));
-#pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const uint32_t q = p[4 + j];
-                    w[j] = __fmaf_rn((float)(q & 15u), d, mn);
-                    w[j + 16] = __fmaf_rn((float)(q >> 4), d, mn);
-                }
-            } else if (t == T_Q6_K) {
-                const int h = g >> 2, tq = g & 3;
-                const float d = h2f(ld_u16(p + 208));
-                const uint8_t* ql = p + 64 * h + ((tq & 1) ? 32 : 0);
-                const uint8_t* qh = p + 128 + 32 * h;
-                const int8_t* sc = reinterpret_cast<const int8_t*>(p + 192 + 8 * h + 2 * tq);
-                const float ds0 = __fmul_rn(d, (float)sc[0]);
-                const float ds1 = __fmul_rn(d, (float)sc[1]);
-#pragma unroll
-                for (int l = 0; l < 32; ++l) {
-                    const uint32_t lo = (tq >= 2) ? (ql[l] >> 4) : (ql[l] & 15u);
-                    const uint32_t hi = (qh[l] >> (2 * tq)) & 3u;
-                    const int q = (int)(lo | (hi << 4)) - 32;
-                    w[l] = __fmul_rn(l < 16 ? ds0 : ds1, (float)q);
-                }
-            } else if (t == T_F16) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) w[j] = h2f(ld_u16(p + 2 * j));
-            } else {  // F32: rows are 4-byte aligned
-                const float* fp = reinterpret_cast<const float*>(p);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) w[j] = fp[j];
-            }
-            const int ebase = e0 + b * be + 32 * g;
-#pragma unroll
-            for (int m = 0; m < MAXM; ++m) {
-                if (m < M) {
-                    const float* xm = xs + m * xl;
-                    float s = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) s = fmaf(xm[xpad(ebase + j)], w[j], s);
-                    acc[m] = scaled ? fmaf(scale, s, acc[m]) : acc[m] + s;
-                }
-            }
-        }
-    }
-}
-
-// ---- embedding row dequantisation into shared memory (dequant_row, src/quant.cpp:133) ---
-__device__ void embed_row(float* xm, const uint8_t* E, int t, long long rb, int K, long long tok) {
-    const uint8_t* row = E + tok * rb;
-    const int be = (t == T_Q6_K) ? 256 : 32;
-    const int bb = (t == T_F32) ? 128 : (t == T_F16) ? 64 : blk_bytes(t);
-    const int tid = threadIdx.x;
-    const int nb = K / be;
-    for (int b = tid; b < nb; b += GV_WARPS * 32) {
-        const uint8_t* p = row + (size_t)b * bb;
-        for (int g = 0; g < be / 32; ++g) {
-            const int e = b * be + 32 * g;
-            for (int j = 0; j < 32; ++j) {
-                float v;
-                if (t == T_Q8_0) {
-                    v = __fmul_rn(h2f(ld_u16(p)), (float)(int8_t)p[2 + j]);
-                } else if (t == T_Q4_0) {
-                    const uint32_t q = p[2 + (j & 15)];
-                    v = __fmul_rn(h2f(ld_u16(p)), (float)((int)((j < 16) ? (q & 15u) : (q >> 4)) - 8));
-                } else if (t == T_Q4_1) {
-                    const uint32_t q = p[4 + (j & 15)];
-                    v = __fmaf_rn((float)((j < 16) ? (q & 15u) : (q >> 4)), h2f(ld_u16(p)), h2f(ld_u16(p + 2)));
-                } else if (t == T_Q6_K) {
-                    const int h = g >> 2, tq = g & 3;
-                    const uint8_t* ql = p + 64 * h + ((tq & 1) ? 32 : 0);
-                    const uint8_t* qh = p + 128 + 32 * h;
-                    const int8_t sc = reinterpret_cast<const int8_t*>(p + 192 + 8 * h + 2 * tq)[j >> 4];
-                    const uint32_t lo = (tq >= 2) ? (ql[j] >> 4) : (ql[j] & 15u);
-                    const uint32_t hi = (qh[j] >> (2 * tq)) & 3u;
-                    v = __fmul_rn(__fmul_rn(h2f(ld_u16(p + 208)), (float)sc), (float)((int)(lo | (hi << 4)) - 32));
-                } else if (t == T_F16) {
-                    v = h2f(ld_u16(p + 2 * (32 * g + j)));
-                } else {
-                    v = reinterpret_cast<const float*>(p)[32 * g + j];
-                }
-                xm[xpad(e + j)] = v;
-            }
-        }
-    }
 }
 
 template <int MAXM>
@@ -210,7 +38,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     uint8_t* stages = smem + xbytes;
     float* red = reinterpret_cast<float*>(stages + (size_t)GV_STAGES * a.stage_bytes);  // [2][W][2][MAXM]
     double* redd = reinterpret_cast<double*>(red + 2 * GV_WARPS * 2 * MAXM);              // [W][MAXM]
-    uint64_t* full = reinterpret_cast<uint64_t*>(redd + GV_WARPS * MAXM);
+    float* pre = reinterpret_cast<float*>(redd + GV_WARPS * MAXM);                        // [MAXM][GV_PRE]
+    uint64_t* full = reinterpret_cast<uint64_t*>(pre + MAXM * GV_PRE);
     uint64_t* empty = full + GV_STAGES;
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + GV_STAGES);
     unsigned long long* ckey = reinterpret_cast<unsigned long long*>(empty + GV_STAGES + 1);
@@ -219,6 +48,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     const int i1 = (int)((long long)a.n_items * (blockIdx.x + 1) / gridDim.x);
     const int RI = GV_WARPS / a.KS;
     const int n_stages = (i1 - i0 + RI - 1) / RI;
+    const bool prefetched = (i1 - i0) <= GV_PRE && (a.epi == EPI_RESID || (a.epi == EPI_STORE && a.bias));
 
     if (tid == 0) {
         for (int s = 0; s < GV_STAGES; ++s) {
@@ -265,8 +95,27 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     }
 
     // ---------------- consumers: prologue ----------------
-    pdl_wait();
     const int nth = GV_WARPS * 32;
+    // static operands first (they do not depend on the previous kernel): bias of this
+    // CTA's rows and the RMSNorm weights of this thread's activation chunks
+    if (prefetched && a.epi == EPI_STORE)
+        for (int i = tid; i < i1 - i0; i += nth) pre[i] = a.bias[i0 + i];
+    const int nq = a.K >> 2;  // float4 chunks per activation row
+    float4 wn[GV_PRO_UNROLL];
+    const bool norm_regs = a.pro != PRO_COPY && nq <= nth * GV_PRO_UNROLL;
+    if (norm_regs) {
+#pragma unroll
+        for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+            const int c = tid + u * nth;
+            wn[u] = c < nq ? reinterpret_cast<const float4*>(a.norm_w)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+    pdl_wait();
+    if (prefetched && a.epi == EPI_RESID)
+        for (int i = tid; i < (i1 - i0) * a.M; i += nth) {
+            const int m = i / (i1 - i0), r = i % (i1 - i0);
+            pre[m * GV_PRE + r] = a.resid[(size_t)m * a.ldr + i0 + r];
+        }
     for (int m = 0; m < a.M; ++m) {
         float* xm = xs + m * xl;
         if (a.pro == PRO_EMBED_RMSNORM) {
@@ -275,25 +124,41 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
                 if (tid == 0) atomicCAS(a.err, 0, ERR_BAD_TOKEN);
                 tok = 0;
             }
-            embed_row(xm, a.embd, a.embd_type, a.embd_rb, a.K, tok);
-            named_bar_compute();
-            if (blockIdx.x == 0)
-                for (int e = tid; e < a.K; e += nth) a.x_out[(size_t)m * a.ldx + e] = xm[xpad(e)];
+            embed_row(xm, a.embd, a.embd_type, a.embd_rb, a.K, tok, GV_WARPS * 32);
         } else {
-            const float* xg = a.x + (size_t)m * a.ldx;
-            for (int e = tid; e < a.K; e += nth) xm[xpad(e)] = xg[e];
+            // all loads of a row issued before any store: one memory round trip
+            const float4* xg = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx);
+            for (int base = tid; base < nq; base += nth * GV_PRO_UNROLL) {
+                float4 v[GV_PRO_UNROLL];
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const int c = base + u * nth;
+                    if (c < nq) v[u] = xg[c];
+                }
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const int c = base + u * nth;
+                    if (c < nq) *reinterpret_cast<float4*>(xm + xpad(4 * c)) = v[u];
+                }
+            }
         }
     }
+    named_bar_compute();
+    if (a.pro == PRO_EMBED_RMSNORM && blockIdx.x == 0)
+        for (int m = 0; m < a.M; ++m)
+            for (int e = tid; e < a.K; e += nth) a.x_out[(size_t)m * a.ldx + e] = xs[m * xl + xpad(e)];
     if (a.pro != PRO_COPY) {
         // rmsnorm (src/layers.cpp:7-12): sum of squares in double, inv in float,
         // out = (x * inv) * w.
-        named_bar_compute();
         for (int m = 0; m < a.M; ++m) {
             const float* xm = xs + m * xl;
             double ss = 0.0;
-            for (int e = tid; e < a.K; e += nth) {
-                const double v = (double)xm[xpad(e)];
-                ss = fma(v, v, ss);
+            for (int c = tid; c < nq; c += nth) {
+                const float4 v = *reinterpret_cast<const float4*>(xm + xpad(4 * c));
+                ss = fma((double)v.x, (double)v.x, ss);
+                ss = fma((double)v.y, (double)v.y, ss);
+                ss = fma((double)v.z, (double)v.z, ss);
+                ss = fma((double)v.w, (double)v.w, ss);
             }
             ss = warp_sum_d(ss);
             if (lane == 0) redd[warp * MAXM + m] = ss;
@@ -304,7 +169,23 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             for (int w = 0; w < GV_WARPS; ++w) ss += redd[w * MAXM + m];
             const float inv = 1.0f / sqrtf((float)(ss / a.K) + a.eps);
             float* xm = xs + m * xl;
-            for (int e = tid; e < a.K; e += nth) xm[xpad(e)] = __fmul_rn(__fmul_rn(xm[xpad(e)], inv), a.norm_w[e]);
+            if (norm_regs) {
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const int c = tid + u * nth;
+                    if (c < nq) {
+                        float4* p = reinterpret_cast<float4*>(xm + xpad(4 * c));
+                        float4 v = *p;
+                        v.x = __fmul_rn(__fmul_rn(v.x, inv), wn[u].x);
+                        v.y = __fmul_rn(__fmul_rn(v.y, inv), wn[u].y);
+                        v.z = __fmul_rn(__fmul_rn(v.z, inv), wn[u].z);
+                        v.w = __fmul_rn(__fmul_rn(v.w, inv), wn[u].w);
+                        *p = v;
+                    }
+                }
+            } else {
+                for (int e = tid; e < a.K; e += nth) xm[xpad(e)] = __fmul_rn(__fmul_rn(xm[xpad(e)], inv), a.norm_w[e]);
+            }
         }
     }
     named_bar_compute();
@@ -321,29 +202,34 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         const bool ok = mbar_wait(&full[slot], (s / GV_STAGES) & 1, a.err, ERR_WAIT_FULL, abort_flag);
         const int si0 = i0 + s * RI, si1 = min(si0 + RI, i1);
         const int item = si0 + my_item;
-        float acc[2][MAXM];
+        float acc0[MAXM], acc1[MAXM];
 #pragma unroll
-        for (int p = 0; p < 2; ++p)
-#pragma unroll
-            for (int m = 0; m < MAXM; ++m) acc[p][m] = 0.f;
+        for (int m = 0; m < MAXM; ++m) acc0[m] = acc1[m] = 0.f;
         if (ok && item < si1) {
             const uintptr_t g = reinterpret_cast<uintptr_t>(a.W + (long long)si0 * a.P * a.rb);
             const uint8_t* sb = stages + (size_t)slot * a.stage_bytes + (g & 15);
             const uint8_t* ib = sb + (long long)my_item * a.P * a.rb;
-            for (int p = 0; p < a.P; ++p) {
-                const uint8_t* rowp = ib + (long long)p * a.rb;
-                float part[MAXM];
 #pragma unroll
-                for (int m = 0; m < MAXM; ++m) part[m] = 0.f;
-                if (a.fast) {
-                    const uint8_t* seg = rowp + (long long)my_ks * (kseg / 64) * 68;
-                    dot_q8_fast<MAXM>(seg, kseg / 64, xs + (size_t)(my_ks * kseg / 64) * 68, xl, a.M, lane, part);
-                } else {
-                    const long long seg_off = row_bytes(a.wtype, (long long)my_ks * kseg);
-                    dot_generic<MAXM>(a.wtype, rowp + seg_off, my_ks * kseg, kseg, xs, xl, a.M, lane, part);
+            for (int p = 0; p < 2; ++p) {
+                if (p < a.P) {
+                    const uint8_t* rowp = ib + (long long)p * a.rb;
+                    float part[MAXM];
+#pragma unroll
+                    for (int m = 0; m < MAXM; ++m) part[m] = 0.f;
+                    if (a.fast) {
+                        const uint8_t* seg = rowp + (long long)my_ks * (kseg / 64) * 68;
+                        dot_q8_fast<MAXM>(seg, kseg / 64, xs + (size_t)(my_ks * kseg / 64) * 68, xl, a.M, lane, part);
+                    } else {
+                        const long long seg_off = row_bytes(a.wtype, (long long)my_ks * kseg);
+                        dot_generic<MAXM>(a.wtype, rowp + seg_off, my_ks * kseg, kseg, xs, xl, a.M, lane, part);
+                    }
+#pragma unroll
+                    for (int m = 0; m < MAXM; ++m) {
+                        const float v = warp_sum(part[m]);
+                        if (p == 0) acc0[m] = v;
+                        else acc1[m] = v;
+                    }
                 }
-#pragma unroll
-                for (int m = 0; m < MAXM; ++m) acc[p][m] = warp_sum(part[m]);
             }
         }
         __syncwarp();
@@ -353,32 +239,43 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         if (a.KS > 1) {
             float* rb = red + ((s & 1) * GV_WARPS + warp) * 2 * MAXM;
             if (lane == 0 && have)
-                for (int p = 0; p < 2; ++p)
-                    for (int m = 0; m < MAXM; ++m) rb[p * MAXM + m] = acc[p][m];
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) {
+                    rb[m] = acc0[m];
+                    rb[MAXM + m] = acc1[m];
+                }
             named_bar_compute();
             have = have && my_ks == 0;
             if (have && lane == 0) {
-                for (int p = 0; p < 2; ++p)
-                    for (int m = 0; m < MAXM; ++m) {
-                        float v = 0.f;
-                        for (int k = 0; k < a.KS; ++k) v += red[((s & 1) * GV_WARPS + warp + k) * 2 * MAXM + p * MAXM + m];
-                        acc[p][m] = v;
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) {
+                    float v0 = 0.f, v1 = 0.f;
+                    for (int k = 0; k < a.KS; ++k) {
+                        const float* q = red + ((s & 1) * GV_WARPS + warp + k) * 2 * MAXM;
+                        v0 += q[m];
+                        v1 += q[MAXM + m];
                     }
+                    acc0[m] = v0;
+                    acc1[m] = v1;
+                }
             }
         }
         if (have && lane == 0) {
             const int row = item;
-            for (int m = 0; m < a.M; ++m) {
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m >= a.M) break;
                 if (a.epi == EPI_STORE) {
-                    const float v = acc[0][m] + (a.bias ? a.bias[row] : 0.f);
-                    a.y[(size_t)m * a.ldy + row] = v;
+                    const float b = a.bias ? (prefetched ? pre[row - i0] : a.bias[row]) : 0.f;
+                    a.y[(size_t)m * a.ldy + row] = acc0[m] + b;
                 } else if (a.epi == EPI_RESID) {
-                    a.resid[(size_t)m * a.ldr + row] += acc[0][m];
+                    const float r = prefetched ? pre[m * GV_PRE + row - i0] : a.resid[(size_t)m * a.ldr + row];
+                    a.resid[(size_t)m * a.ldr + row] = r + acc0[m];
                 } else if (a.epi == EPI_SWIGLU) {
-                    const float g = acc[0][m], u = acc[1][m];
+                    const float g = acc0[m], u = acc1[m];
                     a.y[(size_t)m * a.ldy + row] = __fmul_rn(__fdiv_rn(g, 1.0f + expf(-g)), u);
                 } else {  // EPI_ARGMAX
-                    const float v = acc[0][m];
+                    const float v = acc0[m];
                     a.y[(size_t)m * a.ldy + row] = v;
                     const unsigned long long k = argmax_key(v, (uint32_t)row);
                     best[m] = k > best[m] ? k : best[m];
@@ -422,32 +319,36 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
 size_t gemv_smem_bytes(int M, int K, int stage_bytes, int maxm) {
     const size_t xbytes = ((size_t)M * xpad_len(K) * 4 + 127) & ~(size_t)127;
     return xbytes + (size_t)GV_STAGES * stage_bytes + 2 * GV_WARPS * 2 * maxm * 4 + GV_WARPS * maxm * 8 +
-           2 * GV_STAGES * 8 + 8 + maxm * 8;
+           (size_t)maxm * GV_PRE * 4 + 2 * GV_STAGES * 8 + 8 + maxm * 8;
 }
 
 static int pick_maxm(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 // Choose the k-split and stage size for a weight shape (see GemvArgs).
-void gemv_plan(GemvArgs& a) {
+// k-split and stage size for a weight shape and `warps` consumer warps: the smallest split
+// whose stage (warps/KS items) fits `budget` bytes.
+void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const int be = blk_elems(a.wtype) == 1 ? 32 : blk_elems(a.wtype);
     const bool q8fast = (a.wtype == T_Q8_0) && (a.K % 64 == 0);
     int best = -1;
-    for (int ks = 1; ks <= GV_WARPS; ks <<= 1) {
+    for (int ks = 1; ks <= warps; ks <<= 1) {
         if (a.K % ks) continue;
         const int seg = a.K / ks;
         if (seg % be) continue;
         if (q8fast && seg % 64) continue;
         best = ks;
-        const long long payload = (long long)(GV_WARPS / ks) * a.P * a.rb;
-        if (payload <= GV_STAGE_BUDGET) break;
+        const long long payload = (long long)(warps / ks) * a.P * a.rb;
+        if (payload <= budget) break;
     }
     if (best < 0) best = 1;
     a.KS = best;
     // the fast path reads 4-byte words: rows must start 4-byte aligned
     a.fast = q8fast && ((a.K / best) % 64 == 0) && ((reinterpret_cast<uintptr_t>(a.W) & 3) == 0);
-    const long long payload = (long long)(GV_WARPS / best) * a.P * a.rb;
+    const long long payload = (long long)(warps / best) * a.P * a.rb;
     a.stage_bytes = (int)((payload + 32 + 15) & ~15LL);
 }
+
+void gemv_plan(GemvArgs& a) { gemv_plan_w(a, GV_WARPS, GV_STAGE_BUDGET); }
 
 int gemv_max_rows(int K) {
     // activation rows whose padded copies fit next to the stages
@@ -456,13 +357,22 @@ int gemv_max_rows(int K) {
     return m < 1 ? 1 : (m > GV_MAXM ? GV_MAXM : m);
 }
 
+template <int MAXM>
+static cudaError_t init_one() {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    if (e != cudaSuccess) return e;
+    // every kernel of the step asks for the same (maximal) shared-memory carve-out, so the
+    // SMs never have to drain to re-partition L1 / shared memory between kernels
+    return cudaFuncSetAttribute(gemv_kernel<MAXM>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+}
+
 cudaError_t gemv_init_attrs() {
     cudaError_t e;
-    const int lim = 200 * 1024;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim))) return e;
-    return cudaFuncSetAttribute(gemv_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim);
+    if ((e = init_one<1>())) return e;
+    if ((e = init_one<2>())) return e;
+    if ((e = init_one<4>())) return e;
+    return init_one<8>();
 }
 
 template <int MAXM>
@@ -490,10 +400,26 @@ cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) 
     }
 }
 
+// CTAs per SM for the GEMV grids (TFB200_GEMV_CPS, 1 or 2, default 2).  Two half-size CTAs
+// per SM measured faster for batch-1 decode (1137 vs 814 tok/s on cfg0): while one CTA of a
+// kernel drains its last stages, the other slot takes the next kernel's CTA, which starts
+// its weight prefetch under programmatic dependent launch.
+static int gemv_ctas_per_sm() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_GEMV_CPS");
+        v = e ? atoi(e) : 2;
+        if (v < 1) v = 1;
+        if (v > 2) v = 2;
+    }
+    return v;
+}
+
 int gemv_grid(const GemvArgs& a, int num_sms) {
     const int RI = GV_WARPS / a.KS;
     const int stages = (a.n_items + RI - 1) / RI;
-    return stages < num_sms ? (stages > 0 ? stages : 1) : num_sms;
+    const int cap = num_sms * gemv_ctas_per_sm();
+    return stages < cap ? (stages > 0 ? stages : 1) : cap;
 }
 
 }  // namespace tfb

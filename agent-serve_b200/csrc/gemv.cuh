@@ -15,6 +15,8 @@ constexpr int GV_THREADS = (GV_WARPS + 1) * 32;  // + one producer warp issuing 
 constexpr int GV_STAGES = 4;                     // weight stages in flight per CTA
 constexpr int GV_MAXM = 8;                       // activation rows per launch
 constexpr int GV_STAGE_BUDGET = 18 * 1024;       // target bytes of weights per stage
+constexpr int GV_PRE = 64;                       // epilogue operands prefetched per CTA (rows)
+constexpr int GV_PRO_UNROLL = 8;                 // float4 activation loads in flight per thread
 
 enum : int { PRO_COPY = 0, PRO_RMSNORM = 1, PRO_EMBED_RMSNORM = 2 };
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_mk.cuh"
 #include "engine.cuh"
 
 namespace tfb {
@@ -110,6 +111,11 @@ struct tf_model {
     std::vector<int> hpos;  // host mirror of each slot's position
     std::map<long long, cudaGraphExec_t> graphs;
     int kernels_per_step = 0;
+    // persistent decode kernel (batch 1)
+    bool mk = false;
+    MkPhase* d_phases = nullptr;
+    int n_phases = 0, mk_slot_bytes = 0, mk_slots = 0, mk_xfloats = 0, mk_grid = 0;
+    unsigned* d_bar = nullptr;
     std::string err;
 };
 
@@ -320,6 +326,182 @@ int run_step(tf_model* m, int M, bool head) {
     return 0;
 }
 
+// Phase table of one decode step for the persistent kernel (batch 1): per layer
+// QKV (RMSNorm [+ embedding] + GEMV + bias) | attention | wo (+ residual) |
+// gate/up (RMSNorm + GEMV + SwiGLU) | down (+ residual); then the lm_head (RMSNorm +
+// GEMV + greedy argmax).  Returns the shared-memory plan in m.
+int build_mk_plan(tf_model* m) {
+    std::vector<MkPhase> ph;
+    // Each consumer warp takes 2 rows of a stage, split along K into KS segments (KS divides
+    // MK_WARPS).  Q8_0 rows whose K splits into 2048-element segments use the register
+    // path (one 64-element unit per lane); other shapes use the shared-memory dot.
+    auto gemv_phase = [&](const WeightRef& w, int n_items, int P) {
+        const bool aligned4 = (reinterpret_cast<uintptr_t>(w.p) & 3) == 0;
+        const bool q8fast = w.type == T_Q8_0 && w.K % 64 == 0 && aligned4;
+        const int be = blk_elems(w.type) == 1 ? 32 : blk_elems(w.type);
+        int ks = 0, reg = 0;
+        if (q8fast && w.K % 2048 == 0 && MK_WARPS % (w.K / 2048) == 0) {
+            ks = w.K / 2048;
+            reg = 1;
+        } else {
+            for (int d = 1; d <= MK_WARPS; ++d) {
+                if (MK_WARPS % d || w.K % d) continue;
+                const int seg = w.K / d;
+                if (seg % be || (q8fast && seg % 64)) continue;
+                ks = d;
+                if ((long long)(MK_WARPS / d) * 2 * w.rb <= MK_STAGE_BUDGET) break;
+            }
+            if (!ks) ks = 1;
+        }
+        MkPhase p;
+        memset(&p, 0, sizeof(p));
+        p.kind = PH_GEMV;
+        p.W = w.p;
+        p.rb = w.rb;
+        p.wtype = w.type;
+        p.K = w.K;
+        p.n_items = n_items;
+        p.P = P;
+        p.KS = ks;
+        p.fast = q8fast && (w.K / ks) % 64 == 0;
+        p.reg = reg;
+        p.ri = (MK_WARPS / ks) * (2 / P);
+        return p;
+    };
+    for (int li = 0; li < m->hp.n_layer; ++li) {
+        const LayerDev& Ld = m->L[li];
+        MkPhase q = gemv_phase(Ld.qkv, m->H + 2 * m->KV, 1);
+        q.pro = li == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM;
+        q.x = m->x;
+        q.norm_w = Ld.attn_norm;
+        q.epi = EPI_STORE;
+        q.y = m->qkv;
+        q.bias = Ld.bqkv;
+        ph.push_back(q);
+        MkPhase at;
+        memset(&at, 0, sizeof(at));
+        at.kind = PH_ATTN;
+        at.layer = li;
+        ph.push_back(at);
+        MkPhase o = gemv_phase(Ld.wo, m->D, 1);
+        o.pro = PRO_COPY;
+        o.x = m->attn;
+        o.epi = EPI_RESID;
+        o.resid = m->x;
+        ph.push_back(o);
+        MkPhase gu = gemv_phase(Ld.gateup, m->FF, 2);
+        gu.pro = PRO_RMSNORM;
+        gu.x = m->x;
+        gu.norm_w = Ld.ffn_norm;
+        gu.epi = EPI_SWIGLU;
+        gu.y = m->h;
+        ph.push_back(gu);
+        MkPhase dn = gemv_phase(Ld.down, m->D, 1);
+        dn.pro = PRO_COPY;
+        dn.x = m->h;
+        dn.epi = EPI_RESID;
+        dn.resid = m->x;
+        ph.push_back(dn);
+    }
+    MkPhase lm = gemv_phase(m->outw, m->V, 1);
+    lm.pro = PRO_RMSNORM;
+    lm.x = m->x;
+    lm.norm_w = m->out_norm;
+    lm.epi = EPI_ARGMAX;
+    lm.y = m->logits;
+    ph.push_back(lm);
+
+    int slot = 0, xf = 8 * (2 * m->hd + 1);
+    for (const MkPhase& p : ph) {
+        if (p.kind != PH_GEMV) continue;
+        const long long payload = (long long)p.ri * p.P * p.rb;
+        slot = std::max(slot, (int)((payload + 32 + 15) & ~15LL));
+        xf = std::max(xf, xpad_len(p.K));
+    }
+    xf = (xf + 3) & ~3;
+    MkArgs probe;
+    memset(&probe, 0, sizeof(probe));
+    probe.xfloats = xf;
+    probe.slot_bytes = slot;
+    probe.n_slots = 0;
+    const size_t fixed = mk_smem_bytes(probe);
+    int n_slots = (int)((MK_SMEM_LIMIT - (long long)fixed) / slot);
+    if (n_slots > MK_MAX_SLOTS) n_slots = MK_MAX_SLOTS;
+    if (n_slots < 2) return 1;  // shapes too large for the persistent kernel
+    m->mk_slot_bytes = slot;
+    m->mk_slots = n_slots;
+    m->mk_xfloats = xf;
+    m->n_phases = (int)ph.size();
+    CK(cudaMalloc(&m->d_phases, sizeof(MkPhase) * ph.size()));
+    CK(cudaMemcpy(m->d_phases, ph.data(), sizeof(MkPhase) * ph.size(), cudaMemcpyHostToDevice));
+    CK(cudaMalloc(&m->d_bar, 2 * sizeof(unsigned)));
+    CK(cudaMemset(m->d_bar, 0, 2 * sizeof(unsigned)));
+    // one CTA per SM, all co-resident (cooperative launch); if the kernel cannot be resident
+    // on an SM the engine keeps the per-kernel path
+    MkArgs full;
+    memset(&full, 0, sizeof(full));
+    full.xfloats = xf;
+    full.slot_bytes = slot;
+    full.n_slots = n_slots;
+    const int occ = mk_occupancy(mk_smem_bytes(full));
+    if (occ < 1) {
+        cudaGetLastError();
+        return 1;
+    }
+    m->mk_grid = m->num_sms;
+    m->mk = true;
+    return 0;
+}
+
+// Run `n_steps` batch-1 steps of slot `seq` in one persistent launch: the first n_prompt
+// steps consume prompt[] (device), later ones their own argmax; the lm_head runs from step
+// first_head on; during prompt steps attention starts at ws_prompt.
+int run_mk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps, int first_head, int ws_prompt,
+           int hist_cap) {
+    MkArgs a;
+    memset(&a, 0, sizeof(a));
+    a.ph = m->d_phases;
+    a.n_ph = m->n_phases;
+    a.n_steps = n_steps;
+    a.n_prompt = n_prompt;
+    a.prompt = d_prompt;
+    a.first_head = first_head;
+    a.ws_prompt = ws_prompt;
+    a.slot = seq;
+    a.slot_bytes = m->mk_slot_bytes;
+    a.n_slots = m->mk_slots;
+    a.xfloats = m->mk_xfloats;
+    a.eps = m->hp.rms_eps;
+    a.embd = m->embd.p;
+    a.embd_type = m->embd.type;
+    a.embd_rb = m->embd.rb;
+    a.n_vocab = m->V;
+    a.x_resid = m->x;
+    a.D = m->D;
+    a.kc = m->kc;
+    a.vc = m->vc;
+    a.layer_elems = m->layer_elems;
+    a.slot_elems = m->slot_elems;
+    a.cap = m->opt.max_seq;
+    a.kv_type = m->opt.kv_type;
+    a.cosb = m->cosb;
+    a.sinb = m->sinb;
+    a.n_head = m->hp.n_head;
+    a.n_kv = m->hp.n_kv_head;
+    a.hd = m->hd;
+    a.qkv = m->qkv;
+    a.attn_out = m->attn;
+    a.tok = m->d_tokens;
+    a.pos = m->d_pos;
+    a.hist = m->d_hist;
+    a.hist_cap = hist_cap;
+    a.keys = m->keys;
+    a.bar = m->d_bar;
+    a.err = m->d_err;
+    CK(mk_launch(a, m->mk_grid, m->stream));
+    return 0;
+}
+
 // Synchronise and surface any device-side error word.
 int finish_call(tf_model* m) {
     CK(cudaMemcpyAsync(m->hi + 60, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
@@ -375,7 +557,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl};
+                   m->d_err, m->ctl, m->d_phases, m->d_bar};
     for (void* p : dev)
         if (p) cudaFree(p);
     if (m->hi) cudaFreeHost(m->hi);
@@ -397,6 +579,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     o.device = 0;
     o.kv_type = TF_KV_F32;
     o.use_graph = 1;
+    o.decode_mode = TF_DECODE_KERNELS;
     if (opt_in) o = *opt_in;
     if (o.max_seq <= 0 || o.max_batch <= 0) {
         delete m;
@@ -411,9 +594,13 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     }
     m->hd = hp.n_embd / hp.n_head;  // head_dim = n_embd / n_head always wins (src/model.cpp:22-24)
     if (hp.head_dim != m->hd) m->hp.head_dim = m->hd;
-    if (m->hd % 2 || m->hd > AT_MAX_HD || hp.n_head % hp.n_kv_head || hp.n_head / hp.n_kv_head > AT_MAX_REP) {
+    if (m->hd % 8 || m->hd > AT_MAX_HD || hp.n_head % hp.n_kv_head || hp.n_head / hp.n_kv_head > AT_MAX_REP) {
         delete m;
-        return set_error("unsupported attention shape (head_dim must be even and <= 128, n_head/n_kv_head <= 8)");
+        return set_error("unsupported attention shape (head_dim must be a multiple of 8 up to 128, n_head/n_kv_head <= 8)");
+    }
+    if (o.max_seq > AT_CHUNK * AT_MAX_SPLIT) {
+        delete m;
+        return set_error("max_seq above 16384 is not supported");
     }
     m->D = hp.n_embd;
     m->H = hp.n_head * m->hd;
@@ -625,8 +812,8 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMalloc(&m->part, sizeof(float) * (size_t)T * hp.n_head * m->n_split * (m->hd + 2)));
     CKD(cudaMalloc(&m->counters, sizeof(unsigned) * T * hp.n_kv_head));
     CKD(cudaMemset(m->counters, 0, sizeof(unsigned) * T * hp.n_kv_head));
-    CKD(cudaMalloc(&m->keys, sizeof(unsigned long long) * T));
-    CKD(cudaMemset(m->keys, 0, sizeof(unsigned long long) * T));
+    CKD(cudaMalloc(&m->keys, sizeof(unsigned long long) * (T < 2 ? 2 : T)));
+    CKD(cudaMemset(m->keys, 0, sizeof(unsigned long long) * (T < 2 ? 2 : T)));
     CKD(cudaMalloc(&m->d_tokens, sizeof(int) * T));
     CKD(cudaMemset(m->d_tokens, 0, sizeof(int) * T));
     CKD(cudaMalloc(&m->d_slots, sizeof(int) * T));
@@ -644,6 +831,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
     CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
     m->hpos.assign(o.max_batch, 0);
+    if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
     CKD(cudaDeviceSynchronize());
     {
         int n = 0;
@@ -688,7 +876,11 @@ int tf_cuda_decode(tf_model* m, int seq, int token, float* logits, int* argmax_o
     if (m->hpos[seq] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
     if (token < 0 || token >= m->V) return fail(m, "token id out of range");
     if (set_slot_row(m, 0, seq, token)) return -1;
-    if (run_step(m, 1, true)) return -1;
+    if (m->mk) {
+        if (run_mk(m, seq, m->d_tokens, 1, 1, 0, 0, 0)) return -1;
+    } else if (run_step(m, 1, true)) {
+        return -1;
+    }
     m->hpos[seq] += 1;
     return read_outputs(m, 1, logits, argmax_out);
 }
@@ -705,6 +897,13 @@ int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logit
     int* stage = m->hi + 64;
     memcpy(stage, tokens, sizeof(int) * n);
     CK(cudaMemcpyAsync(m->d_prompt, stage, sizeof(int) * n, cudaMemcpyHostToDevice, m->stream));
+    if (m->mk) {
+        // all n prompt steps in one persistent launch; attention inside the chunk sees the
+        // chunk alone, from its first position; the lm_head runs for the last token only
+        if (run_mk(m, seq, m->d_prompt, n, n, n - 1, m->hpos[seq], 0)) return -1;
+        m->hpos[seq] += n;
+        return read_outputs(m, 1, logits, argmax_out);
+    }
     // attention inside the chunk sees the chunk alone, from its first position
     m->hi[2] = m->hpos[seq];
     m->hi[3] = 0;
@@ -729,11 +928,15 @@ int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eo
     if (m->hpos[seq] + n > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
     if (first_token < 0 || first_token >= m->V) return fail(m, "token id out of range");
     if (set_slot_row(m, 0, seq, first_token)) return -1;
-    StepCtl c = {0u, 0, n, 0};
-    memcpy(m->hi + 4, &c, sizeof(c));
-    CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
-    for (int i = 0; i < n; ++i)
-        if (run_step(m, 1, true)) return -1;
+    if (m->mk) {
+        if (run_mk(m, seq, m->d_tokens, 1, n, 0, 0, n)) return -1;
+    } else {
+        StepCtl c = {0u, 0, n, 0};
+        memcpy(m->hi + 4, &c, sizeof(c));
+        CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
+        for (int i = 0; i < n; ++i)
+            if (run_step(m, 1, true)) return -1;
+    }
     int* hist = m->hi + 64;
     CK(cudaMemcpyAsync(hist, m->d_hist, sizeof(int) * n, cudaMemcpyDeviceToHost, m->stream));
     int rc = finish_call(m);

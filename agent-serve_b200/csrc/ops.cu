@@ -44,6 +44,7 @@ int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, i
     if (K % 32 || K % blk_elems(t)) return set_error("row length not divisible by block size");
     if (M == 0) return 0;
     if (t == T_F32 && (reinterpret_cast<uintptr_t>(W) & 3)) return set_error("F32 weights must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(A) & 15) return set_error("A must be 16-byte aligned");
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int* err = nullptr;
     if (err_word(&err)) return -1;

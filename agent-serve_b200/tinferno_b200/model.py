@@ -33,6 +33,7 @@ class RunConfig:
     device: int = 0
     kv_type: int = native.TF_KV_F32
     use_graph: bool = True
+    decode_mode: int = native.TF_DECODE_KERNELS
     n_predict: int = 64
     temperature: float = 0.0
     top_p: float = 0.9
@@ -103,7 +104,7 @@ class Model:
         self.hp = hparams_from_gguf(self.gguf)
         descs, keep = tensor_descs(self.gguf)
         opt = native.Options(self.cfg.max_seq, self.cfg.max_batch, self.cfg.device, self.cfg.kv_type,
-                             1 if self.cfg.use_graph else 0)
+                             1 if self.cfg.use_graph else 0, self.cfg.decode_mode)
         h = C.c_void_p()
         native.check(self.L.tf_cuda_create(descs, len(descs), C.byref(self.hp), C.byref(opt), C.byref(h)))
         self.h = h

@@ -19,6 +19,7 @@ i32p = C.POINTER(C.c_int)
 
 TF_F32, TF_F16, TF_Q4_0, TF_Q4_1, TF_Q8_0, TF_Q6_K = 0, 1, 2, 3, 8, 14
 TF_KV_F32, TF_KV_F16, TF_KV_BF16 = 0, 1, 2
+TF_DECODE_KERNELS, TF_DECODE_PERSISTENT = 0, 1
 
 
 class TensorDesc(C.Structure):
@@ -37,7 +38,7 @@ class HParams(C.Structure):
 
 class Options(C.Structure):
     _fields_ = [("max_seq", C.c_int), ("max_batch", C.c_int), ("device", C.c_int),
-                ("kv_type", C.c_int), ("use_graph", C.c_int)]
+                ("kv_type", C.c_int), ("use_graph", C.c_int), ("decode_mode", C.c_int)]
 
 
 # (name, restype, argtypes) of every entry point declared in include/tinferno_b200.h

@@ -247,7 +247,7 @@ def run_ours(args, rank, world, local_rank, dist):
         print(json.dumps(line), flush=True)
 
 
-def gemv_roofline(torch, native, m):
+def gemv_roofline(torch, native, m, reps=50, warm=5):
     """Time tf_op_matmul (the engine's dequant-GEMV kernel) on the lm_head shape: 128256 x 2048
     Q8_0 weights (279 MB, > L2) times one fp32 row."""
     from tinferno_b200 import quants
@@ -264,10 +264,9 @@ def gemv_roofline(torch, native, m):
     y = torch.empty(N, device="cuda")
     st = torch.cuda.current_stream()
     L = native.lib()
-    for _ in range(5):
+    for _ in range(warm):
         native.check(L.tf_op_matmul(C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()), native.TF_Q8_0,
                                     C.c_void_p(W.data_ptr()), N, K, 1, C.c_void_p(st.cuda_stream)))
-    reps = 50
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
     for a, b in evs:
         a.record(st)
@@ -292,7 +291,26 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step"],
+                    help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
+                         "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
+                         "eager decode steps")
     args = ap.parse_args()
+    if args.kernel == "lmhead":
+        import torch
+        from tinferno_b200 import native
+        print(json.dumps(gemv_roofline(torch, native, None, reps=3, warm=1)))
+        return
+    if args.kernel == "step":
+        from tinferno_b200.model import Model, RunConfig
+        cfg = synth.mini(CFG, 2, 4096)
+        m = Model(synth.model_path(cfg), RunConfig(max_seq=CFG.max_seq, use_graph=False))
+        t = int(np.argmax(m.prefill(synth.prompt_tokens(cfg, 4))))
+        for _ in range(2):
+            t = int(np.argmax(m.decode(t)))
+        m.close()
+        print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 5 + 1, "last_token": t}))
+        return
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

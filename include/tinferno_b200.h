@@ -61,8 +61,14 @@ typedef struct tf_options {
     int max_batch;
     int device;
     int kv_type;   /* TF_KV_* */
-    int use_graph; /* 1: capture the decode step in a CUDA graph (default) */
+    int use_graph; /* per-kernel path: 1 = capture the decode step in a CUDA graph (default) */
+    int decode_mode; /* batch-1 decode/prefill/generate: TF_DECODE_KERNELS (default, 0)
+                        launches one kernel per phase under programmatic dependent launch,
+                        captured in a CUDA graph (also the path of batched decode);
+                        TF_DECODE_PERSISTENT runs whole steps in one cooperative kernel */
 } tf_options;
+
+enum { TF_DECODE_KERNELS = 0, TF_DECODE_PERSISTENT = 1 };
 
 typedef struct tf_model tf_model;
 
