@@ -153,6 +153,17 @@ TF_API int tf_op_attn_decode(float* out, const float* q, const void* k_cache, co
                       int kv_type, int cap, int n_pos, int n_heads, int n_kv_heads, int head_dim,
                       void* stream);
 
+/* tf_op_attn_decode with no device allocation: no reference counterpart (the reference's
+ * attn_decode runs on the CPU and needs no scratch).  Same arguments and results as
+ * tf_op_attn_decode; the split-K partials live in a static device array of 524288 floats
+ * (n_heads * ceil(n_pos/64) * (head_dim+2) must fit, n_kv_heads <= 64, else an error).
+ * For callers that cannot allocate mid-step.  Calls on one device must not overlap in time
+ * (they share the scratch); the first call on a device does set-up and must precede any
+ * stream capture. */
+TF_API int tf_op_attn_decode_noalloc(float* out, const float* q, const void* k_cache,
+                      const void* v_cache, int kv_type, int cap, int n_pos, int n_heads,
+                      int n_kv_heads, int head_dim, void* stream);
+
 /* attn_prefill(out, q, k, v, seq, n_heads, n_kv_heads, head_dim)  src/attention.hpp:29-30:
  * causal attention within the chunk; q [seq][n_heads][hd], k/v [seq][n_kv][hd]. */
 TF_API int tf_op_attn_prefill(float* out, const float* q, const float* k, const float* v, int seq,
