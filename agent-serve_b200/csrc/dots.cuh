@@ -50,6 +50,108 @@ __device__ __forceinline__ void unit_dot_q8_reg(const uint32_t* wp, const float 
     acc = fmaf(dB, b2.x + b2.y, acc);
 }
 
+// ---- Q8_0 exact-integer path ---------------------------------------------------------------
+// The activation row is turned into three signed-byte digit planes, once per kernel: each
+// 32-element block is scaled by a power of two 2^sh so that its largest magnitude is below
+// 2^22, rounded to integers X, and X = x2*2^16 + x1*2^8 + x0 with x0, x1, x2 in [-128, 127].
+// The planes use the byte layout of a Q8_0 row (34 bytes per block, 0 at the two scale
+// bytes), so a weight word and the plane word at the same offset line up for dp4a and the
+// scale bytes meet zeros.  The block sum sum_j q_j*X_j is then exact in int32 (|.| <= 2^19
+// per plane), and sum_j q_j*x_j = (sum q*x2 * 2^16 + sum q*x1 * 2^8 + sum q*x0) * 2^-sh.
+// Rounding x to 22 significant bits of its block maximum is the only approximation, the same
+// size as the fp32 rounding of the products in src/quant.cpp:266-321; the block scale d is
+// applied to the block sum as the reference does.  Cost per weight byte: one dp4a per plane
+// and word, against the PRMT/FADD/FFMA conversion chain of the fp32 path.
+constexpr int Q8_PLANE_SH_MAX = 126;
+
+// Planes of one activation row held as float4 chunks, chunk c = tid + u*nth for u < NU
+// (elements 4c..4c+3, block c/8).  nth must be a multiple of 32 so a block's 8 chunks sit
+// in 8 consecutive lanes of one warp.  Writes planes[p*pstride + byte] (p = 0, 1, 2; byte in
+// the Q8_0 row layout) and inv[block] = 2^-sh.  Every thread of the warps calls it.
+template <int NU>
+__device__ __forceinline__ void q8_build_planes(const float4 (&v)[NU], int K, int nth, int tid, uint8_t* planes,
+                                                int pstride, float* inv) {
+    const int nq = K >> 2;
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        const int c = tid + u * nth;
+        if (c - (tid & 31) >= nq) break;  // warp-uniform: no chunk of this warp is left
+        const bool valid = c < nq;
+        const float4 x = valid ? v[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float am = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+        if (!valid) continue;
+        // am < 2^(e-126) for a normal am with biased exponent e: 2^sh = 2^(148-e) keeps
+        // |x| * 2^sh below 2^22.  Zero and subnormal blocks take the largest shift.
+        const int e = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+        const int sh = min(148 - e, Q8_PLANE_SH_MAX);
+        const float S = __uint_as_float((uint32_t)(127 + sh) << 23);
+        const float xv[4] = {x.x, x.y, x.z, x.w};
+        uint32_t d0 = 0, d1 = 0, d2 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int X = __float2int_rn(xv[i] * S);  // exact scaling by a power of two
+            const int x0 = (int)(int8_t)(X & 0xFF);
+            const int r = (X - x0) >> 8;
+            const int x1 = (int)(int8_t)(r & 0xFF);
+            const int x2 = (r - x1) >> 8;
+            d0 |= (uint32_t)(x0 & 0xFF) << (8 * i);
+            d1 |= (uint32_t)(x1 & 0xFF) << (8 * i);
+            d2 |= (uint32_t)(x2 & 0xFF) << (8 * i);
+        }
+        const int b = c >> 3;
+        const int off = 34 * b + 2 + 4 * (c & 7);  // even: 16-bit stores
+        uint16_t* q0 = reinterpret_cast<uint16_t*>(planes + off);
+        uint16_t* q1 = reinterpret_cast<uint16_t*>(planes + pstride + off);
+        uint16_t* q2 = reinterpret_cast<uint16_t*>(planes + 2 * pstride + off);
+        q0[0] = (uint16_t)d0;
+        q0[1] = (uint16_t)(d0 >> 16);
+        q1[0] = (uint16_t)d1;
+        q1[1] = (uint16_t)(d1 >> 16);
+        q2[0] = (uint16_t)d2;
+        q2[1] = (uint16_t)(d2 >> 16);
+        if ((c & 7) == 0) {
+            const int so = 34 * b;  // the block's scale bytes meet zeros
+            *reinterpret_cast<uint16_t*>(planes + so) = 0;
+            *reinterpret_cast<uint16_t*>(planes + pstride + so) = 0;
+            *reinterpret_cast<uint16_t*>(planes + 2 * pstride + so) = 0;
+            // a non-finite block maximum makes the block's contribution NaN
+            inv[b] = e == 255 ? __uint_as_float(0x7FC00000u) : __uint_as_float((uint32_t)(127 - sh) << 23);
+        }
+    }
+}
+
+// One 64-element unit (two blocks, 17 words at wp) of one row against the lane's planes
+// (the same unit's 17 words of each plane) and the two blocks' 2^-sh.
+__device__ __forceinline__ float unit_dot_q8_int(const uint32_t* wp, const uint32_t (&pl)[51], float invA,
+                                                 float invB) {
+    int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+    uint32_t w0 = 0, w8 = 0;
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {  // word 8 holds q30, q31 of block A and block B's scale
+        const uint32_t w = wp[i];
+        if (i == 0) w0 = w;
+        if (i == 8) w8 = w;
+        a0 = __dp4a((int)w, (int)pl[i], a0);
+        a1 = __dp4a((int)w, (int)pl[17 + i], a1);
+        a2 = __dp4a((int)w, (int)pl[34 + i], a2);
+    }
+#pragma unroll
+    for (int i = 9; i < 17; ++i) {
+        const uint32_t w = wp[i];
+        b0 = __dp4a((int)w, (int)pl[i], b0);
+        b1 = __dp4a((int)w, (int)pl[17 + i], b1);
+        b2 = __dp4a((int)w, (int)pl[34 + i], b2);
+    }
+    const float dA = h2f(w0);
+    const float dB = h2f(w8 >> 16);
+    const float tA = fmaf((float)a2, 65536.f, (float)(a1 * 256 + a0));
+    const float tB = fmaf((float)b2, 65536.f, (float)(b1 * 256 + b0));
+    return fmaf(dA * invA, tA, (dB * invB) * tB);
+}
+
 // ---- Q8_0 fast path: one row segment of `units` 64-element units -----------------------
 // Products and partial sums use the packed fp32x2 pipe of sm_100 (__ffma2_rn / __fadd2_rn):
 // two weights per instruction, each lane still forming exact fp32 x*q products.

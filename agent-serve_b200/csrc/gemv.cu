@@ -28,7 +28,7 @@ __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
 
-template <int MAXM>
+template <int MAXM, bool INTQ>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -116,7 +116,92 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const int m = i / (i1 - i0), r = i % (i1 - i0);
             pre[m * GV_PRE + r] = a.resid[(size_t)m * a.ldr + i0 + r];
         }
-    for (int m = 0; m < a.M; ++m) {
+    // Q8_0 integer path (M == 1): the activation row stays in registers through the RMSNorm
+    // and leaves as digit planes in the activation region (dots.cuh).
+    constexpr bool use_int = INTQ;
+    static_assert(!INTQ || MAXM == 1, "integer path is for one activation row");
+    const int U = a.K / a.KS / 64;               // 64-element units per row segment
+    const int prow = a.P == 2 ? lane >> 4 : 0;   // row of the item this lane works on
+    const int pu = a.P == 2 ? lane & 15 : lane;  // unit within the segment
+    const bool pact = pu < U;
+    uint32_t pl[INTQ ? 51 : 1];
+    float invA = 0.f, invB = 0.f;
+    if constexpr (INTQ) {
+        {
+            float4 v[GV_PRO_UNROLL];
+            if (a.pro == PRO_EMBED_RMSNORM) {
+                int tok = a.tokens[0];
+                if (tok < 0 || tok >= a.n_vocab) {
+                    if (tid == 0) atomicCAS(a.err, 0, ERR_BAD_TOKEN);
+                    tok = 0;
+                }
+                embed_row(xs, a.embd, a.embd_type, a.embd_rb, a.K, tok, nth);
+                named_bar_compute();
+                if (blockIdx.x == 0)
+                    for (int e = tid; e < a.K; e += nth) a.x_out[e] = xs[xpad(e)];
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const int c = tid + u * nth;
+                    v[u] = c < nq ? *reinterpret_cast<const float4*>(xs + xpad(4 * c)) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            } else {
+                const float4* xg = reinterpret_cast<const float4*>(a.x);
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const int c = tid + u * nth;
+                    v[u] = c < nq ? xg[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            if (a.pro != PRO_COPY) {
+                // rmsnorm (src/layers.cpp:7-12), in the same order as the fp32 path below
+                double ss = 0.0;
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    if (tid + u * nth < nq) {
+                        ss = fma((double)v[u].x, (double)v[u].x, ss);
+                        ss = fma((double)v[u].y, (double)v[u].y, ss);
+                        ss = fma((double)v[u].z, (double)v[u].z, ss);
+                        ss = fma((double)v[u].w, (double)v[u].w, ss);
+                    }
+                }
+                ss = warp_sum_d(ss);
+                if (lane == 0) redd[warp] = ss;
+                named_bar_compute();
+                double tot = 0.0;
+                for (int w = 0; w < GV_WARPS; ++w) tot += redd[w];
+                const float inv = 1.0f / sqrtf((float)(tot / a.K) + a.eps);
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u) {
+                    const float4 wv = wn[u];
+                    v[u].x = __fmul_rn(__fmul_rn(v[u].x, inv), wv.x);
+                    v[u].y = __fmul_rn(__fmul_rn(v[u].y, inv), wv.y);
+                    v[u].z = __fmul_rn(__fmul_rn(v[u].z, inv), wv.z);
+                    v[u].w = __fmul_rn(__fmul_rn(v[u].w, inv), wv.w);
+                }
+            }
+            named_bar_compute();  // every read of the activation region is done
+            uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
+            const int pstride = (int)((a.rb + 15) & ~15LL);
+            float* pinv = reinterpret_cast<float*>(planes + 3 * pstride);
+            q8_build_planes<GV_PRO_UNROLL>(v, a.K, nth, tid, planes, pstride, pinv);
+            named_bar_compute();
+            const int unit = (warp % a.KS) * U + pu;
+#pragma unroll
+            for (int i = 0; i < 51; ++i) pl[i] = 0u;
+            if (pact) {
+                const uint32_t* pw = reinterpret_cast<const uint32_t*>(planes + (size_t)unit * 68);
+#pragma unroll
+                for (int i = 0; i < 17; ++i) {
+                    pl[i] = pw[i];
+                    pl[17 + i] = pw[pstride / 4 + i];
+                    pl[34 + i] = pw[pstride / 2 + i];
+                }
+                invA = pinv[2 * unit];
+                invB = pinv[2 * unit + 1];
+            }
+        }
+    }
+    for (int m = 0; m < a.M && !use_int; ++m) {
         float* xm = xs + m * xl;
         if (a.pro == PRO_EMBED_RMSNORM) {
             int tok = a.tokens[m];
@@ -143,11 +228,11 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             }
         }
     }
-    named_bar_compute();
-    if (a.pro == PRO_EMBED_RMSNORM && blockIdx.x == 0)
+    if (!use_int) named_bar_compute();
+    if (!use_int && a.pro == PRO_EMBED_RMSNORM && blockIdx.x == 0)
         for (int m = 0; m < a.M; ++m)
             for (int e = tid; e < a.K; e += nth) a.x_out[(size_t)m * a.ldx + e] = xs[m * xl + xpad(e)];
-    if (a.pro != PRO_COPY) {
+    if (!use_int && a.pro != PRO_COPY) {
         // rmsnorm (src/layers.cpp:7-12): sum of squares in double, inv in float,
         // out = (x * inv) * w.
         for (int m = 0; m < a.M; ++m) {
@@ -188,7 +273,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             }
         }
     }
-    named_bar_compute();
+    if (!use_int) named_bar_compute();
 
     // ---------------- consumers: main loop ----------------
     const int kseg = a.K / a.KS;
@@ -209,9 +294,25 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const uintptr_t g = reinterpret_cast<uintptr_t>(a.W + (long long)si0 * a.P * a.rb);
             const uint8_t* sb = stages + (size_t)slot * a.stage_bytes + (g & 15);
             const uint8_t* ib = sb + (long long)my_item * a.P * a.rb;
+            if constexpr (INTQ) {
+                {
+                    float v = 0.f;
+                    if (pact && prow < a.P)
+                        v = unit_dot_q8_int(
+                            reinterpret_cast<const uint32_t*>(ib + (long long)prow * a.rb + (size_t)(my_ks * U + pu) * 68),
+                            pl, invA, invB);
+                    v += __shfl_xor_sync(0xffffffffu, v, 8);
+                    v += __shfl_xor_sync(0xffffffffu, v, 4);
+                    v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v += __shfl_xor_sync(0xffffffffu, v, 1);
+                    if (a.P == 1) v += __shfl_xor_sync(0xffffffffu, v, 16);
+                    acc0[0] = __shfl_sync(0xffffffffu, v, 0);
+                    acc1[0] = __shfl_sync(0xffffffffu, v, 16);
+                }
+            }
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                if (p < a.P) {
+                if (p < a.P && !use_int) {
                     const uint8_t* rowp = ib + (long long)p * a.rb;
                     float part[MAXM];
 #pragma unroll
@@ -327,6 +428,17 @@ static int pick_maxm(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 // Choose the k-split and stage size for a weight shape (see GemvArgs).
 // k-split and stage size for a weight shape and `warps` consumer warps: the smallest split
 // whose stage (warps/KS items) fits `budget` bytes.
+// The exact-integer Q8_0 path is the default; TFB200_Q8_INT=0 selects the fp32 path (both
+// are exact-product paths of the same sums; the switch exists for measurement).
+static bool q8_int_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_Q8_INT");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const int be = blk_elems(a.wtype) == 1 ? 32 : blk_elems(a.wtype);
     const bool q8fast = (a.wtype == T_Q8_0) && (a.K % 64 == 0);
@@ -344,6 +456,10 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     a.KS = best;
     // the fast path reads 4-byte words: rows must start 4-byte aligned
     a.fast = q8fast && ((a.K / best) % 64 == 0) && ((reinterpret_cast<uintptr_t>(a.W) & 3) == 0);
+    // integer path: one activation row, every lane of a warp on one 64-element unit of one of
+    // the item's P rows, the whole row prologue held in registers (K <= 8192)
+    const int units = a.K / best / 64;
+    a.intq = a.fast && a.M == 1 && units * a.P <= 32 && a.K <= GV_WARPS * 32 * 4 * GV_PRO_UNROLL && q8_int_enabled();
     const long long payload = (long long)(warps / best) * a.P * a.rb;
     a.stage_bytes = (int)((payload + 32 + 15) & ~15LL);
 }
@@ -357,25 +473,27 @@ int gemv_max_rows(int K) {
     return m < 1 ? 1 : (m > GV_MAXM ? GV_MAXM : m);
 }
 
-template <int MAXM>
+template <int MAXM, bool INTQ>
 static cudaError_t init_one() {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<MAXM>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaError_t e =
+        cudaFuncSetAttribute(gemv_kernel<MAXM, INTQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     // every kernel of the step asks for the same (maximal) shared-memory carve-out, so the
     // SMs never have to drain to re-partition L1 / shared memory between kernels
-    return cudaFuncSetAttribute(gemv_kernel<MAXM>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    return cudaFuncSetAttribute(gemv_kernel<MAXM, INTQ>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                 cudaSharedmemCarveoutMaxShared);
 }
 
 cudaError_t gemv_init_attrs() {
     cudaError_t e;
-    if ((e = init_one<1>())) return e;
-    if ((e = init_one<2>())) return e;
-    if ((e = init_one<4>())) return e;
-    return init_one<8>();
+    if ((e = init_one<1, false>())) return e;
+    if ((e = init_one<1, true>())) return e;
+    if ((e = init_one<2, false>())) return e;
+    if ((e = init_one<4, false>())) return e;
+    return init_one<8, false>();
 }
 
-template <int MAXM>
+template <int MAXM, bool INTQ>
 static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     const size_t smem = gemv_smem_bytes(a.M, a.K, a.stage_bytes, MAXM);
     cudaLaunchConfig_t cfg = {};
@@ -388,15 +506,15 @@ static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<MAXM>, a);
+    return cudaLaunchKernelEx(&cfg, gemv_kernel<MAXM, INTQ>, a);
 }
 
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     switch (pick_maxm(a.M)) {
-        case 1: return launch_t<1>(a, grid, st, pdl);
-        case 2: return launch_t<2>(a, grid, st, pdl);
-        case 4: return launch_t<4>(a, grid, st, pdl);
-        default: return launch_t<8>(a, grid, st, pdl);
+        case 1: return a.intq ? launch_t<1, true>(a, grid, st, pdl) : launch_t<1, false>(a, grid, st, pdl);
+        case 2: return launch_t<2, false>(a, grid, st, pdl);
+        case 4: return launch_t<4, false>(a, grid, st, pdl);
+        default: return launch_t<8, false>(a, grid, st, pdl);
     }
 }
 
