@@ -43,6 +43,73 @@ struct PrefillAttnArgs {
     int seq, n_head, n_kv, hd;
 };
 
+// ---- device helpers shared by the attention kernels ----
+__device__ __forceinline__ float kv_load(const void* base, long long idx, int t) {
+    if (t == KV_F32) return reinterpret_cast<const float*>(base)[idx];
+    if (t == KV_F16) return __half2float(reinterpret_cast<const __half*>(base)[idx]);
+    return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[idx]);
+}
+__device__ __forceinline__ float kv_round(float v, int t) {
+    if (t == KV_F32) return v;
+    if (t == KV_F16) return __half2float(__float2half_rn(v));
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ void kv_store(void* base, long long idx, int t, float v) {
+    if (t == KV_F32) reinterpret_cast<float*>(base)[idx] = v;
+    else if (t == KV_F16) reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+}
+
+// NeoX rotate-half with the reference's contraction (src/attention.cpp:31-41 built by g++:
+// x0*c - x1*s -> fma(x0, c, -(x1*s)); x0*s + x1*c -> fma(x0, s, x1*c)).
+__device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) {
+    const float x0 = a, x1 = b;
+    a = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+    b = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+}
+
+// Loads `n` consecutive cache elements starting at element `e0` into dst[] as floats, all
+// loads in flight before the stores (one memory round trip), 16-byte vectors.
+__device__ __forceinline__ void load_tile(float* dst, int dst_stride, int hd, const void* base, long long e0, int np,
+                                          int kv_type, int nth) {
+    const int tid = threadIdx.x;
+    const int per_vec = kv_type == KV_F32 ? 4 : 8;      // elements per 16-byte vector
+    const int nvec = np * hd / per_vec;
+    for (int v0 = tid; v0 < nvec; v0 += nth * 4) {
+        uint4 r[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int v = v0 + u * nth;
+            if (v < nvec) r[u] = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + (e0 * (kv_type == KV_F32 ? 4 : 2)))[v];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int v = v0 + u * nth;
+            if (v >= nvec) continue;
+            const int e = v * per_vec;
+            const int p = e / hd, d = e % hd;
+            float* o = dst + (size_t)p * dst_stride + d;
+            if (kv_type == KV_F32) {
+                const float4 f = *reinterpret_cast<const float4*>(&r[u]);
+                o[0] = f.x; o[1] = f.y; o[2] = f.z; o[3] = f.w;
+            } else {
+                const uint32_t w4[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const uint32_t lo = w4[j] & 0xFFFFu, hi = w4[j] >> 16;
+                    if (kv_type == KV_F16) {
+                        o[2 * j] = __half2float(__ushort_as_half((unsigned short)lo));
+                        o[2 * j + 1] = __half2float(__ushort_as_half((unsigned short)hi));
+                    } else {
+                        o[2 * j] = __uint_as_float(lo << 16);
+                        o[2 * j + 1] = __uint_as_float(hi << 16);
+                    }
+                }
+            }
+        }
+    }
+}
+
 int attn_pick_split(int cap);
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl);
 cudaError_t attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st);

@@ -80,6 +80,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Polls of a cross-CTA wait (a grid barrier or a flag another CTA of the same grid sets)
+// before it gives up and reports an error.
+constexpr int kGridPolls = 1 << 20;
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // 1-D bulk copy global -> shared (TMA engine), completion signalled on `bar` as tx bytes.
 // dst, src and bytes must be multiples of 16.  No cluster multicast.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

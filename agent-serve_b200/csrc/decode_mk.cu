@@ -29,16 +29,10 @@
 
 namespace tfb {
 
-constexpr int kGridPolls = 1 << 20;
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 2, %0;" ::"n"(MK_THREADS) : "memory"); }
 __device__ __forceinline__ void kbar() { asm volatile("bar.sync 1, %0;" ::"n"(MK_THREADS) : "memory"); }
 
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 // Non-blocking test of an mbarrier phase.
 __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
     uint32_t ok;

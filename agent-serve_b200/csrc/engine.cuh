@@ -16,6 +16,7 @@ namespace tfb {
 void gemv_plan(GemvArgs& a);
 void gemv_plan_w(GemvArgs& a, int warps, int budget);
 int gemv_grid(const GemvArgs& a, int num_sms);
+int gemv_slots(int num_sms);  // resident GEMV CTAs the device holds (SMs x CTAs per SM)
 int gemv_max_rows(int K);
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl);
 cudaError_t gemv_init_attrs();

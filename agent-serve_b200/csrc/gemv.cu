@@ -28,6 +28,181 @@ __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
 
+// ---- fused decode attention (one kv head per CTA, appended to the QKV GEMV grid) ----------
+// Model::layer_decode's apply_rope on q and k, KVCache::store and attn_decode for kv head
+// kvh (src/model.cpp:125-129, src/attention.cpp:31-80), M == 1.  The cached K/V rows are
+// loaded into shared memory before the q/k/v of this step exist (they do not depend on
+// them), so the load overlaps the GEMV CTAs' work; then the CTA waits (bounded) until every
+// GEMV CTA has stored its rows, rotates, stores the new k/v and attends over [ws, pos] in
+// tiles of `tp` positions with an online softmax (one tile up to ~150 positions at hd 64).
+// Per tile the arithmetic is that of attn_decode_kernel for one split.
+__device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int kvh, int G) {
+    const AttnArgs& t = a.at;
+    const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
+    const int hd = t.hd, d2 = hd / 2, n_rep = t.n_head / t.n_kv;
+    float* f = reinterpret_cast<float*>(smem);
+    float* qs = f;                                  // [n_rep][hd]
+    float* kn = qs + n_rep * hd;                    // [hd]
+    float* vn = kn + hd;                            // [hd]
+    float* mx = vn + hd;                            // [n_rep]
+    float* ls = mx + n_rep;                         // [n_rep]
+    float* al = ls + n_rep;                         // [n_rep]
+    int* flag = reinterpret_cast<int*>(al + n_rep); // [1]
+    float* sc = al + n_rep + 4;                     // [n_rep][tp]
+    const int fixed = n_rep * hd + 2 * hd + 3 * n_rep + 4;
+    int tp = (int)((avail / 4 - fixed) / (n_rep + 2 * hd + 1));
+    tp = tp > 256 ? 256 : tp;
+    float* ks = sc + n_rep * tp;                    // [tp][hd + 1]
+    float* vs = ks + (size_t)tp * (hd + 1);         // [tp][hd]
+
+    pdl_trigger();
+    pdl_wait();
+    const int slot = t.slots ? t.slots[0] : 0;
+    const int pos = t.pos[slot];
+    const bool pos_ok = pos >= 0 && pos < t.cap && tp >= 1;
+    const int ws = pos_ok ? ((t.wstart) ? min(max(t.wstart[slot], 0), pos) : 0) : 0;
+    const size_t cache_off = (size_t)slot * t.slot_stride + (size_t)kvh * t.cap * hd;
+    // the first tile's cached rows, before q/k/v are ready
+    if (pos_ok) {
+        const int np = min(pos + 1, ws + tp) - ws;
+        const int npc = (ws + np == pos + 1) ? np - 1 : np;
+        load_tile(ks, hd + 1, hd, t.kc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
+        load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
+    }
+    if (tid == 0) {
+        int ok = 1;
+        if (!pos_ok) {
+            atomicCAS(t.err, 0, ERR_POS);
+            ok = 0;
+        } else {
+            int i = 0;
+            for (; i < kGridPolls; ++i) {
+                if (ld_acquire_gpu(a.sync) >= (unsigned)G) break;
+                if (i > 64) __nanosleep(i > 65536 ? 1024 : 32);
+            }
+            if (i == kGridPolls) {
+                atomicCAS(t.err, 0, ERR_GRID_SYNC);
+                ok = 0;
+            }
+        }
+        *flag = ok;
+    }
+    __syncthreads();
+    if (*flag) {
+        const float* row = t.qkv;
+        for (int i = tid; i < n_rep * hd; i += nth) qs[i] = __ldcg(row + (size_t)kvh * n_rep * hd + i);
+        for (int i = tid; i < hd; i += nth) {
+            kn[i] = __ldcg(row + (size_t)t.n_head * hd + (size_t)kvh * hd + i);
+            vn[i] = __ldcg(row + (size_t)(t.n_head + t.n_kv) * hd + (size_t)kvh * hd + i);
+        }
+        if (tid < n_rep) {
+            mx[tid] = -INFINITY;
+            ls[tid] = 0.f;
+        }
+        __syncthreads();
+        const float* cp = t.cosb + (size_t)pos * d2;
+        const float* sp = t.sinb + (size_t)pos * d2;
+        for (int i = tid; i < (n_rep + 1) * d2; i += nth) {
+            const int h = i / d2, j = i % d2;
+            if (h < n_rep) rope_pair(qs[h * hd + j], qs[h * hd + j + d2], cp[j], sp[j]);
+            else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
+        }
+        __syncthreads();
+        for (int i = tid; i < hd; i += nth) {
+            kv_store(t.kc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, kn[i]);
+            kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
+        }
+        const float scale = 1.0f / sqrtf((float)hd);
+        constexpr int PER = (AT_MAX_REP * AT_MAX_HD + GV_THREADS - 1) / GV_THREADS;
+        float acc[PER];
+#pragma unroll
+        for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+        for (int t0 = ws; t0 <= pos; t0 += tp) {
+            const int np = min(pos + 1, t0 + tp) - t0;
+            const bool last = t0 + np == pos + 1;
+            if (t0 != ws) {
+                load_tile(ks, hd + 1, hd, t.kc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np,
+                          t.kv_type, nth);
+                load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np,
+                          t.kv_type, nth);
+            }
+            if (last)
+                for (int i = tid; i < hd; i += nth) {
+                    // the new key/value enter at the stored precision, as later steps read them
+                    ks[(size_t)(np - 1) * (hd + 1) + i] = kv_round(kn[i], t.kv_type);
+                    vs[(size_t)(np - 1) * hd + i] = kv_round(vn[i], t.kv_type);
+                }
+            __syncthreads();
+            for (int i = tid; i < n_rep * np; i += nth) {
+                const int h = i / np, p = i % np;
+                const float* kp = ks + (size_t)p * (hd + 1);
+                const float* qh = qs + h * hd;
+                float s0 = 0.f, s1 = 0.f;
+                for (int d = 0; d < hd; d += 2) {
+                    s0 = fmaf(qh[d], kp[d], s0);
+                    s1 = fmaf(qh[d + 1], kp[d + 1], s1);
+                }
+                sc[h * tp + p] = scale * (s0 + s1);
+            }
+            __syncthreads();
+            for (int h = warp; h < n_rep; h += nw) {
+                float tm = -INFINITY;
+                for (int i = lane; i < np; i += 32) tm = fmaxf(tm, sc[h * tp + i]);
+                tm = warp_max(tm);
+                const float mnew = fmaxf(mx[h], tm);
+                float lt = 0.f;
+                for (int i = lane; i < np; i += 32) {
+                    const float e = expf(sc[h * tp + i] - mnew);
+                    sc[h * tp + i] = e;
+                    lt += e;
+                }
+                lt = warp_sum(lt);
+                if (lane == 0) {
+                    const float alpha = expf(mx[h] - mnew);  // 0 on the first tile
+                    al[h] = alpha;
+                    ls[h] = fmaf(ls[h], alpha, lt);
+                    mx[h] = mnew;
+                }
+            }
+            __syncthreads();
+#pragma unroll
+            for (int k = 0; k < PER; ++k) {
+                const int i = tid + k * nth;
+                if (i < n_rep * hd) {
+                    const int h = i / hd, d = i % hd;
+                    const float* sh = sc + h * tp;
+                    float a0 = acc[k] * al[h], a1 = 0.f;
+                    int p = 0;
+                    for (; p + 1 < np; p += 2) {
+                        a0 = fmaf(sh[p], vs[(size_t)p * hd + d], a0);
+                        a1 = fmaf(sh[p + 1], vs[(size_t)(p + 1) * hd + d], a1);
+                    }
+                    if (p < np) a0 = fmaf(sh[p], vs[(size_t)p * hd + d], a0);
+                    acc[k] = a0 + a1;
+                }
+            }
+            __syncthreads();
+        }
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {
+            const int i = tid + k * nth;
+            if (i < n_rep * hd) {
+                const int h = i / hd, d = i % hd;
+                t.out[(size_t)(kvh * n_rep + h) * hd + d] = acc[k] / ls[h];
+            }
+        }
+    }
+    // leave; the last attention CTA out clears the counters for this layer's next step
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned d = atomicAdd(a.sync + 1, 1u);
+        if (d == (unsigned)a.attn_ctas - 1) {
+            a.sync[0] = 0u;
+            a.sync[1] = 0u;
+        }
+    }
+}
+
 template <int MAXM, bool INTQ>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -44,8 +219,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + GV_STAGES);
     unsigned long long* ckey = reinterpret_cast<unsigned long long*>(empty + GV_STAGES + 1);
 
-    const int i0 = (int)((long long)a.n_items * blockIdx.x / gridDim.x);
-    const int i1 = (int)((long long)a.n_items * (blockIdx.x + 1) / gridDim.x);
+    // CTAs [0, attn_ctas) are the fused attention CTAs (first, so they are resident and load
+    // their K/V rows while the GEMV CTAs work); GEMV CTA gb = blockIdx.x - attn_ctas
+    const int G = (int)gridDim.x - a.attn_ctas;
+    const int gb = (int)blockIdx.x - a.attn_ctas;
+    if constexpr (INTQ) {
+        if (gb < 0) {
+            fused_attention(a, smem, (size_t)xbytes + (size_t)GV_STAGES * a.stage_bytes, (int)blockIdx.x, G);
+            return;
+        }
+    }
+    const int i0 = (int)((long long)a.n_items * gb / G);
+    const int i1 = (int)((long long)a.n_items * (gb + 1) / G);
     const int RI = GV_WARPS / a.KS;
     const int n_stages = (i1 - i0 + RI - 1) / RI;
     const bool prefetched = (i1 - i0) <= GV_PRE && (a.epi == EPI_RESID || (a.epi == EPI_STORE && a.bias));
@@ -137,7 +322,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
                 }
                 embed_row(xs, a.embd, a.embd_type, a.embd_rb, a.K, tok, nth);
                 named_bar_compute();
-                if (blockIdx.x == 0)
+                if (gb == 0)
                     for (int e = tid; e < a.K; e += nth) a.x_out[e] = xs[xpad(e)];
 #pragma unroll
                 for (int u = 0; u < GV_PRO_UNROLL; ++u) {
@@ -229,7 +414,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         }
     }
     if (!use_int) named_bar_compute();
-    if (!use_int && a.pro == PRO_EMBED_RMSNORM && blockIdx.x == 0)
+    if (!use_int && a.pro == PRO_EMBED_RMSNORM && gb == 0)
         for (int m = 0; m < a.M; ++m)
             for (int e = tid; e < a.K; e += nth) a.x_out[(size_t)m * a.ldx + e] = xs[m * xl + xpad(e)];
     if (!use_int && a.pro != PRO_COPY) {
@@ -388,14 +573,17 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     if (a.epi == EPI_ARGMAX && lane == 0)
         for (int m = 0; m < a.M; ++m)
             if (best[m]) atomicMax(&ckey[m], best[m]);
+    // with fused attention the attention CTAs read this CTA's rows: publish them
+    if (a.attn_ctas && lane == 0) __threadfence();
     named_bar_compute();
+    if (tid == 0 && a.attn_ctas) red_release_gpu_add(a.sync, 1u);
     if (tid == 0) {
         if (a.epi == EPI_ARGMAX)
             for (int m = 0; m < a.M; ++m) atomicMax(&a.keys[m], ckey[m]);
         if (a.fin != FIN_NONE) {
             __threadfence();
             const unsigned t = atomicAdd(&a.ctl->done, 1u);
-            if (t == gridDim.x - 1) {
+            if (t == (unsigned)G - 1) {
                 __threadfence();
                 const int gs = atomicAdd(&a.ctl->gen_step, 0);
                 for (int m = 0; m < a.M; ++m) {
@@ -532,6 +720,8 @@ static int gemv_ctas_per_sm() {
     }
     return v;
 }
+
+int gemv_slots(int num_sms) { return num_sms * gemv_ctas_per_sm(); }
 
 int gemv_grid(const GemvArgs& a, int num_sms) {
     const int RI = GV_WARPS / a.KS;

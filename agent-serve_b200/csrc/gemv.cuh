@@ -6,6 +6,7 @@
 // that Model::layer_decode (src/model.cpp:108-142) makes around each matmul.
 #pragma once
 
+#include "attention.cuh"
 #include "common.cuh"
 
 namespace tfb {
@@ -70,6 +71,13 @@ struct GemvArgs {
     const int* slots;    // slot of activation row m
     int* hist;           // FIN_ARGMAX: generated ids [hist_cap][M] (optional)
     int* err;
+    // fused decode attention (integer path, M == 1, the QKV GEMV): the last attn_ctas CTAs
+    // of the grid own one kv head each (RoPE, KV store, attention of `at`); they wait for
+    // the q/k/v rows through sync[0] (GEMV CTAs arrive when their rows are stored) and
+    // leave through sync[1] (the last one out clears both)
+    int attn_ctas;
+    unsigned* sync;
+    AttnArgs at;
 };
 
 }  // namespace tfb

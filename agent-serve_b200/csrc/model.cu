@@ -100,6 +100,7 @@ struct tf_model {
     int tile = 1;
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
     unsigned* counters = nullptr;
+    unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
     unsigned long long* keys = nullptr;
     int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_wstart = nullptr, *d_hist = nullptr;
     int *d_prompt = nullptr, *d_err = nullptr;
@@ -180,10 +181,58 @@ GemvArgs gemv_base(tf_model* m, const WeightRef& w, int n_items, int P, int M) {
     return a;
 }
 
-int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch) {
+// Decode attention arguments of layer li (fresh step: RoPE + KV store + attention).
+AttnArgs attn_args(tf_model* m, int li) {
+    AttnArgs a;
+    memset(&a, 0, sizeof(a));
+    a.qkv = m->qkv;
+    a.ld_qkv = m->H + 2 * m->KV;
+    const size_t esz = m->opt.kv_type == TF_KV_F32 ? 4 : 2;
+    a.kc = static_cast<uint8_t*>(m->kc) + (size_t)li * m->layer_elems * esz;
+    a.vc = static_cast<uint8_t*>(m->vc) + (size_t)li * m->layer_elems * esz;
+    a.slot_stride = m->slot_elems;
+    a.cap = m->opt.max_seq;
+    a.kv_type = m->opt.kv_type;
+    a.pos = m->d_pos;
+    a.wstart = m->d_wstart;
+    a.slots = m->d_slots;
+    a.cosb = m->cosb;
+    a.sinb = m->sinb;
+    a.n_head = m->hp.n_head;
+    a.n_kv = m->hp.n_kv_head;
+    a.hd = m->hd;
+    a.n_split = m->n_split;
+    a.part = m->part;
+    a.counters = m->counters;
+    a.out = m->attn;
+    a.ld_out = m->H;
+    a.fresh = 1;
+    a.err = m->d_err;
+    return a;
+}
+
+// Decode attention runs inside the QKV kernel (one CTA per kv head appended to its grid)
+// for batch-1 steps that end at or below this position; longer contexts use the split
+// flash-decode kernel, whose CTAs cover the positions in parallel.
+constexpr int kFusedAttnMaxPos = 1024;
+
+static bool fused_attn_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_FUSED_ATTN");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
+// Whether batch-1 steps of slot `seq` up to position end_pos may fuse the attention.
+bool fuse_attn_ok(const tf_model* m, int end_pos) { return fused_attn_enabled() && end_pos <= kFusedAttnMaxPos; }
+
+int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fused) {
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
+    bool fuse = false;
     for (int li = 0; li < m->hp.n_layer; ++li) {
         const LayerDev& Ld = m->L[li];
         {   // [embedding +] rmsnorm + fused QKV GEMV + bias
@@ -203,35 +252,20 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch) {
             a.y = m->qkv;
             a.ldy = ldq;
             a.bias = Ld.bqkv;
-            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            fuse = fused && M == 1 && a.intq;
+            int grid = gemv_grid(a, m->num_sms);
+            if (fuse) {
+                // the attention CTAs take slots of the GEMV grid so that all stay resident
+                a.attn_ctas = m->hp.n_kv_head;
+                a.sync = m->d_async + 2 * li;
+                a.at = attn_args(m, li);
+                grid = std::max(1, std::min(grid, gemv_slots(m->num_sms) - a.attn_ctas));
+            }
+            CK(gemv_launch(a, grid + a.attn_ctas, m->stream, pdl));
             ++launches;
         }
-        {   // RoPE + KV store + attention
-            AttnArgs a;
-            memset(&a, 0, sizeof(a));
-            a.qkv = m->qkv;
-            a.ld_qkv = ldq;
-            const size_t esz = m->opt.kv_type == TF_KV_F32 ? 4 : 2;
-            a.kc = static_cast<uint8_t*>(m->kc) + (size_t)li * m->layer_elems * esz;
-            a.vc = static_cast<uint8_t*>(m->vc) + (size_t)li * m->layer_elems * esz;
-            a.slot_stride = m->slot_elems;
-            a.cap = m->opt.max_seq;
-            a.kv_type = m->opt.kv_type;
-            a.pos = m->d_pos;
-            a.wstart = m->d_wstart;
-            a.slots = m->d_slots;
-            a.cosb = m->cosb;
-            a.sinb = m->sinb;
-            a.n_head = m->hp.n_head;
-            a.n_kv = m->hp.n_kv_head;
-            a.hd = m->hd;
-            a.n_split = m->n_split;
-            a.part = m->part;
-            a.counters = m->counters;
-            a.out = m->attn;
-            a.ld_out = H;
-            a.fresh = 1;
-            a.err = m->d_err;
+        if (!fuse) {   // RoPE + KV store + attention
+            AttnArgs a = attn_args(m, li);
             CK(attn_decode_launch(a, M, m->stream, pdl));
             ++launches;
         }
@@ -302,14 +336,14 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch) {
 }
 
 // Run one step for M rows (tokens in d_tokens[0..M), slots in d_slots[0..M)).
-int run_step(tf_model* m, int M, bool head) {
-    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr);
-    const long long key = (long long)M * 2 + (head ? 1 : 0);
+int run_step(tf_model* m, int M, bool head, bool fused) {
+    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused);
+    const long long key = (long long)M * 4 + (head ? 1 : 0) + (fused ? 2 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(m, M, head, true, nullptr);
+        int rc = enqueue_step(m, M, head, true, nullptr, fused);
         cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -557,7 +591,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_phases, m->d_bar};
+                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async};
     for (void* p : dev)
         if (p) cudaFree(p);
     if (m->hi) cudaFreeHost(m->hi);
@@ -826,6 +860,8 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMalloc(&m->d_prompt, sizeof(int) * ((size_t)o.max_seq + 1)));
     CKD(cudaMalloc(&m->d_err, sizeof(int)));
     CKD(cudaMemset(m->d_err, 0, sizeof(int)));
+    CKD(cudaMalloc(&m->d_async, sizeof(unsigned) * 2 * hp.n_layer));
+    CKD(cudaMemset(m->d_async, 0, sizeof(unsigned) * 2 * hp.n_layer));
     CKD(cudaMalloc(&m->ctl, sizeof(StepCtl)));
     CKD(cudaMemset(m->ctl, 0, sizeof(StepCtl)));
     CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
@@ -838,7 +874,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         // count launches of one step (no device work: enqueue into a throwaway capture)
         cudaGraph_t g = nullptr;
         CKD(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(m, 1, true, true, &n);
+        int rc = enqueue_step(m, 1, true, true, &n, fuse_attn_ok(m, 1));
         cudaStreamEndCapture(m->stream, &g);
         if (g) cudaGraphDestroy(g);
         if (rc) BAD(m->err);
@@ -878,7 +914,7 @@ int tf_cuda_decode(tf_model* m, int seq, int token, float* logits, int* argmax_o
     if (set_slot_row(m, 0, seq, token)) return -1;
     if (m->mk) {
         if (run_mk(m, seq, m->d_tokens, 1, 1, 0, 0, 0)) return -1;
-    } else if (run_step(m, 1, true)) {
+    } else if (run_step(m, 1, true, fuse_attn_ok(m, m->hpos[seq] + 1))) {
         return -1;
     }
     m->hpos[seq] += 1;
@@ -911,7 +947,7 @@ int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logit
     if (set_slot_row(m, 0, seq, tokens[0])) return -1;
     for (int i = 0; i < n; ++i) {
         CK(cudaMemcpyAsync(m->d_tokens, m->d_prompt + i, sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
-        if (run_step(m, 1, i == n - 1)) return -1;
+        if (run_step(m, 1, i == n - 1, fuse_attn_ok(m, m->hpos[seq] + n))) return -1;
     }
     CK(cudaMemcpyAsync(m->d_wstart + seq, m->hi + 3, sizeof(int), cudaMemcpyHostToDevice, m->stream));
     m->hpos[seq] += n;
@@ -934,8 +970,9 @@ int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eo
         StepCtl c = {0u, 0, n, 0};
         memcpy(m->hi + 4, &c, sizeof(c));
         CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
+        const bool fz = fuse_attn_ok(m, m->hpos[seq] + n);
         for (int i = 0; i < n; ++i)
-            if (run_step(m, 1, true)) return -1;
+            if (run_step(m, 1, true, fz)) return -1;
     }
     int* hist = m->hi + 64;
     CK(cudaMemcpyAsync(hist, m->d_hist, sizeof(int) * n, cudaMemcpyDeviceToHost, m->stream));
@@ -982,7 +1019,7 @@ int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int
         memcpy(m->hi + 24, seq_ids + b0, sizeof(int) * T);
         CK(cudaMemcpyAsync(m->d_tokens, m->hi + 8, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
         CK(cudaMemcpyAsync(m->d_slots, m->hi + 24, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
-        if (run_step(m, T, true)) return -1;
+        if (run_step(m, T, true, false)) return -1;
         for (int b = 0; b < T; ++b) m->hpos[seq_ids[b0 + b]] += 1;
         int rc = read_outputs(m, T, logits ? logits + (size_t)b0 * m->V : nullptr, argmax_out ? argmax_out + b0 : nullptr);
         if (rc) return rc;
