@@ -38,6 +38,9 @@ from tinferno_b200 import synth  # noqa: E402
 
 CFG = synth.CFG0
 PROMPT = 32
+# DRAM bytes (read + write) of one lm_head GEMV launch, from an ncu capture of
+# `bench.py --kernel lmhead` (profiles/gemv_q8_0_lmhead_128256x2048.md)
+LMHEAD_TRAFFIC = 284_945_408
 
 
 def peaks():
@@ -281,7 +284,8 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
     ach = alg / t / 1e9
     return {"bound": "hbm", "kernel": "gemv_kernel<1> (Q8_0, lm_head 128256x2048)", "achieved": round(ach, 1),
             "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": kind,
-            "traffic": None, "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
+            "traffic": LMHEAD_TRAFFIC, "traffic_source": "ncu dram__bytes_read+write of one launch, "
+            "profiles/gemv_q8_0_lmhead_128256x2048.md", "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
 
 
 def main():
