@@ -1,0 +1,379 @@
+// Q8_0 GEMM for M >= 16 activation rows on the f16 tensor pipe (see gemm.cuh).
+//
+// CTA tile: 128 weight rows x 128 activation rows, k in stages of 64 (two Q8_0 blocks),
+// double-buffered.  Per stage the CTA dequantises its 128 x 64 weights (one thread per row
+// and block: 34 bytes -> 32 exact products q*d*2^sw -> f16 halves Wh, Wl) into shared memory,
+// while the activation halves Xh, Xl (prepared once per matmul by xprep_kernel) arrive by
+// cp.async.  Eight warps each own 32 weight rows x 64 activation rows and issue
+// mma.m16n8k16 (f16 in, f32 accumulate) three times per fragment pair: Wh*Xh, Wh*Xl, Wl*Xh.
+// The epilogue scales back by 2^-(sw+sx[m]), stages the tile in shared memory and applies
+// the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
+// greedy argmax keys).
+#include "dots.cuh"
+#include "gemm.cuh"
+
+namespace tfb {
+
+// ---- activation preparation ----------------------------------------------------------------
+// One CTA per activation row: [embedding lookup ->] [RMSNorm (src/layers.cpp:7-12) ->]
+// power-of-two scale to |x| < 2^14 -> f16 halves.
+__global__ void __launch_bounds__(256) xprep_kernel(const XPrepArgs a) {
+    extern __shared__ __align__(16) float xrow[];  // xpad layout
+    __shared__ double redd[8];
+    __shared__ float redf[8];
+    const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nth = blockDim.x;
+    const int K = a.K, nq = K >> 2;
+    if (a.embd) {
+        int tok = a.tokens[m];
+        if (tok < 0 || tok >= a.n_vocab) {
+            if (tid == 0) atomicCAS(a.err, 0, ERR_BAD_TOKEN);
+            tok = 0;
+        }
+        embed_row(xrow, a.embd, a.embd_type, a.embd_rb, K, tok, nth);
+        __syncthreads();
+        for (int e = tid; e < K; e += nth) a.x_out[(size_t)m * a.ldx + e] = xrow[xpad(e)];
+    } else {
+        const float4* xg = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx);
+        for (int c = tid; c < nq; c += nth) *reinterpret_cast<float4*>(xrow + xpad(4 * c)) = xg[c];
+    }
+    __syncthreads();
+    if (a.norm_w) {
+        double ss = 0.0;
+        for (int c = tid; c < nq; c += nth) {
+            const float4 v = *reinterpret_cast<const float4*>(xrow + xpad(4 * c));
+            ss = fma((double)v.x, (double)v.x, ss);
+            ss = fma((double)v.y, (double)v.y, ss);
+            ss = fma((double)v.z, (double)v.z, ss);
+            ss = fma((double)v.w, (double)v.w, ss);
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) redd[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < nth / 32; ++w) tot += redd[w];
+        const float inv = 1.0f / sqrtf((float)(tot / K) + a.eps);
+        for (int c = tid; c < nq; c += nth) {
+            float4* p = reinterpret_cast<float4*>(xrow + xpad(4 * c));
+            const float4 w = reinterpret_cast<const float4*>(a.norm_w)[c];
+            float4 v = *p;
+            v.x = __fmul_rn(__fmul_rn(v.x, inv), w.x);
+            v.y = __fmul_rn(__fmul_rn(v.y, inv), w.y);
+            v.z = __fmul_rn(__fmul_rn(v.z, inv), w.z);
+            v.w = __fmul_rn(__fmul_rn(v.w, inv), w.w);
+            *p = v;
+        }
+        __syncthreads();
+    }
+    float am = 0.f;
+    for (int e = tid; e < K; e += nth) am = fmaxf(am, fabsf(xrow[xpad(e)]));
+    am = warp_max(am);
+    if (lane == 0) redf[warp] = am;
+    __syncthreads();
+    am = 0.f;
+    for (int w = 0; w < nth / 32; ++w) am = fmaxf(am, redf[w]);
+    // am < 2^(be-126) for a normal am with biased exponent be: 2^sx = 2^(140-be) keeps the
+    // scaled row below 2^14; zero / subnormal rows take the largest shift
+    const int be = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+    int sx = 140 - be;
+    sx = sx > 100 ? 100 : (sx < -100 ? -100 : sx);
+    const float S = ldexpf(1.0f, sx);
+    __half* xh = a.xh + (size_t)m * K;
+    __half* xl = a.xl + (size_t)m * K;
+    for (int e = tid; e < K; e += nth) {
+        const float v = xrow[xpad(e)] * S;  // exact: a power-of-two scale
+        const __half h = __float2half_rn(v);
+        xh[e] = h;
+        xl[e] = __float2half_rn(v - __half2float(h));
+    }
+    if (tid == 0) a.sx[m] = sx;
+}
+
+// ---- the GEMM ------------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
+// shared memory of one stage: Wh, Wl [BN][LDS], Xh, Xl [BM][LDS] halves
+constexpr int GM_TILE_H = GM_BN * GM_LDS;  // halves per operand tile
+constexpr size_t GM_STAGE_BYTES = (size_t)4 * GM_TILE_H * 2;
+constexpr int GM_EPI_LD = GM_BN + 4;         // epilogue tile row stride (floats)
+
+// The 9 words of weight row r, k-stage kc, block half j (j = 0: bytes 0..35 of the stage's
+// 68-byte unit, j = 1: bytes 32..67).
+__device__ __forceinline__ void gm_load_w(uint32_t (&w)[9], const GemmArgs& a, int n, int kc, int j) {
+    if (n < a.N) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a.W + (long long)n * a.rb + (long long)kc * 68) + 8 * j;
+#pragma unroll
+        for (int i = 0; i < 9; ++i) w[i] = __ldg(p + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 9; ++i) w[i] = 0u;
+    }
+}
+
+// Dequantise one Q8_0 block (from the 9 words) into 32 f16 halves Wh, Wl at dh / dl.
+__device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float wscale, __half* dh, __half* dl) {
+    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+    const float d = __half2float(__ushort_as_half((unsigned short)dbits)) * wscale;  // exact
+    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 8 elements per 16-byte store
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            float v2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int b = b0 + 8 * c + e + u;
+                const int q = (int)(int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
+                v2[u] = (float)q * d;  // exact: 8-bit integer times an 11-bit mantissa
+            }
+            const __half h0 = __float2half_rn(v2[0]), h1 = __float2half_rn(v2[1]);
+            const __half l0 = __float2half_rn(v2[0] - __half2float(h0));
+            const __half l1 = __float2half_rn(v2[1] - __half2float(h1));
+            hv[e >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lv[e >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        reinterpret_cast<uint4*>(dh)[c] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        reinterpret_cast<uint4*>(dl)[c] = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
+__global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * GM_BM;
+    const int wn = warp & 3, wm = warp >> 2;
+    const int nk = a.K / GM_BK;
+    const float wscale = ldexpf(1.0f, a.sw);
+
+    auto stage_ptr = [&](int s, int which) {  // which: 0 Wh, 1 Wl, 2 Xh, 3 Xl
+        return reinterpret_cast<__half*>(smem + (size_t)s * GM_STAGE_BYTES) + (size_t)which * GM_TILE_H;
+    };
+    const int wr = tid >> 1, wj = tid & 1;  // this thread's weight row and block half
+    auto load_x = [&](int s, int kc) {
+        // 128 rows x 64 halves per plane = 8 chunks of 16 B per row
+        for (int i = tid; i < 2 * GM_BM * 8; i += GM_THREADS) {
+            const int pl = i / (GM_BM * 8), r = (i / 8) % GM_BM, c = i % 8;
+            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + r) * a.K + (size_t)kc * GM_BK + 8 * c;
+            cp_async16(stage_ptr(s, 2 + pl) + r * GM_LDS + 8 * c, src);
+        }
+        cp_async_commit();
+    };
+
+    uint32_t wv[9];
+    pdl_trigger();
+    pdl_wait();
+    // prologue: stage 0
+    load_x(0, 0);
+    gm_load_w(wv, a, n0 + wr, 0, wj);
+    gm_dequant(wv, wj, wscale, stage_ptr(0, 0) + wr * GM_LDS + 32 * wj, stage_ptr(0, 1) + wr * GM_LDS + 32 * wj);
+    cp_async_wait_all();
+    __syncthreads();
+
+    float acc[2][8][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
+
+    for (int kc = 0; kc < nk; ++kc) {
+        const int s = kc & 1;
+        const bool more = kc + 1 < nk;
+        if (more) {
+            load_x(s ^ 1, kc + 1);
+            gm_load_w(wv, a, n0 + wr, kc + 1, wj);
+        }
+        const __half* sWh = stage_ptr(s, 0);
+        const __half* sWl = stage_ptr(s, 1);
+        const __half* sXh = stage_ptr(s, 2);
+        const __half* sXl = stage_ptr(s, 3);
+#pragma unroll
+        for (int k16 = 0; k16 < GM_BK / 16; ++k16) {
+            uint32_t ah[2][4], al[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int row = wn * 32 + 16 * i + (lane & 15), col = 16 * k16 + 8 * (lane >> 4);
+                ldsm_x4(ah[i], sWh + row * GM_LDS + col);
+                ldsm_x4(al[i], sWl + row * GM_LDS + col);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                uint32_t bh[4], bl[4];
+                const int q = lane >> 3;
+                const int row = wm * 64 + 8 * (2 * jj + (q >> 1)) + (lane & 7), col = 16 * k16 + 8 * (q & 1);
+                ldsm_x4(bh, sXh + row * GM_LDS + col);
+                ldsm_x4(bl, sXl + row * GM_LDS + col);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int j = 2 * jj + h;
+                        mma16816(acc[i][j], ah[i], bh[2 * h], bh[2 * h + 1]);
+                        mma16816(acc[i][j], ah[i], bl[2 * h], bl[2 * h + 1]);
+                        mma16816(acc[i][j], al[i], bh[2 * h], bh[2 * h + 1]);
+                    }
+                }
+            }
+        }
+        if (more)
+            gm_dequant(wv, wj, wscale, stage_ptr(s ^ 1, 0) + wr * GM_LDS + 32 * wj,
+                       stage_ptr(s ^ 1, 1) + wr * GM_LDS + 32 * wj);
+        cp_async_wait_all();
+        __syncthreads();
+    }
+
+    // ---- epilogue: scale back, stage [m][n] in shared memory, apply ----
+    float* tile = reinterpret_cast<float*>(smem);  // [GM_BM][GM_EPI_LD]
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+            const int mm = wm * 64 + 8 * j + 2 * t4 + cc;
+            const int m = m0 + mm;
+            const float sc = m < a.M ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int nn = wn * 32 + 16 * i + g;
+                tile[mm * GM_EPI_LD + nn] = acc[i][j][cc] * sc;
+                tile[mm * GM_EPI_LD + nn + 8] = acc[i][j][2 + cc] * sc;
+            }
+        }
+    }
+    __syncthreads();
+    if (a.epi == EPI_ARGMAX) {
+        if (tid < GM_BM && m0 + tid < a.M) {
+            const int m = m0 + tid;
+            unsigned long long best = 0ull;
+            for (int nn = 0; nn < GM_BN && n0 + nn < a.N; ++nn) {
+                const float v = tile[tid * GM_EPI_LD + nn];
+                const unsigned long long k = argmax_key(v, (uint32_t)(n0 + nn));
+                best = k > best ? k : best;
+            }
+            if (best) atomicMax(&a.keys[m], best);
+        }
+        if (a.store_logits)
+            for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
+                const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+                if (m < a.M && n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
+            }
+        return;
+    }
+    for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
+        const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+        if (m >= a.M || n >= a.N) continue;
+        const float v = tile[mm * GM_EPI_LD + nn];
+        if (a.epi == EPI_STORE) {
+            a.y[(size_t)m * a.ldy + n] = v + (a.bias ? a.bias[n] : 0.f);
+        } else if (a.epi == EPI_RESID) {
+            a.resid[(size_t)m * a.ldr + n] += v;
+        } else if ((n & 1) == 0) {  // EPI_SWIGLU: rows 2i (gate) and 2i+1 (up)
+            const float gt = v, up = tile[mm * GM_EPI_LD + nn + 1];
+            a.y[(size_t)m * a.ldy + (n >> 1)] = __fmul_rn(__fdiv_rn(gt, 1.0f + expf(-gt)), up);
+        }
+    }
+}
+
+// ---- end of a step at M rows ------------------------------------------------------------------
+__global__ void finish_kernel(const FinishArgs a) {
+    __shared__ int gs_s;
+    pdl_trigger();
+    pdl_wait();
+    if (threadIdx.x == 0) gs_s = a.ctl->gen_step;
+    __syncthreads();
+    const int gs = gs_s;
+    for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
+        if (a.argmax) {
+            const unsigned long long k = a.keys[m];
+            a.keys[m] = 0ull;
+            const int tok = (int)key_index(k);
+            a.tok_next[m] = tok;
+            if (a.hist && gs < a.ctl->hist_cap) a.hist[(size_t)gs * a.M + m] = tok;
+        }
+        a.pos[a.slots[m]] += 1;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && a.argmax) a.ctl->gen_step = gs + 1;
+}
+
+// ---- host ----------------------------------------------------------------------------------------
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
+    const size_t smem = (size_t)xpad_len(a.K) * 4;
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(xprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    xprep_kernel<<<a.M, 256, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
+    if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
+    const size_t smem = 2 * GM_STAGE_BYTES;
+    static bool attr_set[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!attr_set[dev]) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set[dev] = true;
+    }
+    dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM);
+    GemmArgs aa = a;
+    void* args[] = {&aa};
+    return launch_pdl((const void*)gemm_q8_kernel, grid, dim3(GM_THREADS), smem, st, args);
+}
+
+cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {
+    FinishArgs aa = a;
+    void* args[] = {&aa};
+    return launch_pdl((const void*)finish_kernel, dim3(1), dim3(256), 0, st, args);
+}
+
+// 2^sw with |q * d| * 2^sw < 2^14 for every block of the matrix (|q| <= 128).
+int q8_scale_exponent(const uint8_t* blocks, size_t nbytes) {
+    unsigned mx = 0;
+    for (size_t o = 0; o + 34 <= nbytes; o += 34) {
+        const unsigned d = ((unsigned)blocks[o] | ((unsigned)blocks[o + 1] << 8)) & 0x7FFFu;
+        mx = d > mx ? d : mx;
+    }
+    if (mx == 0 || mx >= 0x7C00u) return 0;
+    // |d| < 2^(E-14) for the f16 biased exponent E (subnormals: E = 1), so |q*d| < 2^(E-7)
+    // and 2^(21-E) maps the matrix below 2^14
+    const int E = (mx >> 10) > 0 ? (int)(mx >> 10) : 1;
+    return 21 - E;
+}
+
+}  // namespace tfb

@@ -1,0 +1,80 @@
+// Q8_0 GEMM on the tensor cores for M >= 16 activation rows (batched decode, prefill):
+// Y[m][n] = sum_k X[m][k] * W[n][k], W in its GGUF Q8_0 block layout.  Replaces matmul()
+// (src/matmul.cpp:22-73) at M >= 16 together with the rmsnorm / apply_bias / add_inplace /
+// silu_mul / sample_greedy calls around each matmul of Model::layer_decode/layer_prefill.
+//
+// Arithmetic: fp32-equivalent on the f16 tensor pipe.  Every weight q*d (19 significant bits)
+// is split exactly into two f16 halves Wh + Wl after a per-matrix power-of-two scale 2^sw,
+// and every activation into Xh + Xl after a per-row scale 2^sx; the products Wh*Xh, Wh*Xl and
+// Wl*Xh are accumulated in fp32 (the dropped Wl*Xl term is 2^-22 relative).  The result is
+// scaled back by 2^-(sw+sx) exactly.
+#pragma once
+
+#include "common.cuh"
+#include "gemv.cuh"
+
+namespace tfb {
+
+constexpr int GM_BN = 128;      // weight rows per CTA
+constexpr int GM_BM = 128;      // activation rows per CTA
+constexpr int GM_BK = 64;       // k per pipeline stage (two Q8_0 blocks)
+constexpr int GM_THREADS = 256; // 8 warps: 4 along n x 2 along m (warp tile 32 n x 64 m)
+constexpr int GM_LDS = GM_BK + 8;  // shared row stride in halves (144 B: ldmatrix conflict-free)
+constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
+
+// Activation preparation: optional embedding lookup, optional RMSNorm, then the f16 split.
+struct XPrepArgs {
+    const float* x;       // [M][ldx] input (or the residual stream for RMSNorm)
+    int ldx;
+    const float* norm_w;  // RMSNorm weights or nullptr (no norm)
+    float eps;
+    const uint8_t* embd;  // embedding table: rows are looked up from tokens[] (then x_out)
+    int embd_type;
+    long long embd_rb;
+    int n_vocab;
+    const int* tokens;
+    float* x_out;         // [M][ldx]: the embedded rows (the residual stream)
+    int K, M;
+    __half* xh;           // [M][K]
+    __half* xl;
+    int* sx;              // [M] scale exponents
+    int* err;
+};
+
+struct GemmArgs {
+    const uint8_t* W;     // Q8_0 rows
+    long long rb;
+    int N, K, M;
+    int sw;               // weight scale exponent
+    const __half* xh;     // [>= ceil(M/GM_BM)*GM_BM][K]
+    const __half* xl;
+    const int* sx;        // [M]
+    // epilogue (GemvArgs conventions)
+    int epi;              // EPI_STORE / EPI_RESID / EPI_SWIGLU (interleaved gate/up rows) / EPI_ARGMAX
+    float* y;
+    int ldy;
+    const float* bias;
+    float* resid;
+    int ldr;
+    unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
+    int store_logits;          // EPI_ARGMAX: also store the logits in y
+};
+
+// End of a step at M rows: next tokens from the greedy keys, positions, generated ids.
+struct FinishArgs {
+    int M;
+    unsigned long long* keys;  // reset to 0
+    int* tok_next;
+    int* pos;
+    const int* slots;
+    int* hist;                 // [hist_cap][M] or nullptr
+    StepCtl* ctl;
+    int argmax;                // 0: positions only (a step without lm_head)
+};
+
+cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st);
+cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st);
+cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st);
+int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes);  // per-matrix sw
+
+}  // namespace tfb

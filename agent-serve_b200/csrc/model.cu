@@ -14,6 +14,7 @@
 //   rmsnorm+gate/up GEMV+SwiGLU -> down GEMV+residual ... -> rmsnorm+lm_head GEMV+argmax
 //   (+ end-of-step bookkeeping: next token, history, position), all launched with
 //   programmatic dependent launch and captured once per row count into a CUDA graph.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -22,6 +23,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "gemm.cuh"
 #include "decode_mk.cuh"
 #include "engine.cuh"
 
@@ -55,6 +57,7 @@ struct WeightRef {
     int K = 0;
     long long rb = 0;
     int rows = 0;
+    int sw = 0;  // Q8_0: power-of-two scale of the tensor-core GEMM (gemm.cuh)
 };
 
 struct LayerDev {
@@ -101,6 +104,10 @@ struct tf_model {
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
     unsigned* counters = nullptr;
     unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
+    bool gemm_ok = false;         // every matmul weight is Q8_0 with K % 64 == 0
+    int gtile = 0;                // rows per step on the GEMM path (0: no GEMM path)
+    __half *xh = nullptr, *xl = nullptr;  // GEMM activation halves [round_up(gtile,128)][max K]
+    int* d_sx = nullptr;
     unsigned long long* keys = nullptr;
     int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_wstart = nullptr, *d_hist = nullptr;
     int *d_prompt = nullptr, *d_err = nullptr;
@@ -108,6 +115,7 @@ struct tf_model {
     int n_split = 1;
     // host staging (pinned)
     int* hi = nullptr;      // small int staging
+    int* hb = nullptr;      // batch staging: [rows] tokens in / ids out, [rows] slots
     float* hlog = nullptr;  // logits staging [tile][V]
     std::vector<int> hpos;  // host mirror of each slot's position
     std::map<long long, cudaGraphExec_t> graphs;
@@ -228,7 +236,118 @@ static bool fused_attn_enabled() {
 // Whether batch-1 steps of slot `seq` up to position end_pos may fuse the attention.
 bool fuse_attn_ok(const tf_model* m, int end_pos) { return fused_attn_enabled() && end_pos <= kFusedAttnMaxPos; }
 
+// One step for M >= GM_MIN_M rows on the tensor-core GEMM path: per layer activation
+// preparation (RMSNorm, f16 halves) before each GEMM, the split flash-decode attention over
+// the M rows' slots, and a finishing kernel for the step's tokens and positions.
+int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch) {
+    const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
+    const int ldq = H + 2 * KV;
+    int launches = 0;
+    auto prep = [&](const float* x, int ldx, int K, const float* norm_w) {
+        XPrepArgs p;
+        memset(&p, 0, sizeof(p));
+        p.x = x;
+        p.ldx = ldx;
+        p.norm_w = norm_w;
+        p.eps = m->hp.rms_eps;
+        p.K = K;
+        p.M = M;
+        p.xh = m->xh;
+        p.xl = m->xl;
+        p.sx = m->d_sx;
+        p.err = m->d_err;
+        return p;
+    };
+    auto gemm = [&](const WeightRef& w, int N, int epi) {
+        GemmArgs g;
+        memset(&g, 0, sizeof(g));
+        g.W = w.p;
+        g.rb = w.rb;
+        g.N = N;
+        g.K = w.K;
+        g.M = M;
+        g.sw = w.sw;
+        g.xh = m->xh;
+        g.xl = m->xl;
+        g.sx = m->d_sx;
+        g.epi = epi;
+        return g;
+    };
+    for (int li = 0; li < m->hp.n_layer; ++li) {
+        const LayerDev& Ld = m->L[li];
+        {
+            XPrepArgs p = prep(m->x, D, D, Ld.attn_norm);
+            if (li == 0) {
+                p.embd = m->embd.p;
+                p.embd_type = m->embd.type;
+                p.embd_rb = m->embd.rb;
+                p.n_vocab = V;
+                p.tokens = m->d_tokens;
+                p.x_out = m->x;
+            }
+            CK(xprep_launch(p, m->stream));
+            GemmArgs g = gemm(Ld.qkv, ldq, EPI_STORE);
+            g.y = m->qkv;
+            g.ldy = ldq;
+            g.bias = Ld.bqkv;
+            CK(gemm_launch(g, m->stream));
+            AttnArgs a = attn_args(m, li);
+            CK(attn_decode_launch(a, M, m->stream, true));
+            launches += 3;
+        }
+        {
+            CK(xprep_launch(prep(m->attn, H, H, nullptr), m->stream));
+            GemmArgs g = gemm(Ld.wo, D, EPI_RESID);
+            g.resid = m->x;
+            g.ldr = D;
+            CK(gemm_launch(g, m->stream));
+            launches += 2;
+        }
+        {
+            CK(xprep_launch(prep(m->x, D, D, Ld.ffn_norm), m->stream));
+            GemmArgs g = gemm(Ld.gateup, 2 * FF, EPI_SWIGLU);
+            g.y = m->h;
+            g.ldy = FF;
+            CK(gemm_launch(g, m->stream));
+            launches += 2;
+        }
+        {
+            CK(xprep_launch(prep(m->h, FF, FF, nullptr), m->stream));
+            GemmArgs g = gemm(Ld.down, D, EPI_RESID);
+            g.resid = m->x;
+            g.ldr = D;
+            CK(gemm_launch(g, m->stream));
+            launches += 2;
+        }
+    }
+    if (head) {
+        CK(xprep_launch(prep(m->x, D, D, m->out_norm), m->stream));
+        GemmArgs g = gemm(m->outw, V, EPI_ARGMAX);
+        g.y = m->logits;
+        g.ldy = V;
+        g.keys = m->keys;
+        g.store_logits = 1;
+        CK(gemm_launch(g, m->stream));
+        launches += 2;
+    }
+    FinishArgs f;
+    memset(&f, 0, sizeof(f));
+    f.M = M;
+    f.keys = m->keys;
+    f.tok_next = m->d_tokens;
+    f.pos = m->d_pos;
+    f.slots = m->d_slots;
+    f.hist = m->d_hist;
+    f.ctl = m->ctl;
+    f.argmax = head ? 1 : 0;
+    CK(finish_launch(f, m->stream));
+    ++launches;
+    if (n_launch) *n_launch = launches;
+    return 0;
+}
+
 int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fused) {
+    if (M >= GM_MIN_M && m->gtile >= M) return enqueue_step_gemm(m, M, head, n_launch);
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
@@ -543,9 +662,11 @@ int finish_call(tf_model* m) {
     if (m->hi[60] != 0) {
         const int c = m->hi[60];
         cudaMemsetAsync(m->d_err, 0, sizeof(int), m->stream);
-        cudaMemsetAsync(m->counters, 0, sizeof(unsigned) * (size_t)m->tile * m->hp.n_kv_head, m->stream);
+        const int T = std::max(m->tile, m->gtile);
+        cudaMemsetAsync(m->counters, 0, sizeof(unsigned) * (size_t)T * m->hp.n_kv_head, m->stream);
         cudaMemsetAsync(m->ctl, 0, sizeof(unsigned), m->stream);
-        cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * m->tile, m->stream);
+        cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * T, m->stream);
+        cudaMemsetAsync(m->d_async, 0, sizeof(unsigned) * 2 * m->hp.n_layer, m->stream);
         cudaStreamSynchronize(m->stream);
         return fail(m, err_code_text(c));
     }
@@ -568,11 +689,11 @@ int set_slot_row(tf_model* m, int row, int seq, int token) {
 int read_outputs(tf_model* m, int M, float* logits, int* argmax_out) {
     if (logits)
         CK(cudaMemcpyAsync(m->hlog, m->logits, sizeof(float) * (size_t)M * m->V, cudaMemcpyDeviceToHost, m->stream));
-    if (argmax_out) CK(cudaMemcpyAsync(m->hi + 8, m->d_tokens, sizeof(int) * M, cudaMemcpyDeviceToHost, m->stream));
+    if (argmax_out) CK(cudaMemcpyAsync(m->hb, m->d_tokens, sizeof(int) * M, cudaMemcpyDeviceToHost, m->stream));
     int rc = finish_call(m);
     if (rc) return rc;
     if (logits) memcpy(logits, m->hlog, sizeof(float) * (size_t)M * m->V);
-    if (argmax_out) memcpy(argmax_out, m->hi + 8, sizeof(int) * M);
+    if (argmax_out) memcpy(argmax_out, m->hb, sizeof(int) * M);
     return 0;
 }
 
@@ -591,10 +712,11 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async};
+                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx};
     for (void* p : dev)
         if (p) cudaFree(p);
     if (m->hi) cudaFreeHost(m->hi);
+    if (m->hb) cudaFreeHost(m->hb);
     if (m->hlog) cudaFreeHost(m->hlog);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -778,6 +900,10 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes, L.k->data, L.k->nbytes, cudaMemcpyHostToDevice));
         CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes + L.k->nbytes, L.v->data, L.v->nbytes, cudaMemcpyHostToDevice));
         Ld.qkv = wref(A + pl[i].qkv, L.q->ggml_type, m->D, m->H + 2 * m->KV);
+        if (L.q->ggml_type == T_Q8_0)
+            Ld.qkv.sw = std::min({q8_scale_exponent((const uint8_t*)L.q->data, L.q->nbytes),
+                                  q8_scale_exponent((const uint8_t*)L.k->data, L.k->nbytes),
+                                  q8_scale_exponent((const uint8_t*)L.v->data, L.v->nbytes)});
         Ld.bqkv = nullptr;
         if (L.bq) {
             float* b = reinterpret_cast<float*>(A + pl[i].b);
@@ -788,19 +914,31 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         }
         CKD(cudaMemcpy(A + pl[i].o, L.o->data, L.o->nbytes, cudaMemcpyHostToDevice));
         Ld.wo = wref(A + pl[i].o, L.o->ggml_type, m->H, m->D);
+        if (L.o->ggml_type == T_Q8_0) Ld.wo.sw = q8_scale_exponent((const uint8_t*)L.o->data, L.o->nbytes);
         CKD(cudaMemcpy(A + pl[i].fn, L.fn->data, L.fn->nbytes, cudaMemcpyHostToDevice));
         Ld.ffn_norm = reinterpret_cast<const float*>(A + pl[i].fn);
         const size_t grb = (size_t)row_bytes(L.g->ggml_type, m->D);
         CKD(cudaMemcpy2D(A + pl[i].gu, 2 * grb, L.g->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
         CKD(cudaMemcpy2D(A + pl[i].gu + grb, 2 * grb, L.u->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
         Ld.gateup = wref(A + pl[i].gu, L.g->ggml_type, m->D, 2 * m->FF);
+        if (L.g->ggml_type == T_Q8_0)
+            Ld.gateup.sw = std::min(q8_scale_exponent((const uint8_t*)L.g->data, L.g->nbytes),
+                                    q8_scale_exponent((const uint8_t*)L.u->data, L.u->nbytes));
         CKD(cudaMemcpy(A + pl[i].d, L.d->data, L.d->nbytes, cudaMemcpyHostToDevice));
         Ld.down = wref(A + pl[i].d, L.d->ggml_type, m->FF, m->D);
+        if (L.d->ggml_type == T_Q8_0) Ld.down.sw = q8_scale_exponent((const uint8_t*)L.d->data, L.d->nbytes);
     }
     CKD(cudaMemcpy(A + p_embd, te->data, te->nbytes, cudaMemcpyHostToDevice));
     m->embd = wref(A + p_embd, te->ggml_type, m->D, (int)te->ne[1]);
     if (ow != te) CKD(cudaMemcpy(A + p_out, ow->data, ow->nbytes, cudaMemcpyHostToDevice));
     m->outw = wref(A + p_out, ow->ggml_type, m->D, (int)ow->ne[1]);
+    if (ow->ggml_type == T_Q8_0) m->outw.sw = q8_scale_exponent((const uint8_t*)ow->data, ow->nbytes);
+    {
+        auto gemm_w = [](const WeightRef& w) { return w.type == T_Q8_0 && w.K % GM_BK == 0; };
+        bool ok = gemm_w(m->outw);
+        for (const LayerDev& Ld : m->L) ok = ok && gemm_w(Ld.qkv) && gemm_w(Ld.wo) && gemm_w(Ld.gateup) && gemm_w(Ld.down);
+        m->gemm_ok = ok;
+    }
     CKD(cudaMemcpy(A + p_onorm, on->data, on->nbytes, cudaMemcpyHostToDevice));
     m->out_norm = reinterpret_cast<const float*>(A + p_onorm);
 
@@ -836,8 +974,19 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     int tile = GV_MAXM;
     for (int K : {m->D, m->H, m->FF}) tile = std::min(tile, gemv_max_rows(K));
     m->tile = std::max(1, std::min(tile, o.max_batch));
+    m->gtile = (m->gemm_ok && o.max_batch >= GM_MIN_M) ? o.max_batch : 0;
     m->n_split = attn_pick_split(o.max_seq);
-    const int T = m->tile;
+    const int T = std::max(m->tile, m->gtile);
+    if (m->gtile) {
+        const int Kmax = std::max(m->D, std::max(m->H, m->FF));
+        const size_t rows = (size_t)(m->gtile + GM_BM - 1) / GM_BM * GM_BM;
+        CKD(cudaMalloc(&m->xh, rows * Kmax * sizeof(__half)));
+        CKD(cudaMalloc(&m->xl, rows * Kmax * sizeof(__half)));
+        CKD(cudaMemset(m->xh, 0, rows * Kmax * sizeof(__half)));
+        CKD(cudaMemset(m->xl, 0, rows * Kmax * sizeof(__half)));
+        CKD(cudaMalloc(&m->d_sx, rows * sizeof(int)));
+        CKD(cudaMemset(m->d_sx, 0, rows * sizeof(int)));
+    }
     CKD(cudaMalloc(&m->x, sizeof(float) * T * m->D));
     CKD(cudaMalloc(&m->qkv, sizeof(float) * T * (m->H + 2 * m->KV)));
     CKD(cudaMalloc(&m->attn, sizeof(float) * T * m->H));
@@ -865,6 +1014,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMalloc(&m->ctl, sizeof(StepCtl)));
     CKD(cudaMemset(m->ctl, 0, sizeof(StepCtl)));
     CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
+    CKD(cudaMallocHost(&m->hb, sizeof(int) * 2 * (size_t)T));
     CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
     m->hpos.assign(o.max_batch, 0);
     if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
@@ -1013,12 +1163,15 @@ int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int
         if (m->hpos[seq_ids[b]] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
         if (tokens[b] < 0 || tokens[b] >= m->V) return fail(m, "token id out of range");
     }
-    for (int b0 = 0; b0 < B; b0 += m->tile) {
-        const int T = std::min(m->tile, B - b0);
-        memcpy(m->hi + 8, tokens + b0, sizeof(int) * T);
-        memcpy(m->hi + 24, seq_ids + b0, sizeof(int) * T);
-        CK(cudaMemcpyAsync(m->d_tokens, m->hi + 8, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
-        CK(cudaMemcpyAsync(m->d_slots, m->hi + 24, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+    // rows per step: the tensor-core GEMM path takes up to gtile rows, the GEMV up to tile
+    const int chunk = (m->gtile && B >= GM_MIN_M) ? m->gtile : m->tile;
+    for (int b0 = 0; b0 < B; b0 += chunk) {
+        const int T = std::min(chunk, B - b0);
+        const int TT = std::max(m->tile, m->gtile);
+        memcpy(m->hb, tokens + b0, sizeof(int) * T);
+        memcpy(m->hb + TT, seq_ids + b0, sizeof(int) * T);
+        CK(cudaMemcpyAsync(m->d_tokens, m->hb, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+        CK(cudaMemcpyAsync(m->d_slots, m->hb + TT, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
         if (run_step(m, T, true, false)) return -1;
         for (int b = 0; b < T; ++b) m->hpos[seq_ids[b0 + b]] += 1;
         int rc = read_outputs(m, T, logits ? logits + (size_t)b0 * m->V : nullptr, argmax_out ? argmax_out + b0 : nullptr);
