@@ -39,7 +39,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
     const int slot = a.slots ? a.slots[m] : 0;
-    const int pos = a.fresh ? a.pos[slot] : a.n_pos_fixed - 1;
+    // fresh 2 (prefill chunk of one sequence): row m is the chunk's m-th position
+    const int pos = a.fresh == 2 ? a.pos[slot] + m : (a.fresh ? a.pos[slot] : a.n_pos_fixed - 1);
     if (a.fresh && (pos < 0 || pos >= a.cap)) {
         if (tid == 0 && split == 0) atomicCAS(a.err, 0, ERR_POS);
         return;
@@ -64,18 +65,18 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
 
     // 1) query heads of the group, new k/v, cached K/V of this split: independent loads
     for (int i = tid; i < n_rep * hd; i += AT_THREADS) qs[i / hd][i % hd] = q[i];
-    if (a.fresh)
+    if (a.fresh == 1)
         for (int i = tid; i < hd; i += AT_THREADS) {
             kn[i] = row[(size_t)a.n_head * hd + (size_t)kvh * hd + i];
             vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
         }
-    const int np_cached = (a.fresh && p1 == n_pos) ? np - 1 : np;  // the new position is not read
+    const int np_cached = (a.fresh == 1 && p1 == n_pos) ? np - 1 : np;  // the new position is not read
     load_tile(ks, hd + 1, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
     load_tile(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
     __syncthreads();
 
     // 2) RoPE (fresh): the host table holds the reference's float cos/sin of pos*freq
-    if (a.fresh) {
+    if (a.fresh == 1) {
         const float* cp = a.cosb + (size_t)pos * d2;
         const float* sp = a.sinb + (size_t)pos * d2;
         for (int i = tid; i < (n_rep + 1) * d2; i += AT_THREADS) {
@@ -254,6 +255,43 @@ __global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillA
     }
 }
 
+// ---- prefill chunk, first half: RoPE of q (in place) and k, K/V store -------------------------
+// One CTA per (row, head), a thread per rotation pair; row m is position pos[slot] + m.  The
+// attention of the chunk then runs over the cache alone (fresh == 2), so that every row sees
+// the keys of the rows before it (attn_prefill's causal mask, src/attention.cpp:82-111).
+__global__ void rope_store_kernel(const AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int m = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+    const int hd = a.hd, d2 = hd / 2;
+    const int slot = a.slots ? a.slots[m] : 0;
+    const int pos = a.pos[slot] + m;
+    if (pos < 0 || pos >= a.cap) {
+        if (j == 0) atomicCAS(a.err, 0, ERR_POS);
+        return;
+    }
+    float* row = const_cast<float*>(a.qkv) + (size_t)m * a.ld_qkv;
+    const float c = a.cosb[(size_t)pos * d2 + j], sn = a.sinb[(size_t)pos * d2 + j];
+    if (h < a.n_head) {
+        float* q = row + (size_t)h * hd;
+        float x0 = q[j], x1 = q[j + d2];
+        rope_pair(x0, x1, c, sn);
+        q[j] = x0;
+        q[j + d2] = x1;
+    } else {
+        const int kvh = h - a.n_head;
+        const float* k = row + (size_t)a.n_head * hd + (size_t)kvh * hd;
+        const float* v = row + (size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd;
+        float x0 = k[j], x1 = k[j + d2];
+        rope_pair(x0, x1, c, sn);
+        const size_t off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd + (size_t)pos * hd;
+        kv_store(a.kc, (long long)(off + j), a.kv_type, x0);
+        kv_store(a.kc, (long long)(off + j + d2), a.kv_type, x1);
+        kv_store(a.vc, (long long)(off + j), a.kv_type, v[j]);
+        kv_store(a.vc, (long long)(off + j + d2), a.kv_type, v[j + d2]);
+    }
+}
+
 // ---- host ------------------------------------------------------------------------------
 int attn_pick_split(int cap) {
     const int s = (cap + AT_CHUNK - 1) / AT_CHUNK;
@@ -289,6 +327,20 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+}
+
+cudaError_t rope_store_launch(const AttnArgs& a, int M, cudaStream_t st) {
+    if (a.hd > AT_MAX_HD || a.hd % 2) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(M, a.n_head + a.n_kv);
+    cfg.blockDim = dim3(a.hd / 2);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rope_store_kernel, a);
 }
 
 cudaError_t attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st) {

@@ -30,7 +30,9 @@ struct AttnArgs {
     unsigned* counters;     // [M][n_kv]
     float* out;             // [M][ld_out]
     int ld_out;
-    int fresh;              // 1: decode step (rotate + store + attend over [wstart, pos])
+    int fresh;              // 1: decode step (rotate + store + attend over [wstart, pos]);
+                            // 2: prefill chunk of one sequence after rope_store_kernel: row m
+                            //    at pos[slot] + m attends over the cache [wstart, pos] as given
     int n_pos_fixed;        // fresh == 0: attend over n_pos_fixed cached positions, q as given
     int* err;
 };
@@ -113,5 +115,6 @@ __device__ __forceinline__ void load_tile(float* dst, int dst_stride, int hd, co
 int attn_pick_split(int cap);
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl);
 cudaError_t attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st);
+cudaError_t rope_store_launch(const AttnArgs& a, int M, cudaStream_t st);
 
 }  // namespace tfb

@@ -158,7 +158,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * GM_BM;
     const int wn = warp & 3, wm = warp >> 2;
-    const int nk = a.K / GM_BK;
+    const int nk_all = a.K / GM_BK;
+    // this split's k stages [kb, kb + nk)
+    const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
+    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
 
     auto stage_ptr = [&](int s, int which) {  // which: 0 Wh, 1 Wl, 2 Xh, 3 Xl
@@ -179,8 +182,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
     pdl_trigger();
     pdl_wait();
     // prologue: stage 0
-    load_x(0, 0);
-    gm_load_w(wv, a, n0 + wr, 0, wj);
+    load_x(0, kb);
+    gm_load_w(wv, a, n0 + wr, kb, wj);
     gm_dequant(wv, wj, wscale, stage_ptr(0, 0) + wr * GM_LDS + 32 * wj, stage_ptr(0, 1) + wr * GM_LDS + 32 * wj);
     cp_async_wait_all();
     __syncthreads();
@@ -197,8 +200,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
         const int s = kc & 1;
         const bool more = kc + 1 < nk;
         if (more) {
-            load_x(s ^ 1, kc + 1);
-            gm_load_w(wv, a, n0 + wr, kc + 1, wj);
+            load_x(s ^ 1, kb + kc + 1);
+            gm_load_w(wv, a, n0 + wr, kb + kc + 1, wj);
         }
         const __half* sWh = stage_ptr(s, 0);
         const __half* sWl = stage_ptr(s, 1);
@@ -258,6 +261,34 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
         }
     }
     __syncthreads();
+    if (gridDim.z > 1) {
+        // split-K: publish this split's tile; the last split of the tile sums all in order
+        __shared__ int last_s;
+        float* wz = a.ws + (size_t)blockIdx.z * a.M * a.N;
+        for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
+            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+            if (m < a.M && n < a.N) wz[(size_t)m * a.N + n] = tile[mm * GM_EPI_LD + nn];
+        }
+        __threadfence();
+        __syncthreads();
+        const int tix = blockIdx.y * gridDim.x + blockIdx.x;
+        if (tid == 0) {
+            const unsigned t = atomicAdd(&a.tile_cnt[tix], 1u);
+            last_s = t == gridDim.z - 1;
+        }
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();
+        for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
+            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+            if (m >= a.M || n >= a.N) continue;
+            float v = 0.f;
+            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(a.ws + ((size_t)z * a.M + m) * a.N + n);
+            tile[mm * GM_EPI_LD + nn] = v;
+        }
+        if (tid == 0) a.tile_cnt[tix] = 0u;
+        __syncthreads();
+    }
     if (a.epi == EPI_ARGMAX) {
         if (tid < GM_BM && m0 + tid < a.M) {
             const int m = m0 + tid;
@@ -307,7 +338,7 @@ __global__ void finish_kernel(const FinishArgs a) {
             a.tok_next[m] = tok;
             if (a.hist && gs < a.ctl->hist_cap) a.hist[(size_t)gs * a.M + m] = tok;
         }
-        a.pos[a.slots[m]] += 1;
+        atomicAdd(&a.pos[a.slots[m]], 1);  // rows of one prefill chunk share a slot
     }
     __syncthreads();
     if (threadIdx.x == 0 && a.argmax) a.ctl->gen_step = gs + 1;
@@ -350,7 +381,9 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
-    dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM);
+    const int ks = a.ksplit > 1 ? a.ksplit : 1;
+    if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
+    dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
     GemmArgs aa = a;
     void* args[] = {&aa};
     return launch_pdl((const void*)gemm_q8_kernel, grid, dim3(GM_THREADS), smem, st, args);

@@ -58,7 +58,27 @@ struct GemmArgs {
     int ldr;
     unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
     int store_logits;          // EPI_ARGMAX: also store the logits in y
+    // split-K (grid.z = ksplit > 1): each split writes its scaled tile to ws[z][M][N]; the last
+    // split of a tile (tile_cnt, reset by it) sums the splits in order and applies the epilogue
+    int ksplit;
+    float* ws;
+    unsigned* tile_cnt;
 };
+
+constexpr int GM_MAX_SPLIT = 8;
+// workspace floats / tile counters the split-K path needs for `num_sms` SMs
+inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_BM; }
+inline int gemm_tile_counters(int num_sms) { return num_sms; }
+// k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
+inline int gemm_pick_split(int N, int M, int K, int num_sms) {
+    const int tiles = ((N + GM_BN - 1) / GM_BN) * ((M + GM_BM - 1) / GM_BM);
+    if (tiles >= num_sms) return 1;
+    int s = num_sms / tiles;
+    const int nk = K / GM_BK;
+    s = s > GM_MAX_SPLIT ? GM_MAX_SPLIT : s;
+    s = s > nk / 2 ? nk / 2 : s;
+    return s < 1 ? 1 : s;
+}
 
 // End of a step at M rows: next tokens from the greedy keys, positions, generated ids.
 struct FinishArgs {

@@ -24,6 +24,7 @@
 
 #include "attention.cuh"
 #include "gemm.cuh"
+#include "sample.cuh"
 #include "decode_mk.cuh"
 #include "engine.cuh"
 
@@ -106,8 +107,12 @@ struct tf_model {
     unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
     bool gemm_ok = false;         // every matmul weight is Q8_0 with K % 64 == 0
     int gtile = 0;                // rows per step on the GEMM path (0: no GEMM path)
+    int ptile = 0;                // prompt tokens per prefill chunk on the GEMM path
     __half *xh = nullptr, *xl = nullptr;  // GEMM activation halves [round_up(gtile,128)][max K]
     int* d_sx = nullptr;
+    SampleScratch* smp = nullptr;  // temperature / top-p sampler scratch
+    float* gws = nullptr;         // split-K workspace
+    unsigned* gcnt = nullptr;     // split-K tile counters
     unsigned long long* keys = nullptr;
     int *d_tokens = nullptr, *d_slots = nullptr, *d_pos = nullptr, *d_wstart = nullptr, *d_hist = nullptr;
     int *d_prompt = nullptr, *d_err = nullptr;
@@ -239,7 +244,7 @@ bool fuse_attn_ok(const tf_model* m, int end_pos) { return fused_attn_enabled() 
 // One step for M >= GM_MIN_M rows on the tensor-core GEMM path: per layer activation
 // preparation (RMSNorm, f16 halves) before each GEMM, the split flash-decode attention over
 // the M rows' slots, and a finishing kernel for the step's tokens and positions.
-int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch) {
+int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) {
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
@@ -271,6 +276,9 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch) {
         g.xl = m->xl;
         g.sx = m->d_sx;
         g.epi = epi;
+        g.ksplit = gemm_pick_split(N, M, w.K, m->num_sms);
+        g.ws = m->gws;
+        g.tile_cnt = m->gcnt;
         return g;
     };
     for (int li = 0; li < m->hp.n_layer; ++li) {
@@ -292,6 +300,11 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch) {
             g.bias = Ld.bqkv;
             CK(gemm_launch(g, m->stream));
             AttnArgs a = attn_args(m, li);
+            if (chunk) {  // one sequence's prompt rows: store every row's K/V, then attend
+                CK(rope_store_launch(a, M, m->stream));
+                a.fresh = 2;
+                ++launches;
+            }
             CK(attn_decode_launch(a, M, m->stream, true));
             launches += 3;
         }
@@ -346,8 +359,9 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch) {
     return 0;
 }
 
-int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fused) {
-    if (M >= GM_MIN_M && m->gtile >= M) return enqueue_step_gemm(m, M, head, n_launch);
+int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fused, bool chunk = false) {
+    if (chunk) return enqueue_step_gemm(m, M, head, n_launch, true);
+    if (M >= GM_MIN_M && m->gtile >= M) return enqueue_step_gemm(m, M, head, n_launch, false);
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
@@ -455,14 +469,14 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
 }
 
 // Run one step for M rows (tokens in d_tokens[0..M), slots in d_slots[0..M)).
-int run_step(tf_model* m, int M, bool head, bool fused) {
-    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused);
-    const long long key = (long long)M * 4 + (head ? 1 : 0) + (fused ? 2 : 0);
+int run_step(tf_model* m, int M, bool head, bool fused, bool chunk = false) {
+    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused, chunk);
+    const long long key = (long long)M * 8 + (head ? 1 : 0) + (fused ? 2 : 0) + (chunk ? 4 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(m, M, head, true, nullptr, fused);
+        int rc = enqueue_step(m, M, head, true, nullptr, fused, chunk);
         cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -697,6 +711,19 @@ int read_outputs(tf_model* m, int M, float* logits, int* argmax_out) {
     return 0;
 }
 
+// Outputs of row `row` of the last step (a prefill chunk's last prompt token).
+int read_outputs_row(tf_model* m, int row, float* logits, int* argmax_out) {
+    if (logits)
+        CK(cudaMemcpyAsync(m->hlog, m->logits + (size_t)row * m->V, sizeof(float) * m->V, cudaMemcpyDeviceToHost,
+                           m->stream));
+    if (argmax_out) CK(cudaMemcpyAsync(m->hb, m->d_tokens + row, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    int rc = finish_call(m);
+    if (rc) return rc;
+    if (logits) memcpy(logits, m->hlog, sizeof(float) * m->V);
+    if (argmax_out) *argmax_out = m->hb[0];
+    return 0;
+}
+
 }  // namespace
 
 // ============================== C-ABI ==============================================
@@ -712,9 +739,10 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx};
+                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt};
     for (void* p : dev)
         if (p) cudaFree(p);
+    sample_scratch_destroy(m->smp);
     if (m->hi) cudaFreeHost(m->hi);
     if (m->hb) cudaFreeHost(m->hb);
     if (m->hlog) cudaFreeHost(m->hlog);
@@ -975,17 +1003,22 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     for (int K : {m->D, m->H, m->FF}) tile = std::min(tile, gemv_max_rows(K));
     m->tile = std::max(1, std::min(tile, o.max_batch));
     m->gtile = (m->gemm_ok && o.max_batch >= GM_MIN_M) ? o.max_batch : 0;
+    m->ptile = m->gemm_ok ? std::min(GM_BM, o.max_seq) : 0;
+    if (m->ptile < GM_MIN_M) m->ptile = 0;
     m->n_split = attn_pick_split(o.max_seq);
-    const int T = std::max(m->tile, m->gtile);
-    if (m->gtile) {
+    const int T = std::max(m->tile, std::max(m->gtile, m->ptile));
+    if (m->gtile || m->ptile) {
         const int Kmax = std::max(m->D, std::max(m->H, m->FF));
-        const size_t rows = (size_t)(m->gtile + GM_BM - 1) / GM_BM * GM_BM;
+        const size_t rows = (size_t)(std::max(m->gtile, m->ptile) + GM_BM - 1) / GM_BM * GM_BM;
         CKD(cudaMalloc(&m->xh, rows * Kmax * sizeof(__half)));
         CKD(cudaMalloc(&m->xl, rows * Kmax * sizeof(__half)));
         CKD(cudaMemset(m->xh, 0, rows * Kmax * sizeof(__half)));
         CKD(cudaMemset(m->xl, 0, rows * Kmax * sizeof(__half)));
         CKD(cudaMalloc(&m->d_sx, rows * sizeof(int)));
         CKD(cudaMemset(m->d_sx, 0, rows * sizeof(int)));
+        CKD(cudaMalloc(&m->gws, gemm_ws_floats(m->num_sms) * sizeof(float)));
+        CKD(cudaMalloc(&m->gcnt, gemm_tile_counters(m->num_sms) * sizeof(unsigned)));
+        CKD(cudaMemset(m->gcnt, 0, gemm_tile_counters(m->num_sms) * sizeof(unsigned)));
     }
     CKD(cudaMalloc(&m->x, sizeof(float) * T * m->D));
     CKD(cudaMalloc(&m->qkv, sizeof(float) * T * (m->H + 2 * m->KV)));
@@ -1015,6 +1048,8 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMemset(m->ctl, 0, sizeof(StepCtl)));
     CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
     CKD(cudaMallocHost(&m->hb, sizeof(int) * 2 * (size_t)T));
+    m->smp = sample_scratch_create(m->V);
+    if (!m->smp) BAD("sampler scratch allocation failed");
     CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
     m->hpos.assign(o.max_batch, 0);
     if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
@@ -1094,6 +1129,23 @@ int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logit
     m->hi[2] = m->hpos[seq];
     m->hi[3] = 0;
     CK(cudaMemcpyAsync(m->d_wstart + seq, m->hi + 2, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+    if (m->ptile && n >= GM_MIN_M) {
+        // tensor-core path: the prompt in chunks of up to ptile rows (every chunk >= 16 rows)
+        const int nc = (n + m->ptile - 1) / m->ptile;
+        const int TT = std::max(m->tile, std::max(m->gtile, m->ptile));
+        for (int b = 0; b < m->ptile; ++b) m->hb[TT + b] = seq;
+        CK(cudaMemcpyAsync(m->d_slots, m->hb + TT, sizeof(int) * m->ptile, cudaMemcpyHostToDevice, m->stream));
+        int c0 = 0, rows = 0;
+        for (int c = 0; c < nc; ++c) {
+            rows = (int)((long long)n * (c + 1) / nc) - c0;
+            CK(cudaMemcpyAsync(m->d_tokens, m->d_prompt + c0, sizeof(int) * rows, cudaMemcpyDeviceToDevice, m->stream));
+            if (run_step(m, rows, c == nc - 1, false, true)) return -1;
+            c0 += rows;
+        }
+        CK(cudaMemcpyAsync(m->d_wstart + seq, m->hi + 3, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        m->hpos[seq] += n;
+        return read_outputs_row(m, rows - 1, logits, argmax_out);
+    }
     if (set_slot_row(m, 0, seq, tokens[0])) return -1;
     for (int i = 0; i < n; ++i) {
         CK(cudaMemcpyAsync(m->d_tokens, m->d_prompt + i, sizeof(int), cudaMemcpyDeviceToDevice, m->stream));
@@ -1177,6 +1229,69 @@ int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int
         int rc = read_outputs(m, T, logits ? logits + (size_t)b0 * m->V : nullptr, argmax_out ? argmax_out + b0 : nullptr);
         if (rc) return rc;
     }
+    return 0;
+}
+
+int tf_cuda_prefill_batch(tf_model* m, const int* seq_ids, const int* tokens, int B, int n, int* argmax_out) {
+    if (!m) return set_error("null model");
+    if (B <= 0 || n <= 0) return 0;
+    CK(cudaSetDevice(m->device));
+    if (!seq_ids || !tokens) return fail(m, "null seq_ids or tokens");
+    std::vector<char> seen(m->opt.max_batch, 0);
+    for (int b = 0; b < B; ++b) {
+        if (check_seq(m, seq_ids[b])) return -1;
+        if (seen[seq_ids[b]]) return fail(m, "duplicate sequence slot in one batch");
+        seen[seq_ids[b]] = 1;
+        if (m->hpos[seq_ids[b]] + n > m->opt.max_seq) return fail(m, "prefill exceeds max_seq");
+        for (int t = 0; t < n; ++t)
+            if (tokens[(size_t)b * n + t] < 0 || tokens[(size_t)b * n + t] >= m->V) return fail(m, "token id out of range");
+    }
+    const int TT = std::max(m->tile, m->gtile);
+    const int chunk = (m->gtile && B >= GM_MIN_M) ? m->gtile : m->tile;
+    for (int b0 = 0; b0 < B; b0 += chunk) {
+        const int T = std::min(chunk, B - b0);
+        // attention of each sequence starts at its prompt (src/attention.cpp:82-111)
+        for (int b = 0; b < T; ++b) {
+            const int sq = seq_ids[b0 + b];
+            m->hb[b] = m->hpos[sq];
+            CK(cudaMemcpyAsync(m->d_wstart + sq, m->hb + b, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        }
+        CK(cudaStreamSynchronize(m->stream));
+        memcpy(m->hb + TT, seq_ids + b0, sizeof(int) * T);
+        CK(cudaMemcpyAsync(m->d_slots, m->hb + TT, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+        for (int t = 0; t < n; ++t) {
+            CK(cudaStreamSynchronize(m->stream));  // the staging row is reused each step
+            for (int b = 0; b < T; ++b) m->hb[b] = tokens[(size_t)(b0 + b) * n + t];
+            CK(cudaMemcpyAsync(m->d_tokens, m->hb, sizeof(int) * T, cudaMemcpyHostToDevice, m->stream));
+            if (run_step(m, T, t == n - 1, false)) return -1;
+        }
+        for (int b = 0; b < T; ++b) m->hpos[seq_ids[b0 + b]] += n;
+        m->hi[3] = 0;
+        for (int b = 0; b < T; ++b)
+            CK(cudaMemcpyAsync(m->d_wstart + seq_ids[b0 + b], m->hi + 3, sizeof(int), cudaMemcpyHostToDevice, m->stream));
+        int rc = read_outputs(m, T, nullptr, argmax_out ? argmax_out + b0 : nullptr);
+        if (rc) return rc;
+    }
+    return 0;
+}
+
+int tf_cuda_sample(tf_model* m, int row, float temperature, float top_p, float r, int* out_id) {
+    if (!m) return set_error("null model");
+    if (!out_id) return fail(m, "out_id is null");
+    const int T = std::max(m->tile, std::max(m->gtile, m->ptile));
+    if (row < 0 || row >= T) return fail(m, "row out of range");
+    CK(cudaSetDevice(m->device));
+    const float* lg = m->logits + (size_t)row * m->V;
+    if (temperature <= 0.0f) {  // sample_greedy (src/sampler.cpp:8-13)
+        CK(launch_argmax(lg, m->V, 1, m->d_tokens + row, m->stream));
+        CK(cudaMemcpyAsync(m->hb, m->d_tokens + row, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    } else {
+        CK(sample_launch(m->smp, lg, m->V, temperature, top_p, r, m->stream));
+        CK(cudaMemcpyAsync(m->hb, sample_result(m->smp), sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    }
+    int rc = finish_call(m);
+    if (rc) return rc;
+    *out_id = m->hb[0];
     return 0;
 }
 

@@ -24,6 +24,23 @@ from . import native
 from .gguf import GGUFReader
 
 
+class Mt19937Uniform:
+    """std::uniform_real_distribution<float>(0, 1) over std::mt19937(seed) as libstdc++ draws
+    it: one 32-bit output x per value, r = float(x) * 2^-32 (rounded to float first), and a
+    value that rounds to 1 becomes the float just below 1."""
+
+    def __init__(self, seed: int):
+        self.bg = np.random.MT19937()
+        self.bg._legacy_seeding(seed)  # init_genrand(seed), std::mt19937's seeding
+
+    def next(self) -> float:
+        x = int(self.bg.random_raw())
+        r = np.float32(np.float32(x) / np.float32(4294967296.0))
+        if r >= np.float32(1.0):
+            r = np.nextafter(np.float32(1.0), np.float32(0.0))
+        return float(r)
+
+
 @dataclass
 class RunConfig:
     """RunConfig (src/common.hpp:103-116) fields that apply to the GPU stage."""
@@ -164,6 +181,41 @@ class Model:
                                                  len(t), am.ctypes.data_as(native.i32p),
                                                  lg.ctypes.data_as(native.f32p) if lg is not None else None), self.h)
         return (am, lg) if want_logits else am
+
+    def prefill_batch(self, seq_ids: Sequence[int], prompts) -> np.ndarray:
+        """Prefill equal-length prompts of several sequences at once; returns each sequence's
+        greedy next id."""
+        s = np.ascontiguousarray(seq_ids, dtype=np.int32)
+        t = np.ascontiguousarray(prompts, dtype=np.int32)
+        if t.ndim != 2 or t.shape[0] != len(s):
+            raise ValueError("prompts must be [len(seq_ids)][n]")
+        am = np.zeros(len(s), np.int32)
+        native.check(self.L.tf_cuda_prefill_batch(self.h, s.ctypes.data_as(native.i32p), t.ctypes.data_as(native.i32p),
+                                                  len(s), t.shape[1], am.ctypes.data_as(native.i32p)), self.h)
+        return am
+
+    def sample(self, temperature: float, top_p: float, r: float, row: int = 0) -> int:
+        """sample_logits (src/sampler.cpp:15-52) on the device over the last step's logits of
+        `row`, with the caller's uniform draw r (see Mt19937Uniform)."""
+        out = C.c_int(0)
+        native.check(self.L.tf_cuda_sample(self.h, row, float(temperature), float(top_p), float(r), C.byref(out)),
+                     self.h)
+        return out.value
+
+    def generate(self, prompt: Sequence[int], n: int, temperature: float, top_p: float, seed: int = 42,
+                 eos: int = -1) -> list:
+        """The CLI's generation loop (src/main.cpp:106-122): prefill, then sample / stop at eos
+        (i > 0) / decode, with std::mt19937(seed) draws for temperature > 0."""
+        rng = Mt19937Uniform(seed)
+        self.prefill(prompt)
+        out = []
+        for i in range(n):
+            t = self.sample(temperature, top_p, rng.next() if temperature > 0 else 0.0)
+            if t == eos and i > 0:
+                break
+            out.append(t)
+            self.decode(t)
+        return out
 
     @property
     def stream(self) -> int:

@@ -52,7 +52,7 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms during the timed region."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -64,14 +64,20 @@ class ClockSampler:
         self.path = None
 
     def start(self):
+        """Start sampling and wait (up to 3 s) for the first sample, so that even a short timed
+        region that follows is covered."""
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200", "-i", str(self.idx)], stdout=open(self.path, "w"),
+                                          "-lms", "20", "-i", str(self.idx)], stdout=open(self.path, "w"),
                                          stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0 and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
 
     def stop(self):
         if not self.proc:
@@ -101,9 +107,76 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def model_file():
+def model_file(cfg=None):
     cache = os.environ.get("TFB200_CACHE", "/tmp/tfb200_models")
-    return synth.model_path(CFG, cache)
+    return synth.model_path(cfg or CFG, cache)
+
+
+BATCH_CFG = synth.CFG4
+BATCH_SEQS = 256      # cfg4: 256 independent sequences
+BATCH_PROMPT = 1024   # each with a 1024-token prompt
+
+
+def run_batched(args, rank, world, local_rank, dist):
+    """cfg4 batched greedy decode: the 256 sequences sharded contiguously over the ranks
+    (weights replicated, no collective on the data path).  Each rank prefills its shard
+    (tf_cuda_prefill_batch: 1024 steps of S rows on the tensor-core GEMM path), runs W
+    untimed decode steps, then times K steps of tf_cuda_decode_batch (host token ids in,
+    greedy ids out, every step) with CUDA events; the job value is all sequences' tokens over
+    the slowest rank's time."""
+    import torch
+    from tinferno_b200 import shard
+    from tinferno_b200.model import Model, RunConfig
+
+    cfg = BATCH_CFG
+    steps, warm = args.batched_steps, 3
+    s0, s1 = shard.shard_range(BATCH_SEQS, rank, world)
+    S = s1 - s0
+    if rank == 0:
+        model_file(cfg)
+    if dist:
+        dist.barrier()
+    m = Model(model_file(cfg), RunConfig(max_seq=BATCH_PROMPT + warm + steps, max_batch=S, device=local_rank))
+    stream = torch.cuda.ExternalStream(m.stream)
+    prompts = np.stack([synth.prompt_tokens(cfg, BATCH_PROMPT, stream=1000 + g) for g in range(s0, s1)])
+    slots = list(range(S))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    tok = m.prefill_batch(slots, prompts)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    for _ in range(warm):
+        tok = m.decode_batch(slots, tok.tolist())
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        tok = m.decode_batch(slots, tok.tolist())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms, prefill_s], device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max, prefill_max = float(t[0].item()), float(t[1].item())
+    kps = m.kernels_per_step
+    m.close()
+    wb = synth.weight_bytes(cfg)
+    kv_pos = 2 * cfg.n_layer * cfg.n_kv_head * (cfg.n_embd // cfg.n_head) * 4  # fp32 K+V bytes per position
+    ctx = BATCH_PROMPT + warm + steps / 2
+    step_bytes = wb + S * ctx * kv_pos
+    return {"metric": "batched decode tok/s (cfg4 Qwen2.5-1.5B Q8_0, 256 sequences, 1024-token prompts)",
+            "value": round(BATCH_SEQS * steps / (ms_max / 1e3), 1), "unit": "tok/s", "n_gpus": world,
+            "sequences_per_gpu": S, "steps": steps, "warmup": warm, "ms_per_step": round(ms_max / steps, 3),
+            "scaling": "strong", "prefill_s": round(prefill_max, 2),
+            "prefill_tok_s": round(BATCH_SEQS * BATCH_PROMPT / prefill_max, 1),
+            "hbm_roofline": {"bytes_per_step_per_gpu": int(step_bytes),
+                             "achieved_gbs": round(step_bytes / (ms_max / steps / 1e3) / 1e9, 1),
+                             "frac_of_peak": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / peaks()[0], 4)},
+            "path": "tensor-core GEMM (f16-split mma.sync) at >= 16 rows per step, split flash-decode attention",
+            "e2e": "every step copies S token ids in and S greedy ids out (host)"}
 
 
 def cpu_reference_decode(path, prompt, n_tokens, max_seconds=None):
@@ -247,6 +320,11 @@ def run_ours(args, rank, world, local_rank, dist):
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                         "d2h_bytes_per_step": 4 * CFG.n_vocab + 8},
                 "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk}
+    batched = None
+    if not args.no_batched:
+        batched = run_batched(args, rank, world, local_rank, dist)
+    if rank == 0:
+        line["batched"] = batched
         print(json.dumps(line), flush=True)
 
 
@@ -295,6 +373,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
+    ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
+    ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
     ap.add_argument("--kernel", default="", choices=["", "lmhead", "step"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "

@@ -105,6 +105,20 @@ TF_API int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n,
 TF_API int tf_cuda_decode_batch(tf_model* m, const int* seq_ids, const int* tokens, int B,
                          int* argmax_out, float* logits);
 
+/* Batched prefill: Model::prefill (src/model.cpp:183-195) for B sequences at once, each with
+ * n prompt tokens (tokens[b*n + t]); attention of each sequence sees its own n tokens only,
+ * as prefill does.  argmax_out[b] (host, optional) receives the greedy id after each
+ * sequence's last token.  Runs n steps of B rows (the tensor-core GEMM path at B >= 16). */
+TF_API int tf_cuda_prefill_batch(tf_model* m, const int* seq_ids, const int* tokens, int B, int n,
+                                 int* argmax_out);
+
+/* sample_logits(logits, n, temperature, top_p, rng)  src/sampler.cpp:15-52, on the device,
+ * over the logits of row `row` of the last step (row 0 after decode / prefill).  The caller
+ * draws r = uniform_real_distribution<float>(0, 1)(rng) from its own std::mt19937 (one draw
+ * per sampled token, as src/main.cpp:109-114), so the random stream stays on the host.
+ * temperature <= 0 is sample_greedy. */
+TF_API int tf_cuda_sample(tf_model* m, int row, float temperature, float top_p, float r, int* out_id);
+
 /* Model::reset()  src/model.cpp:80-83 (one slot; seq < 0 resets every slot). */
 TF_API int tf_cuda_reset(tf_model* m, int seq);
 

@@ -72,3 +72,53 @@ def test_batched_gemm_against_oracle(paths):
         assert np.abs(lg[b] - want).max() < LOGIT_TOL
         assert int(am[b]) == int(np.argmax(want))
     m.close()
+
+
+@pytest.mark.parametrize("B", [3, 20])
+def test_prefill_batch_matches_single_prefill(B, paths):
+    """tf_cuda_prefill_batch (n steps of B rows; the GEMM path at B >= 16) gives each
+    sequence the state Model::prefill gives it alone."""
+    cfg = CFGS[1]
+    path = paths[cfg.name]
+    n = 6
+    prompts = np.array([synth.prompt_tokens(cfg, n, stream=500 + b) for b in range(B)], np.int32)
+    solo = Model(path, RunConfig(max_seq=32))
+    want_first, want_next = [], []
+    for p in prompts:
+        solo.reset()
+        want_first.append(int(np.argmax(solo.prefill(p))))
+        want_next.append(solo.decode(want_first[-1]).copy())
+    solo.close()
+    m = Model(path, RunConfig(max_seq=32, max_batch=B + 1))
+    m.decode(5, seq=0)  # another slot with history: untouched by the batch
+    seqs = list(range(1, B + 1))
+    first = m.prefill_batch(seqs, prompts)
+    assert first.tolist() == want_first
+    for b in range(B):
+        assert m.n_pos(seq=b + 1) == n
+    am, lg = m.decode_batch(seqs, first.tolist(), want_logits=True)
+    for b in range(B):
+        assert np.abs(lg[b] - want_next[b]).max() < LOGIT_TOL
+    assert m.n_pos(seq=0) == 1
+    m.close()
+
+
+@pytest.mark.parametrize("n", [16, 40, 300])
+def test_chunked_prefill_matches_oracle(n, paths):
+    """Model::prefill of >= 16 tokens runs in tensor-core chunks of up to 128 rows (RoPE + K/V
+    store for the chunk, then causal attention over the cache): logits and the following
+    greedy stream agree with the reference restatement."""
+    cfg = CFGS[1]
+    path = paths[cfg.name]
+    prompt = synth.prompt_tokens(cfg, n, stream=700 + n)
+    m = Model(path, RunConfig(max_seq=n + 8))
+    orc = po.OracleModel(gguf.GGUFReader(path), n + 8)
+    got, want = m.prefill(prompt), orc.prefill(prompt)
+    assert m.n_pos() == n
+    assert np.abs(got - want).max() < LOGIT_TOL
+    t = int(np.argmax(want))
+    for _ in range(3):
+        got, want = m.decode(t), orc.decode(t)
+        assert np.abs(got - want).max() < LOGIT_TOL
+        t = int(np.argmax(want))
+    m.close()
