@@ -71,8 +71,8 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
             vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
         }
     const int np_cached = (a.fresh == 1 && p1 == n_pos) ? np - 1 : np;  // the new position is not read
-    load_tile(ks, hd + 1, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
-    load_tile(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
+    load_tile<8>(ks, hd + 1, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
+    load_tile<8>(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
     __syncthreads();
 
     // 2) RoPE (fresh): the host table holds the reference's float cos/sin of pos*freq

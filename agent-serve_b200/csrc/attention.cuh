@@ -72,20 +72,21 @@ __device__ __forceinline__ void rope_pair(float& a, float& b, float c, float s) 
 
 // Loads `n` consecutive cache elements starting at element `e0` into dst[] as floats, all
 // loads in flight before the stores (one memory round trip), 16-byte vectors.
+template <int UNR = 4>
 __device__ __forceinline__ void load_tile(float* dst, int dst_stride, int hd, const void* base, long long e0, int np,
                                           int kv_type, int nth) {
     const int tid = threadIdx.x;
     const int per_vec = kv_type == KV_F32 ? 4 : 8;      // elements per 16-byte vector
     const int nvec = np * hd / per_vec;
-    for (int v0 = tid; v0 < nvec; v0 += nth * 4) {
-        uint4 r[4];
+    for (int v0 = tid; v0 < nvec; v0 += nth * UNR) {  // UNR 16-byte loads in flight per thread
+        uint4 r[UNR];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < UNR; ++u) {
             const int v = v0 + u * nth;
             if (v < nvec) r[u] = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(base) + (e0 * (kv_type == KV_F32 ? 4 : 2)))[v];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < UNR; ++u) {
             const int v = v0 + u * nth;
             if (v >= nvec) continue;
             const int e = v * per_vec;

@@ -89,18 +89,20 @@ __device__ __forceinline__ void q8_build_planes(const float4 (&v)[NU], int K, in
         const int sh = min(148 - e, Q8_PLANE_SH_MAX);
         const float S = __uint_as_float((uint32_t)(127 + sh) << 23);
         const float xv[4] = {x.x, x.y, x.z, x.w};
-        uint32_t d0 = 0, d1 = 0, d2 = 0;
+        // X = round(x * 2^sh): the scaling is exact and |X| < 2^22, so adding 1.5 * 2^23 rounds
+        // to the integer (ties to even, as __float2int_rn) in the float's low mantissa bits.
+        // Signed digits: x0 = the low byte of X; x1 = byte 1 of X + 128 (the carry of a
+        // negative x0); x2 = byte 2 of X + 32896 (both carries).
+        uint32_t X[4], Y1[4], Y2[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const int X = __float2int_rn(xv[i] * S);  // exact scaling by a power of two
-            const int x0 = (int)(int8_t)(X & 0xFF);
-            const int r = (X - x0) >> 8;
-            const int x1 = (int)(int8_t)(r & 0xFF);
-            const int x2 = (r - x1) >> 8;
-            d0 |= (uint32_t)(x0 & 0xFF) << (8 * i);
-            d1 |= (uint32_t)(x1 & 0xFF) << (8 * i);
-            d2 |= (uint32_t)(x2 & 0xFF) << (8 * i);
+            X[i] = (uint32_t)(__float_as_int(fmaf(xv[i], S, 12582912.0f)) - 0x4B400000);
+            Y1[i] = X[i] + 128u;
+            Y2[i] = X[i] + 32896u;
         }
+        const uint32_t d0 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+        const uint32_t d1 = __byte_perm(__byte_perm(Y1[0], Y1[1], 0x0051), __byte_perm(Y1[2], Y1[3], 0x0051), 0x5410);
+        const uint32_t d2 = __byte_perm(__byte_perm(Y2[0], Y2[1], 0x0062), __byte_perm(Y2[2], Y2[3], 0x0062), 0x5410);
         const int b = c >> 3;
         const int off = 34 * b + 2 + 4 * (c & 7);  // even: 16-bit stores
         uint16_t* q0 = reinterpret_cast<uint16_t*>(planes + off);

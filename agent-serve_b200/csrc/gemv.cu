@@ -364,7 +364,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
                     v[u].w = __fmul_rn(__fmul_rn(v[u].w, inv), wv.w);
                 }
             }
-            named_bar_compute();  // every read of the activation region is done
+            // the planes overwrite the activation region, which only the embedding path read
+            if (a.pro == PRO_EMBED_RMSNORM) named_bar_compute();
             uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
             const int pstride = (int)((a.rb + 15) & ~15LL);
             float* pinv = reinterpret_cast<float*>(planes + 3 * pstride);
