@@ -395,6 +395,36 @@ cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {
     return launch_pdl((const void*)finish_kernel, dim3(1), dim3(256), 0, st, args);
 }
 
+// Device version of q8_scale_exponent for weights that live only on the device: the largest
+// |d| bits over all blocks (one pass over the scale bytes).
+__global__ void q8_dmax_kernel(const uint8_t* W, long long n_blocks, unsigned* out) {
+    unsigned mx = 0;
+    for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
+        const unsigned d = ((unsigned)W[b * 34] | ((unsigned)W[b * 34 + 1] << 8)) & 0x7FFFu;
+        mx = d > mx ? d : mx;
+    }
+    mx = warp_max_u(mx);
+    if ((threadIdx.x & 31) == 0) atomicMax(out, mx);
+}
+
+int q8_exponent_from_dbits(unsigned mx) {
+    if (mx == 0 || mx >= 0x7C00u) return 0;
+    const int E = (mx >> 10) > 0 ? (int)(mx >> 10) : 1;
+    return 21 - E;
+}
+
+cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(unsigned), st);
+    if (e != cudaSuccess) return e;
+    q8_dmax_kernel<<<296, 256, 0, st>>>(W, n_blocks, scratch);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    unsigned h = 0;
+    if ((e = cudaMemcpyAsync(&h, scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return e;
+    *sw = q8_exponent_from_dbits(h);
+    return cudaSuccess;
+}
+
 // 2^sw with |q * d| * 2^sw < 2^14 for every block of the matrix (|q| <= 128).
 int q8_scale_exponent(const uint8_t* blocks, size_t nbytes) {
     unsigned mx = 0;
@@ -402,11 +432,9 @@ int q8_scale_exponent(const uint8_t* blocks, size_t nbytes) {
         const unsigned d = ((unsigned)blocks[o] | ((unsigned)blocks[o + 1] << 8)) & 0x7FFFu;
         mx = d > mx ? d : mx;
     }
-    if (mx == 0 || mx >= 0x7C00u) return 0;
     // |d| < 2^(E-14) for the f16 biased exponent E (subnormals: E = 1), so |q*d| < 2^(E-7)
     // and 2^(21-E) maps the matrix below 2^14
-    const int E = (mx >> 10) > 0 ? (int)(mx >> 10) : 1;
-    return 21 - E;
+    return q8_exponent_from_dbits(mx);
 }
 
 }  // namespace tfb

@@ -96,5 +96,8 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st);
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st);
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st);
 int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes);  // per-matrix sw
+int q8_exponent_from_dbits(unsigned max_abs_d_bits);
+// sw of device-resident Q8_0 blocks (synchronises `st`); scratch: one device unsigned
+cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st);
 
 }  // namespace tfb

@@ -4,6 +4,7 @@
 
 #include "attention.cuh"
 #include "engine.cuh"
+#include "gemm.cuh"
 
 namespace tfb {
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, cudaStream_t st);
@@ -38,6 +39,81 @@ int err_word(int** out) {
 
 extern "C" {
 
+int tf_op_q8_scale(const void* W, int N, int K, int* sw, void* stream) {
+    if (!W || !sw || N <= 0 || K <= 0 || K % 32) return set_error("bad Q8_0 matrix");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned* scratch = nullptr;
+    if (op_status(cudaMallocAsync((void**)&scratch, sizeof(unsigned), st), "alloc")) return -1;
+    const int rc = op_status(q8_scale_exponent_device(static_cast<const uint8_t*>(W), (long long)N * (K / 32), scratch,
+                                                      sw, st),
+                             "q8_scale");
+    cudaFreeAsync(scratch, st);
+    return rc;
+}
+
+int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, int M, int sw, void* stream) {
+    if (N <= 0 || K <= 0 || M < GM_MIN_M || K % GM_BK) return set_error("tensor-core GEMM needs M >= 16 and K % 64 == 0");
+    if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(W) & 3))
+        return set_error("A must be 16-byte and W 4-byte aligned");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int* err = nullptr;
+    if (err_word(&err)) return -1;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t rows = (size_t)(M + GM_BM - 1) / GM_BM * GM_BM;
+    __half *xh = nullptr, *xl = nullptr;
+    int* sx = nullptr;
+    float* ws = nullptr;
+    unsigned* cnt = nullptr;
+    const int ks = gemm_pick_split(N, M, K, sms);
+    int rc = op_status(cudaMallocAsync((void**)&xh, rows * K * sizeof(__half), st), "alloc");
+    if (!rc) rc = op_status(cudaMallocAsync((void**)&xl, rows * K * sizeof(__half), st), "alloc");
+    if (!rc) rc = op_status(cudaMallocAsync((void**)&sx, rows * sizeof(int), st), "alloc");
+    if (!rc && ks > 1) rc = op_status(cudaMallocAsync((void**)&ws, (size_t)ks * M * N * sizeof(float), st), "alloc");
+    if (!rc && ks > 1) rc = op_status(cudaMallocAsync((void**)&cnt, (size_t)sms * sizeof(unsigned), st), "alloc");
+    if (!rc && ks > 1) rc = op_status(cudaMemsetAsync(cnt, 0, (size_t)sms * sizeof(unsigned), st), "memset");
+    if (!rc) rc = op_status(cudaMemsetAsync(xh, 0, rows * K * sizeof(__half), st), "memset");
+    if (!rc) rc = op_status(cudaMemsetAsync(xl, 0, rows * K * sizeof(__half), st), "memset");
+    if (!rc) {
+        XPrepArgs p;
+        memset(&p, 0, sizeof(p));
+        p.x = A;
+        p.ldx = K;
+        p.K = K;
+        p.M = M;
+        p.xh = xh;
+        p.xl = xl;
+        p.sx = sx;
+        p.err = err;
+        rc = op_status(xprep_launch(p, st), "xprep");
+    }
+    if (!rc) {
+        GemmArgs g;
+        memset(&g, 0, sizeof(g));
+        g.W = static_cast<const uint8_t*>(W);
+        g.rb = row_bytes(T_Q8_0, K);
+        g.N = N;
+        g.K = K;
+        g.M = M;
+        g.sw = sw;
+        g.xh = xh;
+        g.xl = xl;
+        g.sx = sx;
+        g.epi = EPI_STORE;
+        g.y = C;
+        g.ldy = N;
+        g.ksplit = ks;
+        g.ws = ws;
+        g.tile_cnt = cnt;
+        rc = op_status(gemm_launch(g, st), "gemm");
+    }
+    void* bufs[] = {xh, xl, sx, ws, cnt};
+    for (void* b : bufs)
+        if (b) cudaFreeAsync(b, st);
+    return rc;
+}
+
 int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, int M, void* stream) {
     if (!type_ok(t)) return set_error("unsupported ggml type");
     if (N <= 0 || K <= 0 || M < 0) return set_error("bad matmul shape");
@@ -45,6 +121,12 @@ int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, i
     if (M == 0) return 0;
     if (t == T_F32 && (reinterpret_cast<uintptr_t>(W) & 3)) return set_error("F32 weights must be 4-byte aligned");
     if (reinterpret_cast<uintptr_t>(A) & 15) return set_error("A must be 16-byte aligned");
+    if (t == T_Q8_0 && M >= GM_MIN_M && K % GM_BK == 0 && !(reinterpret_cast<uintptr_t>(W) & 3)) {
+        // M >= 16: the tensor-core GEMM (scale of the matrix, then the GEMM)
+        int sw = 0;
+        if (tf_op_q8_scale(W, N, K, &sw, stream)) return -1;
+        return tf_op_matmul_q8_tc(C, A, W, N, K, M, sw, stream);
+    }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int* err = nullptr;
     if (err_word(&err)) return -1;

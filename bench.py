@@ -366,6 +366,64 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
             "profiles/gemv_q8_0_lmhead_128256x2048.md", "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
 
 
+def matmul_sweep():
+    """BASELINE cfg3: Y[M,N] = X[M,K] W[N,K]^T for Q8_0 and Q4_0 weights (N(0, 0.02) quantised),
+    X ~ N(0, 1); K=2048 with N in {512, 2048, 8192, 128256}, K=8192 with N=2048; M in
+    {1, 8, 64, 512}.  Weight copies rotate so that every timed launch reads its weights from
+    HBM (the rotation exceeds the 126 MB L2).  M <= 8 runs the dequant-GEMV, Q8_0 at M >= 16
+    the tensor-core GEMM (timed without the one-off scale pass), Q4_0 at M >= 16 GEMV tiles."""
+    import torch
+    from tinferno_b200 import gguf, native, quants
+    L = native.lib()
+    st = torch.cuda.current_stream()
+    rows = []
+    peak = peaks()[0]
+    for t, tname in ((gguf.GGML_Q8_0, "Q8_0"), (gguf.GGML_Q4_0, "Q4_0")):
+        for K, N in ((2048, 512), (2048, 2048), (2048, 8192), (2048, 128256), (8192, 2048)):
+            rng = np.random.default_rng(K + N)
+            w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+            raw = np.ascontiguousarray(quants.quantize(w, t)).reshape(-1)
+            nbytes = raw.nbytes
+            copies = max(1, int(np.ceil(256e6 / nbytes)))
+            W = [torch.from_numpy(raw).cuda() for _ in range(min(copies, 512))]
+            sw = C.c_int(0)
+            if t == gguf.GGML_Q8_0:
+                native.check(L.tf_op_q8_scale(C.c_void_p(W[0].data_ptr()), N, K, C.byref(sw), C.c_void_p(st.cuda_stream)))
+            for M in (1, 8, 64, 512):
+                X = torch.randn(M, K, device="cuda")
+                Y = torch.empty(M, N, device="cuda")
+                tc = t == gguf.GGML_Q8_0 and M >= 16
+
+                def run(i):
+                    wp = C.c_void_p(W[i % len(W)].data_ptr())
+                    if tc:
+                        native.check(L.tf_op_matmul_q8_tc(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), wp, N, K, M,
+                                                          sw.value, C.c_void_p(st.cuda_stream)))
+                    else:
+                        native.check(L.tf_op_matmul(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), t, wp, N, K, M,
+                                                    C.c_void_p(st.cuda_stream)))
+                for i in range(3):
+                    run(i)
+                reps = 10
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+                for i, (a, b) in enumerate(evs):
+                    a.record(st)
+                    run(i + 3)
+                    b.record(st)
+                torch.cuda.synchronize()
+                ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+                alg = nbytes + M * K * 4 + M * N * 4
+                fl = 2.0 * M * N * K
+                rows.append({"type": tname, "N": N, "K": K, "M": M, "path": "tensor-core GEMM" if tc else "GEMV",
+                             "us": round(ms * 1e3, 2), "GB_s": round(alg / (ms / 1e3) / 1e9, 1),
+                             "hbm_frac": round(alg / (ms / 1e3) / 1e9 / peak, 3),
+                             "TFLOP_s": round(fl / (ms / 1e3) / 1e12, 2)})
+                print(json.dumps(rows[-1]), flush=True)
+            del W
+            torch.cuda.empty_cache()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -375,7 +433,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -384,6 +442,9 @@ def main():
         import torch
         from tinferno_b200 import native
         print(json.dumps(gemv_roofline(torch, native, None, reps=3, warm=1)))
+        return
+    if args.kernel == "sweep":
+        matmul_sweep()
         return
     if args.kernel == "step":
         from tinferno_b200.model import Model, RunConfig

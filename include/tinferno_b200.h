@@ -141,6 +141,14 @@ TF_API const char* tf_cuda_last_error(tf_model* m);
 TF_API int tf_op_matmul(float* C, const float* A, int ggml_type, const void* W, int N, int K, int M,
                  void* stream);
 
+/* Tensor-core Q8_0 GEMM in two parts, no reference counterpart (tf_op_matmul composes them
+ * for M >= 16): tf_op_q8_scale finds the power-of-two scale sw of a Q8_0 matrix (one pass
+ * over its block scales, synchronises the stream); tf_op_matmul_q8_tc computes C = A W^T with
+ * it (M >= 16, K % 64 == 0; f16-split products, fp32 accumulation). */
+TF_API int tf_op_q8_scale(const void* W, int N, int K, int* sw, void* stream);
+TF_API int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, int M, int sw,
+                              void* stream);
+
 /* dequant_row(float* out, const Tensor& t, int64_t row)  src/quant.hpp:42: out[i][K] is
  * row rows[i] of W (embedding lookup). */
 TF_API int tf_op_dequant_rows(float* out, int ggml_type, const void* W, int K, const int* rows,

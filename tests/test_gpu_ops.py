@@ -67,6 +67,28 @@ def test_matmul(t, shape):
     assert_dot_close(got, want, a, quants.dequant(raw, t, k))
 
 
+@pytest.mark.parametrize("shape", [(256, 2048, 16), (1000, 2048, 64), (130, 896, 130), (96, 4864, 33),
+                                   (2048, 8192, 40), (515, 1536, 300)])
+def test_matmul_tensor_core(shape):
+    """Q8_0 at M >= 16 runs the tensor-core GEMM (f16-split products, fp32 accumulation,
+    split-K when the tiles do not cover the SMs)."""
+    n, k, m = shape
+    t = gguf.GGML_Q8_0
+    rng = np.random.default_rng(k + n + m)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    raw = np.ascontiguousarray(quants.quantize(w, t))
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    want = np.zeros((m, n), np.float32)
+    po.oracle_lib().tfo_matmul(fp(want), fp(a), t, raw.ctypes.data, n, k, m, 4)
+    wd = dev(raw.reshape(-1))
+    ad, cd = dev(a), torch.full((m, n), float("nan"), device="cuda")
+    call(native.lib().tf_op_matmul(ptr(cd), ptr(ad), t, ptr(wd), n, k, m, None))
+    got = cd.cpu().numpy()
+    scale = np.abs(a) @ np.abs(quants.dequant(raw, t, k)).T
+    err = np.abs(got - want)
+    assert np.all(err <= 2e-5 * scale + 1e-6), float((err / (scale + 1e-30)).max())
+
+
 @pytest.mark.parametrize("t", TYPES)
 def test_dequant_rows_exact(t):
     k = 512
