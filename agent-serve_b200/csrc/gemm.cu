@@ -9,6 +9,8 @@
 // The epilogue scales back by 2^-(sw+sx[m]), stages the tile in shared memory and applies
 // the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
+#include <cstdlib>
+
 #include "dots.cuh"
 #include "gemm.cuh"
 
@@ -153,6 +155,72 @@ __device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float 
     }
 }
 
+// Split-K reduction and the fused epilogue over a CTA tile staged in shared memory as
+// tile[m - m0][n - n0] (BMT activation rows x GM_BN weight rows, row stride GM_EPI_LD).
+template <int BMT>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0) {
+    const int tid = threadIdx.x;
+    if (gridDim.z > 1) {
+        // split-K: publish this split's tile; the last split of the tile sums all in order
+        __shared__ int last_s;
+        float* wz = a.ws + (size_t)blockIdx.z * a.M * a.N;
+        for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
+            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+            if (m < a.M && n < a.N) wz[(size_t)m * a.N + n] = tile[mm * GM_EPI_LD + nn];
+        }
+        __threadfence();
+        __syncthreads();
+        const int tix = blockIdx.y * gridDim.x + blockIdx.x;
+        if (tid == 0) {
+            const unsigned t = atomicAdd(&a.tile_cnt[tix], 1u);
+            last_s = t == gridDim.z - 1;
+        }
+        __syncthreads();
+        if (!last_s) return;
+        __threadfence();
+        for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
+            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+            if (m >= a.M || n >= a.N) continue;
+            float v = 0.f;
+            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(a.ws + ((size_t)z * a.M + m) * a.N + n);
+            tile[mm * GM_EPI_LD + nn] = v;
+        }
+        if (tid == 0) a.tile_cnt[tix] = 0u;
+        __syncthreads();
+    }
+    if (a.epi == EPI_ARGMAX) {
+        if (tid < BMT && m0 + tid < a.M) {
+            const int m = m0 + tid;
+            unsigned long long best = 0ull;
+            for (int nn = 0; nn < GM_BN && n0 + nn < a.N; ++nn) {
+                const float v = tile[tid * GM_EPI_LD + nn];
+                const unsigned long long k = argmax_key(v, (uint32_t)(n0 + nn));
+                best = k > best ? k : best;
+            }
+            if (best) atomicMax(&a.keys[m], best);
+        }
+        if (a.store_logits)
+            for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
+                const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+                if (m < a.M && n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
+            }
+        return;
+    }
+    for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
+        const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+        if (m >= a.M || n >= a.N) continue;
+        const float v = tile[mm * GM_EPI_LD + nn];
+        if (a.epi == EPI_STORE) {
+            a.y[(size_t)m * a.ldy + n] = v + (a.bias ? a.bias[n] : 0.f);
+        } else if (a.epi == EPI_RESID) {
+            a.resid[(size_t)m * a.ldr + n] += v;
+        } else if ((n & 1) == 0) {  // EPI_SWIGLU: rows 2i (gate) and 2i+1 (up)
+            const float gt = v, up = tile[mm * GM_EPI_LD + nn + 1];
+            a.y[(size_t)m * a.ldy + (n >> 1)] = __fmul_rn(__fdiv_rn(gt, 1.0f + expf(-gt)), up);
+        }
+    }
+}
+
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -261,65 +329,170 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
         }
     }
     __syncthreads();
-    if (gridDim.z > 1) {
-        // split-K: publish this split's tile; the last split of the tile sums all in order
-        __shared__ int last_s;
-        float* wz = a.ws + (size_t)blockIdx.z * a.M * a.N;
-        for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
-            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-            if (m < a.M && n < a.N) wz[(size_t)m * a.N + n] = tile[mm * GM_EPI_LD + nn];
+    gemm_epilogue<GM_BM>(a, tile, m0, n0);
+}
+
+// ---- the GEMM on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) ---------------
+// Same arithmetic and epilogue as gemm_q8_kernel; the products run as tcgen05.mma
+// (kind::f16, M = 128 weight rows, N = NT activation rows, K = 16) issued by one thread, with the
+// fp32 accumulator in tensor memory.  Operands sit in shared memory in the canonical K-major
+// layout without swizzle: 8-row x 16-byte core matrices, row groups SBO = 1024 B apart and
+// 8-element k chunks LBO = 128 B apart (one 64-element k stage = 8 chunks per row group).
+// Two stages: while the tensor cores consume stage s, all threads dequantise the weights and
+// copy the activations of the next stage into s ^ 1; a tcgen05.commit per stage arrives on
+// that stage's mbarrier when its MMAs have read it.
+__device__ __forceinline__ uint64_t umma_desc_k_interleave(uint32_t saddr) {
+    // start >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46), version 1 [46,48), layout 0
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46);
+}
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        :
+        : "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+
+template <int NT>
+constexpr size_t gemm_tc_stage_bytes() {
+    return (size_t)2 * GM_BN * GM_BK * 2 + (size_t)2 * NT * GM_BK * 2;  // Wh, Wl, Xh, Xl
+}
+template <int NT>
+constexpr size_t gemm_tc_smem_bytes() {
+    const size_t pipe = 2 * gemm_tc_stage_bytes<NT>();
+    const size_t epi = (size_t)NT * GM_EPI_LD * 4;
+    return (pipe > epi ? pipe : epi) + 64;  // + mbarriers and the TMEM address
+}
+
+// byte offset of element (row, k) of a [rows][64] f16 operand tile in the canonical layout
+__device__ __forceinline__ uint32_t kint_off(int row, int k) {
+    return (uint32_t)((row >> 3) * 1024 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+}
+
+template <int NT>
+__global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * NT;
+    const int nk_all = a.K / GM_BK;
+    const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
+    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
+    const float wscale = ldexpf(1.0f, a.sw);
+    constexpr size_t SB = gemm_tc_stage_bytes<NT>();
+    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - 64;
+    uint64_t* done = reinterpret_cast<uint64_t*>(tail);            // [2] MMAs of a stage completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail + 32);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 40);
+    auto wh = [&](int s) { return smem + (size_t)s * SB; };
+    auto wl = [&](int s) { return smem + (size_t)s * SB + GM_BN * GM_BK * 2; };
+    auto xh = [&](int s) { return smem + (size_t)s * SB + 2 * GM_BN * GM_BK * 2; };
+    auto xl = [&](int s) { return smem + (size_t)s * SB + 2 * GM_BN * GM_BK * 2 + NT * GM_BK * 2; };
+
+    if (warp == 0) {  // TMEM for the NT x 128 fp32 accumulator (NT columns)
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(NT));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+    }
+    if (tid == 0) {
+        mbar_init(&done[0], 1);
+        mbar_init(&done[1], 1);
+        *abort_flag = 0;
+        mbar_fence_init();
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+    pdl_trigger();
+    pdl_wait();
+
+    // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
+    const int wr = tid >> 1, wj = tid & 1;
+    uint32_t wv[9];
+    auto fill = [&](int s, int kc) {
+        for (int i = tid; i < 2 * NT * 8; i += GM_THREADS) {  // activations: 16-byte chunks
+            const int pl = i / (NT * 8), r = (i / 8) % NT, c = i % 8;
+            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + r) * a.K + (size_t)kc * GM_BK + 8 * c;
+            cp_async16((pl ? xl(s) : xh(s)) + kint_off(r, 8 * c), src);
         }
-        __threadfence();
+        cp_async_commit();
+        gm_load_w(wv, a, n0 + wr, kc, wj);
+        // 32 halves per plane = 4 core-matrix rows of 16 bytes
+        __half hbuf[32], lbuf[32];
+        gm_dequant(wv, wj, wscale, hbuf, lbuf);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(wh(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(hbuf)[c];
+            *reinterpret_cast<uint4*>(wl(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(lbuf)[c];
+        }
+        cp_async_wait_all();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+    };
+
+    bool ok = true;
+    int last_kc = -1;  // the last stage whose MMAs were issued
+    for (int kc = 0; kc < nk && ok; ++kc) {
+        const int s = kc & 1;
+        if (kc >= 2) ok = mbar_wait(&done[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+        if (!ok) break;
+        fill(s, kb + kc);
         __syncthreads();
-        const int tix = blockIdx.y * gridDim.x + blockIdx.x;
+        last_kc = kc;
         if (tid == 0) {
-            const unsigned t = atomicAdd(&a.tile_cnt[tix], 1u);
-            last_s = t == gridDim.z - 1;
-        }
-        __syncthreads();
-        if (!last_s) return;
-        __threadfence();
-        for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
-            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-            if (m >= a.M || n >= a.N) continue;
-            float v = 0.f;
-            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(a.ws + ((size_t)z * a.M + m) * a.N + n);
-            tile[mm * GM_EPI_LD + nn] = v;
-        }
-        if (tid == 0) a.tile_cnt[tix] = 0u;
-        __syncthreads();
-    }
-    if (a.epi == EPI_ARGMAX) {
-        if (tid < GM_BM && m0 + tid < a.M) {
-            const int m = m0 + tid;
-            unsigned long long best = 0ull;
-            for (int nn = 0; nn < GM_BN && n0 + nn < a.N; ++nn) {
-                const float v = tile[tid * GM_EPI_LD + nn];
-                const unsigned long long k = argmax_key(v, (uint32_t)(n0 + nn));
-                best = k > best ? k : best;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(s)), bl = smem_u32(xl(s));
+#pragma unroll
+            for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps = 2 chunks = 256 bytes
+                const uint32_t o = 256u * j;
+                umma_f16(tmem, umma_desc_k_interleave(ah + o), umma_desc_k_interleave(bh + o), idesc,
+                         (kc > 0 || j > 0) ? 1u : 0u);
+                umma_f16(tmem, umma_desc_k_interleave(ah + o), umma_desc_k_interleave(bl + o), idesc, 1u);
+                umma_f16(tmem, umma_desc_k_interleave(al + o), umma_desc_k_interleave(bh + o), idesc, 1u);
             }
-            if (best) atomicMax(&a.keys[m], best);
+            umma_commit(&done[s]);
         }
-        if (a.store_logits)
-            for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
-                const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-                if (m < a.M && n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
+    }
+    // the last stage's commit covers every MMA issued before it
+    if (last_kc >= 0 && !mbar_wait(&done[last_kc & 1], (last_kc >> 1) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    __syncthreads();
+
+    // ---- epilogue: TMEM -> registers -> scaled tile[m][n] in shared memory ----
+    float* tile = reinterpret_cast<float*>(smem);  // [NT][GM_EPI_LD], the pipeline buffers are free
+    {
+        const int row = 32 * (warp & 3) + lane;           // weight row of this thread's TMEM lane
+        const int c0 = (warp >> 2) * (NT / 2);             // warps 4-7 take the upper columns
+        for (int c = c0; c < c0 + NT / 2; c += 16) {
+            uint32_t r[16];
+            tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const int mm = c + u, m = m0 + mm;
+                const float sc = (ok && m < a.M) ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
+                tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * sc;
             }
-        return;
-    }
-    for (int i = tid; i < GM_BM * GM_BN; i += GM_THREADS) {
-        const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-        if (m >= a.M || n >= a.N) continue;
-        const float v = tile[mm * GM_EPI_LD + nn];
-        if (a.epi == EPI_STORE) {
-            a.y[(size_t)m * a.ldy + n] = v + (a.bias ? a.bias[n] : 0.f);
-        } else if (a.epi == EPI_RESID) {
-            a.resid[(size_t)m * a.ldr + n] += v;
-        } else if ((n & 1) == 0) {  // EPI_SWIGLU: rows 2i (gate) and 2i+1 (up)
-            const float gt = v, up = tile[mm * GM_EPI_LD + nn + 1];
-            a.y[(size_t)m * a.ldy + (n >> 1)] = __fmul_rn(__fdiv_rn(gt, 1.0f + expf(-gt)), up);
         }
     }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT));
+    if (!ok) return;  // the error word holds the failure
+    gemm_epilogue<NT>(a, tile, m0, n0);
 }
 
 // ---- end of a step at M rows ------------------------------------------------------------------
@@ -369,6 +542,16 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// tcgen05 path (default) or the mma.sync path (TFB200_GEMM_TC05=0)
+static bool gemm_use_tc05() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_GEMM_TC05");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     const size_t smem = 2 * GM_STAGE_BYTES;
@@ -383,6 +566,24 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     }
     const int ks = a.ksplit > 1 ? a.ksplit : 1;
     if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
+    if (gemm_use_tc05()) {
+        GemmArgs aa = a;
+        void* args[] = {&aa};
+        const bool wide = a.M > 128;
+        const size_t sm = wide ? gemm_tc_smem_bytes<256>() : gemm_tc_smem_bytes<128>();
+        const void* fn = wide ? (const void*)gemm_q8_tc_kernel<256> : (const void*)gemm_q8_tc_kernel<128>;
+        static bool tc_attr[64][2] = {};
+        int dv = 0;
+        cudaGetDevice(&dv);
+        if (dv < 0 || dv >= 64) dv = 0;
+        if (!tc_attr[dv][wide]) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+            if (e != cudaSuccess) return e;
+            tc_attr[dv][wide] = true;
+        }
+        const int nt = wide ? 256 : 128;
+        return launch_pdl(fn, dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks), dim3(GM_THREADS), sm, st, args);
+    }
     dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
     GemmArgs aa = a;
     void* args[] = {&aa};

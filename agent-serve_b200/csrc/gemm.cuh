@@ -46,7 +46,7 @@ struct GemmArgs {
     long long rb;
     int N, K, M;
     int sw;               // weight scale exponent
-    const __half* xh;     // [>= ceil(M/GM_BM)*GM_BM][K]
+    const __half* xh;     // [>= ceil(M/GM_ROW_PAD)*GM_ROW_PAD][K]
     const __half* xl;
     const int* sx;        // [M]
     // epilogue (GemvArgs conventions)
@@ -63,15 +63,19 @@ struct GemmArgs {
     int ksplit;
     float* ws;
     unsigned* tile_cnt;
+    int* err;
 };
+
+constexpr int GM_ROW_PAD = 256;  // activation buffers hold a multiple of this many rows
 
 constexpr int GM_MAX_SPLIT = 8;
 // workspace floats / tile counters the split-K path needs for `num_sms` SMs
-inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_BM; }
+inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_ROW_PAD; }
 inline int gemm_tile_counters(int num_sms) { return num_sms; }
 // k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
 inline int gemm_pick_split(int N, int M, int K, int num_sms) {
-    const int tiles = ((N + GM_BN - 1) / GM_BN) * ((M + GM_BM - 1) / GM_BM);
+    const int mt = M > GM_BM ? GM_ROW_PAD : GM_BM;  // activation rows per CTA tile
+    const int tiles = ((N + GM_BN - 1) / GM_BN) * ((M + mt - 1) / mt);
     if (tiles >= num_sms) return 1;
     int s = num_sms / tiles;
     const int nk = K / GM_BK;

@@ -279,6 +279,7 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) 
         g.ksplit = gemm_pick_split(N, M, w.K, m->num_sms);
         g.ws = m->gws;
         g.tile_cnt = m->gcnt;
+        g.err = m->d_err;
         return g;
     };
     for (int li = 0; li < m->hp.n_layer; ++li) {
@@ -1009,7 +1010,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     const int T = std::max(m->tile, std::max(m->gtile, m->ptile));
     if (m->gtile || m->ptile) {
         const int Kmax = std::max(m->D, std::max(m->H, m->FF));
-        const size_t rows = (size_t)(std::max(m->gtile, m->ptile) + GM_BM - 1) / GM_BM * GM_BM;
+        const size_t rows = (size_t)(std::max(m->gtile, m->ptile) + GM_ROW_PAD - 1) / GM_ROW_PAD * GM_ROW_PAD;
         CKD(cudaMalloc(&m->xh, rows * Kmax * sizeof(__half)));
         CKD(cudaMalloc(&m->xl, rows * Kmax * sizeof(__half)));
         CKD(cudaMemset(m->xh, 0, rows * Kmax * sizeof(__half)));

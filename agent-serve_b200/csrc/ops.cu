@@ -61,7 +61,7 @@ int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, in
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const size_t rows = (size_t)(M + GM_BM - 1) / GM_BM * GM_BM;
+    const size_t rows = (size_t)(M + GM_ROW_PAD - 1) / GM_ROW_PAD * GM_ROW_PAD;
     __half *xh = nullptr, *xl = nullptr;
     int* sx = nullptr;
     float* ws = nullptr;
@@ -106,6 +106,7 @@ int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, in
         g.ksplit = ks;
         g.ws = ws;
         g.tile_cnt = cnt;
+        g.err = err;
         rc = op_status(gemm_launch(g, st), "gemm");
     }
     void* bufs[] = {xh, xl, sx, ws, cnt};
