@@ -157,58 +157,79 @@ __device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float 
 
 // Split-K reduction and the fused epilogue over a CTA tile staged in shared memory as
 // tile[m - m0][n - n0] (BMT activation rows x GM_BN weight rows, row stride GM_EPI_LD).
+// With split-K (grid.z = ks > 1, every CTA of the grid resident: ks x tiles <= SMs) each split
+// publishes its partial tile, waits (bounded) for the other splits of its tile, then sums all
+// partials, in split order, for its own 1/ks of the tile's activation rows and applies the
+// epilogue to those rows: the reduction is spread over the splits and deterministic.
 template <int BMT>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0) {
     const int tid = threadIdx.x;
+    const int rv = min(BMT, a.M - m0);  // valid activation rows of the tile
+    int mlo = 0, mhi = rv;
     if (gridDim.z > 1) {
-        // split-K: publish this split's tile; the last split of the tile sums all in order
-        __shared__ int last_s;
-        float* wz = a.ws + (size_t)blockIdx.z * a.M * a.N;
-        for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
-            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-            if (m < a.M && n < a.N) wz[(size_t)m * a.N + n] = tile[mm * GM_EPI_LD + nn];
+        __shared__ int ok_s;
+        const int ks = (int)gridDim.z, z = (int)blockIdx.z;
+        float* wz = a.ws + (size_t)z * a.M * a.N;
+        for (int i = tid; i < rv * GM_BN; i += GM_THREADS) {
+            const int mm = i / GM_BN, nn = i % GM_BN, n = n0 + nn;
+            if (n < a.N) wz[(size_t)(m0 + mm) * a.N + n] = tile[mm * GM_EPI_LD + nn];
         }
         __threadfence();
         __syncthreads();
-        const int tix = blockIdx.y * gridDim.x + blockIdx.x;
+        unsigned* cnt = a.tile_cnt + 2 * (blockIdx.y * gridDim.x + blockIdx.x);
         if (tid == 0) {
-            const unsigned t = atomicAdd(&a.tile_cnt[tix], 1u);
-            last_s = t == gridDim.z - 1;
+            red_release_gpu_add(cnt, 1u);
+            int i = 0;
+            for (; i < kGridPolls; ++i) {
+                if (ld_acquire_gpu(cnt) >= (unsigned)ks) break;
+                if (i > 64) __nanosleep(i > 65536 ? 1024 : 64);
+            }
+            ok_s = i < kGridPolls;
+            if (!ok_s && a.err) atomicCAS(a.err, 0, ERR_GRID_SYNC);
         }
         __syncthreads();
-        if (!last_s) return;
-        __threadfence();
-        for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
-            const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-            if (m >= a.M || n >= a.N) continue;
-            float v = 0.f;
-            for (int z = 0; z < (int)gridDim.z; ++z) v += __ldcg(a.ws + ((size_t)z * a.M + m) * a.N + n);
-            tile[mm * GM_EPI_LD + nn] = v;
-        }
-        if (tid == 0) a.tile_cnt[tix] = 0u;
+        const bool ok = ok_s != 0;
+        mlo = rv * z / ks;
+        mhi = rv * (z + 1) / ks;
+        if (ok)
+            for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+                const int mm = mlo + i / GM_BN, nn = i % GM_BN, n = n0 + nn;
+                if (n >= a.N) continue;
+                float v = 0.f;
+                for (int q = 0; q < ks; ++q) v += __ldcg(a.ws + ((size_t)q * a.M + m0 + mm) * a.N + n);
+                tile[mm * GM_EPI_LD + nn] = v;
+            }
         __syncthreads();
+        if (tid == 0) {  // the last split out clears the tile's counters for the next launch
+            const unsigned d = atomicAdd(cnt + 1, 1u);
+            if (d == (unsigned)ks - 1) {
+                cnt[0] = 0u;
+                cnt[1] = 0u;
+            }
+        }
+        if (!ok) return;
     }
     if (a.epi == EPI_ARGMAX) {
-        if (tid < BMT && m0 + tid < a.M) {
-            const int m = m0 + tid;
+        if (tid < mhi - mlo) {
+            const int mm = mlo + tid, m = m0 + mm;
             unsigned long long best = 0ull;
             for (int nn = 0; nn < GM_BN && n0 + nn < a.N; ++nn) {
-                const float v = tile[tid * GM_EPI_LD + nn];
+                const float v = tile[mm * GM_EPI_LD + nn];
                 const unsigned long long k = argmax_key(v, (uint32_t)(n0 + nn));
                 best = k > best ? k : best;
             }
             if (best) atomicMax(&a.keys[m], best);
         }
         if (a.store_logits)
-            for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
-                const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-                if (m < a.M && n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
+            for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+                const int mm = mlo + i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+                if (n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
             }
         return;
     }
-    for (int i = tid; i < BMT * GM_BN; i += GM_THREADS) {
-        const int mm = i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
-        if (m >= a.M || n >= a.N) continue;
+    for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+        const int mm = mlo + i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
+        if (n >= a.N) continue;
         const float v = tile[mm * GM_EPI_LD + nn];
         if (a.epi == EPI_STORE) {
             a.y[(size_t)m * a.ldy + n] = v + (a.bias ? a.bias[n] : 0.f);

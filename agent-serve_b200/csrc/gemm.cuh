@@ -71,7 +71,7 @@ constexpr int GM_ROW_PAD = 256;  // activation buffers hold a multiple of this m
 constexpr int GM_MAX_SPLIT = 8;
 // workspace floats / tile counters the split-K path needs for `num_sms` SMs
 inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_ROW_PAD; }
-inline int gemm_tile_counters(int num_sms) { return num_sms; }
+inline int gemm_tile_counters(int num_sms) { return 2 * num_sms; }  // arrivals, departures per tile
 // k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
 inline int gemm_pick_split(int N, int M, int K, int num_sms) {
     const int mt = M > GM_BM ? GM_ROW_PAD : GM_BM;  // activation rows per CTA tile

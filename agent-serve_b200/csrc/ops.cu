@@ -71,8 +71,9 @@ int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, in
     if (!rc) rc = op_status(cudaMallocAsync((void**)&xl, rows * K * sizeof(__half), st), "alloc");
     if (!rc) rc = op_status(cudaMallocAsync((void**)&sx, rows * sizeof(int), st), "alloc");
     if (!rc && ks > 1) rc = op_status(cudaMallocAsync((void**)&ws, (size_t)ks * M * N * sizeof(float), st), "alloc");
-    if (!rc && ks > 1) rc = op_status(cudaMallocAsync((void**)&cnt, (size_t)sms * sizeof(unsigned), st), "alloc");
-    if (!rc && ks > 1) rc = op_status(cudaMemsetAsync(cnt, 0, (size_t)sms * sizeof(unsigned), st), "memset");
+    if (!rc && ks > 1)
+        rc = op_status(cudaMallocAsync((void**)&cnt, (size_t)gemm_tile_counters(sms) * sizeof(unsigned), st), "alloc");
+    if (!rc && ks > 1) rc = op_status(cudaMemsetAsync(cnt, 0, (size_t)gemm_tile_counters(sms) * sizeof(unsigned), st), "memset");
     if (!rc) rc = op_status(cudaMemsetAsync(xh, 0, rows * K * sizeof(__half), st), "memset");
     if (!rc) rc = op_status(cudaMemsetAsync(xl, 0, rows * K * sizeof(__half), st), "memset");
     if (!rc) {
