@@ -32,6 +32,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     __shared__ float cw[AT_MAX_REP][AT_MAX_SPLIT];
     __shared__ float cden[AT_MAX_REP];
     __shared__ int last_s;
+    __shared__ __align__(8) uint64_t kvbar;
 
     pdl_trigger();
     pdl_wait();
@@ -56,24 +57,44 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     const int p0 = ws + split * chunk;
     const int p1 = min(n_pos, p0 + chunk);
     const int np = max(0, p1 - p0);
-    float* ks = tile;                                  // [AT_CHUNK][hd + 1]
-    float* vs = tile + (size_t)AT_CHUNK * (hd + 1);    // [AT_CHUNK][hd]
+    // fp32 caches: K and V rows of the split arrive by two 1-D bulk copies (TMA), rows
+    // unpadded (the score loop rotates its start per position, so the rows of one warp still
+    // meet distinct banks); fp16 / bf16 caches are widened by the threads (K rows padded)
+    const bool bulk = a.kv_type == KV_F32;
+    const int kst = bulk ? hd : hd + 1;
+    float* ks = tile;                                  // [AT_CHUNK][kst]
+    float* vs = tile + (size_t)AT_CHUNK * kst;         // [AT_CHUNK][hd]
 
     const float* row = a.qkv + (size_t)m * a.ld_qkv;
     const float* q = row + (size_t)kvh * n_rep * hd;
     const size_t cache_off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd;
 
-    // 1) query heads of the group, new k/v, cached K/V of this split: independent loads
+    // 1) cached K/V of this split, query heads of the group, new k/v: independent loads
+    const int np_cached = (a.fresh == 1 && p1 == n_pos) ? np - 1 : np;  // the new position is not read
+    if (bulk) {
+        if (tid == 0) {
+            mbar_init(&kvbar, 1);
+            mbar_fence_init();
+            const uint32_t bytes = (uint32_t)np_cached * hd * 4;
+            mbar_expect_tx(&kvbar, 2 * bytes);
+            if (bytes) {
+                const size_t e0 = cache_off + (size_t)p0 * hd;
+                bulk_g2s(ks, static_cast<const float*>(a.kc) + e0, bytes, &kvbar);
+                bulk_g2s(vs, static_cast<const float*>(a.vc) + e0, bytes, &kvbar);
+            }
+        }
+    } else {
+        load_tile<8>(ks, kst, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
+        load_tile<8>(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
+    }
     for (int i = tid; i < n_rep * hd; i += AT_THREADS) qs[i / hd][i % hd] = q[i];
     if (a.fresh == 1)
         for (int i = tid; i < hd; i += AT_THREADS) {
             kn[i] = row[(size_t)a.n_head * hd + (size_t)kvh * hd + i];
             vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
         }
-    const int np_cached = (a.fresh == 1 && p1 == n_pos) ? np - 1 : np;  // the new position is not read
-    load_tile<8>(ks, hd + 1, hd, a.kc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
-    load_tile<8>(vs, hd, hd, a.vc, (long long)(cache_off + (size_t)p0 * hd), np_cached, a.kv_type, AT_THREADS);
     __syncthreads();
+    if (bulk) mbar_wait(&kvbar, 0, a.err, ERR_WAIT_FULL, nullptr);
 
     // 2) RoPE (fresh): the host table holds the reference's float cos/sin of pos*freq
     if (a.fresh == 1) {
@@ -93,7 +114,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
         if (p1 == n_pos)
             for (int i = tid; i < hd; i += AT_THREADS) {
                 // the new key/value enter at the stored precision, as later steps read them
-                ks[(size_t)(np - 1) * (hd + 1) + i] = kv_round(kn[i], a.kv_type);
+                ks[(size_t)(np - 1) * kst + i] = kv_round(kn[i], a.kv_type);
                 vs[(size_t)(np - 1) * hd + i] = kv_round(vn[i], a.kv_type);
             }
         __syncthreads();
@@ -103,11 +124,15 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     const float scale = 1.0f / sqrtf((float)hd);
     for (int i = tid; i < n_rep * np; i += AT_THREADS) {
         const int h = i / np, p = i % np;
-        const float* kp = ks + (size_t)p * (hd + 1);
+        const float* kp = ks + (size_t)p * kst;
+        const int rot = p % hd;  // start of this position's walk over the dims
         float s0 = 0.f, s1 = 0.f;
         for (int d = 0; d < hd; d += 2) {
-            s0 = fmaf(qs[h][d], kp[d], s0);
-            s1 = fmaf(qs[h][d + 1], kp[d + 1], s1);
+            int e0 = d + rot, e1 = d + 1 + rot;
+            e0 -= e0 >= hd ? hd : 0;
+            e1 -= e1 >= hd ? hd : 0;
+            s0 = fmaf(qs[h][e0], kp[e0], s0);
+            s1 = fmaf(qs[h][e1], kp[e1], s1);
         }
         sc[h][p] = scale * (s0 + s1);
     }
