@@ -357,15 +357,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
 // Same arithmetic and epilogue as gemm_q8_kernel; the products run as tcgen05.mma
 // (kind::f16, M = 128 weight rows, N = NT activation rows, K = 16) issued by one thread, with the
 // fp32 accumulator in tensor memory.  Operands sit in shared memory in the canonical K-major
-// layout without swizzle: 8-row x 16-byte core matrices, row groups SBO = 1024 B apart and
-// 8-element k chunks LBO = 128 B apart (one 64-element k stage = 8 chunks per row group).
+// 128-byte-swizzled layout: a row's 64 k values (128 B) form one line of an 8-line, 1024-byte
+// atom, and the 16-byte chunk c of line r is stored at chunk c ^ r, so that the tensor cores'
+// reads of eight lines spread over all banks; atoms of 8 rows are SBO = 1024 B apart, and the
+// 16-element k steps of the stage are 32 B apart within the lines.
 // Two stages: while the tensor cores consume stage s, all threads dequantise the weights and
 // copy the activations of the next stage into s ^ 1; a tcgen05.commit per stage arrives on
 // that stage's mbarrier when its MMAs have read it.
-__device__ __forceinline__ uint64_t umma_desc_k_interleave(uint32_t saddr) {
-    // start >> 4 [0,14), LBO >> 4 [16,30), SBO >> 4 [32,46), version 1 [46,48), layout 0
-    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46);
+__device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
+    // start >> 4 [0,14), LBO [16,30) (1: unused by swizzled K-major), SBO >> 4 [32,46),
+    // version 1 [46,48), base offset 0, layout 2 = 128-byte swizzle [61,64)
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
     asm volatile(
@@ -395,17 +398,19 @@ template <int NT>
 constexpr size_t gemm_tc_smem_bytes() {
     const size_t pipe = 2 * gemm_tc_stage_bytes<NT>();
     const size_t epi = (size_t)NT * GM_EPI_LD * 4;
-    return (pipe > epi ? pipe : epi) + 64;  // + mbarriers and the TMEM address
+    return (pipe > epi ? pipe : epi) + 64 + 1024;  // + mbarriers, the TMEM address, 1024-B alignment
 }
 
-// byte offset of element (row, k) of a [rows][64] f16 operand tile in the canonical layout
+// byte offset of element (row, k) of a [rows][64] f16 operand tile in the swizzled layout
 __device__ __forceinline__ uint32_t kint_off(int row, int k) {
-    return (uint32_t)((row >> 3) * 1024 + (k >> 3) * 128 + (row & 7) * 16 + (k & 7) * 2);
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
 }
 
 template <int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // the swizzle atoms need 1024-byte aligned stage buffers
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * NT;
     const int nk_all = a.K / GM_BK;
@@ -413,7 +418,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
     constexpr size_t SB = gemm_tc_stage_bytes<NT>();
-    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - 64;
+    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - 64 - 1024;
     uint64_t* done = reinterpret_cast<uint64_t*>(tail);            // [2] MMAs of a stage completed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail + 32);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 40);
@@ -444,47 +449,57 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
     const int wr = tid >> 1, wj = tid & 1;
     uint32_t wv[9];
-    auto fill = [&](int s, int kc) {
-        for (int i = tid; i < 2 * NT * 8; i += GM_THREADS) {  // activations: 16-byte chunks
+    auto load_x = [&](int s, int kc) {  // activations of stage kc: 16-byte cp.async chunks
+        for (int i = tid; i < 2 * NT * 8; i += GM_THREADS) {
             const int pl = i / (NT * 8), r = (i / 8) % NT, c = i % 8;
             const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + r) * a.K + (size_t)kc * GM_BK + 8 * c;
             cp_async16((pl ? xl(s) : xh(s)) + kint_off(r, 8 * c), src);
         }
         cp_async_commit();
-        gm_load_w(wv, a, n0 + wr, kc, wj);
-        // 32 halves per plane = 4 core-matrix rows of 16 bytes
-        __half hbuf[32], lbuf[32];
+    };
+    auto store_w = [&](int s) {  // dequantise the held weight words into stage s
+        __half hbuf[32], lbuf[32];  // 32 halves per plane = 4 core-matrix rows of 16 bytes
         gm_dequant(wv, wj, wscale, hbuf, lbuf);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             *reinterpret_cast<uint4*>(wh(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(hbuf)[c];
             *reinterpret_cast<uint4*>(wl(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(lbuf)[c];
         }
-        cp_async_wait_all();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
     };
 
+    // Software pipeline: the weight words of stage kc + 1 are loaded into registers while stage
+    // kc is prepared and multiplied, and the activations of stage kc + 1 are requested as soon
+    // as the MMAs of stage kc - 1 (the previous user of that buffer) have completed.
     bool ok = true;
     int last_kc = -1;  // the last stage whose MMAs were issued
+    if (nk > 0) {
+        load_x(0, kb);
+        gm_load_w(wv, a, n0 + wr, kb, wj);
+    }
     for (int kc = 0; kc < nk && ok; ++kc) {
         const int s = kc & 1;
-        if (kc >= 2) ok = mbar_wait(&done[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
-        if (!ok) break;
-        fill(s, kb + kc);
+        store_w(s);  // stage s is free: its previous MMAs (stage kc - 2) completed before load_x
+        if (kc + 1 < nk) gm_load_w(wv, a, n0 + wr, kb + kc + 1, wj);
+        cp_async_wait_all();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
         __syncthreads();
         last_kc = kc;
         if (tid == 0) {
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(s)), bl = smem_u32(xl(s));
 #pragma unroll
-            for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps = 2 chunks = 256 bytes
-                const uint32_t o = 256u * j;
-                umma_f16(tmem, umma_desc_k_interleave(ah + o), umma_desc_k_interleave(bh + o), idesc,
-                         (kc > 0 || j > 0) ? 1u : 0u);
-                umma_f16(tmem, umma_desc_k_interleave(ah + o), umma_desc_k_interleave(bl + o), idesc, 1u);
-                umma_f16(tmem, umma_desc_k_interleave(al + o), umma_desc_k_interleave(bh + o), idesc, 1u);
+            for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
+                const uint32_t o = 32u * j;
+                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc, (kc > 0 || j > 0) ? 1u : 0u);
+                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
+                umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
             }
             umma_commit(&done[s]);
+        }
+        if (kc + 1 < nk) {
+            // stage s ^ 1 was last read by the MMAs of stage kc - 1
+            if (kc >= 1) ok = mbar_wait(&done[s ^ 1], ((kc - 1) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            if (ok) load_x(s ^ 1, kb + kc + 1);
         }
     }
     // the last stage's commit covers every MMA issued before it

@@ -175,7 +175,7 @@ def run_batched(args, rank, world, local_rank, dist):
             "hbm_roofline": {"bytes_per_step_per_gpu": int(step_bytes),
                              "achieved_gbs": round(step_bytes / (ms_max / steps / 1e3) / 1e9, 1),
                              "frac_of_peak": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / peaks()[0], 4)},
-            "path": "tensor-core GEMM (f16-split mma.sync) at >= 16 rows per step, split flash-decode attention",
+            "path": "tcgen05 GEMM (f16-split, TMEM accumulator) at >= 16 rows per step, split flash-decode attention",
             "e2e": "every step copies S token ids in and S greedy ids out (host)"}
 
 
