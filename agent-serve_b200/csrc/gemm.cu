@@ -127,6 +127,88 @@ __device__ __forceinline__ void gm_load_w(uint32_t (&w)[9], const GemmArgs& a, i
     }
 }
 
+// byte offset of element (row, k) of a [rows][64] f16 operand tile in the swizzled layout
+__device__ __forceinline__ uint32_t kint_off(int row, int k) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+
+// offsets of the 8-half groups of one weight row's block in the swizzled layout
+struct KintRow {
+    int row, k0;
+    __device__ __forceinline__ uint32_t operator()(int c) const { return kint_off(row, k0 + 8 * c); }
+};
+
+// The same split with packed half2 arithmetic and no per-element conversion: q is made exact
+// in f16 from its byte (0x6400 | (q + 128) is 1024 + q + 128), Wh = q * dh rounds the exact
+// 19-bit product once (dh = d * 2^sw, an f16 value), and Wl = fma(q, dh, -Wh) is the exact
+// remainder (at most 8 significant bits).  Equal to gm_dequant_to's Wh, Wl.
+template <int J, class Off>
+__device__ __forceinline__ void gm_dequant_h2_t(const uint32_t (&w)[9], float wscale, uint8_t* dh, uint8_t* dl,
+                                                Off hoff) {
+    constexpr int j = J;  // compile-time, so the word indices below are static (registers)
+    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+    const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
+    const __half2 d2 = __halves2half2(dsc, dsc);
+    const __half2 k1152 = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
+    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words (even: pairs stay in one word)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const int b = b0 + 8 * c + e;
+            const uint32_t wd = w[b >> 2] ^ 0x80808080u;
+            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
+            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
+            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
+            const __half2 hi = __hmul2(q2, d2);
+            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
+            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
+            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
+        }
+        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
+template <class Off>
+__device__ __forceinline__ void gm_dequant_h2(const uint32_t (&w)[9], int j, float wscale, uint8_t* dh, uint8_t* dl,
+                                              Off hoff) {
+    if (j == 0) gm_dequant_h2_t<0>(w, wscale, dh, dl, hoff);
+    else gm_dequant_h2_t<1>(w, wscale, dh, dl, hoff);
+}
+
+// Dequantise one Q8_0 block (from the 9 words) into 32 f16 halves Wh, Wl; the 8-half group c
+// goes to dh + hoff(c) / dl + hoff(c) (bytes).
+template <class Off>
+__device__ __forceinline__ void gm_dequant_to(const uint32_t (&w)[9], int j, float wscale, uint8_t* dh, uint8_t* dl,
+                                              Off hoff) {
+    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+    const float d = __half2float(__ushort_as_half((unsigned short)dbits)) * wscale;  // exact
+    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {  // 8 elements per 16-byte store
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            float v2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int b = b0 + 8 * c + e + u;
+                const int q = (int)(int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
+                v2[u] = (float)q * d;  // exact: 8-bit integer times an 11-bit mantissa
+            }
+            const __half h0 = __float2half_rn(v2[0]), h1 = __float2half_rn(v2[1]);
+            const __half l0 = __float2half_rn(v2[0] - __half2float(h0));
+            const __half l1 = __float2half_rn(v2[1] - __half2float(h1));
+            hv[e >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lv[e >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
 // Dequantise one Q8_0 block (from the 9 words) into 32 f16 halves Wh, Wl at dh / dl.
 __device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float wscale, __half* dh, __half* dl) {
     const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
@@ -401,10 +483,6 @@ constexpr size_t gemm_tc_smem_bytes() {
     return (pipe > epi ? pipe : epi) + 64 + 1024;  // + mbarriers, the TMEM address, 1024-B alignment
 }
 
-// byte offset of element (row, k) of a [rows][64] f16 operand tile in the swizzled layout
-__device__ __forceinline__ uint32_t kint_off(int row, int k) {
-    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
-}
 
 template <int NT>
 __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
@@ -448,38 +526,45 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
     const int wr = tid >> 1, wj = tid & 1;
-    uint32_t wv[9];
-    auto load_x = [&](int s, int kc) {  // activations of stage kc: 16-byte cp.async chunks
-        for (int i = tid; i < 2 * NT * 8; i += GM_THREADS) {
-            const int pl = i / (NT * 8), r = (i / 8) % NT, c = i % 8;
-            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + r) * a.K + (size_t)kc * GM_BK + 8 * c;
-            cp_async16((pl ? xl(s) : xh(s)) + kint_off(r, 8 * c), src);
+    // activations of stage kc: 16-byte cp.async chunks.  Thread t copies chunk c = t % 8 of
+    // rows r = t / 8 + 32 i; r % 8 (its swizzle row) and c are fixed per thread, so source
+    // and destination advance by constant strides.
+    const int xc = tid & 7, xr0 = tid >> 3;
+    const uint32_t xdst0 = kint_off(xr0, 8 * xc);
+    auto load_x = [&](int s, int kc) {
+        static_assert(NT % 32 == 0, "rows per copy pass");
+#pragma unroll
+        for (int pl = 0; pl < 2; ++pl) {
+            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + xr0) * a.K + (size_t)kc * GM_BK + 8 * xc;
+            uint8_t* dst = (pl ? xl(s) : xh(s)) + xdst0;
+#pragma unroll 4
+            for (int i = 0; i < NT / 32; ++i) cp_async16(dst + 4096 * i, src + (size_t)32 * i * a.K);
         }
         cp_async_commit();
     };
-    auto store_w = [&](int s) {  // dequantise the held weight words into stage s
-        __half hbuf[32], lbuf[32];  // 32 halves per plane = 4 core-matrix rows of 16 bytes
-        gm_dequant(wv, wj, wscale, hbuf, lbuf);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-            *reinterpret_cast<uint4*>(wh(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(hbuf)[c];
-            *reinterpret_cast<uint4*>(wl(s) + kint_off(wr, 32 * wj + 8 * c)) = reinterpret_cast<const uint4*>(lbuf)[c];
-        }
-    };
 
-    // Software pipeline: the weight words of stage kc + 1 are loaded into registers while stage
-    // kc is prepared and multiplied, and the activations of stage kc + 1 are requested as soon
-    // as the MMAs of stage kc - 1 (the previous user of that buffer) have completed.
+    // Software pipeline: the weight words of the next GM_WPF stages are in flight in registers
+    // (a stage's 68-byte row pieces come from HBM, so one stage of lookahead leaves the loads
+    // latency-bound), and the activations of stage kc + 1 are requested as soon as the MMAs of
+    // stage kc - 1 (the previous user of that buffer) have completed.
+    constexpr int PF = GM_WPF;
+    uint32_t wbuf[PF][9];  // weight words of stages kc .. kc + PF - 1 (shifted down each stage)
     bool ok = true;
     int last_kc = -1;  // the last stage whose MMAs were issued
-    if (nk > 0) {
-        load_x(0, kb);
-        gm_load_w(wv, a, n0 + wr, kb, wj);
-    }
+    if (nk > 0) load_x(0, kb);
+#pragma unroll
+    for (int u = 0; u < PF; ++u)
+        if (u < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + u, wj);
     for (int kc = 0; kc < nk && ok; ++kc) {
         const int s = kc & 1;
-        store_w(s);  // stage s is free: its previous MMAs (stage kc - 2) completed before load_x
-        if (kc + 1 < nk) gm_load_w(wv, a, n0 + wr, kb + kc + 1, wj);
+        // dequantise the held weight words into stage s (free: its previous MMAs completed
+        // before load_x refilled it)
+        gm_dequant_h2(wbuf[0], wj, wscale, wh(s), wl(s), KintRow{wr, 32 * wj});
+#pragma unroll
+        for (int u = 0; u + 1 < PF; ++u)
+#pragma unroll
+            for (int i = 0; i < 9; ++i) wbuf[u][i] = wbuf[u + 1][i];
+        if (kc + PF < nk) gm_load_w(wbuf[PF - 1], a, n0 + wr, kb + kc + PF, wj);
         cp_async_wait_all();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
         __syncthreads();
@@ -490,7 +575,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
 #pragma unroll
             for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
                 const uint32_t o = 32u * j;
-                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc, (kc > 0 || j > 0) ? 1u : 0u);
+                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
+                         (kc > 0 || j > 0) ? 1u : 0u);
                 umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
                 umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
             }
