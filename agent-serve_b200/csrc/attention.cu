@@ -23,6 +23,55 @@ namespace tfb {
 // positions hit distinct banks) and the V tile of its <= AT_CHUNK positions, in fp32.
 static inline size_t attn_smem_bytes(int hd) { return (size_t)AT_CHUNK * (2 * hd + 1) * sizeof(float); }
 
+// The last CTA of (row m, kv head kvh) to finish combines the nsp split partials
+// (max, sum, weighted V) into the normalised output; the others return.  cw: [AT_MAX_REP]
+// [AT_MAX_SPLIT] and cden: [AT_MAX_REP] shared scratch; nth threads.
+__device__ __forceinline__ void attn_combine(const AttnArgs& a, int m, int kvh, int nsp, float* cwp, float* cden, int nth) {
+    __shared__ int last_s;
+    const int tid = threadIdx.x, hd = a.hd, n_rep = a.n_head / a.n_kv;
+    float (*cw)[AT_MAX_SPLIT] = reinterpret_cast<float (*)[AT_MAX_SPLIT]>(cwp);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned t = atomicAdd(&a.counters[(size_t)m * a.n_kv + kvh], 1u);
+        last_s = (t == (unsigned)nsp - 1);
+    }
+    __syncthreads();
+    if (!last_s) return;
+    __threadfence();
+    const float* pbase = a.part + ((size_t)m * a.n_head + (size_t)kvh * n_rep) * a.n_split * (hd + 2);
+    for (int i = tid; i < n_rep * nsp; i += nth) {
+        const int h = i / nsp, s = i % nsp;
+        cw[h][s] = __ldcg(pbase + ((size_t)h * a.n_split + s) * (hd + 2));
+    }
+    __syncthreads();
+    if (tid < n_rep) {
+        float M = -INFINITY;
+        for (int s = 0; s < nsp; ++s) M = fmaxf(M, cw[tid][s]);
+        float den = 0.f;
+        for (int s = 0; s < nsp; ++s) {
+            const float w = expf(cw[tid][s] - M);
+            den = fmaf(w, __ldcg(pbase + ((size_t)tid * a.n_split + s) * (hd + 2) + 1), den);
+            cw[tid][s] = w;
+        }
+        cden[tid] = den;
+    }
+    __syncthreads();
+    for (int i = tid; i < n_rep * hd; i += nth) {
+        const int h = i / hd, d = i % hd;
+        const float* pb = pbase + (size_t)h * a.n_split * (hd + 2) + 2 + d;
+        float num0 = 0.f, num1 = 0.f;
+        int s = 0;
+        for (; s + 1 < nsp; s += 2) {
+            num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
+            num1 = fmaf(cw[h][s + 1], __ldcg(pb + (size_t)(s + 1) * (hd + 2)), num1);
+        }
+        if (s < nsp) num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
+        a.out[(size_t)m * a.ld_out + (size_t)(kvh * n_rep + h) * hd + d] = (num0 + num1) / cden[h];
+    }
+    if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
+}
+
 __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
     extern __shared__ float tile[];
     __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
@@ -31,7 +80,6 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP];
     __shared__ float cw[AT_MAX_REP][AT_MAX_SPLIT];
     __shared__ float cden[AT_MAX_REP];
-    __shared__ int last_s;
     __shared__ __align__(8) uint64_t kvbar;
 
     pdl_trigger();
@@ -180,47 +228,186 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
     }
     if (nsp == 1) return;
 
-    // 6) the last CTA of (row, kv head) combines the active splits
-    __threadfence();
-    __syncthreads();
+    attn_combine(a, m, kvh, nsp, &cw[0][0], cden, AT_THREADS);
+}
+
+// ---- streaming decode attention (fp32 caches, many rows) -------------------------------------
+// One CTA per (row, kv head, position split) walks its positions in tiles of AS_TILE: the K and
+// V rows of tile t + 1 arrive by 1-D bulk copies (TMA) while tile t is scored, with an online
+// softmax (running max, sum and weighted V in registers), so a split streams its whole range
+// instead of one 64-position chunk per CTA.  Splits only where rows x kv heads alone do not
+// fill the GPU; their partials are combined as in attn_decode_kernel.  Same semantics as
+// attn_decode_kernel (fresh modes, windows, the new position taken from shared memory).
+constexpr int AS_THREADS = 256;
+constexpr int AS_TILE = 32;
+
+static inline size_t attn_stream_smem_bytes(int hd) { return (size_t)2 * 2 * AS_TILE * hd * sizeof(float); }
+
+__global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float kvt[];  // [2 buffers][K | V][AS_TILE][hd]
+    __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
+    __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
+    __shared__ float sc[AT_MAX_REP][AS_TILE];
+    __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP], al_s[AT_MAX_REP];
+    __shared__ __align__(8) uint64_t full[2];
+
+    pdl_trigger();
+    pdl_wait();
+    const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
+    const int slot = a.slots ? a.slots[m] : 0;
+    const int pos = a.fresh == 2 ? a.pos[slot] + m : (a.fresh ? a.pos[slot] : a.n_pos_fixed - 1);
+    if (a.fresh && (pos < 0 || pos >= a.cap)) {
+        if (tid == 0 && split == 0) atomicCAS(a.err, 0, ERR_POS);
+        return;
+    }
+    const int n_pos = pos + 1;
+    const int ws = (a.fresh && a.wstart) ? min(max(a.wstart[slot], 0), pos) : 0;
+    const int n_att = n_pos - ws;
+    const int nsp = min((int)gridDim.y, (n_att + 4 * AS_TILE - 1) / (4 * AS_TILE));  // >= 4 tiles a split
+    if (split >= nsp) return;
+    const int span = (n_att + nsp - 1) / nsp;
+    const int p0 = ws + split * span, p1 = min(n_pos, p0 + span);
+    const int n_tiles = (p1 - p0 + AS_TILE - 1) / AS_TILE;
+    const float* row = a.qkv + (size_t)m * a.ld_qkv;
+    const size_t cache_off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd;
+    const float* kc = static_cast<const float*>(a.kc) + cache_off;
+    const float* vc = static_cast<const float*>(a.vc) + cache_off;
+    const bool fresh_last = a.fresh == 1 && p1 == n_pos;  // this split holds the new position
+
+    auto issue = [&](int t) {  // tile t into buffer t & 1 (thread 0)
+        const int b = t & 1, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
+        const int qc = (fresh_last && q0 + qn == n_pos) ? qn - 1 : qn;  // cached rows of the tile
+        const uint32_t bytes = (uint32_t)qc * hd * 4;
+        mbar_expect_tx(&full[b], 2 * bytes);
+        if (bytes) {
+            bulk_g2s(kvt + (size_t)(2 * b) * AS_TILE * hd, kc + (size_t)q0 * hd, bytes, &full[b]);
+            bulk_g2s(kvt + (size_t)(2 * b + 1) * AS_TILE * hd, vc + (size_t)q0 * hd, bytes, &full[b]);
+        }
+    };
     if (tid == 0) {
-        const unsigned t = atomicAdd(&a.counters[(size_t)m * a.n_kv + kvh], 1u);
-        last_s = (t == (unsigned)nsp - 1);
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        mbar_fence_init();
+        issue(0);
+        if (n_tiles > 1) issue(1);
     }
-    __syncthreads();
-    if (!last_s) return;
-    __threadfence();
-    const float* pbase = a.part + ((size_t)m * a.n_head + (size_t)kvh * n_rep) * a.n_split * (hd + 2);
-    for (int i = tid; i < n_rep * nsp; i += AT_THREADS) {
-        const int h = i / nsp, s = i % nsp;
-        cw[h][s] = __ldcg(pbase + ((size_t)h * a.n_split + s) * (hd + 2));
-    }
-    __syncthreads();
-    if (tid < n_rep) {
-        float M = -INFINITY;
-        for (int s = 0; s < nsp; ++s) M = fmaxf(M, cw[tid][s]);
-        float den = 0.f;
-        for (int s = 0; s < nsp; ++s) {
-            const float w = expf(cw[tid][s] - M);
-            den = fmaf(w, __ldcg(pbase + ((size_t)tid * a.n_split + s) * (hd + 2) + 1), den);
-            cw[tid][s] = w;
+    // query heads of the group (and the new k/v), rotated for a decode step
+    for (int i = tid; i < n_rep * hd; i += AS_THREADS) qs[i / hd][i % hd] = row[(size_t)kvh * n_rep * hd + i];
+    if (a.fresh == 1)
+        for (int i = tid; i < hd; i += AS_THREADS) {
+            kn[i] = row[(size_t)a.n_head * hd + (size_t)kvh * hd + i];
+            vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
         }
-        cden[tid] = den;
+    if (tid < AT_MAX_REP) {
+        mx_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
     }
     __syncthreads();
-    for (int i = tid; i < n_rep * hd; i += AT_THREADS) {
-        const int h = i / hd, d = i % hd;
-        const float* pb = pbase + (size_t)h * a.n_split * (hd + 2) + 2 + d;
-        float num0 = 0.f, num1 = 0.f;
-        int s = 0;
-        for (; s + 1 < nsp; s += 2) {
-            num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
-            num1 = fmaf(cw[h][s + 1], __ldcg(pb + (size_t)(s + 1) * (hd + 2)), num1);
+    if (a.fresh == 1) {
+        const float* cp = a.cosb + (size_t)pos * d2;
+        const float* sp = a.sinb + (size_t)pos * d2;
+        for (int i = tid; i < (n_rep + 1) * d2; i += AS_THREADS) {
+            const int h = i / d2, j = i % d2;
+            if (h < n_rep) rope_pair(qs[h][j], qs[h][j + d2], cp[j], sp[j]);
+            else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
         }
-        if (s < nsp) num0 = fmaf(cw[h][s], __ldcg(pb + (size_t)s * (hd + 2)), num0);
-        a.out[(size_t)m * a.ld_out + (size_t)(kvh * n_rep + h) * hd + d] = (num0 + num1) / cden[h];
+        __syncthreads();
+        if (split == 0)
+            for (int i = tid; i < hd; i += AS_THREADS) {
+                kv_store(a.kc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, kn[i]);
+                kv_store(a.vc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, vn[i]);
+            }
     }
-    if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
+    const float scale = 1.0f / sqrtf((float)hd);
+    constexpr int PER = (AT_MAX_REP * AT_MAX_HD + AS_THREADS - 1) / AS_THREADS;
+    float acc[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+    bool ok = true;
+    for (int t = 0; t < n_tiles; ++t) {
+        const int b = t & 1, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
+        float* ks = kvt + (size_t)(2 * b) * AS_TILE * hd;
+        float* vs = kvt + (size_t)(2 * b + 1) * AS_TILE * hd;
+        if (!mbar_wait(&full[b], (t >> 1) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
+        if (fresh_last && q0 + qn == n_pos)
+            for (int i = tid; i < hd; i += AS_THREADS) {
+                ks[(size_t)(qn - 1) * hd + i] = kn[i];  // fp32 cache: stored exactly
+                vs[(size_t)(qn - 1) * hd + i] = vn[i];
+            }
+        __syncthreads();
+        // scores (attn_decode, src/attention.cpp:63-64): thread per (head, position), a walk
+        // over the dims rotated by the position so one warp's rows meet distinct banks
+        for (int i = tid; i < n_rep * qn; i += AS_THREADS) {
+            const int h = i / qn, p = i % qn;
+            const float* kp = ks + (size_t)p * hd;
+            const int rot = p % hd;
+            float s0 = 0.f, s1 = 0.f;
+            for (int d = 0; d < hd; d += 2) {
+                int e0 = d + rot, e1 = d + 1 + rot;
+                e0 -= e0 >= hd ? hd : 0;
+                e1 -= e1 >= hd ? hd : 0;
+                s0 = fmaf(qs[h][e0], kp[e0], s0);
+                s1 = fmaf(qs[h][e1], kp[e1], s1);
+            }
+            sc[h][p] = scale * (s0 + s1);
+        }
+        __syncthreads();
+        for (int h = warp; h < n_rep; h += AS_THREADS / 32) {  // running max and sum
+            float tm = lane < qn ? sc[h][lane] : -INFINITY;
+            tm = warp_max(tm);
+            const float mnew = fmaxf(mx_s[h], tm);
+            const float e = lane < qn ? expf(sc[h][lane] - mnew) : 0.f;
+            if (lane < qn) sc[h][lane] = e;
+            const float lt = warp_sum(e);
+            if (lane == 0) {
+                const float alpha = expf(mx_s[h] - mnew);  // 0 on the first tile
+                al_s[h] = alpha;
+                l_s[h] = fmaf(l_s[h], alpha, lt);
+                mx_s[h] = mnew;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < PER; ++k) {  // weighted V: thread per (head, dim)
+            const int i = tid + k * AS_THREADS;
+            if (i < n_rep * hd) {
+                const int h = i / hd, d = i % hd;
+                float a0 = acc[k] * al_s[h], a1 = 0.f;
+                int p = 0;
+                for (; p + 1 < qn; p += 2) {
+                    a0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], a0);
+                    a1 = fmaf(sc[h][p + 1], vs[(size_t)(p + 1) * hd + d], a1);
+                }
+                if (p < qn) a0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], a0);
+                acc[k] = a0 + a1;
+            }
+        }
+        __syncthreads();  // buffer b is free again
+        if (tid == 0 && t + 2 < n_tiles) issue(t + 2);
+    }
+    if (!ok) return;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+        const int i = tid + k * AS_THREADS;
+        if (i < n_rep * hd) {
+            const int h = i / hd, d = i % hd;
+            const int head = kvh * n_rep + h;
+            if (nsp == 1) {
+                a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = acc[k] / l_s[h];
+            } else {
+                float* pp = a.part + (((size_t)m * a.n_head + head) * a.n_split + split) * (hd + 2);
+                pp[2 + d] = acc[k];
+                if (d == 0) {
+                    pp[0] = mx_s[h];
+                    pp[1] = l_s[h];
+                }
+            }
+        }
+    }
+    // the combine's scratch reuses the tile buffers (no copies are in flight any more)
+    if (nsp > 1) attn_combine(a, m, kvh, nsp, kvt, kvt + AT_MAX_REP * AT_MAX_SPLIT, AS_THREADS);
 }
 
 // ---- prefill attention (attn_prefill): one CTA per (query row i, head h) -----------------
@@ -323,8 +510,41 @@ int attn_pick_split(int cap) {
     return s < 1 ? 1 : (s > AT_MAX_SPLIT ? AT_MAX_SPLIT : s);
 }
 
+// rows x kv heads that fill the GPU without position splits for the streaming kernel
+static int attn_stream_splits(const AttnArgs& a, int M) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int pairs = M * a.n_kv;
+    int s = (2 * sms + pairs - 1) / pairs;
+    return s < 1 ? 1 : (s > a.n_split ? a.n_split : s);
+}
+
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
     if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
+    if (a.kv_type == KV_F32 && M * a.n_kv >= 16) {  // many rows: streaming kernel
+        static bool sattr[64] = {false};
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (dev < 0 || dev >= 64) dev = 0;
+        if (!sattr[dev]) {
+            cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)attn_stream_smem_bytes(AT_MAX_HD));
+            if (e != cudaSuccess) return e;
+            sattr[dev] = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(a.n_kv, attn_stream_splits(a, M), M);
+        cfg.blockDim = dim3(AS_THREADS);
+        cfg.dynamicSmemBytes = attn_stream_smem_bytes(a.hd);
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, attn_stream_kernel, a);
+    }
     const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;
     if ((max_pos + a.n_split - 1) / a.n_split > AT_CHUNK || a.n_split > AT_MAX_SPLIT) return cudaErrorInvalidValue;
     const size_t smem = attn_smem_bytes(a.hd);
