@@ -36,23 +36,27 @@ __device__ __forceinline__ void named_bar_compute() {
 // GEMV CTA has stored its rows, rotates, stores the new k/v and attends over [ws, pos] in
 // tiles of `tp` positions with an online softmax (one tile up to ~150 positions at hd 64).
 // Per tile the arithmetic is that of attn_decode_kernel for one split.
-__device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int kvh, int G) {
+__device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int cta, int G) {
     const AttnArgs& t = a.at;
     const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
     const int hd = t.hd, d2 = hd / 2, n_rep = t.n_head / t.n_kv;
+    // this CTA: kv head kvh, query heads [h0, h0 + nh) of its group (the first CTA of a kv
+    // head also stores the new key / value)
+    const int nh = a.attn_hpc, nsub = n_rep / nh;
+    const int kvh = cta / nsub, h0 = (cta % nsub) * nh;
     float* f = reinterpret_cast<float*>(smem);
-    float* qs = f;                                  // [n_rep][hd]
-    float* kn = qs + n_rep * hd;                    // [hd]
+    float* qs = f;                                  // [nh][hd]
+    float* kn = qs + nh * hd;                       // [hd]
     float* vn = kn + hd;                            // [hd]
-    float* mx = vn + hd;                            // [n_rep]
-    float* ls = mx + n_rep;                         // [n_rep]
-    float* al = ls + n_rep;                         // [n_rep]
-    int* flag = reinterpret_cast<int*>(al + n_rep); // [1]
-    float* sc = al + n_rep + 4;                     // [n_rep][tp]
-    const int fixed = n_rep * hd + 2 * hd + 3 * n_rep + 4;
-    int tp = (int)((avail / 4 - fixed) / (n_rep + 2 * hd + 1));
+    float* mx = vn + hd;                            // [nh]
+    float* ls = mx + nh;                            // [nh]
+    float* al = ls + nh;                            // [nh]
+    int* flag = reinterpret_cast<int*>(al + nh);    // [1]
+    float* sc = al + nh + 4;                        // [nh][tp]
+    const int fixed = nh * hd + 2 * hd + 3 * nh + 4;
+    int tp = (int)((avail / 4 - fixed) / (nh + 2 * hd + 1));
     tp = tp > 256 ? 256 : tp;
-    float* ks = sc + n_rep * tp;                    // [tp][hd + 1]
+    float* ks = sc + nh * tp;                       // [tp][hd + 1]
     float* vs = ks + (size_t)tp * (hd + 1);         // [tp][hd]
 
     pdl_trigger();
@@ -90,28 +94,29 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     __syncthreads();
     if (*flag) {
         const float* row = t.qkv;
-        for (int i = tid; i < n_rep * hd; i += nth) qs[i] = __ldcg(row + (size_t)kvh * n_rep * hd + i);
+        for (int i = tid; i < nh * hd; i += nth) qs[i] = __ldcg(row + (size_t)(kvh * n_rep + h0) * hd + i);
         for (int i = tid; i < hd; i += nth) {
             kn[i] = __ldcg(row + (size_t)t.n_head * hd + (size_t)kvh * hd + i);
             vn[i] = __ldcg(row + (size_t)(t.n_head + t.n_kv) * hd + (size_t)kvh * hd + i);
         }
-        if (tid < n_rep) {
+        if (tid < nh) {
             mx[tid] = -INFINITY;
             ls[tid] = 0.f;
         }
         __syncthreads();
         const float* cp = t.cosb + (size_t)pos * d2;
         const float* sp = t.sinb + (size_t)pos * d2;
-        for (int i = tid; i < (n_rep + 1) * d2; i += nth) {
+        for (int i = tid; i < (nh + 1) * d2; i += nth) {
             const int h = i / d2, j = i % d2;
-            if (h < n_rep) rope_pair(qs[h * hd + j], qs[h * hd + j + d2], cp[j], sp[j]);
+            if (h < nh) rope_pair(qs[h * hd + j], qs[h * hd + j + d2], cp[j], sp[j]);
             else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
         }
         __syncthreads();
-        for (int i = tid; i < hd; i += nth) {
-            kv_store(t.kc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, kn[i]);
-            kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
-        }
+        if (h0 == 0)
+            for (int i = tid; i < hd; i += nth) {
+                kv_store(t.kc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, kn[i]);
+                kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
+            }
         const float scale = 1.0f / sqrtf((float)hd);
         constexpr int PER = (AT_MAX_REP * AT_MAX_HD + GV_THREADS - 1) / GV_THREADS;
         float acc[PER];
@@ -133,7 +138,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
                     vs[(size_t)(np - 1) * hd + i] = kv_round(vn[i], t.kv_type);
                 }
             __syncthreads();
-            for (int i = tid; i < n_rep * np; i += nth) {
+            for (int i = tid; i < nh * np; i += nth) {
                 const int h = i / np, p = i % np;
                 const float* kp = ks + (size_t)p * (hd + 1);
                 const float* qh = qs + h * hd;
@@ -145,7 +150,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
                 sc[h * tp + p] = scale * (s0 + s1);
             }
             __syncthreads();
-            for (int h = warp; h < n_rep; h += nw) {
+            for (int h = warp; h < nh; h += nw) {
                 float tm = -INFINITY;
                 for (int i = lane; i < np; i += 32) tm = fmaxf(tm, sc[h * tp + i]);
                 tm = warp_max(tm);
@@ -168,7 +173,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
 #pragma unroll
             for (int k = 0; k < PER; ++k) {
                 const int i = tid + k * nth;
-                if (i < n_rep * hd) {
+                if (i < nh * hd) {
                     const int h = i / hd, d = i % hd;
                     const float* sh = sc + h * tp;
                     float a0 = acc[k] * al[h], a1 = 0.f;
@@ -186,9 +191,9 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
 #pragma unroll
         for (int k = 0; k < PER; ++k) {
             const int i = tid + k * nth;
-            if (i < n_rep * hd) {
+            if (i < nh * hd) {
                 const int h = i / hd, d = i % hd;
-                t.out[(size_t)(kvh * n_rep + h) * hd + d] = acc[k] / ls[h];
+                t.out[(size_t)(kvh * n_rep + h0 + h) * hd + d] = acc[k] / ls[h];
             }
         }
     }

@@ -76,6 +76,7 @@ struct GemvArgs {
     // the q/k/v rows through sync[0] (GEMV CTAs arrive when their rows are stored) and
     // leave through sync[1] (the last one out clears both)
     int attn_ctas;
+    int attn_hpc;        // query heads per attention CTA (divides n_head / n_kv)
     unsigned* sync;
     AttnArgs at;
 };

@@ -390,7 +390,10 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             int grid = gemv_grid(a, m->num_sms);
             if (fuse) {
                 // the attention CTAs take slots of the GEMV grid so that all stay resident
-                a.attn_ctas = m->hp.n_kv_head;
+                // one attention CTA per query head: the tail after the GEMV is then the
+                // latency of one head's scores / softmax / weighted V
+                a.attn_hpc = 1;
+                a.attn_ctas = m->hp.n_head;
                 a.sync = m->d_async + 2 * li;
                 a.at = attn_args(m, li);
                 grid = std::max(1, std::min(grid, gemv_slots(m->num_sms) - a.attn_ctas));
