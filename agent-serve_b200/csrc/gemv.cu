@@ -24,6 +24,9 @@
 
 namespace tfb {
 
+// floats of the cross-warp reduction buffer: two parities x warps x (2 rows x max(M, 2))
+__host__ __device__ constexpr int gv_red_floats(int maxm) { return 2 * GV_WARPS * 2 * (maxm < 2 ? 2 : maxm); }
+
 __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
@@ -216,8 +219,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     const int xbytes = ((a.M * xl * 4) + 127) & ~127;
     float* xs = reinterpret_cast<float*>(smem);
     uint8_t* stages = smem + xbytes;
-    float* red = reinterpret_cast<float*>(stages + (size_t)GV_STAGES * a.stage_bytes);  // [2][W][2][MAXM]
-    double* redd = reinterpret_cast<double*>(red + 2 * GV_WARPS * 2 * MAXM);              // [W][MAXM]
+    float* red = reinterpret_cast<float*>(stages + (size_t)GV_STAGES * a.stage_bytes);  // [2][W][2][max(MAXM, 2)]
+    double* redd = reinterpret_cast<double*>(red + gv_red_floats(MAXM));                   // [W][MAXM]
     float* pre = reinterpret_cast<float*>(redd + GV_WARPS * MAXM);                        // [MAXM][GV_PRE]
     uint64_t* full = reinterpret_cast<uint64_t*>(pre + MAXM * GV_PRE);
     uint64_t* empty = full + GV_STAGES;
@@ -473,7 +476,86 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
 #pragma unroll
     for (int m = 0; m < MAXM; ++m) best[m] = 0ull;
 
-    for (int s = 0; s < n_stages; ++s) {
+    if constexpr (INTQ) {
+        // Two stages per iteration: each warp dots its item of stage s and of stage s + 1 (two
+        // independent dp4a chains), one shuffle tree reduces both, KS > 1 partials meet after
+        // one named barrier, and the two items' epilogues run in parallel in two lanes.
+        const int P = a.P, KS = a.KS;
+        const int lane_off = (my_item * P + prow) * (int)a.rb + (my_ks * U + (pact ? pu : 0)) * 68;
+        const bool lane_ok = pact && prow < P;
+        // after the reduction: lanes [0, 16) hold item 0 and [16, 32) item 1 (P == 1); for
+        // P == 2 lanes [0, 8) / [8, 16) the first row (gate) of items 0 / 1, [16, 24) / [24, 32)
+        // the second row (up)
+        const int rsel = P == 1 ? (lane >> 4) & 1 : (lane >> 3) & 1;
+        const bool leader = (lane & (P == 1 ? 15 : 7)) == 0;
+        const bool first_row = P == 1 || lane < 16;
+        const long long step_bytes = (long long)RI * P * a.rb;
+        for (int s = 0, it = 0; s < n_stages; s += 2, ++it) {
+            const bool two = s + 1 < n_stages;
+            const int slot0 = s % GV_STAGES, slot1 = (s + 1) % GV_STAGES;
+            bool ok = mbar_wait(&full[slot0], (s / GV_STAGES) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            if (two && ok) ok = mbar_wait(&full[slot1], ((s + 1) / GV_STAGES) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            const int item0 = i0 + s * RI + my_item, item1 = item0 + RI;
+            const uintptr_t g0 = reinterpret_cast<uintptr_t>(a.W) + (uintptr_t)((long long)s * step_bytes +
+                                                                               (long long)i0 * P * a.rb);
+            const uintptr_t g1 = g0 + (uintptr_t)step_bytes;
+            // both dots run unconditionally (a stale or partly filled slot is still inside the
+            // stage buffer); invalid results are selected away, never multiplied
+            const float d0 = unit_dot_q8_int(
+                reinterpret_cast<const uint32_t*>(stages + (size_t)slot0 * a.stage_bytes + (g0 & 15) + lane_off), pl,
+                invA, invB);
+            const float d1 = unit_dot_q8_int(
+                reinterpret_cast<const uint32_t*>(stages + (size_t)slot1 * a.stage_bytes + (g1 & 15) + lane_off), pl,
+                invA, invB);
+            const bool ok0 = ok && item0 < i1, ok1 = ok && two && item1 < i1;
+            const float v0 = (ok0 && lane_ok) ? d0 : 0.f;
+            const float v1 = (ok1 && lane_ok) ? d1 : 0.f;
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[slot0]);
+                if (two) mbar_arrive(&empty[slot1]);
+            }
+            const int hx = P == 1 ? 16 : 8;
+            const bool hi = (lane & hx) != 0;
+            float keep = hi ? v1 : v0;
+            keep += __shfl_xor_sync(0xffffffffu, hi ? v0 : v1, hx);
+            if (P == 1) keep += __shfl_xor_sync(0xffffffffu, keep, 8);
+            keep += __shfl_xor_sync(0xffffffffu, keep, 4);
+            keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+            keep += __shfl_xor_sync(0xffffffffu, keep, 1);
+            bool mine = true;
+            if (KS > 1) {
+                float* rb = red + ((it & 1) * GV_WARPS + warp) * 4;
+                if (leader) rb[rsel * 2 + (first_row ? 0 : 1)] = keep;
+                named_bar_compute();
+                mine = my_ks == 0;
+                if (mine && leader) {
+                    float v = 0.f;
+                    for (int k = 0; k < KS; ++k) v += red[((it & 1) * GV_WARPS + warp + k) * 4 + rsel * 2 + (first_row ? 0 : 1)];
+                    keep = v;
+                }
+            }
+            const float other = __shfl_xor_sync(0xffffffffu, keep, 16);  // P == 2: the up row's sum
+            const bool okr = rsel ? ok1 : ok0;
+            if (mine && leader && first_row && okr) {
+                const int row = rsel ? item1 : item0;
+                if (a.epi == EPI_STORE) {
+                    const float b = a.bias ? (prefetched ? pre[row - i0] : a.bias[row]) : 0.f;
+                    a.y[row] = keep + b;
+                } else if (a.epi == EPI_RESID) {
+                    const float r = prefetched ? pre[row - i0] : a.resid[row];
+                    a.resid[row] = r + keep;
+                } else if (a.epi == EPI_SWIGLU) {
+                    a.y[row] = __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other);
+                } else {  // EPI_ARGMAX
+                    a.y[row] = keep;
+                    const unsigned long long k = argmax_key(keep, (uint32_t)row);
+                    best[0] = k > best[0] ? k : best[0];
+                }
+            }
+        }
+    }
+    for (int s = 0; s < n_stages && !INTQ; ++s) {
         const int slot = s % GV_STAGES;
         const bool ok = mbar_wait(&full[slot], (s / GV_STAGES) & 1, a.err, ERR_WAIT_FULL, abort_flag);
         const int si0 = i0 + s * RI, si1 = min(si0 + RI, i1);
@@ -485,25 +567,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const uintptr_t g = reinterpret_cast<uintptr_t>(a.W + (long long)si0 * a.P * a.rb);
             const uint8_t* sb = stages + (size_t)slot * a.stage_bytes + (g & 15);
             const uint8_t* ib = sb + (long long)my_item * a.P * a.rb;
-            if constexpr (INTQ) {
-                {
-                    float v = 0.f;
-                    if (pact && prow < a.P)
-                        v = unit_dot_q8_int(
-                            reinterpret_cast<const uint32_t*>(ib + (long long)prow * a.rb + (size_t)(my_ks * U + pu) * 68),
-                            pl, invA, invB);
-                    v += __shfl_xor_sync(0xffffffffu, v, 8);
-                    v += __shfl_xor_sync(0xffffffffu, v, 4);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    if (a.P == 1) v += __shfl_xor_sync(0xffffffffu, v, 16);
-                    acc0[0] = __shfl_sync(0xffffffffu, v, 0);
-                    acc1[0] = __shfl_sync(0xffffffffu, v, 16);
-                }
-            }
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                if (p < a.P && !use_int) {
+                if (p < a.P) {
                     const uint8_t* rowp = ib + (long long)p * a.rb;
                     float part[MAXM];
 #pragma unroll
@@ -576,7 +642,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         }
     }
 
-    if (a.epi == EPI_ARGMAX && lane == 0)
+    if (a.epi == EPI_ARGMAX)  // the lanes that ran argmax epilogues
         for (int m = 0; m < a.M; ++m)
             if (best[m]) atomicMax(&ckey[m], best[m]);
     // with fused attention the attention CTAs read this CTA's rows: publish them
@@ -613,7 +679,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
 
 size_t gemv_smem_bytes(int M, int K, int stage_bytes, int maxm) {
     const size_t xbytes = ((size_t)M * xpad_len(K) * 4 + 127) & ~(size_t)127;
-    return xbytes + (size_t)GV_STAGES * stage_bytes + 2 * GV_WARPS * 2 * maxm * 4 + GV_WARPS * maxm * 8 +
+    return xbytes + (size_t)GV_STAGES * stage_bytes + (size_t)gv_red_floats(maxm) * 4 + GV_WARPS * maxm * 8 +
            (size_t)maxm * GV_PRE * 4 + 2 * GV_STAGES * 8 + 8 + maxm * 8;
 }
 
