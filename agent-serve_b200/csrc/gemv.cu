@@ -31,50 +31,57 @@ __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
 
-// ---- fused decode attention (one kv head per CTA, appended to the QKV GEMV grid) ----------
-// Model::layer_decode's apply_rope on q and k, KVCache::store and attn_decode for kv head
-// kvh (src/model.cpp:125-129, src/attention.cpp:31-80), M == 1.  The cached K/V rows are
-// loaded into shared memory before the q/k/v of this step exist (they do not depend on
-// them), so the load overlaps the GEMV CTAs' work; then the CTA waits (bounded) until every
-// GEMV CTA has stored its rows, rotates, stores the new k/v and attends over [ws, pos] in
-// tiles of `tp` positions with an online softmax (one tile up to ~150 positions at hd 64).
-// Per tile the arithmetic is that of attn_decode_kernel for one split.
+// ---- fused decode attention (one query head per CTA, appended to the QKV GEMV grid) -------
+// Model::layer_decode's apply_rope on q and k, KVCache::store and attn_decode for query head
+// `cta` (src/model.cpp:125-129, src/attention.cpp:31-80), M == 1.  The cached K/V rows and the
+// position's cos/sin are loaded into shared memory before the q/k/v of this step exist (they
+// do not depend on them), so the loads overlap the GEMV CTAs' work; then the CTA waits
+// (bounded) until every GEMV CTA has stored its rows, rotates, stores the new k/v (the first
+// query head of each kv group) and attends over [ws, pos] in tiles of `tp` positions with an
+// online softmax.  Every phase uses the whole CTA: one position per thread for the scores
+// (float4 reads of q and of K rows padded to hd + 4 floats), CTA-wide max / sum, and ng
+// groups of hd threads for the weighted V sum (group g takes positions g, g + ng, ...).
 __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int cta, int G) {
     const AttnArgs& t = a.at;
     const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
     const int hd = t.hd, d2 = hd / 2, n_rep = t.n_head / t.n_kv;
-    // this CTA: kv head kvh, query heads [h0, h0 + nh) of its group (the first CTA of a kv
-    // head also stores the new key / value)
-    const int nh = a.attn_hpc, nsub = n_rep / nh;
-    const int kvh = cta / nsub, h0 = (cta % nsub) * nh;
+    const int qh = cta, kvh = cta / n_rep;
+    const bool storer = cta % n_rep == 0;
+    const int kst = hd + 4;
+    const int ng = min(8, nth / hd);
     float* f = reinterpret_cast<float*>(smem);
-    float* qs = f;                                  // [nh][hd]
-    float* kn = qs + nh * hd;                       // [hd]
-    float* vn = kn + hd;                            // [hd]
-    float* mx = vn + hd;                            // [nh]
-    float* ls = mx + nh;                            // [nh]
-    float* al = ls + nh;                            // [nh]
-    int* flag = reinterpret_cast<int*>(al + nh);    // [1]
-    float* sc = al + nh + 4;                        // [nh][tp]
-    const int fixed = nh * hd + 2 * hd + 3 * nh + 4;
-    int tp = (int)((avail / 4 - fixed) / (nh + 2 * hd + 1));
-    tp = tp > 256 ? 256 : tp;
-    float* ks = sc + nh * tp;                       // [tp][hd + 1]
-    float* vs = ks + (size_t)tp * (hd + 1);         // [tp][hd]
+    float* qs = f;                   // [hd]
+    float* kn = qs + hd;             // [hd]
+    float* vn = kn + hd;             // [hd]
+    float* cs = vn + hd;             // [d2] cos / sin of pos
+    float* sn = cs + d2;             // [d2]
+    float* red = sn + d2;            // [2][32] per-warp maxima / sums
+    int* flag = reinterpret_cast<int*>(red + 64);
+    float* pacc = red + 68;          // [ng][hd]
+    float* sc = pacc + ng * hd;      // [tp] exp(score - max)
+    const int fixed = 4 * hd + 68 + ng * hd;
+    int tp = (int)((avail / 4 - fixed) / (1 + kst + hd));
+    tp = (tp > 256 ? 256 : tp) & ~3;  // <= one position per thread; keeps ks 16-byte aligned
+    float* ks = sc + tp;             // [tp][kst]
+    float* vs = ks + (size_t)tp * kst;  // [tp][hd]
 
     pdl_trigger();
     pdl_wait();
     const int slot = t.slots ? t.slots[0] : 0;
     const int pos = t.pos[slot];
-    const bool pos_ok = pos >= 0 && pos < t.cap && tp >= 1;
+    const bool pos_ok = pos >= 0 && pos < t.cap && tp >= 4;
     const int ws = pos_ok ? ((t.wstart) ? min(max(t.wstart[slot], 0), pos) : 0) : 0;
     const size_t cache_off = (size_t)slot * t.slot_stride + (size_t)kvh * t.cap * hd;
-    // the first tile's cached rows, before q/k/v are ready
+    // the first tile's cached rows and the rotation of pos, before q/k/v are ready
     if (pos_ok) {
         const int np = min(pos + 1, ws + tp) - ws;
         const int npc = (ws + np == pos + 1) ? np - 1 : np;
-        load_tile(ks, hd + 1, hd, t.kc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
+        load_tile(ks, kst, hd, t.kc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
         load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
+        for (int i = tid; i < d2; i += nth) {
+            cs[i] = t.cosb[(size_t)pos * d2 + i];
+            sn[i] = t.sinb[(size_t)pos * d2 + i];
+        }
     }
     if (tid == 0) {
         int ok = 1;
@@ -97,107 +104,95 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     __syncthreads();
     if (*flag) {
         const float* row = t.qkv;
-        for (int i = tid; i < nh * hd; i += nth) qs[i] = __ldcg(row + (size_t)(kvh * n_rep + h0) * hd + i);
         for (int i = tid; i < hd; i += nth) {
+            qs[i] = __ldcg(row + (size_t)qh * hd + i);
             kn[i] = __ldcg(row + (size_t)t.n_head * hd + (size_t)kvh * hd + i);
             vn[i] = __ldcg(row + (size_t)(t.n_head + t.n_kv) * hd + (size_t)kvh * hd + i);
         }
-        if (tid < nh) {
-            mx[tid] = -INFINITY;
-            ls[tid] = 0.f;
+        __syncthreads();
+        for (int i = tid; i < hd; i += nth) {
+            const int j = i % d2;
+            if (i < d2) rope_pair(qs[j], qs[j + d2], cs[j], sn[j]);
+            else rope_pair(kn[j], kn[j + d2], cs[j], sn[j]);
         }
         __syncthreads();
-        const float* cp = t.cosb + (size_t)pos * d2;
-        const float* sp = t.sinb + (size_t)pos * d2;
-        for (int i = tid; i < (nh + 1) * d2; i += nth) {
-            const int h = i / d2, j = i % d2;
-            if (h < nh) rope_pair(qs[h * hd + j], qs[h * hd + j + d2], cp[j], sp[j]);
-            else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
-        }
-        __syncthreads();
-        if (h0 == 0)
+        if (storer)
             for (int i = tid; i < hd; i += nth) {
                 kv_store(t.kc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, kn[i]);
                 kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
             }
         const float scale = 1.0f / sqrtf((float)hd);
-        constexpr int PER = (AT_MAX_REP * AT_MAX_HD + GV_THREADS - 1) / GV_THREADS;
-        float acc[PER];
-#pragma unroll
-        for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+        const bool pv_thread = tid < ng * hd;
+        const int pg = tid / hd, pd = tid % hd;
+        float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
         for (int t0 = ws; t0 <= pos; t0 += tp) {
             const int np = min(pos + 1, t0 + tp) - t0;
             const bool last = t0 + np == pos + 1;
             if (t0 != ws) {
-                load_tile(ks, hd + 1, hd, t.kc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np,
-                          t.kv_type, nth);
-                load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np,
-                          t.kv_type, nth);
+                load_tile(ks, kst, hd, t.kc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np, t.kv_type,
+                          nth);
+                load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np, t.kv_type,
+                          nth);
             }
             if (last)
                 for (int i = tid; i < hd; i += nth) {
                     // the new key/value enter at the stored precision, as later steps read them
-                    ks[(size_t)(np - 1) * (hd + 1) + i] = kv_round(kn[i], t.kv_type);
+                    ks[(size_t)(np - 1) * kst + i] = kv_round(kn[i], t.kv_type);
                     vs[(size_t)(np - 1) * hd + i] = kv_round(vn[i], t.kv_type);
                 }
             __syncthreads();
-            for (int i = tid; i < nh * np; i += nth) {
-                const int h = i / np, p = i % np;
-                const float* kp = ks + (size_t)p * (hd + 1);
-                const float* qh = qs + h * hd;
-                float s0 = 0.f, s1 = 0.f;
-                for (int d = 0; d < hd; d += 2) {
-                    s0 = fmaf(qh[d], kp[d], s0);
-                    s1 = fmaf(qh[d + 1], kp[d + 1], s1);
+            // scores: scale * q.k, one position per thread
+            float sv = -INFINITY;
+            if (tid < np) {
+                const float4* kp = reinterpret_cast<const float4*>(ks + (size_t)tid * kst);
+                const float4* q4 = reinterpret_cast<const float4*>(qs);
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                for (int d = 0; d < hd / 4; ++d) {
+                    const float4 k = kp[d], q = q4[d];
+                    s0 = fmaf(q.x, k.x, s0);
+                    s1 = fmaf(q.y, k.y, s1);
+                    s2 = fmaf(q.z, k.z, s2);
+                    s3 = fmaf(q.w, k.w, s3);
                 }
-                sc[h * tp + p] = scale * (s0 + s1);
+                sv = scale * ((s0 + s1) + (s2 + s3));
             }
+            float tm = warp_max(sv);
+            if (lane == 0) red[warp] = tm;
             __syncthreads();
-            for (int h = warp; h < nh; h += nw) {
-                float tm = -INFINITY;
-                for (int i = lane; i < np; i += 32) tm = fmaxf(tm, sc[h * tp + i]);
-                tm = warp_max(tm);
-                const float mnew = fmaxf(mx[h], tm);
-                float lt = 0.f;
-                for (int i = lane; i < np; i += 32) {
-                    const float e = expf(sc[h * tp + i] - mnew);
-                    sc[h * tp + i] = e;
-                    lt += e;
-                }
-                lt = warp_sum(lt);
-                if (lane == 0) {
-                    const float alpha = expf(mx[h] - mnew);  // 0 on the first tile
-                    al[h] = alpha;
-                    ls[h] = fmaf(ls[h], alpha, lt);
-                    mx[h] = mnew;
-                }
+            tm = red[0];
+            for (int w = 1; w < nw; ++w) tm = fmaxf(tm, red[w]);
+            const float mnew = fmaxf(m_run, tm);
+            float e = 0.f;
+            if (tid < np) {
+                e = expf(sv - mnew);
+                sc[tid] = e;
             }
+            e = warp_sum(e);
+            if (lane == 0) red[32 + warp] = e;
             __syncthreads();
-#pragma unroll
-            for (int k = 0; k < PER; ++k) {
-                const int i = tid + k * nth;
-                if (i < nh * hd) {
-                    const int h = i / hd, d = i % hd;
-                    const float* sh = sc + h * tp;
-                    float a0 = acc[k] * al[h], a1 = 0.f;
-                    int p = 0;
-                    for (; p + 1 < np; p += 2) {
-                        a0 = fmaf(sh[p], vs[(size_t)p * hd + d], a0);
-                        a1 = fmaf(sh[p + 1], vs[(size_t)(p + 1) * hd + d], a1);
-                    }
-                    if (p < np) a0 = fmaf(sh[p], vs[(size_t)p * hd + d], a0);
-                    acc[k] = a0 + a1;
+            float lt = 0.f;
+            for (int w = 0; w < nw; ++w) lt += red[32 + w];
+            const float alpha = expf(m_run - mnew);  // 0 on the first tile
+            l_run = fmaf(l_run, alpha, lt);
+            m_run = mnew;
+            if (pv_thread) {
+                float a0 = 0.f, a1 = 0.f;
+                int p = pg;
+                for (; p + ng < np; p += 2 * ng) {
+                    a0 = fmaf(sc[p], vs[(size_t)p * hd + pd], a0);
+                    a1 = fmaf(sc[p + ng], vs[(size_t)(p + ng) * hd + pd], a1);
                 }
+                if (p < np) a0 = fmaf(sc[p], vs[(size_t)p * hd + pd], a0);
+                acc = fmaf(acc, alpha, a0 + a1);
             }
             __syncthreads();
         }
-#pragma unroll
-        for (int k = 0; k < PER; ++k) {
-            const int i = tid + k * nth;
-            if (i < nh * hd) {
-                const int h = i / hd, d = i % hd;
-                t.out[(size_t)(kvh * n_rep + h0 + h) * hd + d] = acc[k] / ls[h];
-            }
+        if (pv_thread) pacc[tid] = acc;
+        __syncthreads();
+        for (int d = tid; d < hd; d += nth) {
+            float o = 0.f;
+            for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
+            t.out[(size_t)qh * hd + d] = o / l_run;
         }
     }
     // leave; the last attention CTA out clears the counters for this layer's next step

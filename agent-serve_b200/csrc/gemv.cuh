@@ -71,12 +71,11 @@ struct GemvArgs {
     const int* slots;    // slot of activation row m
     int* hist;           // FIN_ARGMAX: generated ids [hist_cap][M] (optional)
     int* err;
-    // fused decode attention (integer path, M == 1, the QKV GEMV): the last attn_ctas CTAs
-    // of the grid own one kv head each (RoPE, KV store, attention of `at`); they wait for
-    // the q/k/v rows through sync[0] (GEMV CTAs arrive when their rows are stored) and
-    // leave through sync[1] (the last one out clears both)
+    // fused decode attention (integer path, M == 1, the QKV GEMV): the first attn_ctas ==
+    // n_head CTAs of the grid own one query head each (RoPE, KV store, attention of `at`);
+    // they wait for the q/k/v rows through sync[0] (GEMV CTAs arrive when their rows are
+    // stored) and leave through sync[1] (the last one out clears both)
     int attn_ctas;
-    int attn_hpc;        // query heads per attention CTA (divides n_head / n_kv)
     unsigned* sync;
     AttnArgs at;
 };

@@ -386,13 +386,12 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             a.y = m->qkv;
             a.ldy = ldq;
             a.bias = Ld.bqkv;
-            fuse = fused && M == 1 && a.intq;
+            fuse = fused && M == 1 && a.intq && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
             int grid = gemv_grid(a, m->num_sms);
             if (fuse) {
                 // the attention CTAs take slots of the GEMV grid so that all stay resident
                 // one attention CTA per query head: the tail after the GEMV is then the
                 // latency of one head's scores / softmax / weighted V
-                a.attn_hpc = 1;
                 a.attn_ctas = m->hp.n_head;
                 a.sync = m->d_async + 2 * li;
                 a.at = attn_args(m, li);
