@@ -125,6 +125,30 @@ __device__ __forceinline__ void q8_build_planes(const float4 (&v)[NU], int K, in
     }
 }
 
+// Bytes of one row's planes in memory: three planes of pstride bytes (the Q8_0 row layout,
+// rounded up to 16 bytes) followed by the blocks' 2^-sh as floats.
+__host__ __device__ constexpr int q8_plane_stride(int K) { return ((K / 32) * 34 + 15) & ~15; }
+__host__ __device__ constexpr int q8_plane_bytes(int K) { return 3 * q8_plane_stride(K) + 4 * (K / 32); }
+
+// Planes of one 32-element block b held one element per lane of a full warp: the same digits
+// and 2^-sh as q8_build_planes, stored byte-wise at planes (any memory space).
+__device__ __forceinline__ void q8_block_planes_warp(float x, int b, uint8_t* planes, int pstride, float* inv) {
+    const int lane = threadIdx.x & 31;
+    float am = fabsf(x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int e = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+    const int sh = min(148 - e, Q8_PLANE_SH_MAX);
+    const float S = __uint_as_float((uint32_t)(127 + sh) << 23);
+    const uint32_t X = (uint32_t)(__float_as_int(fmaf(x, S, 12582912.0f)) - 0x4B400000);
+    uint8_t* q = planes + 34 * b + 2 + lane;
+    q[0] = (uint8_t)X;
+    q[pstride] = (uint8_t)((X + 128u) >> 8);
+    q[2 * pstride] = (uint8_t)((X + 32896u) >> 16);
+    if (lane < 6) planes[(lane >> 1) * pstride + 34 * b + (lane & 1)] = 0;  // the scale bytes
+    if (lane == 0) inv[b] = e == 255 ? __uint_as_float(0x7FC00000u) : __uint_as_float((uint32_t)(127 - sh) << 23);
+}
+
 // One 64-element unit (two blocks, 17 words at wp) of one row against the lane's planes
 // (the same unit's 17 words of each plane) and the two blocks' 2^-sh.
 __device__ __forceinline__ float unit_dot_q8_int(const uint32_t* wp, const uint32_t (&pl)[51], float invA,

@@ -189,10 +189,16 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
         }
         if (pv_thread) pacc[tid] = acc;
         __syncthreads();
-        for (int d = tid; d < hd; d += nth) {
+        for (int d = tid; d < hd; d += nth) {  // whole warps (hd is a multiple of 32)
             float o = 0.f;
             for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
-            t.out[(size_t)qh * hd + d] = o / l_run;
+            o = o / l_run;
+            t.out[(size_t)qh * hd + d] = o;
+            if (a.yplanes) {
+                const int pstride = q8_plane_stride(t.n_head * hd);
+                q8_block_planes_warp(o, (qh * hd + d) >> 5, a.yplanes, pstride,
+                                     reinterpret_cast<float*>(a.yplanes + 3 * pstride));
+            }
         }
     }
     // leave; the last attention CTA out clears the counters for this layer's next step
@@ -232,8 +238,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             return;
         }
     }
-    const int i0 = (int)((long long)a.n_items * gb / G);
-    const int i1 = (int)((long long)a.n_items * (gb + 1) / G);
+    const int al = a.align > 1 ? a.align : 1;  // n_items is a multiple of al
+    const int i0 = al * (int)((long long)(a.n_items / al) * gb / G);
+    const int i1 = al * (int)((long long)(a.n_items / al) * (gb + 1) / G);
     const int RI = GV_WARPS / a.KS;
     const int n_stages = (i1 - i0 + RI - 1) / RI;
     const bool prefetched = (i1 - i0) <= GV_PRE && (a.epi == EPI_RESID || (a.epi == EPI_STORE && a.bias));
@@ -290,7 +297,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         for (int i = tid; i < i1 - i0; i += nth) pre[i] = a.bias[i0 + i];
     const int nq = a.K >> 2;  // float4 chunks per activation row
     float4 wn[GV_PRO_UNROLL];
-    const bool norm_regs = a.pro != PRO_COPY && nq <= nth * GV_PRO_UNROLL;
+    const bool norm_regs = (a.pro == PRO_RMSNORM || a.pro == PRO_EMBED_RMSNORM) && nq <= nth * GV_PRO_UNROLL;
     if (norm_regs) {
 #pragma unroll
         for (int u = 0; u < GV_PRO_UNROLL; ++u) {
@@ -315,7 +322,44 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     uint32_t pl[INTQ ? 51 : 1];
     float invA = 0.f, invB = 0.f;
     if constexpr (INTQ) {
-        {
+        if (a.pro == PRO_PLANES) {
+            // the previous kernel left the activation as planes: one coalesced copy into the
+            // activation region (all loads in flight before the stores), then the lanes read
+            // their units from shared memory as below
+            const int pstride = q8_plane_stride(a.K);
+            const int nw4 = q8_plane_bytes(a.K) / 4;
+            const int n16 = nw4 / 4;
+            const uint4* src = reinterpret_cast<const uint4*>(a.xplanes);
+            uint4* dst = reinterpret_cast<uint4*>(xs);
+            for (int base = tid; base < n16; base += nth * GV_PRO_UNROLL) {
+                uint4 r[GV_PRO_UNROLL];
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u)
+                    if (base + u * nth < n16) r[u] = __ldcg(src + base + u * nth);
+#pragma unroll
+                for (int u = 0; u < GV_PRO_UNROLL; ++u)
+                    if (base + u * nth < n16) dst[base + u * nth] = r[u];
+            }
+            for (int i = 4 * n16 + tid; i < nw4; i += nth)
+                reinterpret_cast<uint32_t*>(xs)[i] = __ldcg(reinterpret_cast<const uint32_t*>(a.xplanes) + i);
+            named_bar_compute();
+            const uint8_t* planes = reinterpret_cast<const uint8_t*>(xs);
+            const float* pinv = reinterpret_cast<const float*>(planes + 3 * pstride);
+            const int unit = (warp % a.KS) * U + pu;
+#pragma unroll
+            for (int i = 0; i < 51; ++i) pl[i] = 0u;
+            if (pact) {
+                const uint32_t* pw = reinterpret_cast<const uint32_t*>(planes + (size_t)unit * 68);
+#pragma unroll
+                for (int i = 0; i < 17; ++i) {
+                    pl[i] = pw[i];
+                    pl[17 + i] = pw[pstride / 4 + i];
+                    pl[34 + i] = pw[pstride / 2 + i];
+                }
+                invA = pinv[2 * unit];
+                invB = pinv[2 * unit + 1];
+            }
+        } else {
             float4 v[GV_PRO_UNROLL];
             if (a.pro == PRO_EMBED_RMSNORM) {
                 int tok = a.tokens[0];
@@ -541,7 +585,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
                     const float r = prefetched ? pre[row - i0] : a.resid[row];
                     a.resid[row] = r + keep;
                 } else if (a.epi == EPI_SWIGLU) {
-                    a.y[row] = __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other);
+                    const float hv = __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other);
+                    a.y[row] = hv;
+                    if (a.yplanes) pre[row - i0] = hv;
                 } else {  // EPI_ARGMAX
                     a.y[row] = keep;
                     const unsigned long long k = argmax_key(keep, (uint32_t)row);
@@ -644,6 +690,13 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     if (a.attn_ctas && lane == 0) __threadfence();
     named_bar_compute();
     if (tid == 0 && a.attn_ctas) red_release_gpu_add(a.sync, 1u);
+    if (INTQ && a.epi == EPI_SWIGLU && a.yplanes) {
+        // this CTA's SwiGLU rows (whole 32-row blocks, in `pre`) as planes for the next kernel
+        const int pstride = q8_plane_stride(a.n_items);
+        float* inv = reinterpret_cast<float*>(a.yplanes + 3 * pstride);
+        for (int b = warp; b < (i1 - i0) / 32; b += GV_WARPS)
+            q8_block_planes_warp(pre[b * 32 + lane], i0 / 32 + b, a.yplanes, pstride, inv);
+    }
     if (tid == 0) {
         if (a.epi == EPI_ARGMAX)
             for (int m = 0; m < a.M; ++m) atomicMax(&a.keys[m], ckey[m]);

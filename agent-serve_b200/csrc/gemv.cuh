@@ -19,7 +19,9 @@ constexpr int GV_STAGE_BUDGET = 18 * 1024;       // target bytes of weights per 
 constexpr int GV_PRE = 64;                       // epilogue operands prefetched per CTA (rows)
 constexpr int GV_PRO_UNROLL = 8;                 // float4 activation loads in flight per thread
 
-enum : int { PRO_COPY = 0, PRO_RMSNORM = 1, PRO_EMBED_RMSNORM = 2 };
+// PRO_PLANES (integer path only): the activation arrives as Q8 digit planes written by the
+// previous kernel (xplanes); no activation load, norm or plane build in the prologue
+enum : int { PRO_COPY = 0, PRO_RMSNORM = 1, PRO_EMBED_RMSNORM = 2, PRO_PLANES = 3 };
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 enum : int { FIN_NONE = 0, FIN_ADVANCE = 1, FIN_ARGMAX = 2 };
 
@@ -78,6 +80,13 @@ struct GemvArgs {
     int attn_ctas;
     unsigned* sync;
     AttnArgs at;
+    // digit-plane handoff between integer-path kernels (layout of q8_plane_bytes): xplanes
+    // feeds PRO_PLANES; yplanes receives this kernel's output activation as planes (the
+    // SwiGLU rows of EPI_SWIGLU, or the fused attention's heads), written per 32-item
+    // block, so EPI_SWIGLU partitions its items in multiples of `align` = 32
+    const uint8_t* xplanes;
+    uint8_t* yplanes;
+    int align;
 };
 
 }  // namespace tfb

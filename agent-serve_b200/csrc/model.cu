@@ -23,6 +23,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "dots.cuh"
 #include "gemm.cuh"
 #include "sample.cuh"
 #include "decode_mk.cuh"
@@ -103,6 +104,7 @@ struct tf_model {
     // scratch for up to `tile` activation rows
     int tile = 1;
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
+    uint8_t* xplanes = nullptr;  // digit planes handed from one integer-path GEMV step kernel to the next
     unsigned* counters = nullptr;
     unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
     bool gemm_ok = false;         // every matmul weight is Q8_0 with K % 64 == 0
@@ -238,6 +240,17 @@ static bool fused_attn_enabled() {
     return v != 0;
 }
 
+// Digit-plane handoff (gemv.cuh xplanes / yplanes) between the integer-path kernels of a
+// batch-1 step: attention -> wo and gate/up -> down (TFB200_PLANES=0 turns it off).
+static bool planes_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_PLANES");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 // Whether batch-1 steps of slot `seq` up to position end_pos may fuse the attention.
 bool fuse_attn_ok(const tf_model* m, int end_pos) { return fused_attn_enabled() && end_pos <= kFusedAttnMaxPos; }
 
@@ -366,7 +379,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
-    bool fuse = false;
+    bool fuse = false, planes_wo = false, planes_down = false;
     for (int li = 0; li < m->hp.n_layer; ++li) {
         const LayerDev& Ld = m->L[li];
         {   // [embedding +] rmsnorm + fused QKV GEMV + bias
@@ -387,6 +400,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             a.ldy = ldq;
             a.bias = Ld.bqkv;
             fuse = fused && M == 1 && a.intq && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
+            planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && gemv_base(m, Ld.wo, D, 1, M).intq;
             int grid = gemv_grid(a, m->num_sms);
             if (fuse) {
                 // the attention CTAs take slots of the GEMV grid so that all stay resident
@@ -396,6 +410,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
                 a.sync = m->d_async + 2 * li;
                 a.at = attn_args(m, li);
                 grid = std::max(1, std::min(grid, gemv_slots(m->num_sms) - a.attn_ctas));
+                if (planes_wo) a.yplanes = m->xplanes;
             }
             CK(gemv_launch(a, grid + a.attn_ctas, m->stream, pdl));
             ++launches;
@@ -407,7 +422,8 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
         }
         {   // wo GEMV + residual
             GemvArgs a = gemv_base(m, Ld.wo, D, 1, M);
-            a.pro = PRO_COPY;
+            a.pro = planes_wo ? PRO_PLANES : PRO_COPY;
+            a.xplanes = m->xplanes;
             a.x = m->attn;
             a.ldx = H;
             a.epi = EPI_RESID;
@@ -426,12 +442,26 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             a.epi = EPI_SWIGLU;
             a.y = m->h;
             a.ldy = FF;
-            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
+            int grid = gemv_grid(a, m->num_sms);
+            // the SwiGLU rows leave as planes when both kernels take the integer path and each
+            // CTA's whole 32-row blocks fit its row buffer
+            const int nblk = FF / 32;
+            grid = std::min(grid, nblk);
+            planes_down = planes_enabled() && a.intq && FF % 32 == 0 && grid > 0 &&
+                          (nblk + grid - 1) / grid * 32 <= GV_PRE && gemv_base(m, Ld.down, D, 1, M).intq;
+            if (planes_down) {
+                a.align = 32;
+                a.yplanes = m->xplanes;
+            } else {
+                grid = gemv_grid(a, m->num_sms);
+            }
+            CK(gemv_launch(a, grid, m->stream, pdl));
             ++launches;
         }
         {   // down GEMV + residual
             GemvArgs a = gemv_base(m, Ld.down, D, 1, M);
-            a.pro = PRO_COPY;
+            a.pro = planes_down ? PRO_PLANES : PRO_COPY;
+            a.xplanes = m->xplanes;
             a.x = m->h;
             a.ldx = FF;
             a.epi = EPI_RESID;
@@ -742,7 +772,8 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt};
+                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
+                   m->xplanes};
     for (void* p : dev)
         if (p) cudaFree(p);
     sample_scratch_destroy(m->smp);
@@ -1026,6 +1057,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMalloc(&m->x, sizeof(float) * T * m->D));
     CKD(cudaMalloc(&m->qkv, sizeof(float) * T * (m->H + 2 * m->KV)));
     CKD(cudaMalloc(&m->attn, sizeof(float) * T * m->H));
+    CKD(cudaMalloc(&m->xplanes, (size_t)q8_plane_bytes(std::max(m->FF, m->H))));
     CKD(cudaMalloc(&m->h, sizeof(float) * T * m->FF));
     CKD(cudaMalloc(&m->logits, sizeof(float) * (size_t)T * m->V));
     CKD(cudaMalloc(&m->part, sizeof(float) * (size_t)T * hp.n_head * m->n_split * (m->hd + 2)));
