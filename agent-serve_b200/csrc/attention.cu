@@ -15,6 +15,8 @@
 // and the V-weighted sum over its positions.  The last CTA of a (row, kv head) combines the
 // split partials (max, sum, acc) into the normalised output.  The new position's k/v are
 // taken from shared memory, never re-read from the cache slot being written.
+#include <cstdlib>
+
 #include "attention.cuh"
 
 namespace tfb {
@@ -232,30 +234,45 @@ __global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs 
 }
 
 // ---- streaming decode attention (fp32 caches, many rows) -------------------------------------
-// One CTA per (row, kv head, position split) walks its positions in tiles of AS_TILE: the K and
-// V rows of tile t + 1 arrive by 1-D bulk copies (TMA) while tile t is scored, with an online
-// softmax (running max, sum and weighted V in registers), so a split streams its whole range
-// instead of one 64-position chunk per CTA.  Splits only where rows x kv heads alone do not
-// fill the GPU; their partials are combined as in attn_decode_kernel.  Same semantics as
-// attn_decode_kernel (fresh modes, windows, the new position taken from shared memory).
+// One CTA per (row, kv head, position split) walks its positions in tiles of AS_TILE held in
+// a ring of AS_NB shared-memory buffers filled by 1-D bulk copies (TMA engine): the K rows one
+// copy each into rows padded to hd + 4 floats, the V rows in one copy.  Per tile, with the
+// whole group of query heads of the kv head (GQA) sharing the tile:
+//   scores   lane = position, warp = a slice of hd/8 dims: float4 K reads (the padding puts
+//            consecutive positions on distinct banks), q read as warp-wide broadcasts, the 8
+//            slices' partial dots summed in a fixed order through shared memory;
+//   softmax  warp = query head, lane = position: running max / sum (attn_decode's softmax,
+//            src/attention.cpp:63-72, as an online softmax over tiles);
+//   P.V      warp = positions p = warp (mod 8), lane = 4 dims, every head of the group held
+//            in registers; the 8 warps' sums meet once per split at the end.
+// Two CTA barriers per tile; the buffer of tile t - 1 is refilled with tile t + 2 after the
+// first one.  Splits of one row combine through attn_combine.
 constexpr int AS_THREADS = 256;
 constexpr int AS_TILE = 32;
+constexpr int AS_NB = 3;
+static inline size_t attn_stream_smem_bytes(int hd) {
+    const size_t tiles = (size_t)AS_NB * AS_TILE * (2 * hd + 4) * sizeof(float);
+    const size_t fin = (size_t)(AS_THREADS / 32) * AT_MAX_REP * hd * sizeof(float);  // final sums
+    const size_t comb = (size_t)(AT_MAX_REP * AT_MAX_SPLIT + AT_MAX_SPLIT) * sizeof(float);
+    size_t m = tiles > fin ? tiles : fin;
+    return m > comb ? m : comb;
+}
 
-static inline size_t attn_stream_smem_bytes(int hd) { return (size_t)2 * 2 * AS_TILE * hd * sizeof(float); }
-
-__global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) float kvt[];  // [2 buffers][K | V][AS_TILE][hd]
-    __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
+__global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnArgs a) {
+    extern __shared__ __align__(16) float kvt[];
+    __shared__ __align__(16) float qs[AT_MAX_REP][AT_MAX_HD];
+    __shared__ float red[AS_THREADS / 32][AT_MAX_REP][AS_TILE];  // partial scores per dim slice
+    __shared__ __align__(16) float ep[AS_TILE][8];                // exp(score - max), [position][head]
     __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
-    __shared__ float sc[AT_MAX_REP][AS_TILE];
-    __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP], al_s[AT_MAX_REP];
-    __shared__ __align__(8) uint64_t full[2];
+    __shared__ __align__(16) float al_s[8];
+    __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP];
+    __shared__ __align__(8) uint64_t full[AS_NB];
 
     pdl_trigger();
     pdl_wait();
     const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
+    const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv, kst = hd + 4, cpw = hd / 32;
     const int slot = a.slots ? a.slots[m] : 0;
     const int pos = a.fresh == 2 ? a.pos[slot] + m : (a.fresh ? a.pos[slot] : a.n_pos_fixed - 1);
     if (a.fresh && (pos < 0 || pos >= a.cap)) {
@@ -275,21 +292,28 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(const AttnArgs 
     const float* kc = static_cast<const float*>(a.kc) + cache_off;
     const float* vc = static_cast<const float*>(a.vc) + cache_off;
     const bool fresh_last = a.fresh == 1 && p1 == n_pos;  // this split holds the new position
+    float* kbuf = kvt;                                     // [AS_NB][AS_TILE][kst]
+    float* vbuf = kvt + (size_t)AS_NB * AS_TILE * kst;     // [AS_NB][AS_TILE][hd]
 
-    auto issue = [&](int t) {  // tile t into buffer t & 1 (thread 0)
-        const int b = t & 1, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
+    // tile t into buffer t % AS_NB, issued by the last warp: lane r copies K row r
+    constexpr int IW = AS_THREADS / 32 - 1;
+    auto issue = [&](int t) {
+        const int b = t % AS_NB, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
         const int qc = (fresh_last && q0 + qn == n_pos) ? qn - 1 : qn;  // cached rows of the tile
-        const uint32_t bytes = (uint32_t)qc * hd * 4;
-        mbar_expect_tx(&full[b], 2 * bytes);
-        if (bytes) {
-            bulk_g2s(kvt + (size_t)(2 * b) * AS_TILE * hd, kc + (size_t)q0 * hd, bytes, &full[b]);
-            bulk_g2s(kvt + (size_t)(2 * b + 1) * AS_TILE * hd, vc + (size_t)q0 * hd, bytes, &full[b]);
-        }
+        if (lane == 0) mbar_expect_tx(&full[b], (uint32_t)(2 * qc * hd * 4));
+        __syncwarp();
+        if (lane < qc)
+            bulk_g2s(kbuf + ((size_t)b * AS_TILE + lane) * kst, kc + (size_t)(q0 + lane) * hd, (uint32_t)hd * 4,
+                     &full[b]);
+        if (lane == 0 && qc)
+            bulk_g2s(vbuf + (size_t)b * AS_TILE * hd, vc + (size_t)q0 * hd, (uint32_t)(qc * hd * 4), &full[b]);
     };
     if (tid == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int b = 0; b < AS_NB; ++b) mbar_init(&full[b], 1);
         mbar_fence_init();
+    }
+    __syncthreads();
+    if (warp == IW) {
         issue(0);
         if (n_tiles > 1) issue(1);
     }
@@ -304,6 +328,7 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(const AttnArgs 
         mx_s[tid] = -INFINITY;
         l_s[tid] = 0.f;
     }
+    if (tid < 8) al_s[tid] = 0.f;
     __syncthreads();
     if (a.fresh == 1) {
         const float* cp = a.cosb + (size_t)pos * d2;
@@ -321,93 +346,131 @@ __global__ void __launch_bounds__(AS_THREADS) attn_stream_kernel(const AttnArgs 
             }
     }
     const float scale = 1.0f / sqrtf((float)hd);
-    constexpr int PER = (AT_MAX_REP * AT_MAX_HD + AS_THREADS - 1) / AS_THREADS;
-    float acc[PER];
+    float acc[AT_MAX_REP][4];
 #pragma unroll
-    for (int k = 0; k < PER; ++k) acc[k] = 0.f;
+    for (int h = 0; h < AT_MAX_REP; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
+    const bool pv_lane = lane < hd / 4;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
-        const int b = t & 1, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
-        float* ks = kvt + (size_t)(2 * b) * AS_TILE * hd;
-        float* vs = kvt + (size_t)(2 * b + 1) * AS_TILE * hd;
-        if (!mbar_wait(&full[b], (t >> 1) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
-        if (fresh_last && q0 + qn == n_pos)
+        const int b = t % AS_NB, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
+        float* ks = kbuf + (size_t)b * AS_TILE * kst;
+        float* vs = vbuf + (size_t)b * AS_TILE * hd;
+        if (!mbar_wait(&full[b], (t / AS_NB) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
+        if (fresh_last && q0 + qn == n_pos) {  // uniform: the new key / value enter the tile
             for (int i = tid; i < hd; i += AS_THREADS) {
-                ks[(size_t)(qn - 1) * hd + i] = kn[i];  // fp32 cache: stored exactly
+                ks[(size_t)(qn - 1) * kst + i] = kn[i];  // fp32 cache: stored exactly
                 vs[(size_t)(qn - 1) * hd + i] = vn[i];
             }
-        __syncthreads();
-        // scores (attn_decode, src/attention.cpp:63-64): thread per (head, position), a walk
-        // over the dims rotated by the position so one warp's rows meet distinct banks
-        for (int i = tid; i < n_rep * qn; i += AS_THREADS) {
-            const int h = i / qn, p = i % qn;
-            const float* kp = ks + (size_t)p * hd;
-            const int rot = p % hd;
-            float s0 = 0.f, s1 = 0.f;
-            for (int d = 0; d < hd; d += 2) {
-                int e0 = d + rot, e1 = d + 1 + rot;
-                e0 -= e0 >= hd ? hd : 0;
-                e1 -= e1 >= hd ? hd : 0;
-                s0 = fmaf(qs[h][e0], kp[e0], s0);
-                s1 = fmaf(qs[h][e1], kp[e1], s1);
+            __syncthreads();
+        }
+        {   // partial scores of this warp's dim slice (attn_decode, src/attention.cpp:63-64)
+            float sp[AT_MAX_REP];
+#pragma unroll
+            for (int h = 0; h < AT_MAX_REP; ++h) sp[h] = 0.f;
+            if (lane < qn) {
+                const float4* kr = reinterpret_cast<const float4*>(ks + (size_t)lane * kst) + warp * cpw;
+                for (int c = 0; c < cpw; ++c) {
+                    const float4 k4 = kr[c];
+#pragma unroll
+                    for (int h = 0; h < AT_MAX_REP; ++h) {
+                        if (h < n_rep) {
+                            const float4 q4 = reinterpret_cast<const float4*>(qs[h])[warp * cpw + c];
+                            sp[h] = fmaf(q4.x, k4.x, sp[h]);
+                            sp[h] = fmaf(q4.y, k4.y, sp[h]);
+                            sp[h] = fmaf(q4.z, k4.z, sp[h]);
+                            sp[h] = fmaf(q4.w, k4.w, sp[h]);
+                        }
+                    }
+                }
             }
-            sc[h][p] = scale * (s0 + s1);
+#pragma unroll
+            for (int h = 0; h < AT_MAX_REP; ++h)
+                if (h < n_rep) red[warp][h][lane] = sp[h];
         }
         __syncthreads();
-        for (int h = warp; h < n_rep; h += AS_THREADS / 32) {  // running max and sum
-            float tm = lane < qn ? sc[h][lane] : -INFINITY;
-            tm = warp_max(tm);
-            const float mnew = fmaxf(mx_s[h], tm);
-            const float e = lane < qn ? expf(sc[h][lane] - mnew) : 0.f;
-            if (lane < qn) sc[h][lane] = e;
+        // every thread has finished tile t - 1's P.V: its buffer takes tile t + 2
+        if (warp == IW && t + 2 < n_tiles) issue(t + 2);
+        if (warp < n_rep) {  // running max and sum of head `warp`
+            const int h = warp;
+            float sv = -INFINITY;
+            if (lane < qn) {
+                float v = 0.f;
+#pragma unroll
+                for (int w = 0; w < AS_THREADS / 32; ++w) v += red[w][h][lane];
+                sv = scale * v;
+            }
+            const float tm = warp_max(sv);
+            const float mold = mx_s[h];
+            const float mnew = fmaxf(mold, tm);
+            const float e = lane < qn ? expf(sv - mnew) : 0.f;
+            ep[lane][h] = e;
             const float lt = warp_sum(e);
             if (lane == 0) {
-                const float alpha = expf(mx_s[h] - mnew);  // 0 on the first tile
+                const float alpha = expf(mold - mnew);  // 0 on the first tile
                 al_s[h] = alpha;
                 l_s[h] = fmaf(l_s[h], alpha, lt);
                 mx_s[h] = mnew;
             }
         }
         __syncthreads();
+        if (pv_lane) {  // weighted V over positions warp, warp + 8, ...
+            const float4 a0 = reinterpret_cast<const float4*>(al_s)[0], a1 = reinterpret_cast<const float4*>(al_s)[1];
+            const float al[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-        for (int k = 0; k < PER; ++k) {  // weighted V: thread per (head, dim)
-            const int i = tid + k * AS_THREADS;
-            if (i < n_rep * hd) {
-                const int h = i / hd, d = i % hd;
-                float a0 = acc[k] * al_s[h], a1 = 0.f;
-                int p = 0;
-                for (; p + 1 < qn; p += 2) {
-                    a0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], a0);
-                    a1 = fmaf(sc[h][p + 1], vs[(size_t)(p + 1) * hd + d], a1);
+            for (int h = 0; h < AT_MAX_REP; ++h) {
+                acc[h][0] *= al[h];
+                acc[h][1] *= al[h];
+                acc[h][2] *= al[h];
+                acc[h][3] *= al[h];
+            }
+            for (int p = warp; p < qn; p += AS_THREADS / 32) {
+                const float4 v4 = reinterpret_cast<const float4*>(vs + (size_t)p * hd)[lane];
+                const float4 e0 = reinterpret_cast<const float4*>(ep[p])[0], e1 = reinterpret_cast<const float4*>(ep[p])[1];
+                const float e[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+#pragma unroll
+                for (int h = 0; h < AT_MAX_REP; ++h) {
+                    acc[h][0] = fmaf(e[h], v4.x, acc[h][0]);
+                    acc[h][1] = fmaf(e[h], v4.y, acc[h][1]);
+                    acc[h][2] = fmaf(e[h], v4.z, acc[h][2]);
+                    acc[h][3] = fmaf(e[h], v4.w, acc[h][3]);
                 }
-                if (p < qn) a0 = fmaf(sc[h][p], vs[(size_t)p * hd + d], a0);
-                acc[k] = a0 + a1;
             }
         }
-        __syncthreads();  // buffer b is free again
-        if (tid == 0 && t + 2 < n_tiles) issue(t + 2);
     }
-    if (!ok) return;
+    // the 8 warps' P.V sums (tile buffers are free: every issued copy was waited for)
+    __syncthreads();
+    float* fin = kvt;  // [warp][head][hd]
+    if (pv_lane)
 #pragma unroll
-    for (int k = 0; k < PER; ++k) {
-        const int i = tid + k * AS_THREADS;
-        if (i < n_rep * hd) {
+        for (int h = 0; h < AT_MAX_REP; ++h)
+            if (h < n_rep)
+                reinterpret_cast<float4*>(fin + ((size_t)warp * AT_MAX_REP + h) * hd)[lane] =
+                    make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+    __syncthreads();
+    if (ok)
+        for (int i = tid; i < n_rep * hd; i += AS_THREADS) {
             const int h = i / hd, d = i % hd;
+            float o = 0.f;
+#pragma unroll
+            for (int w = 0; w < AS_THREADS / 32; ++w) o += fin[((size_t)w * AT_MAX_REP + h) * hd + d];
             const int head = kvh * n_rep + h;
             if (nsp == 1) {
-                a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = acc[k] / l_s[h];
+                a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = o / l_s[h];
             } else {
                 float* pp = a.part + (((size_t)m * a.n_head + head) * a.n_split + split) * (hd + 2);
-                pp[2 + d] = acc[k];
+                pp[2 + d] = o;
                 if (d == 0) {
                     pp[0] = mx_s[h];
                     pp[1] = l_s[h];
                 }
             }
         }
+    if (!ok) return;
+    // the combine's scratch reuses the tile buffers
+    if (nsp > 1) {
+        __syncthreads();
+        attn_combine(a, m, kvh, nsp, kvt, kvt + AT_MAX_REP * AT_MAX_SPLIT, AS_THREADS);
     }
-    // the combine's scratch reuses the tile buffers (no copies are in flight any more)
-    if (nsp > 1) attn_combine(a, m, kvh, nsp, kvt, kvt + AT_MAX_REP * AT_MAX_SPLIT, AS_THREADS);
 }
 
 // ---- prefill attention (attn_prefill): one CTA per (query row i, head h) -----------------
@@ -515,14 +578,24 @@ static int attn_stream_splits(const AttnArgs& a, int M) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // one wave of the two resident CTAs per SM (TFB200_ATTN_WAVES): a CTA's set-up and
+    // combine cost a few microseconds, so fewer, longer splits measured faster (cfg4 at 256
+    // rows x 512 positions: 9.95 ms per step at one wave, 10.9 at four); the kernel itself
+    // keeps at least four tiles per split
+    static int waves = -1;
+    if (waves < 0) {
+        const char* e = getenv("TFB200_ATTN_WAVES");
+        waves = e ? atoi(e) : 1;
+        if (waves < 1) waves = 1;
+    }
     const int pairs = M * a.n_kv;
-    int s = (2 * sms + pairs - 1) / pairs;
+    int s = (waves * 2 * sms + pairs - 1) / pairs;
     return s < 1 ? 1 : (s > a.n_split ? a.n_split : s);
 }
 
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
     if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
-    if (a.kv_type == KV_F32 && M * a.n_kv >= 16) {  // many rows: streaming kernel
+    if (a.kv_type == KV_F32 && M * a.n_kv >= 16 && a.hd % 32 == 0) {  // many rows: streaming kernel
         static bool sattr[64] = {false};
         int dev = 0;
         cudaGetDevice(&dev);
@@ -530,6 +603,10 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
         if (!sattr[dev]) {
             cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)attn_stream_smem_bytes(AT_MAX_HD));
+            if (e != cudaSuccess) return e;
+            // two CTAs per SM need the whole shared-memory carve-out
+            e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
             sattr[dev] = true;
         }
