@@ -479,7 +479,7 @@ constexpr size_t gemm_tc_stage_bytes() {
 template <int NT>
 constexpr size_t gemm_tc_smem_bytes() {
     const size_t pipe = 2 * gemm_tc_stage_bytes<NT>();
-    const size_t epi = (size_t)NT * GM_EPI_LD * 4;
+    const size_t epi = (size_t)NT * GM_EPI_LD * 4 + (size_t)NT * 4;  // tile + column scales
     return (pipe > epi ? pipe : epi) + 64 + 1024;  // + mbarriers, the TMEM address, 1024-B alignment
 }
 
@@ -520,12 +520,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    // the weight words of the first PF stages do not depend on earlier kernels: request them
+    // before waiting for the previous kernel of the step
+    constexpr int PF = GM_WPF;
+    const int wr = tid >> 1, wj = tid & 1;
+    uint32_t wbuf[PF][9];  // weight words of stage kc in slot kc % PF
+#pragma unroll
+    for (int u = 0; u < PF; ++u)
+        if (u < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + u, wj);
     pdl_trigger();
     pdl_wait();
 
     // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
-    const int wr = tid >> 1, wj = tid & 1;
     // activations of stage kc: 16-byte cp.async chunks.  Thread t copies chunk c = t % 8 of
     // rows r = t / 8 + 32 i; r % 8 (its swizzle row) and c are fixed per thread, so source
     // and destination advance by constant strides.
@@ -547,45 +554,46 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     // (a stage's 68-byte row pieces come from HBM, so one stage of lookahead leaves the loads
     // latency-bound), and the activations of stage kc + 1 are requested as soon as the MMAs of
     // stage kc - 1 (the previous user of that buffer) have completed.
-    constexpr int PF = GM_WPF;
-    uint32_t wbuf[PF][9];  // weight words of stages kc .. kc + PF - 1 (shifted down each stage)
     bool ok = true;
     int last_kc = -1;  // the last stage whose MMAs were issued
     if (nk > 0) load_x(0, kb);
+    // Stage kc's weight words sit in slot kc % PF: the k loop is unrolled by PF so every slot
+    // index is static (registers) and a slot is refilled right after its dequantisation, PF
+    // stages ahead of its use (a shift of the slots would wait on the newest load every stage).
+    for (int kc0 = 0; kc0 < nk && ok; kc0 += PF) {
 #pragma unroll
-    for (int u = 0; u < PF; ++u)
-        if (u < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + u, wj);
-    for (int kc = 0; kc < nk && ok; ++kc) {
-        const int s = kc & 1;
-        // dequantise the held weight words into stage s (free: its previous MMAs completed
-        // before load_x refilled it)
-        gm_dequant_h2(wbuf[0], wj, wscale, wh(s), wl(s), KintRow{wr, 32 * wj});
+        for (int u = 0; u < PF; ++u) {
+            const int kc = kc0 + u;
+            if (kc < nk && ok) {
+                const int s = kc & 1;
+                // dequantise the held weight words into stage s (free: its previous MMAs
+                // completed before load_x refilled it)
+                gm_dequant_h2(wbuf[u], wj, wscale, wh(s), wl(s), KintRow{wr, 32 * wj});
+                if (kc + PF < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + kc + PF, wj);
+                cp_async_wait_all();
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
+                __syncthreads();
+                last_kc = kc;
+                if (tid == 0) {
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(s)),
+                                   bl = smem_u32(xl(s));
 #pragma unroll
-        for (int u = 0; u + 1 < PF; ++u)
-#pragma unroll
-            for (int i = 0; i < 9; ++i) wbuf[u][i] = wbuf[u + 1][i];
-        if (kc + PF < nk) gm_load_w(wbuf[PF - 1], a, n0 + wr, kb + kc + PF, wj);
-        cp_async_wait_all();
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
-        __syncthreads();
-        last_kc = kc;
-        if (tid == 0) {
-            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(s)), bl = smem_u32(xl(s));
-#pragma unroll
-            for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
-                const uint32_t o = 32u * j;
-                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
-                         (kc > 0 || j > 0) ? 1u : 0u);
-                umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
-                umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
+                    for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
+                        const uint32_t o = 32u * j;
+                        umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
+                                 (kc > 0 || j > 0) ? 1u : 0u);
+                        umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
+                        umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
+                    }
+                    umma_commit(&done[s]);
+                }
+                if (kc + 1 < nk) {
+                    // stage s ^ 1 was last read by the MMAs of stage kc - 1
+                    if (kc >= 1) ok = mbar_wait(&done[s ^ 1], ((kc - 1) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+                    if (ok) load_x(s ^ 1, kb + kc + 1);
+                }
             }
-            umma_commit(&done[s]);
-        }
-        if (kc + 1 < nk) {
-            // stage s ^ 1 was last read by the MMAs of stage kc - 1
-            if (kc >= 1) ok = mbar_wait(&done[s ^ 1], ((kc - 1) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
-            if (ok) load_x(s ^ 1, kb + kc + 1);
         }
     }
     // the last stage's commit covers every MMA issued before it
@@ -595,6 +603,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
 
     // ---- epilogue: TMEM -> registers -> scaled tile[m][n] in shared memory ----
     float* tile = reinterpret_cast<float*>(smem);  // [NT][GM_EPI_LD], the pipeline buffers are free
+    // 2^-(sw + sx[m]) of every activation row of the tile (0 for rows past M or after an error),
+    // kept beside the tile
+    float* colsc = tile + (size_t)NT * GM_EPI_LD;
+    if (tid < NT) {
+        const int m = m0 + tid;
+        colsc[tid] = (ok && m < a.M) ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
+    }
+    __syncthreads();
     {
         const int row = 32 * (warp & 3) + lane;           // weight row of this thread's TMEM lane
         const int c0 = (warp >> 2) * (NT / 2);             // warps 4-7 take the upper columns
@@ -604,9 +620,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
             for (int u = 0; u < 16; ++u) {
-                const int mm = c + u, m = m0 + mm;
-                const float sc = (ok && m < a.M) ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
-                tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * sc;
+                const int mm = c + u;
+                tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[mm];
             }
         }
     }
@@ -664,6 +679,15 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+int gemm_tile_rows(int M) {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_GEMM_NT");
+        v = (e && atoi(e) == 128) ? 128 : 256;
+    }
+    return (M > 128 && v == 256) ? 256 : 128;
+}
+
 // tcgen05 path (default) or the mma.sync path (TFB200_GEMM_TC05=0)
 static bool gemm_use_tc05() {
     static int v = -1;
@@ -691,7 +715,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (gemm_use_tc05()) {
         GemmArgs aa = a;
         void* args[] = {&aa};
-        const bool wide = a.M > 128;
+        const bool wide = gemm_tile_rows(a.M) == 256;
         const size_t sm = wide ? gemm_tc_smem_bytes<256>() : gemm_tc_smem_bytes<128>();
         const void* fn = wide ? (const void*)gemm_q8_tc_kernel<256> : (const void*)gemm_q8_tc_kernel<128>;
         static bool tc_attr[64][2] = {};

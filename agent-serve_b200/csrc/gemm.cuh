@@ -73,9 +73,12 @@ constexpr int GM_MAX_SPLIT = 8;
 // workspace floats / tile counters the split-K path needs for `num_sms` SMs
 inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_ROW_PAD; }
 inline int gemm_tile_counters(int num_sms) { return 2 * num_sms; }  // arrivals, departures per tile
+// activation rows per tcgen05 CTA tile for an M-row GEMM (128 or 256; TFB200_GEMM_NT=128
+// keeps 128-row tiles at every M)
+int gemm_tile_rows(int M);
 // k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
 inline int gemm_pick_split(int N, int M, int K, int num_sms) {
-    const int mt = M > GM_BM ? GM_ROW_PAD : GM_BM;  // activation rows per CTA tile
+    const int mt = gemm_tile_rows(M);  // activation rows per CTA tile
     const int tiles = ((N + GM_BN - 1) / GM_BN) * ((M + mt - 1) / mt);
     if (tiles >= num_sms) return 1;
     int s = num_sms / tiles;
