@@ -243,12 +243,53 @@ __device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float 
 // publishes its partial tile, waits (bounded) for the other splits of its tile, then sums all
 // partials, in split order, for its own 1/ks of the tile's activation rows and applies the
 // epilogue to those rows: the reduction is spread over the splits and deterministic.
-template <int BMT>
-__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0) {
+// ---- thread-block cluster helpers (split-K reduction through distributed shared memory) ----
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float4 ld_cluster_v4(uint32_t local_addr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(r)
+                 : "memory");
+    return v;
+}
+
+// CLUSTER: the k splits of a tile are one thread-block cluster (grid.z = cluster size = ks), so
+// each split reduces its slice of rows by reading the other splits' tiles straight from their
+// shared memory; otherwise the splits meet through the global workspace and tile counters.
+// Either way the splits are summed in split order (deterministic).
+template <int BMT, bool CLUSTER = false>
+__device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0, bool ok_in = true) {
     const int tid = threadIdx.x;
     const int rv = min(BMT, a.M - m0);  // valid activation rows of the tile
     int mlo = 0, mhi = rv;
-    if (gridDim.z > 1) {
+    if (CLUSTER && gridDim.z > 1) {
+        const int ks = (int)gridDim.z, z = (int)blockIdx.z;  // cluster rank z holds split z
+        cluster_sync_all();  // every split's tile is in its shared memory
+        mlo = rv * z / ks;
+        mhi = rv * (z + 1) / ks;
+        // this CTA's rows of the tile are read by no other split: the sums overwrite them
+        for (int i = tid; i < (mhi - mlo) * (GM_BN / 4); i += GM_THREADS) {
+            const int mm = mlo + i / (GM_BN / 4), n4 = i % (GM_BN / 4);
+            float* t = tile + mm * GM_EPI_LD + 4 * n4;
+            const uint32_t la = smem_u32(t);
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < ks; ++q) {
+                const float4 u = ld_cluster_v4(la, q);
+                v.x += u.x;
+                v.y += u.y;
+                v.z += u.z;
+                v.w += u.w;
+            }
+            *reinterpret_cast<float4*>(t) = v;
+        }
+        cluster_sync_all();  // no split leaves while another still reads its tile
+        if (!ok_in) return;  // the error word holds the failure (the barriers were still kept)
+    } else if (gridDim.z > 1) {
         __shared__ int ok_s;
         const int ks = (int)gridDim.z, z = (int)blockIdx.z;
         float* wz = a.ws + (size_t)z * a.M * a.N;
@@ -628,8 +669,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT));
-    if (!ok) return;  // the error word holds the failure
-    gemm_epilogue<NT>(a, tile, m0, n0);
+    // with k splits the cluster's barriers are kept even after an error (gemm_epilogue returns
+    // after them); without, the error word holds the failure
+    if (!ok && gridDim.z == 1) return;
+    gemm_epilogue<NT, true>(a, tile, m0, n0, ok);
 }
 
 // ---- end of a step at M rows ------------------------------------------------------------------
@@ -728,7 +771,23 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
             tc_attr[dv][wide] = true;
         }
         const int nt = wide ? 256 : 128;
-        return launch_pdl(fn, dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks), dim3(GM_THREADS), sm, st, args);
+        // the k splits of a tile form one cluster (their reduction goes through distributed
+        // shared memory)
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks);
+        cfg.blockDim = dim3(GM_THREADS);
+        cfg.dynamicSmemBytes = sm;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[2];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        attr[1].id = cudaLaunchAttributeClusterDimension;
+        attr[1].val.clusterDim.x = 1;
+        attr[1].val.clusterDim.y = 1;
+        attr[1].val.clusterDim.z = (unsigned)ks;
+        cfg.attrs = attr;
+        cfg.numAttrs = 2;
+        return cudaLaunchKernelExC(&cfg, fn, args);
     }
     dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
     GemmArgs aa = a;
