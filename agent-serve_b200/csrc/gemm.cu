@@ -127,6 +127,22 @@ __device__ __forceinline__ void gm_load_w(uint32_t (&w)[9], const GemmArgs& a, i
     }
 }
 
+// The weight words a thread of the 512-thread tcgen05 kernel needs for weight row r, k-stage
+// kc, 16-weight piece jh = 2 * block + half: w[0] holds the block's fp16 scale (word 0 or 8 of
+// the stage's 68-byte unit), w[1..5] the five words 4*jh .. 4*jh + 4 (bytes 16*jh .. 16*jh +
+// 19), whose bytes 2 * block + 2 .. + 17 are the piece's 16 quants.
+__device__ __forceinline__ void gm_load_w16(uint32_t (&w)[6], const GemmArgs& a, int n, int kc, int jh) {
+    if (n < a.N) {
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a.W + (long long)n * a.rb + (long long)kc * 68);
+        w[0] = __ldg(p + 8 * (jh >> 1));
+#pragma unroll
+        for (int i = 0; i < 5; ++i) w[1 + i] = __ldg(p + 4 * jh + i);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 6; ++i) w[i] = 0u;
+    }
+}
+
 // byte offset of element (row, k) of a [rows][64] f16 operand tile in the swizzled layout
 __device__ __forceinline__ uint32_t kint_off(int row, int k) {
     return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
@@ -158,6 +174,36 @@ __device__ __forceinline__ void gm_dequant_h2_t(const uint32_t (&w)[9], float ws
         for (int e = 0; e < 8; e += 2) {
             const int b = b0 + 8 * c + e;
             const uint32_t wd = w[b >> 2] ^ 0x80808080u;
+            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
+            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
+            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
+            const __half2 hi = __hmul2(q2, d2);
+            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
+            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
+            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
+        }
+        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
+// gm_dequant_h2_t for one 16-weight piece (gm_load_w16's words, block J): the two 8-half
+// groups go to dh / dl + hoff(0), hoff(1).
+template <int J, class Off>
+__device__ __forceinline__ void gm_dequant16_t(const uint32_t (&w)[6], float wscale, uint8_t* dh, uint8_t* dl,
+                                               Off hoff) {
+    const uint32_t dbits = J == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+    const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
+    const __half2 d2 = __halves2half2(dsc, dsc);
+    const __half2 k1152 = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
+    constexpr int b0 = 2 * J + 2;  // first quant byte within the five window words (even)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const int b = b0 + 8 * c + e;
+            const uint32_t wd = w[1 + (b >> 2)] ^ 0x80808080u;
             const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
             const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
             const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
@@ -262,7 +308,7 @@ __device__ __forceinline__ float4 ld_cluster_v4(uint32_t local_addr, int rank) {
 // each split reduces its slice of rows by reading the other splits' tiles straight from their
 // shared memory; otherwise the splits meet through the global workspace and tile counters.
 // Either way the splits are summed in split order (deterministic).
-template <int BMT, bool CLUSTER = false>
+template <int BMT, bool CLUSTER = false, int NTH = GM_THREADS>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0, bool ok_in = true) {
     const int tid = threadIdx.x;
     const int rv = min(BMT, a.M - m0);  // valid activation rows of the tile
@@ -273,7 +319,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
         mlo = rv * z / ks;
         mhi = rv * (z + 1) / ks;
         // this CTA's rows of the tile are read by no other split: the sums overwrite them
-        for (int i = tid; i < (mhi - mlo) * (GM_BN / 4); i += GM_THREADS) {
+        for (int i = tid; i < (mhi - mlo) * (GM_BN / 4); i += NTH) {
             const int mm = mlo + i / (GM_BN / 4), n4 = i % (GM_BN / 4);
             float* t = tile + mm * GM_EPI_LD + 4 * n4;
             const uint32_t la = smem_u32(t);
@@ -293,7 +339,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
         __shared__ int ok_s;
         const int ks = (int)gridDim.z, z = (int)blockIdx.z;
         float* wz = a.ws + (size_t)z * a.M * a.N;
-        for (int i = tid; i < rv * GM_BN; i += GM_THREADS) {
+        for (int i = tid; i < rv * GM_BN; i += NTH) {
             const int mm = i / GM_BN, nn = i % GM_BN, n = n0 + nn;
             if (n < a.N) wz[(size_t)(m0 + mm) * a.N + n] = tile[mm * GM_EPI_LD + nn];
         }
@@ -315,7 +361,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
         mlo = rv * z / ks;
         mhi = rv * (z + 1) / ks;
         if (ok)
-            for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+            for (int i = tid; i < (mhi - mlo) * GM_BN; i += NTH) {
                 const int mm = mlo + i / GM_BN, nn = i % GM_BN, n = n0 + nn;
                 if (n >= a.N) continue;
                 float v = 0.f;
@@ -344,13 +390,13 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
             if (best) atomicMax(&a.keys[m], best);
         }
         if (a.store_logits)
-            for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+            for (int i = tid; i < (mhi - mlo) * GM_BN; i += NTH) {
                 const int mm = mlo + i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
                 if (n < a.N) a.y[(size_t)m * a.ldy + n] = tile[mm * GM_EPI_LD + nn];
             }
         return;
     }
-    for (int i = tid; i < (mhi - mlo) * GM_BN; i += GM_THREADS) {
+    for (int i = tid; i < (mhi - mlo) * GM_BN; i += NTH) {
         const int mm = mlo + i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
         if (n >= a.N) continue;
         const float v = tile[mm * GM_EPI_LD + nn];
@@ -526,7 +572,7 @@ constexpr size_t gemm_tc_smem_bytes() {
 
 
 template <int NT>
-__global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the swizzle atoms need 1024-byte aligned stage buffers
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -564,11 +610,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     // the weight words of the first PF stages do not depend on earlier kernels: request them
     // before waiting for the previous kernel of the step
     constexpr int PF = GM_WPF;
-    const int wr = tid >> 1, wj = tid & 1;
-    uint32_t wbuf[PF][9];  // weight words of stage kc in slot kc % PF
+    // thread: weight row wr, 16-weight piece wjh (block wjh >> 1, half wjh & 1) of each stage
+    const int wr = tid >> 2, wjh = tid & 3;
+    uint32_t wbuf[PF][6];  // weight words of stage kc in slot kc % PF
 #pragma unroll
     for (int u = 0; u < PF; ++u)
-        if (u < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + u, wj);
+        if (u < nk) gm_load_w16(wbuf[u], a, n0 + wr, kb + u, wjh);
     pdl_trigger();
     pdl_wait();
 
@@ -577,16 +624,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     // activations of stage kc: 16-byte cp.async chunks.  Thread t copies chunk c = t % 8 of
     // rows r = t / 8 + 32 i; r % 8 (its swizzle row) and c are fixed per thread, so source
     // and destination advance by constant strides.
-    const int xc = tid & 7, xr0 = tid >> 3;
+    const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0 + 64 i
     const uint32_t xdst0 = kint_off(xr0, 8 * xc);
     auto load_x = [&](int s, int kc) {
-        static_assert(NT % 32 == 0, "rows per copy pass");
+        static_assert(NT % 64 == 0, "rows per copy pass");
 #pragma unroll
         for (int pl = 0; pl < 2; ++pl) {
             const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + xr0) * a.K + (size_t)kc * GM_BK + 8 * xc;
             uint8_t* dst = (pl ? xl(s) : xh(s)) + xdst0;
 #pragma unroll 4
-            for (int i = 0; i < NT / 32; ++i) cp_async16(dst + 4096 * i, src + (size_t)32 * i * a.K);
+            for (int i = 0; i < NT / 64; ++i) cp_async16(dst + 8192 * i, src + (size_t)64 * i * a.K);
         }
         cp_async_commit();
     };
@@ -609,8 +656,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
                 const int s = kc & 1;
                 // dequantise the held weight words into stage s (free: its previous MMAs
                 // completed before load_x refilled it)
-                gm_dequant_h2(wbuf[u], wj, wscale, wh(s), wl(s), KintRow{wr, 32 * wj});
-                if (kc + PF < nk) gm_load_w(wbuf[u], a, n0 + wr, kb + kc + PF, wj);
+                if (wjh < 2) gm_dequant16_t<0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
+                else gm_dequant16_t<1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
+                if (kc + PF < nk) gm_load_w16(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
                 cp_async_wait_all();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
                 __syncthreads();
@@ -654,8 +702,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     __syncthreads();
     {
         const int row = 32 * (warp & 3) + lane;           // weight row of this thread's TMEM lane
-        const int c0 = (warp >> 2) * (NT / 2);             // warps 4-7 take the upper columns
-        for (int c = c0; c < c0 + NT / 2; c += 16) {
+        const int c0 = (warp >> 2) * (NT / 4);             // four column groups of warps
+        for (int c = c0; c < c0 + NT / 4; c += 16) {
             uint32_t r[16];
             tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
@@ -672,7 +720,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_tc_kernel(const GemmArg
     // with k splits the cluster's barriers are kept even after an error (gemm_epilogue returns
     // after them); without, the error word holds the failure
     if (!ok && gridDim.z == 1) return;
-    gemm_epilogue<NT, true>(a, tile, m0, n0, ok);
+    gemm_epilogue<NT, true, GM_TC_THREADS>(a, tile, m0, n0, ok);
 }
 
 // ---- end of a step at M rows ------------------------------------------------------------------
@@ -775,7 +823,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         // shared memory)
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks);
-        cfg.blockDim = dim3(GM_THREADS);
+        cfg.blockDim = dim3(GM_TC_THREADS);
         cfg.dynamicSmemBytes = sm;
         cfg.stream = st;
         cudaLaunchAttribute attr[2];

@@ -19,6 +19,7 @@ constexpr int GM_BN = 128;      // weight rows per CTA
 constexpr int GM_BM = 128;      // activation rows per CTA
 constexpr int GM_BK = 64;       // k per pipeline stage (two Q8_0 blocks)
 constexpr int GM_THREADS = 256; // 8 warps: 4 along n x 2 along m (warp tile 32 n x 64 m)
+constexpr int GM_TC_THREADS = 512;  // tcgen05 kernel: 4 threads per weight row (16 weights each)
 constexpr int GM_LDS = GM_BK + 8;  // shared row stride in halves (144 B: ldmatrix conflict-free)
 constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
 constexpr int GM_WPF = 4;       // tcgen05 GEMM: weight stages in flight per thread (registers)
