@@ -258,21 +258,33 @@ static inline size_t attn_stream_smem_bytes(int hd) {
     return m > comb ? m : comb;
 }
 
+template <int R>  // query heads per kv head
 __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) float kvt[];
-    __shared__ __align__(16) float qs[AT_MAX_REP][AT_MAX_HD];
-    __shared__ float red[AS_THREADS / 32][AT_MAX_REP][AS_TILE];  // partial scores per dim slice
-    __shared__ __align__(16) float ep[AS_TILE][8];                // exp(score - max), [position][head]
+    __shared__ __align__(16) float qs[R][AT_MAX_HD];
+    __shared__ float red[AS_THREADS / 32][R][AS_TILE];  // partial scores per dim slice
+    __shared__ __align__(16) float ep[AS_TILE][8];       // exp(score - max), [position][head]
     __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
     __shared__ __align__(16) float al_s[8];
-    __shared__ float mx_s[AT_MAX_REP], l_s[AT_MAX_REP];
+    __shared__ float mx_s[R], l_s[R];
     __shared__ __align__(8) uint64_t full[AS_NB];
 
-    pdl_trigger();
-    pdl_wait();
     const int kvh = blockIdx.x, split = blockIdx.y, m = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv, kst = hd + 4, cpw = hd / 32;
+    // set-up that depends on no earlier kernel
+    if (tid == 0) {
+        for (int b = 0; b < AS_NB; ++b) mbar_init(&full[b], 1);
+        mbar_fence_init();
+    }
+    if (tid < R) {
+        mx_s[tid] = -INFINITY;
+        l_s[tid] = 0.f;
+    }
+    if (tid < 8) al_s[tid] = 0.f;
+    __syncthreads();
+    pdl_trigger();
+    pdl_wait();
+    const int hd = a.hd, d2 = hd / 2, kst = hd + 4, cpw = hd / 32;
     const int slot = a.slots ? a.slots[m] : 0;
     const int pos = a.fresh == 2 ? a.pos[slot] + m : (a.fresh ? a.pos[slot] : a.n_pos_fixed - 1);
     if (a.fresh && (pos < 0 || pos >= a.cap)) {
@@ -308,47 +320,43 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
         if (lane == 0 && qc)
             bulk_g2s(vbuf + (size_t)b * AS_TILE * hd, vc + (size_t)q0 * hd, (uint32_t)(qc * hd * 4), &full[b]);
     };
-    if (tid == 0) {
-        for (int b = 0; b < AS_NB; ++b) mbar_init(&full[b], 1);
-        mbar_fence_init();
-    }
-    __syncthreads();
     if (warp == IW) {
         issue(0);
         if (n_tiles > 1) issue(1);
     }
-    // query heads of the group (and the new k/v), rotated for a decode step
-    for (int i = tid; i < n_rep * hd; i += AS_THREADS) qs[i / hd][i % hd] = row[(size_t)kvh * n_rep * hd + i];
-    if (a.fresh == 1)
-        for (int i = tid; i < hd; i += AS_THREADS) {
-            kn[i] = row[(size_t)a.n_head * hd + (size_t)kvh * hd + i];
-            vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
-        }
-    if (tid < AT_MAX_REP) {
-        mx_s[tid] = -INFINITY;
-        l_s[tid] = 0.f;
-    }
-    if (tid < 8) al_s[tid] = 0.f;
-    __syncthreads();
-    if (a.fresh == 1) {
+    // the group's query heads and the new key, rotated for a decode step (q, k, cos, sin in one
+    // round of loads), and the new value
+    {
         const float* cp = a.cosb + (size_t)pos * d2;
         const float* sp = a.sinb + (size_t)pos * d2;
-        for (int i = tid; i < (n_rep + 1) * d2; i += AS_THREADS) {
+        for (int i = tid; i < (R + 1) * d2; i += AS_THREADS) {
             const int h = i / d2, j = i % d2;
-            if (h < n_rep) rope_pair(qs[h][j], qs[h][j + d2], cp[j], sp[j]);
-            else rope_pair(kn[j], kn[j + d2], cp[j], sp[j]);
-        }
-        __syncthreads();
-        if (split == 0)
-            for (int i = tid; i < hd; i += AS_THREADS) {
-                kv_store(a.kc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, kn[i]);
-                kv_store(a.vc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, vn[i]);
+            const float* src = h < R ? row + (size_t)(kvh * R + h) * hd : row + (size_t)a.n_head * hd + (size_t)kvh * hd;
+            float x0 = src[j], x1 = src[j + d2];
+            if (a.fresh == 1) rope_pair(x0, x1, cp[j], sp[j]);
+            if (h < R) {
+                qs[h][j] = x0;
+                qs[h][j + d2] = x1;
+            } else {
+                kn[j] = x0;
+                kn[j + d2] = x1;
             }
+        }
+        if (a.fresh == 1)
+            for (int i = tid; i < hd; i += AS_THREADS) vn[i] = row[(size_t)(a.n_head + a.n_kv) * hd + (size_t)kvh * hd + i];
     }
+    __syncthreads();
+    if (a.fresh == 1 && split == 0)
+        for (int i = tid; i < hd; i += AS_THREADS) {
+            kv_store(a.kc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, kn[i]);
+            kv_store(a.vc, (long long)(cache_off + (size_t)pos * hd + i), a.kv_type, vn[i]);
+        }
     const float scale = 1.0f / sqrtf((float)hd);
-    float acc[AT_MAX_REP][4];
+    // P.V accumulators: head pairs (2hp, 2hp + 1) packed per dim, RP pairs x 4 dims
+    constexpr int RP = (R + 1) / 2;
+    float2 acc[RP][4];
 #pragma unroll
-    for (int h = 0; h < AT_MAX_REP; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = 0.f;
+    for (int h = 0; h < RP; ++h) acc[h][0] = acc[h][1] = acc[h][2] = acc[h][3] = make_float2(0.f, 0.f);
     const bool pv_lane = lane < hd / 4;
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
@@ -364,33 +372,30 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
             __syncthreads();
         }
         {   // partial scores of this warp's dim slice (attn_decode, src/attention.cpp:63-64)
-            float sp[AT_MAX_REP];
+            // packed fp32 pairs (even, odd dims), summed at the end
+            float2 sp[R];
 #pragma unroll
-            for (int h = 0; h < AT_MAX_REP; ++h) sp[h] = 0.f;
+            for (int h = 0; h < R; ++h) sp[h] = make_float2(0.f, 0.f);
             if (lane < qn) {
                 const float4* kr = reinterpret_cast<const float4*>(ks + (size_t)lane * kst) + warp * cpw;
                 for (int c = 0; c < cpw; ++c) {
                     const float4 k4 = kr[c];
+                    const float2 k01 = make_float2(k4.x, k4.y), k23 = make_float2(k4.z, k4.w);
 #pragma unroll
-                    for (int h = 0; h < AT_MAX_REP; ++h) {
-                        if (h < n_rep) {
-                            const float4 q4 = reinterpret_cast<const float4*>(qs[h])[warp * cpw + c];
-                            sp[h] = fmaf(q4.x, k4.x, sp[h]);
-                            sp[h] = fmaf(q4.y, k4.y, sp[h]);
-                            sp[h] = fmaf(q4.z, k4.z, sp[h]);
-                            sp[h] = fmaf(q4.w, k4.w, sp[h]);
-                        }
+                    for (int h = 0; h < R; ++h) {
+                        const float4 q4 = reinterpret_cast<const float4*>(qs[h])[warp * cpw + c];
+                        sp[h] = __ffma2_rn(make_float2(q4.x, q4.y), k01, sp[h]);
+                        sp[h] = __ffma2_rn(make_float2(q4.z, q4.w), k23, sp[h]);
                     }
                 }
             }
 #pragma unroll
-            for (int h = 0; h < AT_MAX_REP; ++h)
-                if (h < n_rep) red[warp][h][lane] = sp[h];
+            for (int h = 0; h < R; ++h) red[warp][h][lane] = sp[h].x + sp[h].y;
         }
         __syncthreads();
         // every thread has finished tile t - 1's P.V: its buffer takes tile t + 2
         if (warp == IW && t + 2 < n_tiles) issue(t + 2);
-        if (warp < n_rep) {  // running max and sum of head `warp`
+        if (warp < R) {  // running max and sum of head `warp`
             const int h = warp;
             float sv = -INFINITY;
             if (lane < qn) {
@@ -415,24 +420,29 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
         __syncthreads();
         if (pv_lane) {  // weighted V over positions warp, warp + 8, ...
             const float4 a0 = reinterpret_cast<const float4*>(al_s)[0], a1 = reinterpret_cast<const float4*>(al_s)[1];
-            const float al[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float2 alp[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w), make_float2(a1.x, a1.y),
+                                   make_float2(a1.z, a1.w)};
 #pragma unroll
-            for (int h = 0; h < AT_MAX_REP; ++h) {
-                acc[h][0] *= al[h];
-                acc[h][1] *= al[h];
-                acc[h][2] *= al[h];
-                acc[h][3] *= al[h];
+            for (int h = 0; h < RP; ++h) {
+                acc[h][0] = __fmul2_rn(acc[h][0], alp[h]);
+                acc[h][1] = __fmul2_rn(acc[h][1], alp[h]);
+                acc[h][2] = __fmul2_rn(acc[h][2], alp[h]);
+                acc[h][3] = __fmul2_rn(acc[h][3], alp[h]);
             }
             for (int p = warp; p < qn; p += AS_THREADS / 32) {
                 const float4 v4 = reinterpret_cast<const float4*>(vs + (size_t)p * hd)[lane];
-                const float4 e0 = reinterpret_cast<const float4*>(ep[p])[0], e1 = reinterpret_cast<const float4*>(ep[p])[1];
-                const float e[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+                const float4 e0 = reinterpret_cast<const float4*>(ep[p])[0];
+                const float4 e1 = R > 4 ? reinterpret_cast<const float4*>(ep[p])[1] : e0;
+                const float2 ep2[4] = {make_float2(e0.x, e0.y), make_float2(e0.z, e0.w), make_float2(e1.x, e1.y),
+                                       make_float2(e1.z, e1.w)};
+                const float2 vx = make_float2(v4.x, v4.x), vy = make_float2(v4.y, v4.y);
+                const float2 vz = make_float2(v4.z, v4.z), vw = make_float2(v4.w, v4.w);
 #pragma unroll
-                for (int h = 0; h < AT_MAX_REP; ++h) {
-                    acc[h][0] = fmaf(e[h], v4.x, acc[h][0]);
-                    acc[h][1] = fmaf(e[h], v4.y, acc[h][1]);
-                    acc[h][2] = fmaf(e[h], v4.z, acc[h][2]);
-                    acc[h][3] = fmaf(e[h], v4.w, acc[h][3]);
+                for (int h = 0; h < RP; ++h) {
+                    acc[h][0] = __ffma2_rn(ep2[h], vx, acc[h][0]);
+                    acc[h][1] = __ffma2_rn(ep2[h], vy, acc[h][1]);
+                    acc[h][2] = __ffma2_rn(ep2[h], vz, acc[h][2]);
+                    acc[h][3] = __ffma2_rn(ep2[h], vw, acc[h][3]);
                 }
             }
         }
@@ -442,18 +452,21 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
     float* fin = kvt;  // [warp][head][hd]
     if (pv_lane)
 #pragma unroll
-        for (int h = 0; h < AT_MAX_REP; ++h)
-            if (h < n_rep)
-                reinterpret_cast<float4*>(fin + ((size_t)warp * AT_MAX_REP + h) * hd)[lane] =
-                    make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        for (int h = 0; h < R; ++h) {
+            const int hp = h >> 1;
+            const bool odd = h & 1;
+            reinterpret_cast<float4*>(fin + ((size_t)warp * R + h) * hd)[lane] =
+                odd ? make_float4(acc[hp][0].y, acc[hp][1].y, acc[hp][2].y, acc[hp][3].y)
+                    : make_float4(acc[hp][0].x, acc[hp][1].x, acc[hp][2].x, acc[hp][3].x);
+        }
     __syncthreads();
     if (ok)
-        for (int i = tid; i < n_rep * hd; i += AS_THREADS) {
+        for (int i = tid; i < R * hd; i += AS_THREADS) {
             const int h = i / hd, d = i % hd;
             float o = 0.f;
 #pragma unroll
-            for (int w = 0; w < AS_THREADS / 32; ++w) o += fin[((size_t)w * AT_MAX_REP + h) * hd + d];
-            const int head = kvh * n_rep + h;
+            for (int w = 0; w < AS_THREADS / 32; ++w) o += fin[((size_t)w * R + h) * hd + d];
+            const int head = kvh * R + h;
             if (nsp == 1) {
                 a.out[(size_t)m * a.ld_out + (size_t)head * hd + d] = o / l_s[h];
             } else {
@@ -596,19 +609,24 @@ static int attn_stream_splits(const AttnArgs& a, int M) {
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
     if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
     if (a.kv_type == KV_F32 && M * a.n_kv >= 16 && a.hd % 32 == 0) {  // many rows: streaming kernel
-        static bool sattr[64] = {false};
+        static const void* const fns[AT_MAX_REP] = {
+            (const void*)attn_stream_kernel<1>, (const void*)attn_stream_kernel<2>, (const void*)attn_stream_kernel<3>,
+            (const void*)attn_stream_kernel<4>, (const void*)attn_stream_kernel<5>, (const void*)attn_stream_kernel<6>,
+            (const void*)attn_stream_kernel<7>, (const void*)attn_stream_kernel<8>};
+        const int R = a.n_head / a.n_kv;
+        const void* fn = fns[R - 1];
+        static bool sattr[64][AT_MAX_REP] = {};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 0 || dev >= 64) dev = 0;
-        if (!sattr[dev]) {
-            cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (!sattr[dev][R - 1]) {
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  (int)attn_stream_smem_bytes(AT_MAX_HD));
             if (e != cudaSuccess) return e;
             // two CTAs per SM need the whole shared-memory carve-out
-            e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     cudaSharedmemCarveoutMaxShared);
+            e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
-            sattr[dev] = true;
+            sattr[dev][R - 1] = true;
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(a.n_kv, attn_stream_splits(a, M), M);
@@ -620,7 +638,9 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
         attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, attn_stream_kernel, a);
+        AttnArgs aa = a;
+        void* args[] = {&aa};
+        return cudaLaunchKernelExC(&cfg, fn, args);
     }
     const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;
     if ((max_pos + a.n_split - 1) / a.n_split > AT_CHUNK || a.n_split > AT_MAX_SPLIT) return cudaErrorInvalidValue;
