@@ -433,7 +433,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -454,7 +454,25 @@ def main():
         for _ in range(2):
             t = int(np.argmax(m.decode(t)))
         m.close()
-        print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 5 + 1, "last_token": t}))
+        print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 4 + 1, "last_token": t}))
+        return
+    if args.kernel == "bstep":
+        # one cfg4 batched decode step (128 rows at context ~530) between cudaProfilerStart /
+        # Stop, for a launch list under `ncu --profile-from-start off`
+        import torch
+        from tinferno_b200.model import Model, RunConfig
+        S, P = 128, 512
+        m = Model(synth.model_path(synth.CFG4), RunConfig(max_seq=P + 16, max_batch=S))
+        prompts = np.stack([synth.prompt_tokens(synth.CFG4, P, stream=1000 + g) for g in range(S)])
+        tok = m.prefill_batch(list(range(S)), prompts)
+        tok = m.decode_batch(list(range(S)), tok.tolist())
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        tok = m.decode_batch(list(range(S)), tok.tolist())
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        m.close()
+        print(json.dumps({"kernel": "bstep", "rows": S, "context": P + 2, "first_ids": [int(v) for v in tok[:4]]}))
         return
     if args.warmup < 3:
         args.warmup = 3
