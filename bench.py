@@ -40,7 +40,7 @@ CFG = synth.CFG0
 PROMPT = 32
 # DRAM bytes (read + write) of one lm_head GEMV launch, from an ncu capture of
 # `bench.py --kernel lmhead` (profiles/gemv_q8_0_lmhead_128256x2048.md)
-LMHEAD_TRAFFIC = 284_945_408
+LMHEAD_TRAFFIC = 283_513_088
 
 
 def peaks():
