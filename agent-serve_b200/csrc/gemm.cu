@@ -131,12 +131,18 @@ __device__ __forceinline__ void gm_load_w(uint32_t (&w)[9], const GemmArgs& a, i
 // kc, 16-weight piece jh = 2 * block + half: w[0] holds the block's fp16 scale (word 0 or 8 of
 // the stage's 68-byte unit), w[1..5] the five words 4*jh .. 4*jh + 4 (bytes 16*jh .. 16*jh +
 // 19), whose bytes 2 * block + 2 .. + 17 are the piece's 16 quants.
+// Q4_0 (Q4): the stage's 36-byte unit holds two 18-byte blocks; both halves of block j read
+// the five words 4j .. 4j + 4, whose first word carries the block's scale (low half for block
+// 0, high half for block 1) and whose bytes 2j + 2 .. + 17 are its 16 quant bytes (weight i
+// in the low nibble of byte i, weight 16 + i in the high nibble).
+template <bool Q4>
 __device__ __forceinline__ void gm_load_w16(uint32_t (&w)[6], const GemmArgs& a, int n, int kc, int jh) {
     if (n < a.N) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(a.W + (long long)n * a.rb + (long long)kc * 68);
-        w[0] = __ldg(p + 8 * (jh >> 1));
+        const uint32_t* p = reinterpret_cast<const uint32_t*>(a.W + (long long)n * a.rb + (long long)kc * (Q4 ? 36 : 68));
+        const int w0 = Q4 ? 4 * (jh >> 1) : 4 * jh;
+        w[0] = __ldg(p + (Q4 ? w0 : 8 * (jh >> 1)));
 #pragma unroll
-        for (int i = 0; i < 5; ++i) w[1 + i] = __ldg(p + 4 * jh + i);
+        for (int i = 0; i < 5; ++i) w[1 + i] = __ldg(p + w0 + i);
     } else {
 #pragma unroll
         for (int i = 0; i < 6; ++i) w[i] = 0u;
@@ -207,6 +213,37 @@ __device__ __forceinline__ void gm_dequant16_t(const uint32_t (&w)[6], float wsc
             const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
             const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
             const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
+            const __half2 hi = __hmul2(q2, d2);
+            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
+            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
+            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
+        }
+        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    }
+}
+
+// Q4_0 piece (block J, nibble half H) from gm_load_w16<true>'s words: q = nibble - 8 made
+// exact in f16 as (0x6400 | nibble) - 1032, then the same exact Wh / Wl split (|q| <= 8, so
+// q * dh has at most 15 significant bits and Wl at most 4).
+template <int J, int H, class Off>
+__device__ __forceinline__ void gm_dequant16_q4_t(const uint32_t (&w)[6], float wscale, uint8_t* dh, uint8_t* dl,
+                                                  Off hoff) {
+    const uint32_t dbits = J == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+    const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
+    const __half2 d2 = __halves2half2(dsc, dsc);
+    const __half2 k1032 = __halves2half2(__ushort_as_half((unsigned short)0x6408u), __ushort_as_half((unsigned short)0x6408u));
+    constexpr int b0 = 2 * J + 2;  // first quant byte within the five window words (even)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const int b = b0 + 8 * c + e;
+            const uint32_t wd = H ? ((w[1 + (b >> 2)] >> 4) & 0x0F0F0F0Fu) : (w[1 + (b >> 2)] & 0x0F0F0F0Fu);
+            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
+            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
+            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1032);
             const __half2 hi = __hmul2(q2, d2);
             const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
             hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
@@ -571,7 +608,7 @@ constexpr size_t gemm_tc_smem_bytes() {
 }
 
 
-template <int NT>
+template <int NT, bool Q4>
 __global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the swizzle atoms need 1024-byte aligned stage buffers
@@ -615,7 +652,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const Gemm
     uint32_t wbuf[PF][6];  // weight words of stage kc in slot kc % PF
 #pragma unroll
     for (int u = 0; u < PF; ++u)
-        if (u < nk) gm_load_w16(wbuf[u], a, n0 + wr, kb + u, wjh);
+        if (u < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + u, wjh);
     pdl_trigger();
     pdl_wait();
 
@@ -656,9 +693,16 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const Gemm
                 const int s = kc & 1;
                 // dequantise the held weight words into stage s (free: its previous MMAs
                 // completed before load_x refilled it)
-                if (wjh < 2) gm_dequant16_t<0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
-                else gm_dequant16_t<1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
-                if (kc + PF < nk) gm_load_w16(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
+                if constexpr (Q4) {
+                    if (wjh == 0) gm_dequant16_q4_t<0, 0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 0});
+                    else if (wjh == 1) gm_dequant16_q4_t<0, 1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16});
+                    else if (wjh == 2) gm_dequant16_q4_t<1, 0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 32});
+                    else gm_dequant16_q4_t<1, 1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 48});
+                } else {
+                    if (wjh < 2) gm_dequant16_t<0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
+                    else gm_dequant16_t<1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
+                }
+                if (kc + PF < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
                 cp_async_wait_all();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
                 __syncthreads();
@@ -808,15 +852,17 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         void* args[] = {&aa};
         const bool wide = gemm_tile_rows(a.M) == 256;
         const size_t sm = wide ? gemm_tc_smem_bytes<256>() : gemm_tc_smem_bytes<128>();
-        const void* fn = wide ? (const void*)gemm_q8_tc_kernel<256> : (const void*)gemm_q8_tc_kernel<128>;
-        static bool tc_attr[64][2] = {};
+        const bool q4 = a.wq4 != 0;
+        const void* fn = q4 ? (wide ? (const void*)gemm_q8_tc_kernel<256, true> : (const void*)gemm_q8_tc_kernel<128, true>)
+                            : (wide ? (const void*)gemm_q8_tc_kernel<256, false> : (const void*)gemm_q8_tc_kernel<128, false>);
+        static bool tc_attr[64][2][2] = {};
         int dv = 0;
         cudaGetDevice(&dv);
         if (dv < 0 || dv >= 64) dv = 0;
-        if (!tc_attr[dv][wide]) {
+        if (!tc_attr[dv][wide][q4]) {
             cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
             if (e != cudaSuccess) return e;
-            tc_attr[dv][wide] = true;
+            tc_attr[dv][wide][q4] = true;
         }
         const int nt = wide ? 256 : 128;
         // the k splits of a tile form one cluster (their reduction goes through distributed
@@ -837,6 +883,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         cfg.numAttrs = 2;
         return cudaLaunchKernelExC(&cfg, fn, args);
     }
+    if (a.wq4) return cudaErrorInvalidValue;  // the mma.sync kernel reads Q8_0 blocks only
     dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
     GemmArgs aa = a;
     void* args[] = {&aa};
@@ -851,10 +898,10 @@ cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {
 
 // Device version of q8_scale_exponent for weights that live only on the device: the largest
 // |d| bits over all blocks (one pass over the scale bytes).
-__global__ void q8_dmax_kernel(const uint8_t* W, long long n_blocks, unsigned* out) {
+__global__ void q8_dmax_kernel(const uint8_t* W, long long n_blocks, int block_bytes, unsigned* out) {
     unsigned mx = 0;
     for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
-        const unsigned d = ((unsigned)W[b * 34] | ((unsigned)W[b * 34 + 1] << 8)) & 0x7FFFu;
+        const unsigned d = ((unsigned)W[b * block_bytes] | ((unsigned)W[b * block_bytes + 1] << 8)) & 0x7FFFu;
         mx = d > mx ? d : mx;
     }
     mx = warp_max_u(mx);
@@ -867,10 +914,11 @@ int q8_exponent_from_dbits(unsigned mx) {
     return 21 - E;
 }
 
-cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st) {
+cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st,
+                                     int block_bytes) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(unsigned), st);
     if (e != cudaSuccess) return e;
-    q8_dmax_kernel<<<296, 256, 0, st>>>(W, n_blocks, scratch);
+    q8_dmax_kernel<<<296, 256, 0, st>>>(W, n_blocks, block_bytes, scratch);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     unsigned h = 0;
     if ((e = cudaMemcpyAsync(&h, scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;

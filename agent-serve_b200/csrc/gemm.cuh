@@ -44,7 +44,8 @@ struct XPrepArgs {
 };
 
 struct GemmArgs {
-    const uint8_t* W;     // Q8_0 rows
+    const uint8_t* W;     // Q8_0 rows (Q4_0 rows when wq4)
+    int wq4;              // 1: Q4_0 weights (18-byte blocks) on the tcgen05 path
     long long rb;
     int N, K, M;
     int sw;               // weight scale exponent
@@ -107,6 +108,7 @@ cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st);
 int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes);  // per-matrix sw
 int q8_exponent_from_dbits(unsigned max_abs_d_bits);
 // sw of device-resident Q8_0 blocks (synchronises `st`); scratch: one device unsigned
-cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st);
+cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st,
+                                     int block_bytes = 34);  // 18 for Q4_0 blocks
 
 }  // namespace tfb

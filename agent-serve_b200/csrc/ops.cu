@@ -51,7 +51,11 @@ int tf_op_q8_scale(const void* W, int N, int K, int* sw, void* stream) {
     return rc;
 }
 
-int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, int M, int sw, void* stream) {
+}  // extern "C"
+
+namespace {
+// C = A W^T on the tcgen05 GEMM for Q8_0 or Q4_0 weights (t), with the matrix scale sw.
+int matmul_tc(float* C, const float* A, int t, const void* W, int N, int K, int M, int sw, void* stream) {
     if (N <= 0 || K <= 0 || M < GM_MIN_M || K % GM_BK) return set_error("tensor-core GEMM needs M >= 16 and K % 64 == 0");
     if ((reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(W) & 3))
         return set_error("A must be 16-byte and W 4-byte aligned");
@@ -93,7 +97,8 @@ int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, in
         GemmArgs g;
         memset(&g, 0, sizeof(g));
         g.W = static_cast<const uint8_t*>(W);
-        g.rb = row_bytes(T_Q8_0, K);
+        g.rb = row_bytes(t, K);
+        g.wq4 = t == T_Q4_0 ? 1 : 0;
         g.N = N;
         g.K = K;
         g.M = M;
@@ -116,6 +121,32 @@ int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, in
     return rc;
 }
 
+}  // namespace
+
+extern "C" {
+
+int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, int M, int sw, void* stream) {
+    return matmul_tc(C, A, T_Q8_0, W, N, K, M, sw, stream);
+}
+
+int tf_op_weight_scale(const void* W, int t, int N, int K, int* sw, void* stream) {
+    if (t != T_Q8_0 && t != T_Q4_0) return set_error("tensor-core path takes Q8_0 or Q4_0 weights");
+    if (!W || !sw || N <= 0 || K <= 0 || K % 32) return set_error("bad weight matrix");
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    unsigned* scratch = nullptr;
+    if (op_status(cudaMallocAsync((void**)&scratch, sizeof(unsigned), st), "alloc")) return -1;
+    const int rc = op_status(q8_scale_exponent_device(static_cast<const uint8_t*>(W), (long long)N * (K / 32), scratch,
+                                                      sw, st, t == T_Q8_0 ? 34 : 18),
+                             "weight_scale");
+    cudaFreeAsync(scratch, st);
+    return rc;
+}
+
+int tf_op_matmul_tc(float* C, const float* A, int t, const void* W, int N, int K, int M, int sw, void* stream) {
+    if (t != T_Q8_0 && t != T_Q4_0) return set_error("tensor-core path takes Q8_0 or Q4_0 weights");
+    return matmul_tc(C, A, t, W, N, K, M, sw, stream);
+}
+
 int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, int M, void* stream) {
     if (!type_ok(t)) return set_error("unsupported ggml type");
     if (N <= 0 || K <= 0 || M < 0) return set_error("bad matmul shape");
@@ -123,11 +154,11 @@ int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, i
     if (M == 0) return 0;
     if (t == T_F32 && (reinterpret_cast<uintptr_t>(W) & 3)) return set_error("F32 weights must be 4-byte aligned");
     if (reinterpret_cast<uintptr_t>(A) & 15) return set_error("A must be 16-byte aligned");
-    if (t == T_Q8_0 && M >= GM_MIN_M && K % GM_BK == 0 && !(reinterpret_cast<uintptr_t>(W) & 3)) {
+    if ((t == T_Q8_0 || t == T_Q4_0) && M >= GM_MIN_M && K % GM_BK == 0 && !(reinterpret_cast<uintptr_t>(W) & 3)) {
         // M >= 16: the tensor-core GEMM (scale of the matrix, then the GEMM)
         int sw = 0;
-        if (tf_op_q8_scale(W, N, K, &sw, stream)) return -1;
-        return tf_op_matmul_q8_tc(C, A, W, N, K, M, sw, stream);
+        if (tf_op_weight_scale(W, t, N, K, &sw, stream)) return -1;
+        return matmul_tc(C, A, t, W, N, K, M, sw, stream);
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     int* err = nullptr;

@@ -69,6 +69,8 @@ SIGNATURES = [
     ("tf_op_attn_decode", C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_q8_scale", C.c_int, [_V, C.c_int, C.c_int, i32p, _V]),
     ("tf_op_matmul_q8_tc", C.c_int, [_V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
+    ("tf_op_weight_scale", C.c_int, [_V, C.c_int, C.c_int, C.c_int, i32p, _V]),
+    ("tf_op_matmul_tc", C.c_int, [_V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_attn_decode_noalloc", C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_attn_prefill", C.c_int, [_V, _V, _V, _V, C.c_int, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_argmax", C.c_int, [_V, C.c_int, C.c_int, _V, _V]),

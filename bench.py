@@ -370,8 +370,8 @@ def matmul_sweep():
     """BASELINE cfg3: Y[M,N] = X[M,K] W[N,K]^T for Q8_0 and Q4_0 weights (N(0, 0.02) quantised),
     X ~ N(0, 1); K=2048 with N in {512, 2048, 8192, 128256}, K=8192 with N=2048; M in
     {1, 8, 64, 512}.  Weight copies rotate so that every timed launch reads its weights from
-    HBM (the rotation exceeds the 126 MB L2).  M <= 8 runs the dequant-GEMV, Q8_0 at M >= 16
-    the tensor-core GEMM (timed without the one-off scale pass), Q4_0 at M >= 16 GEMV tiles."""
+    HBM (the rotation exceeds the 126 MB L2).  M <= 8 runs the dequant-GEMV, M >= 16 the
+    tensor-core GEMM for both types (timed without the one-off scale pass of the matrix)."""
     import torch
     from tinferno_b200 import gguf, native, quants
     L = native.lib()
@@ -387,18 +387,17 @@ def matmul_sweep():
             copies = max(1, int(np.ceil(256e6 / nbytes)))
             W = [torch.from_numpy(raw).cuda() for _ in range(min(copies, 512))]
             sw = C.c_int(0)
-            if t == gguf.GGML_Q8_0:
-                native.check(L.tf_op_q8_scale(C.c_void_p(W[0].data_ptr()), N, K, C.byref(sw), C.c_void_p(st.cuda_stream)))
+            native.check(L.tf_op_weight_scale(C.c_void_p(W[0].data_ptr()), t, N, K, C.byref(sw), C.c_void_p(st.cuda_stream)))
             for M in (1, 8, 64, 512):
                 X = torch.randn(M, K, device="cuda")
                 Y = torch.empty(M, N, device="cuda")
-                tc = t == gguf.GGML_Q8_0 and M >= 16
+                tc = M >= 16
 
                 def run(i):
                     wp = C.c_void_p(W[i % len(W)].data_ptr())
                     if tc:
-                        native.check(L.tf_op_matmul_q8_tc(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), wp, N, K, M,
-                                                          sw.value, C.c_void_p(st.cuda_stream)))
+                        native.check(L.tf_op_matmul_tc(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), t, wp, N, K,
+                                                       M, sw.value, C.c_void_p(st.cuda_stream)))
                     else:
                         native.check(L.tf_op_matmul(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), t, wp, N, K, M,
                                                     C.c_void_p(st.cuda_stream)))
@@ -433,7 +432,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -455,6 +454,35 @@ def main():
             t = int(np.argmax(m.decode(t)))
         m.close()
         print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 4 + 1, "last_token": t}))
+        return
+    if args.kernel == "gemm":
+        # the cfg4 gate/up GEMM of a 256-row batched step (N = 2 x 8960, K = 1536), Q8_0,
+        # 1 warm-up + 3 launches through tf_op_matmul_tc (for an ncu capture of launch 2)
+        import torch
+        from tinferno_b200 import gguf, native, quants
+        L = native.lib()
+        N, K, M = 17920, 1536, 256
+        rng = np.random.default_rng(7)
+        raw = np.ascontiguousarray(quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
+                                                   gguf.GGML_Q8_0)).reshape(-1)
+        W = torch.from_numpy(raw).cuda()
+        X = torch.randn(M, K, device="cuda")
+        Y = torch.empty(M, N, device="cuda")
+        st = torch.cuda.current_stream()
+        sw = C.c_int(0)
+        native.check(L.tf_op_weight_scale(C.c_void_p(W.data_ptr()), gguf.GGML_Q8_0, N, K, C.byref(sw),
+                                          C.c_void_p(st.cuda_stream)))
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for i in range(4):
+            if i == 3:
+                ev[0].record(st)
+            native.check(L.tf_op_matmul_tc(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), gguf.GGML_Q8_0,
+                                           C.c_void_p(W.data_ptr()), N, K, M, sw.value, C.c_void_p(st.cuda_stream)))
+        ev[1].record(st)
+        torch.cuda.synchronize()
+        us = ev[0].elapsed_time(ev[1]) * 1e3
+        print(json.dumps({"kernel": "gemm", "N": N, "K": K, "M": M, "us_incl_prep": round(us, 2),
+                          "TFLOP_s": round(2 * N * K * M / us / 1e6, 1)}))
         return
     if args.kernel == "bstep":
         # one cfg4 batched decode step (128 rows at context ~530) between cudaProfilerStart /

@@ -148,6 +148,11 @@ TF_API int tf_op_matmul(float* C, const float* A, int ggml_type, const void* W, 
 TF_API int tf_op_q8_scale(const void* W, int N, int K, int* sw, void* stream);
 TF_API int tf_op_matmul_q8_tc(float* C, const float* A, const void* W, int N, int K, int M, int sw,
                               void* stream);
+/* The same two steps for a ggml type t of the tensor-core path (Q8_0 or Q4_0): the scale sw of
+ * the matrix, then C = A W^T at M >= 16 (K % 64 == 0). */
+TF_API int tf_op_weight_scale(const void* W, int t, int N, int K, int* sw, void* stream);
+TF_API int tf_op_matmul_tc(float* C, const float* A, int t, const void* W, int N, int K, int M, int sw,
+                           void* stream);
 
 /* dequant_row(float* out, const Tensor& t, int64_t row)  src/quant.hpp:42: out[i][K] is
  * row rows[i] of W (embedding lookup). */

@@ -67,13 +67,13 @@ def test_matmul(t, shape):
     assert_dot_close(got, want, a, quants.dequant(raw, t, k))
 
 
+@pytest.mark.parametrize("t", [gguf.GGML_Q8_0, gguf.GGML_Q4_0])
 @pytest.mark.parametrize("shape", [(256, 2048, 16), (1000, 2048, 64), (130, 896, 130), (96, 4864, 33),
                                    (2048, 8192, 40), (515, 1536, 300)])
-def test_matmul_tensor_core(shape):
-    """Q8_0 at M >= 16 runs the tensor-core GEMM (f16-split products, fp32 accumulation,
-    split-K when the tiles do not cover the SMs)."""
+def test_matmul_tensor_core(shape, t):
+    """Q8_0 and Q4_0 at M >= 16 run the tensor-core GEMM (f16-split products, fp32
+    accumulation, split-K clusters when the tiles do not cover the SMs)."""
     n, k, m = shape
-    t = gguf.GGML_Q8_0
     rng = np.random.default_rng(k + n + m)
     w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
     raw = np.ascontiguousarray(quants.quantize(w, t))
