@@ -1,14 +1,20 @@
-// Q8_0 GEMM for M >= 16 activation rows on the f16 tensor pipe (see gemm.cuh).
+// Q8_0 / Q4_0 GEMM for M >= 16 activation rows (see gemm.cuh).
 //
-// CTA tile: 128 weight rows x 128 activation rows, k in stages of 64 (two Q8_0 blocks),
-// double-buffered.  Per stage the CTA dequantises its 128 x 64 weights (one thread per row
-// and block: 34 bytes -> 32 exact products q*d*2^sw -> f16 halves Wh, Wl) into shared memory,
-// while the activation halves Xh, Xl (prepared once per matmul by xprep_kernel) arrive by
-// cp.async.  Eight warps each own 32 weight rows x 64 activation rows and issue
-// mma.m16n8k16 (f16 in, f32 accumulate) three times per fragment pair: Wh*Xh, Wh*Xl, Wl*Xh.
-// The epilogue scales back by 2^-(sw+sx[m]), stages the tile in shared memory and applies
-// the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
+// Default path, gemm_q8_tc_kernel (5th-gen tensor cores): a CTA of 512 threads owns 128
+// weight rows x NT (128 or 256) activation rows, k in stages of 64, double-buffered in
+// 128-byte swizzled K-major shared memory.  Four threads per weight row dequantise 16-weight
+// pieces from registers (the words of a stage are requested four stages ahead, the first
+// ones before the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw; the activation halves
+// Xh, Xl (prepared once per matmul by xprep_kernel) arrive by cp.async.  Thread 0 issues
+// tcgen05.mma (kind::f16, fp32 accumulator in TMEM) three times per k step: Wh*Xh, Wh*Xl,
+// Wl*Xh.  The epilogue reads TMEM, scales back by 2^-(sw+sx[m]) (per-column factors computed
+// once), stages the tile in shared memory and, when the k range is split, sums the splits of
+// the tile through distributed shared memory of their thread-block cluster in split order;
+// then the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
+//
+// Comparison path, gemm_q8_kernel (TFB200_GEMM_TC05=0): the same arithmetic on
+// mma.sync.m16n8k16 with 256 threads and a global-workspace split-K reduction.
 #include <cstdlib>
 
 #include "dots.cuh"

@@ -1,9 +1,10 @@
-// Q8_0 GEMM on the tensor cores for M >= 16 activation rows (batched decode, prefill):
-// Y[m][n] = sum_k X[m][k] * W[n][k], W in its GGUF Q8_0 block layout.  Replaces matmul()
+// Q8_0 (and, at op level, Q4_0) GEMM on the tensor cores for M >= 16 activation rows
+// (batched decode, prefill): Y[m][n] = sum_k X[m][k] * W[n][k], W in its GGUF block layout.  Replaces matmul()
 // (src/matmul.cpp:22-73) at M >= 16 together with the rmsnorm / apply_bias / add_inplace /
 // silu_mul / sample_greedy calls around each matmul of Model::layer_decode/layer_prefill.
 //
-// Arithmetic: fp32-equivalent on the f16 tensor pipe.  Every weight q*d (19 significant bits)
+// Arithmetic: fp32-equivalent on the f16 tensor pipe.  Every weight q*d (at most 19
+// significant bits for Q8_0, 15 for Q4_0)
 // is split exactly into two f16 halves Wh + Wl after a per-matrix power-of-two scale 2^sw,
 // and every activation into Xh + Xl after a per-row scale 2^sx; the products Wh*Xh, Wh*Xl and
 // Wl*Xh are accumulated in fp32 (the dropped Wl*Xl term is 2^-22 relative).  The result is
@@ -61,8 +62,9 @@ struct GemmArgs {
     int ldr;
     unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
     int store_logits;          // EPI_ARGMAX: also store the logits in y
-    // split-K (grid.z = ksplit > 1): each split writes its scaled tile to ws[z][M][N]; the last
-    // split of a tile (tile_cnt, reset by it) sums the splits in order and applies the epilogue
+    // split-K (grid.z = ksplit > 1): on the tcgen05 path the splits of a tile are one cluster
+    // and sum through distributed shared memory; on the mma.sync path each split writes its
+    // scaled tile to ws[z][M][N] and the splits meet through tile_cnt (arrivals, departures)
     int ksplit;
     float* ws;
     unsigned* tile_cnt;
