@@ -70,6 +70,26 @@ def test_mini_stream_matches_reference(cfg, mini_models):
     m.close()
 
 
+def test_long_context_crosses_fused_attention_limit(mini_models):
+    """Batch-1 decode across position 1024, where the attention fused into the QKV kernel hands
+    over to the split flash-decode kernel (long-context decode): token-exact and logits within
+    1e-2 of the oracle over a 1016-token prompt (chunked tensor-core prefill) + 16 steps."""
+    cfg = MINI[0]
+    path = mini_models[cfg.name]
+    prompt = synth.prompt_tokens(cfg, 1016, stream=4242)
+    m = Model(path, RunConfig(max_seq=2048))
+    ids, steps = greedy(m, prompt, 16)
+    assert m.n_pos() == 1016 + 16
+    orc = po.OracleModel(gguf.GGUFReader(path), 2048)
+    o_ids, o_steps = po.greedy_stream(orc, prompt, 16, keep_logits=True)
+    assert o_ids == ids
+    err = max(np.abs(a - b).max() for a, b in zip(steps, o_steps))
+    assert err < LOGIT_TOL, err
+    print(f"long context: positions 1016..1031 token-exact, max |logit diff| {err:.2e}")
+    m.close()
+    orc.close()
+
+
 @pytest.mark.parametrize("cfg", MINI, ids=lambda c: c.name)
 def test_persistent_mode_matches_reference(cfg, mini_models):
     """The one-launch-per-call persistent kernel: same golden stream, logits within

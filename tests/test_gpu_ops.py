@@ -160,7 +160,8 @@ def test_argmax_ties_and_nan():
 
 
 @pytest.mark.parametrize("kv_type", [native.TF_KV_F32, native.TF_KV_F16, native.TF_KV_BF16])
-@pytest.mark.parametrize("shape", [(1, 32, 8, 64), (300, 14, 2, 64), (1100, 12, 2, 128), (9, 4, 2, 8)])
+@pytest.mark.parametrize("shape", [(1, 32, 8, 64), (300, 14, 2, 64), (1100, 12, 2, 128), (9, 4, 2, 8),
+                                   (8192, 32, 8, 64)])
 def test_attn_decode(kv_type, shape):
     n_pos, H, KV, hd = shape
     cap = n_pos + 5
