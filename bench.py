@@ -366,6 +366,46 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
             "profiles/gemv_q8_0_lmhead_128256x2048.md", "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
 
 
+def config_runs():
+    """Batch-1 runs of cfg0 / cfg1 / cfg2 as BASELINE states them (prompt, decode tokens): the
+    prompt prefill (tf_cuda_prefill, chunked tensor-core GEMM for Q8_0 models, token steps for
+    the mixed-quant cfg2) and the device-resident greedy decode (tf_cuda_generate_greedy), each
+    timed with CUDA events; decode against the weight + KV bytes per token."""
+    import torch
+    from tinferno_b200 import native
+    from tinferno_b200.model import Model, RunConfig
+    peak = peaks()[0]
+    out = []
+    for cfg, n_prompt, n_decode in ((synth.CFG0, 32, 64), (synth.CFG1, 512, 128), (synth.CFG2, 128, 128)):
+        m = Model(model_file(cfg), RunConfig(max_seq=cfg.max_seq))
+        stream = torch.cuda.ExternalStream(m.stream)
+        prompt = synth.prompt_tokens(cfg, n_prompt)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        for rep in range(2):  # the second prefill and decode are timed (graphs captured, warm)
+            m.reset(0)
+            torch.cuda.synchronize()
+            ev[0].record(stream)
+            first = int(np.argmax(m.prefill(prompt)))
+            ev[1].record(stream)
+            ids = np.zeros(n_decode, np.int32)
+            n_out = C.c_int(0)
+            ev[2].record(stream)
+            native.check(m.L.tf_cuda_generate_greedy(m.h, 0, first, n_decode, -1, ids.ctypes.data_as(native.i32p),
+                                                     C.byref(n_out)), m.h)
+            ev[3].record(stream)
+            torch.cuda.synchronize()
+        pre_ms, dec_ms = ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])
+        kv_per_pos = 2 * cfg.n_layer * cfg.n_kv_head * (cfg.n_embd // cfg.n_head) * 4
+        mean_pos = n_prompt + n_decode / 2
+        bytes_tok = synth.weight_bytes(cfg) + kv_per_pos * mean_pos
+        tok_s = n_decode / (dec_ms / 1e3)
+        out.append({"config": cfg.name, "prompt": n_prompt, "decode": n_decode,
+                    "prefill_tok_s": round(n_prompt / (pre_ms / 1e3), 1), "decode_tok_s": round(tok_s, 1),
+                    "bytes_per_token": int(bytes_tok), "hbm_frac": round(bytes_tok * tok_s / 1e9 / peak, 3)})
+        m.close()
+    return out
+
+
 def matmul_sweep():
     """BASELINE cfg3: Y[M,N] = X[M,K] W[N,K]^T for Q8_0 and Q4_0 weights (N(0, 0.02) quantised),
     X ~ N(0, 1); K=2048 with N in {512, 2048, 8192, 128256}, K=8192 with N=2048; M in
@@ -432,7 +472,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm", "configs"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -483,6 +523,10 @@ def main():
         us = ev[0].elapsed_time(ev[1]) * 1e3
         print(json.dumps({"kernel": "gemm", "N": N, "K": K, "M": M, "us_incl_prep": round(us, 2),
                           "TFLOP_s": round(2 * N * K * M / us / 1e6, 1)}))
+        return
+    if args.kernel == "configs":
+        for line in config_runs():
+            print(json.dumps(line), flush=True)
         return
     if args.kernel == "bstep":
         # one cfg4 batched decode step (128 rows at context ~530) between cudaProfilerStart /
