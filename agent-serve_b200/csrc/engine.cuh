@@ -18,6 +18,7 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget);
 int gemv_grid(const GemvArgs& a, int num_sms);
 int gemv_slots(int num_sms);  // resident GEMV CTAs the device holds (SMs x CTAs per SM)
 int gemv_max_rows(int K);
+int fused_attn_tile(const GemvArgs& a, int hd);  // positions per fused-attention tile of a QKV launch
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl);
 cudaError_t gemv_init_attrs();
 

@@ -17,6 +17,7 @@
 // conflict-free shared loads at a 17-word lane stride); int8 -> fp32 conversion uses the
 // exact magic-number construction 0x4B0000xx - (2^23 + 128) (one PRMT + one FADD), which
 // keeps the conversion off the 16/clk conversion pipe.
+#include <algorithm>
 #include <cstdlib>
 
 #include "dots.cuh"
@@ -724,6 +725,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
 }
 
 // ---- host side --------------------------------------------------------------------------
+
+// Positions per tile of the attention fused into an integer-path QKV launch `a` (M == 1): the
+// same arithmetic as fused_attention's tile size over the shared memory it is given.
+int fused_attn_tile(const GemvArgs& a, int hd) {
+    const size_t xbytes = ((size_t)xpad_len(a.K) * 4 + 127) & ~(size_t)127;
+    const size_t avail = xbytes + (size_t)GV_STAGES * a.stage_bytes;
+    const int ng = std::min(8, GV_THREADS / hd);
+    const int fixed = 4 * hd + 68 + ng * hd;
+    int tp = (int)((avail / 4 - fixed) / (size_t)(1 + (hd + 4) + hd));
+    tp = (tp > 256 ? 256 : tp) & ~3;
+    return tp > 0 ? tp : 0;
+}
 
 size_t gemv_smem_bytes(int M, int K, int stage_bytes, int maxm) {
     const size_t xbytes = ((size_t)M * xpad_len(K) * 4 + 127) & ~(size_t)127;

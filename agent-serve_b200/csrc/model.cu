@@ -105,6 +105,7 @@ struct tf_model {
     int tile = 1;
     float *x = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *logits = nullptr, *part = nullptr;
     uint8_t* xplanes = nullptr;  // digit planes handed from one integer-path GEMV step kernel to the next
+    int attn_tile = 0;           // positions per tile of the fused decode attention
     unsigned* counters = nullptr;
     unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
     bool gemm_ok = false;         // every matmul weight is Q8_0 with K % 64 == 0
@@ -226,10 +227,14 @@ AttnArgs attn_args(tf_model* m, int li) {
     return a;
 }
 
-// Decode attention runs inside the QKV kernel (one CTA per kv head appended to its grid)
-// for batch-1 steps that end at or below this position; longer contexts use the split
-// flash-decode kernel, whose CTAs cover the positions in parallel.
+// Decode attention runs inside the QKV kernel (one CTA per query head appended to its grid)
+// for batch-1 steps whose context fits in two of its tiles (a tile is what the QKV launch's
+// shared memory holds: ~140 positions for cfg0, ~60 for cfg1) and ends at or below
+// kFusedAttnMaxPos; longer contexts use the split flash-decode kernel, whose CTAs cover the
+// positions in parallel (cfg1 at positions 512-640: 962 tok/s split vs 759 fused; cfg0 at
+// 32-96: 1872 fused vs 1523 split).
 constexpr int kFusedAttnMaxPos = 1024;
+constexpr int kFusedAttnTiles = 2;
 
 static bool fused_attn_enabled() {
     static int v = -1;
@@ -252,7 +257,9 @@ static bool planes_enabled() {
 }
 
 // Whether batch-1 steps of slot `seq` up to position end_pos may fuse the attention.
-bool fuse_attn_ok(const tf_model* m, int end_pos) { return fused_attn_enabled() && end_pos <= kFusedAttnMaxPos; }
+bool fuse_attn_ok(const tf_model* m, int end_pos) {
+    return fused_attn_enabled() && end_pos <= std::min(kFusedAttnMaxPos, kFusedAttnTiles * m->attn_tile);
+}
 
 // One step for M >= GM_MIN_M rows on the tensor-core GEMM path: per layer activation
 // preparation (RMSNorm, f16 halves) before each GEMM, the split flash-decode attention over
@@ -1088,6 +1095,10 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
     m->hpos.assign(o.max_batch, 0);
     if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
+    {   // positions per tile of the attention fused into the QKV kernel (same for every layer)
+        const GemvArgs q = gemv_base(m, m->L[0].qkv, m->H + 2 * m->KV, 1, 1);
+        m->attn_tile = q.intq ? fused_attn_tile(q, m->hd) : 0;
+    }
     CKD(cudaDeviceSynchronize());
     {
         int n = 0;

@@ -70,22 +70,24 @@ def test_mini_stream_matches_reference(cfg, mini_models):
     m.close()
 
 
-def test_long_context_crosses_fused_attention_limit(mini_models):
-    """Batch-1 decode across position 1024, where the attention fused into the QKV kernel hands
-    over to the split flash-decode kernel (long-context decode): token-exact and logits within
-    1e-2 of the oracle over a 1016-token prompt (chunked tensor-core prefill) + 16 steps."""
+@pytest.mark.parametrize("n_prompt,n_decode", [(270, 24), (1016, 16)])
+def test_long_context_crosses_fused_attention_limit(n_prompt, n_decode, mini_models):
+    """Batch-1 decode where the attention fused into the QKV kernel hands over to the split
+    flash-decode kernel (two fused tiles, ~280 positions for this model) and at long context
+    (across position 1024): token-exact and logits within 1e-2 of the oracle after a chunked
+    tensor-core prefill."""
     cfg = MINI[0]
     path = mini_models[cfg.name]
-    prompt = synth.prompt_tokens(cfg, 1016, stream=4242)
+    prompt = synth.prompt_tokens(cfg, n_prompt, stream=4242)
     m = Model(path, RunConfig(max_seq=2048))
-    ids, steps = greedy(m, prompt, 16)
-    assert m.n_pos() == 1016 + 16
+    ids, steps = greedy(m, prompt, n_decode)
+    assert m.n_pos() == n_prompt + n_decode
     orc = po.OracleModel(gguf.GGUFReader(path), 2048)
-    o_ids, o_steps = po.greedy_stream(orc, prompt, 16, keep_logits=True)
+    o_ids, o_steps = po.greedy_stream(orc, prompt, n_decode, keep_logits=True)
     assert o_ids == ids
     err = max(np.abs(a - b).max() for a, b in zip(steps, o_steps))
     assert err < LOGIT_TOL, err
-    print(f"long context: positions 1016..1031 token-exact, max |logit diff| {err:.2e}")
+    print(f"positions {n_prompt}..{n_prompt + n_decode - 1} token-exact, max |logit diff| {err:.2e}")
     m.close()
     orc.close()
 
