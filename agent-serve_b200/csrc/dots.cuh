@@ -125,6 +125,64 @@ __device__ __forceinline__ void q8_build_planes(const float4 (&v)[NU], int K, in
     }
 }
 
+// Q4_0 variant of the planes (the integer path for Q4_0 rows): the digits of block b sit in
+// natural element order, plane p at planes[p*pstride + 32*b + j] (pstride = K), so a quant
+// word's low nibbles (elements 4i..4i+3 of the block) meet plane word i and its high nibbles
+// (elements 16+4i..) plane word 4+i; sums[4*b + p] = the signed digit sum of block b in plane
+// p, for the -8 offset of the nibbles; inv[b] = 2^-sh.  Same digits as q8_build_planes.
+template <int NU>
+__device__ __forceinline__ void q4_build_planes(const float4 (&v)[NU], int K, int nth, int tid, uint8_t* planes,
+                                                int pstride, float* inv, int* sums) {
+    const int nq = K >> 2;
+#pragma unroll
+    for (int u = 0; u < NU; ++u) {
+        const int c = tid + u * nth;
+        if (c - (tid & 31) >= nq) break;  // warp-uniform: no chunk of this warp is left
+        const bool valid = c < nq;
+        const float4 x = valid ? v[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+        float am = fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w)));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+        am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+        const int e = (int)((__float_as_uint(am) >> 23) & 0xFFu);
+        const int sh = min(148 - e, Q8_PLANE_SH_MAX);
+        const float S = __uint_as_float((uint32_t)(127 + sh) << 23);
+        const float xv[4] = {x.x, x.y, x.z, x.w};
+        uint32_t X[4], Y1[4], Y2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            X[i] = (uint32_t)(__float_as_int(fmaf(xv[i], S, 12582912.0f)) - 0x4B400000);
+            Y1[i] = X[i] + 128u;
+            Y2[i] = X[i] + 32896u;
+        }
+        const uint32_t d0 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
+        const uint32_t d1 = __byte_perm(__byte_perm(Y1[0], Y1[1], 0x0051), __byte_perm(Y1[2], Y1[3], 0x0051), 0x5410);
+        const uint32_t d2 = __byte_perm(__byte_perm(Y2[0], Y2[1], 0x0062), __byte_perm(Y2[2], Y2[3], 0x0062), 0x5410);
+        // block digit sums per plane over the block's 8 lanes
+        int s0 = valid ? __dp4a((int)d0, 0x01010101, 0) : 0;
+        int s1 = valid ? __dp4a((int)d1, 0x01010101, 0) : 0;
+        int s2 = valid ? __dp4a((int)d2, 0x01010101, 0) : 0;
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (!valid) continue;
+        const int b = c >> 3;
+        const int off = 32 * b + 4 * (c & 7);
+        *reinterpret_cast<uint32_t*>(planes + off) = d0;
+        *reinterpret_cast<uint32_t*>(planes + pstride + off) = d1;
+        *reinterpret_cast<uint32_t*>(planes + 2 * pstride + off) = d2;
+        if ((c & 7) == 0) {
+            sums[4 * b] = s0;
+            sums[4 * b + 1] = s1;
+            sums[4 * b + 2] = s2;
+            inv[b] = e == 255 ? __uint_as_float(0x7FC00000u) : __uint_as_float((uint32_t)(127 - sh) << 23);
+        }
+    }
+}
+
 // Bytes of one row's planes in memory: three planes of pstride bytes (the Q8_0 row layout,
 // rounded up to 16 bytes) followed by the blocks' 2^-sh as floats.
 __host__ __device__ constexpr int q8_plane_stride(int K) { return ((K / 32) * 34 + 15) & ~15; }
@@ -173,6 +231,49 @@ __device__ __forceinline__ float unit_dot_q8_int(const uint32_t* wp, const uint3
     }
     const float dA = h2f(w0);
     const float dB = h2f(w8 >> 16);
+    const float tA = fmaf((float)a2, 65536.f, (float)(a1 * 256 + a0));
+    const float tB = fmaf((float)b2, 65536.f, (float)(b1 * 256 + b0));
+    return fmaf(dA * invA, tA, (dB * invB) * tB);
+}
+
+// One 64-element unit of a Q4_0 row (two 18-byte blocks, 9 words at wp) against the lane's
+// Q4_0 planes: pl[16p .. 16p+16) plane p's words of the two blocks, pl[48 + p] the two blocks'
+// digit sums of plane p (block A in the low, block B in the high 16 bits).  Nibbles 0..15 are
+// valid signed bytes for dp4a; the reference's q - 8 (src/quant.cpp:323-363) enters as
+// -8 * (digit sum) per plane, so each plane's block sum stays an exact integer.
+__device__ __forceinline__ float unit_dot_q4_int(const uint32_t* wp, const uint32_t (&pl)[51], float invA,
+                                                 float invB) {
+    uint32_t w[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) w[i] = wp[i];
+    int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint32_t qa = __byte_perm(w[i], w[i + 1], 0x5432);  // block A's quant bytes 4i..4i+3
+        const int la = (int)(qa & 0x0F0F0F0Fu), ha = (int)((qa >> 4) & 0x0F0F0F0Fu);
+        a0 = __dp4a(la, (int)pl[i], a0);
+        a0 = __dp4a(ha, (int)pl[4 + i], a0);
+        a1 = __dp4a(la, (int)pl[16 + i], a1);
+        a1 = __dp4a(ha, (int)pl[20 + i], a1);
+        a2 = __dp4a(la, (int)pl[32 + i], a2);
+        a2 = __dp4a(ha, (int)pl[36 + i], a2);
+        const uint32_t qb = w[5 + i];  // block B's quant bytes
+        const int lb = (int)(qb & 0x0F0F0F0Fu), hb = (int)((qb >> 4) & 0x0F0F0F0Fu);
+        b0 = __dp4a(lb, (int)pl[8 + i], b0);
+        b0 = __dp4a(hb, (int)pl[12 + i], b0);
+        b1 = __dp4a(lb, (int)pl[24 + i], b1);
+        b1 = __dp4a(hb, (int)pl[28 + i], b1);
+        b2 = __dp4a(lb, (int)pl[40 + i], b2);
+        b2 = __dp4a(hb, (int)pl[44 + i], b2);
+    }
+    a0 -= 8 * (int)(short)(pl[48] & 0xFFFFu);
+    a1 -= 8 * (int)(short)(pl[49] & 0xFFFFu);
+    a2 -= 8 * (int)(short)(pl[50] & 0xFFFFu);
+    b0 -= 8 * ((int)pl[48] >> 16);
+    b1 -= 8 * ((int)pl[49] >> 16);
+    b2 -= 8 * ((int)pl[50] >> 16);
+    const float dA = h2f(w[0]);
+    const float dB = h2f(w[4] >> 16);
     const float tA = fmaf((float)a2, 65536.f, (float)(a1 * 256 + a0));
     const float tB = fmaf((float)b2, 65536.f, (float)(b1 * 256 + b0));
     return fmaf(dA * invA, tA, (dB * invB) * tB);

@@ -415,11 +415,34 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             // the planes overwrite the activation region, which only the embedding path read
             if (a.pro == PRO_EMBED_RMSNORM) named_bar_compute();
             uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
+            const int unit = (warp % a.KS) * U + pu;
+            if (a.q4) {
+                float* pinv = reinterpret_cast<float*>(planes + 3 * a.K);
+                int* psum = reinterpret_cast<int*>(pinv + a.K / 32);
+                q4_build_planes<GV_PRO_UNROLL>(v, a.K, nth, tid, planes, a.K, pinv, psum);
+                named_bar_compute();
+#pragma unroll
+                for (int i = 0; i < 51; ++i) pl[i] = 0u;
+                if (pact) {
+                    const uint32_t* pw = reinterpret_cast<const uint32_t*>(planes) + 16 * unit;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        pl[i] = pw[i];
+                        pl[16 + i] = pw[a.K / 4 + i];
+                        pl[32 + i] = pw[a.K / 2 + i];
+                    }
+#pragma unroll
+                    for (int p = 0; p < 3; ++p)
+                        pl[48 + p] = ((uint32_t)psum[4 * (2 * unit) + p] & 0xFFFFu) |
+                                     ((uint32_t)psum[4 * (2 * unit + 1) + p] << 16);
+                    invA = pinv[2 * unit];
+                    invB = pinv[2 * unit + 1];
+                }
+            } else {
             const int pstride = (int)((a.rb + 15) & ~15LL);
             float* pinv = reinterpret_cast<float*>(planes + 3 * pstride);
             q8_build_planes<GV_PRO_UNROLL>(v, a.K, nth, tid, planes, pstride, pinv);
             named_bar_compute();
-            const int unit = (warp % a.KS) * U + pu;
 #pragma unroll
             for (int i = 0; i < 51; ++i) pl[i] = 0u;
             if (pact) {
@@ -432,6 +455,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
                 }
                 invA = pinv[2 * unit];
                 invB = pinv[2 * unit + 1];
+            }
             }
         }
     }
@@ -521,7 +545,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         // independent dp4a chains), one shuffle tree reduces both, KS > 1 partials meet after
         // one named barrier, and the two items' epilogues run in parallel in two lanes.
         const int P = a.P, KS = a.KS;
-        const int lane_off = (my_item * P + prow) * (int)a.rb + (my_ks * U + (pact ? pu : 0)) * 68;
+        const int ubytes = a.q4 ? 36 : 68;  // bytes of a 64-element unit
+        const int lane_off = (my_item * P + prow) * (int)a.rb + (my_ks * U + (pact ? pu : 0)) * ubytes;
         const bool lane_ok = pact && prow < P;
         // after the reduction: lanes [0, 16) hold item 0 and [16, 32) item 1 (P == 1); for
         // P == 2 lanes [0, 8) / [8, 16) the first row (gate) of items 0 / 1, [16, 24) / [24, 32)
@@ -541,12 +566,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const uintptr_t g1 = g0 + (uintptr_t)step_bytes;
             // both dots run unconditionally (a stale or partly filled slot is still inside the
             // stage buffer); invalid results are selected away, never multiplied
-            const float d0 = unit_dot_q8_int(
-                reinterpret_cast<const uint32_t*>(stages + (size_t)slot0 * a.stage_bytes + (g0 & 15) + lane_off), pl,
-                invA, invB);
-            const float d1 = unit_dot_q8_int(
-                reinterpret_cast<const uint32_t*>(stages + (size_t)slot1 * a.stage_bytes + (g1 & 15) + lane_off), pl,
-                invA, invB);
+            const uint32_t* wp0 =
+                reinterpret_cast<const uint32_t*>(stages + (size_t)slot0 * a.stage_bytes + (g0 & 15) + lane_off);
+            const uint32_t* wp1 =
+                reinterpret_cast<const uint32_t*>(stages + (size_t)slot1 * a.stage_bytes + (g1 & 15) + lane_off);
+            float d0, d1;
+            if (a.q4) {
+                d0 = unit_dot_q4_int(wp0, pl, invA, invB);
+                d1 = unit_dot_q4_int(wp1, pl, invA, invB);
+            } else {
+                d0 = unit_dot_q8_int(wp0, pl, invA, invB);
+                d1 = unit_dot_q8_int(wp1, pl, invA, invB);
+            }
             const bool ok0 = ok && item0 < i1, ok1 = ok && two && item1 < i1;
             const float v0 = (ok0 && lane_ok) ? d0 : 0.f;
             const float v1 = (ok1 && lane_ok) ? d1 : 0.f;
@@ -760,15 +791,23 @@ static bool q8_int_enabled() {
     return v != 0;
 }
 
+constexpr long long kQ4IntMinBytes = 32ll << 20;
+
 void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const int be = blk_elems(a.wtype) == 1 ? 32 : blk_elems(a.wtype);
     const bool q8fast = (a.wtype == T_Q8_0) && (a.K % 64 == 0);
+    // Q4_0 takes the integer path only for large matrices: its plane build (with block digit
+    // sums) lengthens the prologue, which the small matrices of a decode step cannot hide
+    // (cfg2 decode 476 tok/s with it on every layer, 509 without; the 128256 x 2048 lm_head
+    // shape 3263 GB/s with it, 840 without)
+    const bool q4int = (a.wtype == T_Q4_0) && (a.K % 64 == 0) && a.M == 1 &&
+                       (long long)a.n_items * a.P * a.rb >= kQ4IntMinBytes;
     int best = -1;
     for (int ks = 1; ks <= warps; ks <<= 1) {
         if (a.K % ks) continue;
         const int seg = a.K / ks;
         if (seg % be) continue;
-        if (q8fast && seg % 64) continue;
+        if ((q8fast || q4int) && seg % 64) continue;
         best = ks;
         const long long payload = (long long)(warps / ks) * a.P * a.rb;
         if (payload <= budget) break;
@@ -780,7 +819,11 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     // integer path: one activation row, every lane of a warp on one 64-element unit of one of
     // the item's P rows, the whole row prologue held in registers (K <= 8192)
     const int units = a.K / best / 64;
-    a.intq = a.fast && a.M == 1 && units * a.P <= 32 && a.K <= GV_WARPS * 32 * 4 * GV_PRO_UNROLL && q8_int_enabled();
+    const bool w4 = (reinterpret_cast<uintptr_t>(a.W) & 3) == 0;
+    const bool q4ok = q4int && (a.K / best) % 64 == 0 && w4;
+    a.intq = (a.fast || q4ok) && a.M == 1 && units * a.P <= 32 && a.K <= GV_WARPS * 32 * 4 * GV_PRO_UNROLL &&
+             q8_int_enabled();
+    a.q4 = a.intq && a.wtype == T_Q4_0;
     const long long payload = (long long)(warps / best) * a.P * a.rb;
     a.stage_bytes = (int)((payload + 32 + 15) & ~15LL);
 }

@@ -44,7 +44,8 @@ struct GemvArgs {
     int M;              // activation rows (<= GV_MAXM)
     int stage_bytes;    // bytes of one stage buffer (multiple of 16)
     int fast;           // 1: Q8_0 64-element-unit path
-    int intq;           // 1: Q8_0 exact-integer path (M == 1, activation as digit planes)
+    int intq;           // 1: exact-integer path (M == 1, activation as digit planes)
+    int q4;             // with intq: Q4_0 rows (natural-order planes), else Q8_0
     // prologue
     int pro;
     const float* x;     // [M][ldx]

@@ -407,7 +407,10 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             a.ldy = ldq;
             a.bias = Ld.bqkv;
             fuse = fused && M == 1 && a.intq && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
-            planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && gemv_base(m, Ld.wo, D, 1, M).intq;
+            {   // the planes handed over are in the Q8_0 layout: the consumer must take it
+                const GemvArgs wo_plan = gemv_base(m, Ld.wo, D, 1, M);
+                planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && wo_plan.intq && !wo_plan.q4;
+            }
             int grid = gemv_grid(a, m->num_sms);
             if (fuse) {
                 // the attention CTAs take slots of the GEMV grid so that all stay resident
@@ -455,7 +458,11 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             const int nblk = FF / 32;
             grid = std::min(grid, nblk);
             planes_down = planes_enabled() && a.intq && FF % 32 == 0 && grid > 0 &&
-                          (nblk + grid - 1) / grid * 32 <= GV_PRE && gemv_base(m, Ld.down, D, 1, M).intq;
+                          (nblk + grid - 1) / grid * 32 <= GV_PRE;
+            {
+                const GemvArgs down_plan = gemv_base(m, Ld.down, D, 1, M);
+                planes_down = planes_down && down_plan.intq && !down_plan.q4;
+            }
             if (planes_down) {
                 a.align = 32;
                 a.yplanes = m->xplanes;

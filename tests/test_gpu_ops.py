@@ -67,6 +67,25 @@ def test_matmul(t, shape):
     assert_dot_close(got, want, a, quants.dequant(raw, t, k))
 
 
+@pytest.mark.parametrize("shape", [(30000, 2048, 1), (8200, 8192, 1)])
+def test_matmul_q4_integer_path(shape):
+    """Q4_0 matrices of 32 MB and more take the exact-integer GEMV (nibbles against the
+    activation's digit planes, the -8 offset through per-block digit sums)."""
+    n, k, m = shape
+    t = gguf.GGML_Q4_0
+    rng = np.random.default_rng(n + k)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    raw = np.ascontiguousarray(quants.quantize(w, t))
+    assert raw.nbytes >= 32 << 20
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    want = np.zeros((m, n), np.float32)
+    po.oracle_lib().tfo_matmul(fp(want), fp(a), t, raw.ctypes.data, n, k, m, 4)
+    wd = dev(raw.reshape(-1))
+    ad, cd = dev(a), torch.full((m, n), float("nan"), device="cuda")
+    call(native.lib().tf_op_matmul(ptr(cd), ptr(ad), t, ptr(wd), n, k, m, None))
+    assert_dot_close(cd.cpu().numpy(), want, a, quants.dequant(raw, t, k))
+
+
 @pytest.mark.parametrize("t", [gguf.GGML_Q8_0, gguf.GGML_Q4_0])
 @pytest.mark.parametrize("shape", [(256, 2048, 16), (1000, 2048, 64), (130, 896, 130), (96, 4864, 33),
                                    (2048, 8192, 40), (515, 1536, 300)])
