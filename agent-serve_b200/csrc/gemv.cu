@@ -213,7 +213,9 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     }
 }
 
-template <int MAXM, bool INTQ>
+// INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path (its own function, so the Q8_0
+// kernel that every GEMV of a Q8_0 step runs carries no Q4_0 code)
+template <int MAXM, int INTQ>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -314,7 +316,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         }
     // Q8_0 integer path (M == 1): the activation row stays in registers through the RMSNorm
     // and leaves as digit planes in the activation region (dots.cuh).
-    constexpr bool use_int = INTQ;
+    constexpr bool use_int = INTQ != 0;
+    constexpr bool q4 = INTQ == 2;
     static_assert(!INTQ || MAXM == 1, "integer path is for one activation row");
     const int U = a.K / a.KS / 64;               // 64-element units per row segment
     const int prow = a.P == 2 ? lane >> 4 : 0;   // row of the item this lane works on
@@ -416,7 +419,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             if (a.pro == PRO_EMBED_RMSNORM) named_bar_compute();
             uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
             const int unit = (warp % a.KS) * U + pu;
-            if (a.q4) {
+            if constexpr (q4) {
                 float* pinv = reinterpret_cast<float*>(planes + 3 * a.K);
                 int* psum = reinterpret_cast<int*>(pinv + a.K / 32);
                 q4_build_planes<GV_PRO_UNROLL>(v, a.K, nth, tid, planes, a.K, pinv, psum);
@@ -545,7 +548,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         // independent dp4a chains), one shuffle tree reduces both, KS > 1 partials meet after
         // one named barrier, and the two items' epilogues run in parallel in two lanes.
         const int P = a.P, KS = a.KS;
-        const int ubytes = a.q4 ? 36 : 68;  // bytes of a 64-element unit
+        constexpr int ubytes = q4 ? 36 : 68;  // bytes of a 64-element unit
         const int lane_off = (my_item * P + prow) * (int)a.rb + (my_ks * U + (pact ? pu : 0)) * ubytes;
         const bool lane_ok = pact && prow < P;
         // after the reduction: lanes [0, 16) hold item 0 and [16, 32) item 1 (P == 1); for
@@ -571,7 +574,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const uint32_t* wp1 =
                 reinterpret_cast<const uint32_t*>(stages + (size_t)slot1 * a.stage_bytes + (g1 & 15) + lane_off);
             float d0, d1;
-            if (a.q4) {
+            if constexpr (q4) {
                 d0 = unit_dot_q4_int(wp0, pl, invA, invB);
                 d1 = unit_dot_q4_int(wp1, pl, invA, invB);
             } else {
@@ -837,7 +840,7 @@ int gemv_max_rows(int K) {
     return m < 1 ? 1 : (m > GV_MAXM ? GV_MAXM : m);
 }
 
-template <int MAXM, bool INTQ>
+template <int MAXM, int INTQ>
 static cudaError_t init_one() {
     cudaError_t e =
         cudaFuncSetAttribute(gemv_kernel<MAXM, INTQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -850,14 +853,15 @@ static cudaError_t init_one() {
 
 cudaError_t gemv_init_attrs() {
     cudaError_t e;
-    if ((e = init_one<1, false>())) return e;
-    if ((e = init_one<1, true>())) return e;
-    if ((e = init_one<2, false>())) return e;
-    if ((e = init_one<4, false>())) return e;
-    return init_one<8, false>();
+    if ((e = init_one<1, 0>())) return e;
+    if ((e = init_one<1, 1>())) return e;
+    if ((e = init_one<1, 2>())) return e;
+    if ((e = init_one<2, 0>())) return e;
+    if ((e = init_one<4, 0>())) return e;
+    return init_one<8, 0>();
 }
 
-template <int MAXM, bool INTQ>
+template <int MAXM, int INTQ>
 static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     const size_t smem = gemv_smem_bytes(a.M, a.K, a.stage_bytes, MAXM);
     cudaLaunchConfig_t cfg = {};
@@ -875,10 +879,12 @@ static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool p
 
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     switch (pick_maxm(a.M)) {
-        case 1: return a.intq ? launch_t<1, true>(a, grid, st, pdl) : launch_t<1, false>(a, grid, st, pdl);
-        case 2: return launch_t<2, false>(a, grid, st, pdl);
-        case 4: return launch_t<4, false>(a, grid, st, pdl);
-        default: return launch_t<8, false>(a, grid, st, pdl);
+        case 1:
+            if (!a.intq) return launch_t<1, 0>(a, grid, st, pdl);
+            return a.q4 ? launch_t<1, 2>(a, grid, st, pdl) : launch_t<1, 1>(a, grid, st, pdl);
+        case 2: return launch_t<2, 0>(a, grid, st, pdl);
+        case 4: return launch_t<4, 0>(a, grid, st, pdl);
+        default: return launch_t<8, 0>(a, grid, st, pdl);
     }
 }
 
