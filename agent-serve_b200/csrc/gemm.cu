@@ -839,6 +839,8 @@ static bool gemm_use_tc05() {
     return v != 0;
 }
 
+bool gemm_takes_q4() { return gemm_use_tc05(); }
+
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     const size_t smem = 2 * GM_STAGE_BYTES;
@@ -933,10 +935,11 @@ cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsig
     return cudaSuccess;
 }
 
-// 2^sw with |q * d| * 2^sw < 2^14 for every block of the matrix (|q| <= 128).
-int q8_scale_exponent(const uint8_t* blocks, size_t nbytes) {
+// 2^sw with |q * d| * 2^sw < 2^14 for every block of the matrix (|q| <= 128; Q4_0 blocks,
+// |q| <= 8, take the same bound).  The fp16 d leads every Q8_0 and Q4_0 block.
+int q8_scale_exponent(const uint8_t* blocks, size_t nbytes, int block_bytes) {
     unsigned mx = 0;
-    for (size_t o = 0; o + 34 <= nbytes; o += 34) {
+    for (size_t o = 0; o + block_bytes <= nbytes; o += block_bytes) {
         const unsigned d = ((unsigned)blocks[o] | ((unsigned)blocks[o + 1] << 8)) & 0x7FFFu;
         mx = d > mx ? d : mx;
     }

@@ -107,7 +107,10 @@ struct FinishArgs {
 cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st);
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st);
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st);
-int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes);  // per-matrix sw
+// per-matrix sw of host-resident blocks (block_bytes 34 for Q8_0, 18 for Q4_0)
+int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes, int block_bytes = 34);
+// whether gemm_launch takes Q4_0 weights (the tcgen05 kernel; the mma.sync one reads Q8_0 only)
+bool gemm_takes_q4();
 int q8_exponent_from_dbits(unsigned max_abs_d_bits);
 // sw of device-resident Q8_0 blocks (synchronises `st`); scratch: one device unsigned
 cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsigned* scratch, int* sw, cudaStream_t st,

@@ -59,8 +59,13 @@ struct WeightRef {
     int K = 0;
     long long rb = 0;
     int rows = 0;
-    int sw = 0;  // Q8_0: power-of-two scale of the tensor-core GEMM (gemm.cuh)
+    int sw = 0;  // Q8_0 / Q4_0: power-of-two scale of the tensor-core GEMM (gemm.cuh)
 };
+
+// Whether the tensor-core GEMM takes this matrix (Q8_0, or Q4_0 on the tcgen05 kernel).
+bool gemm_weight_ok(const WeightRef& w) {
+    return (w.type == T_Q8_0 || (w.type == T_Q4_0 && gemm_takes_q4())) && w.K % GM_BK == 0;
+}
 
 struct LayerDev {
     const float* attn_norm;
@@ -108,7 +113,7 @@ struct tf_model {
     int attn_tile = 0;           // positions per tile of the fused decode attention
     unsigned* counters = nullptr;
     unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
-    bool gemm_ok = false;         // every matmul weight is Q8_0 with K % 64 == 0
+    bool gemm_ok = false;         // most layer weight bytes are in GEMM-able matrices
     int gtile = 0;                // rows per step on the GEMM path (0: no GEMM path)
     int ptile = 0;                // prompt tokens per prefill chunk on the GEMM path
     __half *xh = nullptr, *xl = nullptr;  // GEMM activation halves [round_up(gtile,128)][max K]
@@ -263,63 +268,118 @@ bool fuse_attn_ok(const tf_model* m, int end_pos) {
 
 // One step for M >= GM_MIN_M rows on the tensor-core GEMM path: per layer activation
 // preparation (RMSNorm, f16 halves) before each GEMM, the split flash-decode attention over
-// the M rows' slots, and a finishing kernel for the step's tokens and positions.
+// the M rows' slots, and a finishing kernel for the step's tokens and positions.  A matrix the
+// GEMM does not take (Q4_1, Q6_K, F16, F32) runs the multi-row GEMV over row groups of up to
+// `tile` rows with the same prologue and epilogue.  A prefill chunk (`chunk`) computes the
+// lm_head for its last row only: Model::prefill returns that row's logits alone
+// (src/model.cpp:183-195).
 int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) {
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
-    auto prep = [&](const float* x, int ldx, int K, const float* norm_w) {
-        XPrepArgs p;
-        memset(&p, 0, sizeof(p));
-        p.x = x;
-        p.ldx = ldx;
-        p.norm_w = norm_w;
-        p.eps = m->hp.rms_eps;
-        p.K = K;
-        p.M = M;
-        p.xh = m->xh;
-        p.xl = m->xl;
-        p.sx = m->d_sx;
-        p.err = m->d_err;
-        return p;
+    // y[M][N] (+ epilogue) = op(x)[M][K] W^T: op = RMSNorm with norm_w (embedding lookup of
+    // d_tokens first when `embed`), else the rows as they are; rows [r0, r0 + rows) only
+    struct Mm {
+        const WeightRef* w;
+        int n_items, P, epi;
+        const float* x;
+        int ldx;
+        const float* norm_w;
+        bool embed;
+        float* y;
+        int ldy;
+        const float* bias;
+        float* resid;
+        unsigned long long* keys;
     };
-    auto gemm = [&](const WeightRef& w, int N, int epi) {
-        GemmArgs g;
-        memset(&g, 0, sizeof(g));
-        g.W = w.p;
-        g.rb = w.rb;
-        g.N = N;
-        g.K = w.K;
-        g.M = M;
-        g.sw = w.sw;
-        g.xh = m->xh;
-        g.xl = m->xl;
-        g.sx = m->d_sx;
-        g.epi = epi;
-        g.ksplit = gemm_pick_split(N, M, w.K, m->num_sms);
-        g.ws = m->gws;
-        g.tile_cnt = m->gcnt;
-        g.err = m->d_err;
-        return g;
-    };
-    for (int li = 0; li < m->hp.n_layer; ++li) {
-        const LayerDev& Ld = m->L[li];
-        {
-            XPrepArgs p = prep(m->x, D, D, Ld.attn_norm);
-            if (li == 0) {
+    auto matmul = [&](const Mm& q, int r0, int rows) -> int {
+        const WeightRef& w = *q.w;
+        if (gemm_weight_ok(w) && rows >= GM_MIN_M) {
+            XPrepArgs p;
+            memset(&p, 0, sizeof(p));
+            p.x = q.x + (size_t)r0 * q.ldx;
+            p.ldx = q.ldx;
+            p.norm_w = q.norm_w;
+            p.eps = m->hp.rms_eps;
+            p.K = w.K;
+            p.M = rows;
+            p.xh = m->xh;
+            p.xl = m->xl;
+            p.sx = m->d_sx;
+            p.err = m->d_err;
+            if (q.embed) {
                 p.embd = m->embd.p;
                 p.embd_type = m->embd.type;
                 p.embd_rb = m->embd.rb;
                 p.n_vocab = V;
-                p.tokens = m->d_tokens;
-                p.x_out = m->x;
+                p.tokens = m->d_tokens + r0;
+                p.x_out = m->x + (size_t)r0 * D;
             }
             CK(xprep_launch(p, m->stream));
-            GemmArgs g = gemm(Ld.qkv, ldq, EPI_STORE);
-            g.y = m->qkv;
-            g.ldy = ldq;
-            g.bias = Ld.bqkv;
+            GemmArgs g;
+            memset(&g, 0, sizeof(g));
+            g.W = w.p;
+            g.wq4 = w.type == T_Q4_0 ? 1 : 0;
+            g.rb = w.rb;
+            g.N = q.n_items * q.P;
+            g.K = w.K;
+            g.M = rows;
+            g.sw = w.sw;
+            g.xh = m->xh;
+            g.xl = m->xl;
+            g.sx = m->d_sx;
+            g.epi = q.epi;
+            g.ksplit = gemm_pick_split(g.N, rows, w.K, m->num_sms);
+            g.ws = m->gws;
+            g.tile_cnt = m->gcnt;
+            g.err = m->d_err;
+            g.y = q.y ? q.y + (size_t)r0 * q.ldy : nullptr;
+            g.ldy = q.ldy;
+            g.bias = q.bias;
+            g.resid = q.resid ? q.resid + (size_t)r0 * D : nullptr;
+            g.ldr = D;
+            if (q.keys) {
+                g.keys = q.keys + r0;
+                g.store_logits = 1;
+            }
             CK(gemm_launch(g, m->stream));
+            launches += 2;
+            return 0;
+        }
+        for (int b = 0; b < rows; b += m->tile) {
+            const int mc = std::min(m->tile, rows - b), r = r0 + b;
+            GemvArgs a = gemv_base(m, w, q.n_items, q.P, mc);
+            a.pro = q.embed ? PRO_EMBED_RMSNORM : q.norm_w ? PRO_RMSNORM : PRO_COPY;
+            a.x = q.x + (size_t)r * q.ldx;
+            a.ldx = q.ldx;
+            a.norm_w = q.norm_w;
+            a.eps = m->hp.rms_eps;
+            if (q.embed) {
+                a.embd = m->embd.p;
+                a.embd_type = m->embd.type;
+                a.embd_rb = m->embd.rb;
+                a.n_vocab = V;
+                a.tokens = m->d_tokens + r;
+                a.x_out = m->x + (size_t)r * D;
+            }
+            a.epi = q.epi;
+            a.y = q.y ? q.y + (size_t)r * q.ldy : nullptr;
+            a.ldy = q.ldy;
+            a.bias = q.bias;
+            a.resid = q.resid ? q.resid + (size_t)r * D : nullptr;
+            a.ldr = D;
+            a.keys = q.keys ? q.keys + r : nullptr;
+            CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, true));
+            ++launches;
+        }
+        return 0;
+    };
+    for (int li = 0; li < m->hp.n_layer; ++li) {
+        const LayerDev& Ld = m->L[li];
+        if (matmul({&Ld.qkv, ldq, 1, EPI_STORE, m->x, D, Ld.attn_norm, li == 0, m->qkv, ldq, Ld.bqkv, nullptr, nullptr},
+                   0, M))
+            return -1;
+        {
             AttnArgs a = attn_args(m, li);
             if (chunk) {  // one sequence's prompt rows: store every row's K/V, then attend
                 CK(rope_store_launch(a, M, m->stream));
@@ -327,42 +387,21 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) 
                 ++launches;
             }
             CK(attn_decode_launch(a, M, m->stream, true));
-            launches += 3;
+            ++launches;
         }
-        {
-            CK(xprep_launch(prep(m->attn, H, H, nullptr), m->stream));
-            GemmArgs g = gemm(Ld.wo, D, EPI_RESID);
-            g.resid = m->x;
-            g.ldr = D;
-            CK(gemm_launch(g, m->stream));
-            launches += 2;
-        }
-        {
-            CK(xprep_launch(prep(m->x, D, D, Ld.ffn_norm), m->stream));
-            GemmArgs g = gemm(Ld.gateup, 2 * FF, EPI_SWIGLU);
-            g.y = m->h;
-            g.ldy = FF;
-            CK(gemm_launch(g, m->stream));
-            launches += 2;
-        }
-        {
-            CK(xprep_launch(prep(m->h, FF, FF, nullptr), m->stream));
-            GemmArgs g = gemm(Ld.down, D, EPI_RESID);
-            g.resid = m->x;
-            g.ldr = D;
-            CK(gemm_launch(g, m->stream));
-            launches += 2;
-        }
+        if (matmul({&Ld.wo, D, 1, EPI_RESID, m->attn, H, nullptr, false, nullptr, 0, nullptr, m->x, nullptr}, 0, M))
+            return -1;
+        if (matmul({&Ld.gateup, FF, 2, EPI_SWIGLU, m->x, D, Ld.ffn_norm, false, m->h, FF, nullptr, nullptr, nullptr},
+                   0, M))
+            return -1;
+        if (matmul({&Ld.down, D, 1, EPI_RESID, m->h, FF, nullptr, false, nullptr, 0, nullptr, m->x, nullptr}, 0, M))
+            return -1;
     }
     if (head) {
-        CK(xprep_launch(prep(m->x, D, D, m->out_norm), m->stream));
-        GemmArgs g = gemm(m->outw, V, EPI_ARGMAX);
-        g.y = m->logits;
-        g.ldy = V;
-        g.keys = m->keys;
-        g.store_logits = 1;
-        CK(gemm_launch(g, m->stream));
-        launches += 2;
+        const Mm q = {&m->outw, V, 1, EPI_ARGMAX, m->x, D, m->out_norm, false, m->logits, V, nullptr, nullptr, m->keys};
+        // a prefill chunk needs its last row's logits only (one GEMV row); a batched step
+        // needs every row's
+        if (chunk ? matmul(q, M - 1, 1) : matmul(q, 0, M)) return -1;
     }
     FinishArgs f;
     memset(&f, 0, sizeof(f));
@@ -966,6 +1005,13 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         w.rows = rows;
         return w;
     };
+    // power-of-two scale of a matrix for the tensor-core GEMM (Q8_0 and Q4_0 rows)
+    auto wscale = [](const tf_tensor_desc* t) {
+        const uint8_t* b = static_cast<const uint8_t*>(t->data);
+        if (t->ggml_type == T_Q8_0) return q8_scale_exponent(b, t->nbytes, 34);
+        if (t->ggml_type == T_Q4_0) return q8_scale_exponent(b, t->nbytes, 18);
+        return 0;
+    };
     m->L.resize(hp.n_layer);
     for (int i = 0; i < hp.n_layer; ++i) {
         LDesc& L = ld[i];
@@ -976,10 +1022,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes, L.k->data, L.k->nbytes, cudaMemcpyHostToDevice));
         CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes + L.k->nbytes, L.v->data, L.v->nbytes, cudaMemcpyHostToDevice));
         Ld.qkv = wref(A + pl[i].qkv, L.q->ggml_type, m->D, m->H + 2 * m->KV);
-        if (L.q->ggml_type == T_Q8_0)
-            Ld.qkv.sw = std::min({q8_scale_exponent((const uint8_t*)L.q->data, L.q->nbytes),
-                                  q8_scale_exponent((const uint8_t*)L.k->data, L.k->nbytes),
-                                  q8_scale_exponent((const uint8_t*)L.v->data, L.v->nbytes)});
+        Ld.qkv.sw = std::min({wscale(L.q), wscale(L.k), wscale(L.v)});
         Ld.bqkv = nullptr;
         if (L.bq) {
             float* b = reinterpret_cast<float*>(A + pl[i].b);
@@ -990,30 +1033,35 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         }
         CKD(cudaMemcpy(A + pl[i].o, L.o->data, L.o->nbytes, cudaMemcpyHostToDevice));
         Ld.wo = wref(A + pl[i].o, L.o->ggml_type, m->H, m->D);
-        if (L.o->ggml_type == T_Q8_0) Ld.wo.sw = q8_scale_exponent((const uint8_t*)L.o->data, L.o->nbytes);
+        Ld.wo.sw = wscale(L.o);
         CKD(cudaMemcpy(A + pl[i].fn, L.fn->data, L.fn->nbytes, cudaMemcpyHostToDevice));
         Ld.ffn_norm = reinterpret_cast<const float*>(A + pl[i].fn);
         const size_t grb = (size_t)row_bytes(L.g->ggml_type, m->D);
         CKD(cudaMemcpy2D(A + pl[i].gu, 2 * grb, L.g->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
         CKD(cudaMemcpy2D(A + pl[i].gu + grb, 2 * grb, L.u->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
         Ld.gateup = wref(A + pl[i].gu, L.g->ggml_type, m->D, 2 * m->FF);
-        if (L.g->ggml_type == T_Q8_0)
-            Ld.gateup.sw = std::min(q8_scale_exponent((const uint8_t*)L.g->data, L.g->nbytes),
-                                    q8_scale_exponent((const uint8_t*)L.u->data, L.u->nbytes));
+        Ld.gateup.sw = std::min(wscale(L.g), wscale(L.u));
         CKD(cudaMemcpy(A + pl[i].d, L.d->data, L.d->nbytes, cudaMemcpyHostToDevice));
         Ld.down = wref(A + pl[i].d, L.d->ggml_type, m->FF, m->D);
-        if (L.d->ggml_type == T_Q8_0) Ld.down.sw = q8_scale_exponent((const uint8_t*)L.d->data, L.d->nbytes);
+        Ld.down.sw = wscale(L.d);
     }
     CKD(cudaMemcpy(A + p_embd, te->data, te->nbytes, cudaMemcpyHostToDevice));
     m->embd = wref(A + p_embd, te->ggml_type, m->D, (int)te->ne[1]);
     if (ow != te) CKD(cudaMemcpy(A + p_out, ow->data, ow->nbytes, cudaMemcpyHostToDevice));
     m->outw = wref(A + p_out, ow->ggml_type, m->D, (int)ow->ne[1]);
-    if (ow->ggml_type == T_Q8_0) m->outw.sw = q8_scale_exponent((const uint8_t*)ow->data, ow->nbytes);
+    m->outw.sw = wscale(ow);
     {
-        auto gemm_w = [](const WeightRef& w) { return w.type == T_Q8_0 && w.K % GM_BK == 0; };
-        bool ok = gemm_w(m->outw);
-        for (const LayerDev& Ld : m->L) ok = ok && gemm_w(Ld.qkv) && gemm_w(Ld.wo) && gemm_w(Ld.gateup) && gemm_w(Ld.down);
-        m->gemm_ok = ok;
+        // steps of >= 16 rows take the tensor-core path when the matrices it can run (Q8_0,
+        // Q4_0) hold most of the layer weight bytes; the others of such a step (Q4_1, Q6_K,
+        // F16, F32) run the multi-row GEMV inside it
+        long long tc = 0, all = 0;
+        for (const LayerDev& Ld : m->L)
+            for (const WeightRef* w : {&Ld.qkv, &Ld.wo, &Ld.gateup, &Ld.down}) {
+                const long long b = w->rb * w->rows;
+                all += b;
+                if (gemm_weight_ok(*w)) tc += b;
+            }
+        m->gemm_ok = all > 0 && 2 * tc >= all;
     }
     CKD(cudaMemcpy(A + p_onorm, on->data, on->nbytes, cudaMemcpyHostToDevice));
     m->out_norm = reinterpret_cast<const float*>(A + p_onorm);

@@ -373,8 +373,9 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
 
 def config_runs():
     """Batch-1 runs of cfg0 / cfg1 / cfg2 as BASELINE states them (prompt, decode tokens): the
-    prompt prefill (tf_cuda_prefill, chunked tensor-core GEMM for Q8_0 models, token steps for
-    the mixed-quant cfg2) and the device-resident greedy decode (tf_cuda_generate_greedy), each
+    prompt prefill (tf_cuda_prefill: chunked tensor-core GEMM for the Q8_0 / Q4_0 matrices, the
+    multi-row GEMV for cfg2's Q4_1 / Q6_K ones) and the device-resident greedy decode
+    (tf_cuda_generate_greedy), each
     timed with CUDA events; decode against the weight + KV bytes per token."""
     import torch
     from tinferno_b200 import native

@@ -1,5 +1,7 @@
-"""Batched decode at M >= 16 rows (the tensor-core GEMM path: f16-split Q8_0 GEMM, split
-flash-decode attention over the rows' slots) against the batch-1 path and the oracle."""
+"""Batched decode at M >= 16 rows (the tensor-core GEMM path: f16-split Q8_0 / Q4_0 GEMM,
+split flash-decode attention over the rows' slots) against the batch-1 path and the oracle.
+The mixed-quant cfg2 model runs its Q4_0 matrices on the GEMM and its Q4_1 ffn_down and Q6_K
+lm_head on the multi-row GEMV inside the same steps."""
 import numpy as np
 import pytest
 
@@ -9,7 +11,8 @@ from tinferno_b200.model import Model, RunConfig
 
 pytestmark = pytest.mark.gpu
 
-CFGS = [synth.mini(synth.CFG0, 2, 4096), synth.mini(synth.CFG1, 2, 4096), synth.mini(synth.CFG4, 2, 4096)]
+CFGS = [synth.mini(synth.CFG0, 2, 4096), synth.mini(synth.CFG1, 2, 4096), synth.mini(synth.CFG4, 2, 4096),
+        synth.mini(synth.CFG2, 2, 4096)]
 LOGIT_TOL = 2e-3  # observed ~1e-5: the split keeps 22 significant bits of weights and activations
 
 
@@ -103,12 +106,14 @@ def test_prefill_batch_matches_single_prefill(B, paths):
     m.close()
 
 
-@pytest.mark.parametrize("n", [16, 40, 300])
-def test_chunked_prefill_matches_oracle(n, paths):
+@pytest.mark.parametrize("ci,n", [(1, 16), (1, 40), (1, 300), (3, 16), (3, 40), (3, 150)],
+                         ids=lambda v: str(v))
+def test_chunked_prefill_matches_oracle(ci, n, paths):
     """Model::prefill of >= 16 tokens runs in tensor-core chunks of up to 128 rows (RoPE + K/V
-    store for the chunk, then causal attention over the cache): logits and the following
-    greedy stream agree with the reference restatement."""
-    cfg = CFGS[1]
+    store for the chunk, then causal attention over the cache; the lm_head on the chunk's last
+    row): logits and the following greedy stream agree with the reference restatement.  cfg2
+    (ci 3): Q4_0 GEMMs, the Q4_1 ffn_down of layer 0 and the Q6_K lm_head on the GEMV."""
+    cfg = CFGS[ci]
     path = paths[cfg.name]
     prompt = synth.prompt_tokens(cfg, n, stream=700 + n)
     m = Model(path, RunConfig(max_seq=n + 8))
