@@ -130,7 +130,9 @@ __device__ __forceinline__ void q8_build_planes(const float4 (&v)[NU], int K, in
 // word's low nibbles (elements 4i..4i+3 of the block) meet plane word i and its high nibbles
 // (elements 16+4i..) plane word 4+i; sums[4*b + p] = the signed digit sum of block b in plane
 // p, for the -8 offset of the nibbles; inv[b] = 2^-sh.  Same digits as q8_build_planes.
-template <int NU>
+// SUM16 (the Q6_K path): the sums are taken over 16-element halves instead and stored as
+// 16-bit fields, word 4*b + p = (first half) | (second half) << 16 (|sum| <= 16 * 128).
+template <int NU, bool SUM16 = false>
 __device__ __forceinline__ void q4_build_planes(const float4 (&v)[NU], int K, int nth, int tid, uint8_t* planes,
                                                 int pstride, float* inv, int* sums) {
     const int nq = K >> 2;
@@ -158,12 +160,12 @@ __device__ __forceinline__ void q4_build_planes(const float4 (&v)[NU], int K, in
         const uint32_t d0 = __byte_perm(__byte_perm(X[0], X[1], 0x0040), __byte_perm(X[2], X[3], 0x0040), 0x5410);
         const uint32_t d1 = __byte_perm(__byte_perm(Y1[0], Y1[1], 0x0051), __byte_perm(Y1[2], Y1[3], 0x0051), 0x5410);
         const uint32_t d2 = __byte_perm(__byte_perm(Y2[0], Y2[1], 0x0062), __byte_perm(Y2[2], Y2[3], 0x0062), 0x5410);
-        // block digit sums per plane over the block's 8 lanes
+        // digit sums per plane over the block's 8 lanes (SUM16: over each group of 4 lanes)
         int s0 = valid ? __dp4a((int)d0, 0x01010101, 0) : 0;
         int s1 = valid ? __dp4a((int)d1, 0x01010101, 0) : 0;
         int s2 = valid ? __dp4a((int)d2, 0x01010101, 0) : 0;
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
+        for (int o = 1; o < (SUM16 ? 4 : 8); o <<= 1) {
             s0 += __shfl_xor_sync(0xffffffffu, s0, o);
             s1 += __shfl_xor_sync(0xffffffffu, s1, o);
             s2 += __shfl_xor_sync(0xffffffffu, s2, o);
@@ -174,12 +176,20 @@ __device__ __forceinline__ void q4_build_planes(const float4 (&v)[NU], int K, in
         *reinterpret_cast<uint32_t*>(planes + off) = d0;
         *reinterpret_cast<uint32_t*>(planes + pstride + off) = d1;
         *reinterpret_cast<uint32_t*>(planes + 2 * pstride + off) = d2;
-        if ((c & 7) == 0) {
+        if constexpr (SUM16) {
+            if ((c & 3) == 0) {
+                int16_t* h16 = reinterpret_cast<int16_t*>(sums + 4 * b) + ((c >> 2) & 1);
+                h16[0] = (int16_t)s0;
+                h16[2] = (int16_t)s1;
+                h16[4] = (int16_t)s2;
+            }
+        } else if ((c & 7) == 0) {
             sums[4 * b] = s0;
             sums[4 * b + 1] = s1;
             sums[4 * b + 2] = s2;
-            inv[b] = e == 255 ? __uint_as_float(0x7FC00000u) : __uint_as_float((uint32_t)(127 - sh) << 23);
         }
+        if ((c & 7) == 0)
+            inv[b] = e == 255 ? __uint_as_float(0x7FC00000u) : __uint_as_float((uint32_t)(127 - sh) << 23);
     }
 }
 
@@ -279,6 +289,72 @@ __device__ __forceinline__ float unit_dot_q4_int(const uint32_t* wp, const uint3
     return fmaf(dA * invA, tA, (dB * invB) * tB);
 }
 
+// One 64-element unit of a Q6_K row against the lane's natural-order planes (the Q4_0
+// layout).  Unit (h, j) of a 256-element super-block (h = half, j = 0 / 1) holds the groups
+// tq = j and tq = j + 2 of dequant_q6_K_row (src/quant.cpp:101-127): both read the 32 ql bytes
+// at 64h + 32j (low / high nibbles) and the 32 qh bytes at 128 + 32h (bit pairs 2j / 2j + 4),
+// so the unit is elements 128h + 32j + [0, 32) (activation block A) and 128h + 32(j + 2) +
+// [0, 32) (block B = A + 2).  The six-bit u = ql nibble | qh bits << 4 (0..63) is a valid
+// signed byte for dp4a; q = u - 32 enters as -32 * (the 16-element digit sums) per plane, so
+// every 16-element sub-block sum stays an exact integer, which its int8 scale and the fp16 d
+// then multiply.
+//   sb:  the super-block (2-byte aligned: 210-byte blocks); sel: 0x3210 when sb is 4-byte
+//        aligned, 0x5432 when it sits 2 bytes past a word (the words are realigned by PRMT)
+//   pl:  pl[16p + i] plane p's words of block A (i < 8) and B (8 <= i < 16)
+//   ss:  the SUM16 digit sums of block A (words 0..2: plane p, first half in the low and second
+//        half in the high 16 bits) and of block B (words 8..10), in shared memory
+__device__ __forceinline__ float unit_dot_q6k_int(const uint8_t* sb, int h, int j, uint32_t sel,
+                                                  const uint32_t (&pl)[48], const uint32_t* ss, float invA,
+                                                  float invB) {
+    const uint32_t* aw = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(sb) & ~(uintptr_t)3);
+    const int qlw0 = (64 * h + 32 * j) >> 2, qhw0 = (128 + 32 * h) >> 2;
+    const uint16_t* hw = reinterpret_cast<const uint16_t*>(sb);  // sb is 2-byte aligned
+    const uint32_t scA = hw[96 + 4 * h + j];                     // scales[8h + 2j], [8h + 2j + 1]
+    const uint32_t scB = hw[96 + 4 * h + j + 2];                 // scales[8h + 2j + 4], [.. + 5]
+    const float d = h2f(hw[104]);
+    const int shA = 4 - 2 * j, shB = 2 * j;
+    float fA = 0.f, fB = 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+        uint32_t ql[5], qh[5];  // this half's words (one more for the realignment)
+#pragma unroll
+        for (int k = 0; k < 5; ++k) {
+            ql[k] = aw[qlw0 + 4 * half + k];
+            qh[k] = aw[qhw0 + 4 * half + k];
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = 4 * half + k;
+            const uint32_t lw = __byte_perm(ql[k], ql[k + 1], sel);
+            const uint32_t hq = __byte_perm(qh[k], qh[k + 1], sel);
+            const int uA = (int)((lw & 0x0F0F0F0Fu) | ((hq << shA) & 0x30303030u));
+            const int uB = (int)(((lw >> 4) & 0x0F0F0F0Fu) | ((hq >> shB) & 0x30303030u));
+            a0 = __dp4a(uA, (int)pl[i], a0);
+            a1 = __dp4a(uA, (int)pl[16 + i], a1);
+            a2 = __dp4a(uA, (int)pl[32 + i], a2);
+            b0 = __dp4a(uB, (int)pl[8 + i], b0);
+            b1 = __dp4a(uB, (int)pl[24 + i], b1);
+            b2 = __dp4a(uB, (int)pl[40 + i], b2);
+        }
+        // 16-element digit sums of this half (signed 16-bit fields)
+        const int sh16 = half ? 0 : 16;
+        const uint4 sa = *reinterpret_cast<const uint4*>(ss), sbb = *reinterpret_cast<const uint4*>(ss + 8);
+        a0 -= 32 * ((int)(sa.x << sh16) >> 16);
+        a1 -= 32 * ((int)(sa.y << sh16) >> 16);
+        a2 -= 32 * ((int)(sa.z << sh16) >> 16);
+        b0 -= 32 * ((int)(sbb.x << sh16) >> 16);
+        b1 -= 32 * ((int)(sbb.y << sh16) >> 16);
+        b2 -= 32 * ((int)(sbb.z << sh16) >> 16);
+        const float tA = fmaf((float)a2, 65536.f, (float)(a1 * 256 + a0));
+        const float tB = fmaf((float)b2, 65536.f, (float)(b1 * 256 + b0));
+        const float sA = (float)(int8_t)(scA >> (8 * half)), sB = (float)(int8_t)(scB >> (8 * half));
+        fA = fmaf(sA, tA, fA);
+        fB = fmaf(sB, tB, fB);
+    }
+    return d * fmaf(invA, fA, invB * fB);
+}
+
 // ---- Q8_0 fast path: one row segment of `units` 64-element units -----------------------
 // Products and partial sums use the packed fp32x2 pipe of sm_100 (__ffma2_rn / __fadd2_rn):
 // two weights per instruction, each lane still forming exact fp32 x*q products.
@@ -339,20 +415,22 @@ __device__ __forceinline__ void dot_q8_fast(const uint8_t* seg, int units, const
     }
 }
 
-// ---- generic path: one lane per block (32 elements; 256 for Q6_K) ----------------------
+// ---- generic path: one lane per 32-element group of a block -------------------------------
 // Produces either (scale, q[32]) with the block scale applied to the block sum (Q8_0, Q4_0,
 // as src/quant.cpp:266-363 do) or dequantised w[32] (Q4_1, Q6_K, F16, F32, as
-// dequant_row + dot_f32 do).
+// dequant_row + dot_f32 do).  A Q6_K super-block's eight groups go to eight lanes, so a
+// 2048-element row keeps every lane of the warp busy.
 template <int MAXM>
 __device__ __forceinline__ void dot_generic(int t, const uint8_t* seg, int e0, int nelem, const float* xs, int xl,
                                             int M, int lane, float (&acc)[MAXM]) {
     const int be = (t == T_Q6_K) ? 256 : 32;
     const int bb = (t == T_F32) ? 128 : (t == T_F16) ? 64 : blk_bytes(t);
-    const int nblk = nelem / be;
-    for (int b = lane; b < nblk; b += 32) {
+    const int groups = be / 32;
+    const int nwork = (nelem / be) * groups;
+    for (int wi = lane; wi < nwork; wi += 32) {
+        const int b = groups == 1 ? wi : wi >> 3, g = groups == 1 ? 0 : wi & 7;
         const uint8_t* p = seg + (size_t)b * bb;
-        const int groups = be / 32;
-        for (int g = 0; g < groups; ++g) {
+        {
             float w[32];
             float scale = 1.f;
             bool scaled = false;

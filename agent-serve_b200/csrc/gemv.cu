@@ -213,8 +213,8 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     }
 }
 
-// INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path (its own function, so the Q8_0
-// kernel that every GEMV of a Q8_0 step runs carries no Q4_0 code)
+// INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path, 3 Q6_K integer path (each its
+// own function, so the Q8_0 kernel that every GEMV of a Q8_0 step runs carries no other code)
 template <int MAXM, int INTQ>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -318,15 +318,17 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     // and leaves as digit planes in the activation region (dots.cuh).
     constexpr bool use_int = INTQ != 0;
     constexpr bool q4 = INTQ == 2;
+    constexpr bool q6 = INTQ == 3;  // Q6_K rows: the Q4_0 planes, 64-element units of super-blocks
     static_assert(!INTQ || MAXM == 1, "integer path is for one activation row");
     const int U = a.K / a.KS / 64;               // 64-element units per row segment
     const int prow = a.P == 2 ? lane >> 4 : 0;   // row of the item this lane works on
     const int pu = a.P == 2 ? lane & 15 : lane;  // unit within the segment
     const bool pact = pu < U;
-    uint32_t pl[INTQ ? 51 : 1];
+    uint32_t pl[INTQ ? (q6 ? 48 : 51) : 1];
     float invA = 0.f, invB = 0.f;
+    const uint32_t* q6sum = nullptr;  // Q6_K: this lane's 16-element digit sums (shared memory)
     if constexpr (INTQ) {
-        if (a.pro == PRO_PLANES) {
+        if (INTQ == 1 && a.pro == PRO_PLANES) {
             // the previous kernel left the activation as planes: one coalesced copy into the
             // activation region (all loads in flight before the stores), then the lanes read
             // their units from shared memory as below
@@ -419,7 +421,30 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             if (a.pro == PRO_EMBED_RMSNORM) named_bar_compute();
             uint8_t* planes = reinterpret_cast<uint8_t*>(xs);
             const int unit = (warp % a.KS) * U + pu;
-            if constexpr (q4) {
+            if constexpr (q6) {
+                float* pinv = reinterpret_cast<float*>(planes + 3 * a.K);
+                int* psum = reinterpret_cast<int*>(pinv + a.K / 32);
+                q4_build_planes<GV_PRO_UNROLL, true>(v, a.K, nth, tid, planes, a.K, pinv, psum);
+                named_bar_compute();
+#pragma unroll
+                for (int i = 0; i < 48; ++i) pl[i] = 0u;
+                // unit (h, j) of super-block sbg: activation blocks A = 8 sbg + 4h + j, B = A + 2
+                const int sbg = (warp % a.KS) * (a.K / a.KS / 256) + (pact ? pu >> 2 : 0);
+                const int blkA = 8 * sbg + 4 * ((pu >> 1) & 1) + (pu & 1), blkB = blkA + 2;
+                q6sum = reinterpret_cast<const uint32_t*>(psum) + 4 * blkA;
+                if (pact) {
+                    const uint32_t* pw = reinterpret_cast<const uint32_t*>(planes);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+#pragma unroll
+                        for (int p = 0; p < 3; ++p) {
+                            pl[16 * p + i] = pw[p * (a.K / 4) + 8 * blkA + i];
+                            pl[16 * p + 8 + i] = pw[p * (a.K / 4) + 8 * blkB + i];
+                        }
+                    invA = pinv[blkA];
+                    invB = pinv[blkB];
+                }
+            } else if constexpr (q4) {
                 float* pinv = reinterpret_cast<float*>(planes + 3 * a.K);
                 int* psum = reinterpret_cast<int*>(pinv + a.K / 32);
                 q4_build_planes<GV_PRO_UNROLL>(v, a.K, nth, tid, planes, a.K, pinv, psum);
@@ -548,8 +573,13 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
         // independent dp4a chains), one shuffle tree reduces both, KS > 1 partials meet after
         // one named barrier, and the two items' epilogues run in parallel in two lanes.
         const int P = a.P, KS = a.KS;
-        constexpr int ubytes = q4 ? 36 : 68;  // bytes of a 64-element unit
-        const int lane_off = (my_item * P + prow) * (int)a.rb + (my_ks * U + (pact ? pu : 0)) * ubytes;
+        constexpr int ubytes = q4 ? 36 : 68;  // bytes of a 64-element unit (Q4_0 / Q8_0)
+        // Q6_K: the lane's unit is (h, j) of super-block my_ks * U / 4 + pu / 4 of its row
+        const int lane_off = (my_item * P + prow) * (int)a.rb +
+                             (q6 ? (my_ks * (U / 4) + (pact ? pu >> 2 : 0)) * 210
+                                 : (my_ks * U + (pact ? pu : 0)) * ubytes);
+        const int q6h = (pu >> 1) & 1, q6j = pu & 1;
+        const uint32_t q6sel = (lane_off & 2) ? 0x5432u : 0x3210u;
         const bool lane_ok = pact && prow < P;
         // after the reduction: lanes [0, 16) hold item 0 and [16, 32) item 1 (P == 1); for
         // P == 2 lanes [0, 8) / [8, 16) the first row (gate) of items 0 / 1, [16, 24) / [24, 32)
@@ -574,7 +604,10 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
             const uint32_t* wp1 =
                 reinterpret_cast<const uint32_t*>(stages + (size_t)slot1 * a.stage_bytes + (g1 & 15) + lane_off);
             float d0, d1;
-            if constexpr (q4) {
+            if constexpr (q6) {
+                d0 = unit_dot_q6k_int(reinterpret_cast<const uint8_t*>(wp0), q6h, q6j, q6sel, pl, q6sum, invA, invB);
+                d1 = unit_dot_q6k_int(reinterpret_cast<const uint8_t*>(wp1), q6h, q6j, q6sel, pl, q6sum, invA, invB);
+            } else if constexpr (q4) {
                 d0 = unit_dot_q4_int(wp0, pl, invA, invB);
                 d1 = unit_dot_q4_int(wp1, pl, invA, invB);
             } else {
@@ -796,6 +829,16 @@ static bool q8_int_enabled() {
 
 constexpr long long kQ4IntMinBytes = 32ll << 20;
 
+// TFB200_Q6_INT=0 keeps Q6_K rows on the fp32 dequant path (for measurement)
+static bool q6_int_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_Q6_INT");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const int be = blk_elems(a.wtype) == 1 ? 32 : blk_elems(a.wtype);
     const bool q8fast = (a.wtype == T_Q8_0) && (a.K % 64 == 0);
@@ -805,6 +848,10 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     // shape 3263 GB/s with it, 840 without)
     const bool q4int = (a.wtype == T_Q4_0) && (a.K % 64 == 0) && a.M == 1 &&
                        (long long)a.n_items * a.P * a.rb >= kQ4IntMinBytes;
+    // Q6_K rows (cfg2's 215 MB lm_head) take the integer path at any size: the fp32 dequant
+    // of a 256-element super-block is several times the plane build's cost.  K % 512 keeps the
+    // rows (210 bytes per super-block) 4-byte aligned.
+    const bool q6int = (a.wtype == T_Q6_K) && (a.K % 512 == 0) && a.M == 1;
     int best = -1;
     for (int ks = 1; ks <= warps; ks <<= 1) {
         if (a.K % ks) continue;
@@ -824,9 +871,11 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const int units = a.K / best / 64;
     const bool w4 = (reinterpret_cast<uintptr_t>(a.W) & 3) == 0;
     const bool q4ok = q4int && (a.K / best) % 64 == 0 && w4;
-    a.intq = (a.fast || q4ok) && a.M == 1 && units * a.P <= 32 && a.K <= GV_WARPS * 32 * 4 * GV_PRO_UNROLL &&
-             q8_int_enabled();
+    const bool q6ok = q6int && (a.K / best) % 256 == 0 && w4 && q6_int_enabled();
+    a.intq = (a.fast || q4ok || q6ok) && a.M == 1 && units * a.P <= 32 &&
+             a.K <= GV_WARPS * 32 * 4 * GV_PRO_UNROLL && q8_int_enabled();
     a.q4 = a.intq && a.wtype == T_Q4_0;
+    a.q6 = a.intq && a.wtype == T_Q6_K;
     const long long payload = (long long)(warps / best) * a.P * a.rb;
     a.stage_bytes = (int)((payload + 32 + 15) & ~15LL);
 }
@@ -856,6 +905,7 @@ cudaError_t gemv_init_attrs() {
     if ((e = init_one<1, 0>())) return e;
     if ((e = init_one<1, 1>())) return e;
     if ((e = init_one<1, 2>())) return e;
+    if ((e = init_one<1, 3>())) return e;
     if ((e = init_one<2, 0>())) return e;
     if ((e = init_one<4, 0>())) return e;
     return init_one<8, 0>();
@@ -881,6 +931,7 @@ cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) 
     switch (pick_maxm(a.M)) {
         case 1:
             if (!a.intq) return launch_t<1, 0>(a, grid, st, pdl);
+            if (a.q6) return launch_t<1, 3>(a, grid, st, pdl);
             return a.q4 ? launch_t<1, 2>(a, grid, st, pdl) : launch_t<1, 1>(a, grid, st, pdl);
         case 2: return launch_t<2, 0>(a, grid, st, pdl);
         case 4: return launch_t<4, 0>(a, grid, st, pdl);

@@ -45,7 +45,8 @@ struct GemvArgs {
     int stage_bytes;    // bytes of one stage buffer (multiple of 16)
     int fast;           // 1: Q8_0 64-element-unit path
     int intq;           // 1: exact-integer path (M == 1, activation as digit planes)
-    int q4;             // with intq: Q4_0 rows (natural-order planes), else Q8_0
+    int q4;             // with intq: Q4_0 rows (natural-order planes)
+    int q6;             // with intq: Q6_K rows (natural-order planes); neither: Q8_0
     // prologue
     int pro;
     const float* x;     // [M][ldx]

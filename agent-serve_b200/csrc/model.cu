@@ -448,7 +448,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             fuse = fused && M == 1 && a.intq && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
             {   // the planes handed over are in the Q8_0 layout: the consumer must take it
                 const GemvArgs wo_plan = gemv_base(m, Ld.wo, D, 1, M);
-                planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && wo_plan.intq && !wo_plan.q4;
+                planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && wo_plan.intq && !wo_plan.q4 && !wo_plan.q6;
             }
             int grid = gemv_grid(a, m->num_sms);
             if (fuse) {
@@ -500,7 +500,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
                           (nblk + grid - 1) / grid * 32 <= GV_PRE;
             {
                 const GemvArgs down_plan = gemv_base(m, Ld.down, D, 1, M);
-                planes_down = planes_down && down_plan.intq && !down_plan.q4;
+                planes_down = planes_down && down_plan.intq && !down_plan.q4 && !down_plan.q6;
             }
             if (planes_down) {
                 a.align = 32;

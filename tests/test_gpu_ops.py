@@ -67,16 +67,19 @@ def test_matmul(t, shape):
     assert_dot_close(got, want, a, quants.dequant(raw, t, k))
 
 
-@pytest.mark.parametrize("shape", [(30000, 2048, 1), (8200, 8192, 1)])
-def test_matmul_q4_integer_path(shape):
+@pytest.mark.parametrize("t,shape", [(gguf.GGML_Q4_0, (30000, 2048, 1)), (gguf.GGML_Q4_0, (8200, 8192, 1)),
+                                     (gguf.GGML_Q6_K, (30000, 2048, 1)), (gguf.GGML_Q6_K, (2100, 8192, 1)),
+                                     (gguf.GGML_Q6_K, (77, 512, 1))])
+def test_matmul_integer_path_large(t, shape):
     """Q4_0 matrices of 32 MB and more take the exact-integer GEMV (nibbles against the
-    activation's digit planes, the -8 offset through per-block digit sums)."""
+    activation's digit planes, the -8 offset through per-block digit sums); Q6_K rows with
+    K % 512 == 0 take it at any size (six-bit quants against the same planes, the -32 offset
+    through 16-element digit sums, super-blocks at 2-byte offsets realigned)."""
     n, k, m = shape
-    t = gguf.GGML_Q4_0
-    rng = np.random.default_rng(n + k)
+    rng = np.random.default_rng(n + k + t)
     w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
     raw = np.ascontiguousarray(quants.quantize(w, t))
-    assert raw.nbytes >= 32 << 20
+    assert t == gguf.GGML_Q6_K or raw.nbytes >= 32 << 20
     a = rng.standard_normal((m, k)).astype(np.float32)
     want = np.zeros((m, n), np.float32)
     po.oracle_lib().tfo_matmul(fp(want), fp(a), t, raw.ctypes.data, n, k, m, 4)
