@@ -32,6 +32,60 @@ __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
 
+// Split fused attention, after the tile loop: this split's partial (max, sum, weighted V;
+// every split CTA leaves one, an empty or failed one with max -inf and sum 0, so the head's
+// ticket count stays whole) goes to part[qh][sp]; the last of the head's CTAs combines the
+// nsf partials in split order (deterministic) into out and the wo digit planes.  pacc holds
+// the ng groups' weighted V sums; scratch (3 * nsf floats) and flag[1] are shared memory.
+// Out of line, with plain arguments, so that the QKV GEMV's register allocation does not
+// carry it.
+__device__ __noinline__ void fused_attn_split_out(float* part, int n_split, unsigned* ticket, float* out,
+                                                  uint8_t* yplanes, int n_head, int qh, int sp, int nsf, int hd,
+                                                  int ng, const float* pacc, float* scratch, int* flag, float m_run,
+                                                  float l_run) {
+    const int tid = threadIdx.x, nth = blockDim.x;
+    float* pp = part + ((size_t)qh * n_split + sp) * (hd + 2);
+    for (int d = tid; d < hd; d += nth) {
+        float o = 0.f;
+        for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
+        pp[2 + d] = o;
+    }
+    if (tid == 0) {
+        pp[0] = m_run;
+        pp[1] = l_run;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) flag[1] = atomicAdd(ticket + qh, 1u) == (unsigned)nsf - 1;
+    __syncthreads();
+    if (!flag[1]) return;
+    __threadfence();
+    float* cm = scratch;  // [nsf] maxima, [nsf] sums, [nsf] weights
+    const float* pb = part + (size_t)qh * n_split * (hd + 2);
+    for (int q = tid; q < nsf; q += nth) {
+        cm[q] = __ldcg(pb + (size_t)q * (hd + 2));
+        cm[nsf + q] = __ldcg(pb + (size_t)q * (hd + 2) + 1);
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int q = 0; q < nsf; ++q) mx = fmaxf(mx, cm[q]);
+    for (int q = tid; q < nsf; q += nth) cm[2 * nsf + q] = expf(cm[q] - mx);
+    __syncthreads();
+    float den = 0.f;
+    for (int q = 0; q < nsf; ++q) den = fmaf(cm[2 * nsf + q], cm[nsf + q], den);
+    for (int d = tid; d < hd; d += nth) {  // whole warps (hd is a multiple of 32)
+        float num = 0.f;
+        for (int q = 0; q < nsf; ++q) num = fmaf(cm[2 * nsf + q], __ldcg(pb + (size_t)q * (hd + 2) + 2 + d), num);
+        const float o = num / den;
+        out[(size_t)qh * hd + d] = o;
+        if (yplanes) {
+            const int pstride = q8_plane_stride(n_head * hd);
+            q8_block_planes_warp(o, (qh * hd + d) >> 5, yplanes, pstride, reinterpret_cast<float*>(yplanes + 3 * pstride));
+        }
+    }
+    if (tid == 0) ticket[qh] = 0u;
+}
+
 // ---- fused decode attention (one query head per CTA, appended to the QKV GEMV grid) -------
 // Model::layer_decode's apply_rope on q and k, KVCache::store and attn_decode for query head
 // `cta` (src/model.cpp:125-129, src/attention.cpp:31-80), M == 1.  The cached K/V rows and the
@@ -42,12 +96,16 @@ __device__ __forceinline__ void named_bar_compute() {
 // online softmax.  Every phase uses the whole CTA: one position per thread for the scores
 // (float4 reads of q and of K rows padded to hd + 4 floats), CTA-wide max / sum, and ng
 // groups of hd threads for the weighted V sum (group g takes positions g, g + ng, ...).
+// SPLIT (its own kernel instantiation, launched only when a head's positions are split):
+// CTA cta owns query head cta % n_head and position split cta / n_head of attn_nsf.
+template <bool SPLIT>
 __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int cta, int G) {
     const AttnArgs& t = a.at;
     const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
     const int hd = t.hd, d2 = hd / 2, n_rep = t.n_head / t.n_kv;
-    const int qh = cta, kvh = cta / n_rep;
-    const bool storer = cta % n_rep == 0;
+    const int nsf = SPLIT ? (a.attn_nsf > 1 ? a.attn_nsf : 1) : 1;  // position splits per query head
+    const int qh = SPLIT ? cta % t.n_head : cta, sp = SPLIT ? cta / t.n_head : 0, kvh = qh / n_rep;
+    const bool storer = qh % n_rep == 0 && sp == 0;
     const int kst = hd + 4;
     const int ng = min(8, nth / hd);
     float* f = reinterpret_cast<float*>(smem);
@@ -73,12 +131,21 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     const bool pos_ok = pos >= 0 && pos < t.cap && tp >= 4;
     const int ws = pos_ok ? ((t.wstart) ? min(max(t.wstart[slot], 0), pos) : 0) : 0;
     const size_t cache_off = (size_t)slot * t.slot_stride + (size_t)kvh * t.cap * hd;
+    // this split's positions [s0, s1) of [ws, pos] (split 0 is never empty)
+    int s0 = ws, s1 = pos + 1;
+    if constexpr (SPLIT) {
+        const int span = pos_ok ? (pos + 1 - ws + nsf - 1) / nsf : 0;
+        s0 = ws + sp * span;
+        s1 = pos_ok ? min(pos + 1, s0 + span) : s0;
+    }
     // the first tile's cached rows and the rotation of pos, before q/k/v are ready
     if (pos_ok) {
-        const int np = min(pos + 1, ws + tp) - ws;
-        const int npc = (ws + np == pos + 1) ? np - 1 : np;
-        load_tile(ks, kst, hd, t.kc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
-        load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)ws * hd), npc, t.kv_type, nth);
+        if (!SPLIT || s0 < s1) {
+            const int np = min(s1, s0 + tp) - s0;
+            const int npc = (s0 + np == pos + 1) ? np - 1 : np;
+            load_tile(ks, kst, hd, t.kc, (long long)(cache_off + (size_t)s0 * hd), npc, t.kv_type, nth);
+            load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)s0 * hd), npc, t.kv_type, nth);
+        }
         for (int i = tid; i < d2; i += nth) {
             cs[i] = t.cosb[(size_t)pos * d2 + i];
             sn[i] = t.sinb[(size_t)pos * d2 + i];
@@ -103,6 +170,8 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
         *flag = ok;
     }
     __syncthreads();
+    float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
+    const bool pv_thread = tid < ng * hd;
     if (*flag) {
         const float* row = t.qkv;
         for (int i = tid; i < hd; i += nth) {
@@ -123,13 +192,11 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
                 kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
             }
         const float scale = 1.0f / sqrtf((float)hd);
-        const bool pv_thread = tid < ng * hd;
         const int pg = tid / hd, pd = tid % hd;
-        float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
-        for (int t0 = ws; t0 <= pos; t0 += tp) {
-            const int np = min(pos + 1, t0 + tp) - t0;
+        for (int t0 = s0; t0 < s1; t0 += tp) {
+            const int np = min(s1, t0 + tp) - t0;
             const bool last = t0 + np == pos + 1;
-            if (t0 != ws) {
+            if (t0 != s0) {
                 load_tile(ks, kst, hd, t.kc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np, t.kv_type,
                           nth);
                 load_tile(vs, hd, hd, t.vc, (long long)(cache_off + (size_t)t0 * hd), last ? np - 1 : np, t.kv_type,
@@ -188,19 +255,27 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
             }
             __syncthreads();
         }
-        if (pv_thread) pacc[tid] = acc;
-        __syncthreads();
-        for (int d = tid; d < hd; d += nth) {  // whole warps (hd is a multiple of 32)
-            float o = 0.f;
-            for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
-            o = o / l_run;
-            t.out[(size_t)qh * hd + d] = o;
-            if (a.yplanes) {
-                const int pstride = q8_plane_stride(t.n_head * hd);
-                q8_block_planes_warp(o, (qh * hd + d) >> 5, a.yplanes, pstride,
-                                     reinterpret_cast<float*>(a.yplanes + 3 * pstride));
+        if constexpr (!SPLIT) {
+            if (pv_thread) pacc[tid] = acc;
+            __syncthreads();
+            for (int d = tid; d < hd; d += nth) {  // whole warps (hd is a multiple of 32)
+                float o = 0.f;
+                for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
+                o = o / l_run;
+                t.out[(size_t)qh * hd + d] = o;
+                if (a.yplanes) {
+                    const int pstride = q8_plane_stride(t.n_head * hd);
+                    q8_block_planes_warp(o, (qh * hd + d) >> 5, a.yplanes, pstride,
+                                         reinterpret_cast<float*>(a.yplanes + 3 * pstride));
+                }
             }
         }
+    }
+    if constexpr (SPLIT) {
+        if (pv_thread) pacc[tid] = acc;
+        __syncthreads();
+        fused_attn_split_out(t.part, t.n_split, a.aticket, t.out, a.yplanes, t.n_head, qh, sp, nsf, hd, ng, pacc, ks,
+                             flag, m_run, l_run);
     }
     // leave; the last attention CTA out clears the counters for this layer's next step
     __syncthreads();
@@ -213,7 +288,8 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     }
 }
 
-// INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path, 3 Q6_K integer path (each its
+// INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path, 3 Q6_K integer path, 4 the Q8_0
+// integer path whose fused attention splits each head's positions over several CTAs (each its
 // own function, so the Q8_0 kernel that every GEMV of a Q8_0 step runs carries no other code)
 template <int MAXM, int INTQ>
 __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
@@ -235,9 +311,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     // their K/V rows while the GEMV CTAs work); GEMV CTA gb = blockIdx.x - attn_ctas
     const int G = (int)gridDim.x - a.attn_ctas;
     const int gb = (int)blockIdx.x - a.attn_ctas;
-    if constexpr (INTQ) {
+    if constexpr (INTQ == 1 || INTQ == 4) {  // the attention fuses into Q8_0 QKV launches only
         if (gb < 0) {
-            fused_attention(a, smem, (size_t)xbytes + (size_t)GV_STAGES * a.stage_bytes, (int)blockIdx.x, G);
+            fused_attention<INTQ == 4>(a, smem, (size_t)xbytes + (size_t)GV_STAGES * a.stage_bytes, (int)blockIdx.x, G);
             return;
         }
     }
@@ -328,7 +404,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
     float invA = 0.f, invB = 0.f;
     const uint32_t* q6sum = nullptr;  // Q6_K: this lane's 16-element digit sums (shared memory)
     if constexpr (INTQ) {
-        if (INTQ == 1 && a.pro == PRO_PLANES) {
+        if ((INTQ == 1 || INTQ == 4) && a.pro == PRO_PLANES) {
             // the previous kernel left the activation as planes: one coalesced copy into the
             // activation region (all loads in flight before the stores), then the lanes read
             // their units from shared memory as below
@@ -827,7 +903,16 @@ static bool q8_int_enabled() {
     return v != 0;
 }
 
-constexpr long long kQ4IntMinBytes = 32ll << 20;
+// Smallest Q4_0 matrix on the integer path (TFB200_Q4_INT_MIN_MB overrides the 32 MB default).
+static long long q4_int_min_bytes() {
+    static long long v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_Q4_INT_MIN_MB");
+        v = e ? (long long)atoi(e) << 20 : 32ll << 20;
+        if (v < 0) v = 0;
+    }
+    return v;
+}
 
 // TFB200_Q6_INT=0 keeps Q6_K rows on the fp32 dequant path (for measurement)
 static bool q6_int_enabled() {
@@ -847,7 +932,7 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     // (cfg2 decode 476 tok/s with it on every layer, 509 without; the 128256 x 2048 lm_head
     // shape 3263 GB/s with it, 840 without)
     const bool q4int = (a.wtype == T_Q4_0) && (a.K % 64 == 0) && a.M == 1 &&
-                       (long long)a.n_items * a.P * a.rb >= kQ4IntMinBytes;
+                       (long long)a.n_items * a.P * a.rb >= q4_int_min_bytes();
     // Q6_K rows (cfg2's 215 MB lm_head) take the integer path at any size: the fp32 dequant
     // of a 256-element super-block is several times the plane build's cost.  K % 512 keeps the
     // rows (210 bytes per super-block) 4-byte aligned.
@@ -906,6 +991,7 @@ cudaError_t gemv_init_attrs() {
     if ((e = init_one<1, 1>())) return e;
     if ((e = init_one<1, 2>())) return e;
     if ((e = init_one<1, 3>())) return e;
+    if ((e = init_one<1, 4>())) return e;
     if ((e = init_one<2, 0>())) return e;
     if ((e = init_one<4, 0>())) return e;
     return init_one<8, 0>();
@@ -932,7 +1018,8 @@ cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) 
         case 1:
             if (!a.intq) return launch_t<1, 0>(a, grid, st, pdl);
             if (a.q6) return launch_t<1, 3>(a, grid, st, pdl);
-            return a.q4 ? launch_t<1, 2>(a, grid, st, pdl) : launch_t<1, 1>(a, grid, st, pdl);
+            if (a.q4) return launch_t<1, 2>(a, grid, st, pdl);
+            return a.attn_nsf > 1 ? launch_t<1, 4>(a, grid, st, pdl) : launch_t<1, 1>(a, grid, st, pdl);
         case 2: return launch_t<2, 0>(a, grid, st, pdl);
         case 4: return launch_t<4, 0>(a, grid, st, pdl);
         default: return launch_t<8, 0>(a, grid, st, pdl);

@@ -76,10 +76,14 @@ struct GemvArgs {
     int* hist;           // FIN_ARGMAX: generated ids [hist_cap][M] (optional)
     int* err;
     // fused decode attention (integer path, M == 1, the QKV GEMV): the first attn_ctas ==
-    // n_head CTAs of the grid own one query head each (RoPE, KV store, attention of `at`);
-    // they wait for the q/k/v rows through sync[0] (GEMV CTAs arrive when their rows are
-    // stored) and leave through sync[1] (the last one out clears both)
+    // n_head * attn_nsf CTAs of the grid own one query head and one of attn_nsf position
+    // splits each (RoPE, KV store, attention of `at`); they wait for the q/k/v rows through
+    // sync[0] (GEMV CTAs arrive when their rows are stored) and leave through sync[1] (the
+    // last one out clears both).  With attn_nsf > 1 a split leaves its partial (max, sum,
+    // weighted V) in at.part and the last of the head's CTAs (aticket[head]) combines.
     int attn_ctas;
+    int attn_nsf;
+    unsigned* aticket;
     unsigned* sync;
     AttnArgs at;
     // digit-plane handoff between integer-path kernels (layout of q8_plane_bytes): xplanes

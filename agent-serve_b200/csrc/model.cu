@@ -112,7 +112,8 @@ struct tf_model {
     uint8_t* xplanes = nullptr;  // digit planes handed from one integer-path GEMV step kernel to the next
     int attn_tile = 0;           // positions per tile of the fused decode attention
     unsigned* counters = nullptr;
-    unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters
+    unsigned* d_async = nullptr;  // [n_layer][2] fused-attention arrival / departure counters,
+                                  // then [n_head] tickets of the split fused attention
     bool gemm_ok = false;         // most layer weight bytes are in GEMM-able matrices
     int gtile = 0;                // rows per step on the GEMM path (0: no GEMM path)
     int ptile = 0;                // prompt tokens per prefill chunk on the GEMM path
@@ -232,12 +233,14 @@ AttnArgs attn_args(tf_model* m, int li) {
     return a;
 }
 
-// Decode attention runs inside the QKV kernel (one CTA per query head appended to its grid)
-// for batch-1 steps whose context fits in two of its tiles (a tile is what the QKV launch's
+// Decode attention runs inside the QKV kernel (CTAs per query head appended to its grid) for
+// batch-1 steps.  A context that fits in two of its tiles (a tile is what the QKV launch's
 // shared memory holds: ~140 positions for cfg0, ~60 for cfg1) and ends at or below
-// kFusedAttnMaxPos; longer contexts use the split flash-decode kernel, whose CTAs cover the
-// positions in parallel (cfg1 at positions 512-640: 962 tok/s split vs 759 fused; cfg0 at
-// 32-96: 1872 fused vs 1523 split).
+// kFusedAttnMaxPos takes one CTA per head; a longer one is split over positions into nsf
+// CTAs per head of at most two tiles each (the last of a head to finish combines), while
+// n_head * nsf stays within half the GEMV slots; beyond that the separate split flash-decode
+// kernel runs.  One CTA per head walking many tiles measured slower than the separate
+// kernel (cfg1 at positions 512-640: 759 vs 962 tok/s); cfg0 at 32-96: 1872 fused vs 1523.
 constexpr int kFusedAttnMaxPos = 1024;
 constexpr int kFusedAttnTiles = 2;
 
@@ -261,9 +264,26 @@ static bool planes_enabled() {
     return v != 0;
 }
 
-// Whether batch-1 steps of slot `seq` up to position end_pos may fuse the attention.
-bool fuse_attn_ok(const tf_model* m, int end_pos) {
-    return fused_attn_enabled() && end_pos <= std::min(kFusedAttnMaxPos, kFusedAttnTiles * m->attn_tile);
+// TFB200_FUSED_SPLIT=0: no position splits in the fused attention (measurement switch)
+static bool fused_split_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_FUSED_SPLIT");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
+// CTAs per query head of the attention fused into batch-1 steps up to position end_pos, or 0
+// when the separate attention kernel runs.
+int fuse_attn_ok(const tf_model* m, int end_pos) {
+    if (!fused_attn_enabled() || m->attn_tile <= 0) return 0;
+    const int per = kFusedAttnTiles * m->attn_tile;
+    if (end_pos <= std::min(kFusedAttnMaxPos, per)) return 1;
+    if (!fused_split_enabled()) return 0;
+    const int nsf = (end_pos + per - 1) / per;
+    if (nsf > m->n_split || nsf * m->hp.n_head > gemv_slots(m->num_sms) / 2) return 0;
+    return nsf;
 }
 
 // One step for M >= GM_MIN_M rows on the tensor-core GEMM path: per layer activation
@@ -419,7 +439,8 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) 
     return 0;
 }
 
-int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fused, bool chunk = false) {
+// fused: CTAs per query head of the attention fused into the QKV kernel (0: separate kernel)
+int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fused, bool chunk = false) {
     if (chunk) return enqueue_step_gemm(m, M, head, n_launch, true);
     if (M >= GM_MIN_M && m->gtile >= M) return enqueue_step_gemm(m, M, head, n_launch, false);
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
@@ -445,7 +466,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
             a.y = m->qkv;
             a.ldy = ldq;
             a.bias = Ld.bqkv;
-            fuse = fused && M == 1 && a.intq && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
+            fuse = fused > 0 && M == 1 && a.intq && !a.q4 && !a.q6 && m->hd % 4 == 0 && m->hd <= AT_MAX_HD;
             {   // the planes handed over are in the Q8_0 layout: the consumer must take it
                 const GemvArgs wo_plan = gemv_base(m, Ld.wo, D, 1, M);
                 planes_wo = fuse && planes_enabled() && m->hd % 32 == 0 && wo_plan.intq && !wo_plan.q4 && !wo_plan.q6;
@@ -455,7 +476,9 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
                 // the attention CTAs take slots of the GEMV grid so that all stay resident
                 // one attention CTA per query head: the tail after the GEMV is then the
                 // latency of one head's scores / softmax / weighted V
-                a.attn_ctas = m->hp.n_head;
+                a.attn_ctas = m->hp.n_head * fused;
+                a.attn_nsf = fused;
+                a.aticket = m->d_async + 2 * m->hp.n_layer;
                 a.sync = m->d_async + 2 * li;
                 a.at = attn_args(m, li);
                 grid = std::max(1, std::min(grid, gemv_slots(m->num_sms) - a.attn_ctas));
@@ -555,9 +578,9 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, bool fu
 }
 
 // Run one step for M rows (tokens in d_tokens[0..M), slots in d_slots[0..M)).
-int run_step(tf_model* m, int M, bool head, bool fused, bool chunk = false) {
+int run_step(tf_model* m, int M, bool head, int fused, bool chunk = false) {
     if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused, chunk);
-    const long long key = (long long)M * 8 + (head ? 1 : 0) + (fused ? 2 : 0) + (chunk ? 4 : 0);
+    const long long key = ((long long)fused << 40) + (long long)M * 8 + (head ? 1 : 0) + (chunk ? 4 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
@@ -766,7 +789,7 @@ int finish_call(tf_model* m) {
         cudaMemsetAsync(m->counters, 0, sizeof(unsigned) * (size_t)T * m->hp.n_kv_head, m->stream);
         cudaMemsetAsync(m->ctl, 0, sizeof(unsigned), m->stream);
         cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * T, m->stream);
-        cudaMemsetAsync(m->d_async, 0, sizeof(unsigned) * 2 * m->hp.n_layer, m->stream);
+        cudaMemsetAsync(m->d_async, 0, sizeof(unsigned) * (2 * m->hp.n_layer + m->hp.n_head), m->stream);
         cudaStreamSynchronize(m->stream);
         return fail(m, err_code_text(c));
     }
@@ -1139,8 +1162,8 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(cudaMalloc(&m->d_prompt, sizeof(int) * ((size_t)o.max_seq + 1)));
     CKD(cudaMalloc(&m->d_err, sizeof(int)));
     CKD(cudaMemset(m->d_err, 0, sizeof(int)));
-    CKD(cudaMalloc(&m->d_async, sizeof(unsigned) * 2 * hp.n_layer));
-    CKD(cudaMemset(m->d_async, 0, sizeof(unsigned) * 2 * hp.n_layer));
+    CKD(cudaMalloc(&m->d_async, sizeof(unsigned) * (2 * hp.n_layer + hp.n_head)));
+    CKD(cudaMemset(m->d_async, 0, sizeof(unsigned) * (2 * hp.n_layer + hp.n_head)));
     CKD(cudaMalloc(&m->ctl, sizeof(StepCtl)));
     CKD(cudaMemset(m->ctl, 0, sizeof(StepCtl)));
     CKD(cudaMallocHost(&m->hi, sizeof(int) * 64 + sizeof(int) * ((size_t)o.max_seq + 1) * 2));
@@ -1152,7 +1175,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
     {   // positions per tile of the attention fused into the QKV kernel (same for every layer)
         const GemvArgs q = gemv_base(m, m->L[0].qkv, m->H + 2 * m->KV, 1, 1);
-        m->attn_tile = q.intq ? fused_attn_tile(q, m->hd) : 0;
+        m->attn_tile = (q.intq && !q.q4 && !q.q6) ? fused_attn_tile(q, m->hd) : 0;
     }
     CKD(cudaDeviceSynchronize());
     {
@@ -1273,7 +1296,7 @@ int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eo
         StepCtl c = {0u, 0, n, 0};
         memcpy(m->hi + 4, &c, sizeof(c));
         CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
-        const bool fz = fuse_attn_ok(m, m->hpos[seq] + n);
+        const int fz = fuse_attn_ok(m, m->hpos[seq] + n);
         for (int i = 0; i < n; ++i)
             if (run_step(m, 1, true, fz)) return -1;
     }

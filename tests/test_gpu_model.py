@@ -70,13 +70,14 @@ def test_mini_stream_matches_reference(cfg, mini_models):
     m.close()
 
 
-@pytest.mark.parametrize("n_prompt,n_decode", [(270, 24), (1016, 16)])
-def test_long_context_crosses_fused_attention_limit(n_prompt, n_decode, mini_models):
-    """Batch-1 decode where the attention fused into the QKV kernel hands over to the split
-    flash-decode kernel (two fused tiles, ~280 positions for this model) and at long context
-    (across position 1024): token-exact and logits within 1e-2 of the oracle after a chunked
-    tensor-core prefill."""
-    cfg = MINI[0]
+@pytest.mark.parametrize("ci,n_prompt,n_decode", [(0, 270, 24), (0, 1016, 16), (1, 500, 16), (0, 1500, 8)])
+def test_long_context_crosses_fused_attention_limit(ci, n_prompt, n_decode, mini_models):
+    """Batch-1 decode across the fused attention's hand-overs: one CTA per query head up to
+    two tiles (~280 positions for cfg0, ~120 for cfg1), then position splits inside the QKV
+    kernel (cfg0 across 1024, cfg1 at 500-516: five splits of 14 heads), then the separate
+    split flash-decode kernel (cfg0 at 1500: more splits than half the GEMV slots hold):
+    token-exact and logits within 1e-2 of the oracle after a chunked tensor-core prefill."""
+    cfg = MINI[ci]
     path = mini_models[cfg.name]
     prompt = synth.prompt_tokens(cfg, n_prompt, stream=4242)
     m = Model(path, RunConfig(max_seq=2048))
