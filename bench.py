@@ -371,6 +371,42 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
             "profiles/gemv_q8_0_lmhead_128256x2048.md", "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
 
 
+def q6k_gemv():
+    """The Q6_K integer-path GEMV (the kind of cfg2's 215 MB lm_head) on 16384 x 2048 weights
+    (N(0, 0.02) quantised, 27.5 MB) times one N(0, 1) fp32 row: eight device copies rotate so
+    every timed launch reads its weights from HBM (220 MB > L2); CUDA events, median of 20."""
+    import torch
+    from tinferno_b200 import native, quants, gguf
+    N, K = 16384, CFG.n_embd
+    rng = np.random.default_rng(6)
+    raw = np.ascontiguousarray(quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
+                                               gguf.GGML_Q6_K)).reshape(-1)
+    W = [torch.from_numpy(raw).cuda() for _ in range(8)]
+    x = torch.randn(K, device="cuda")
+    y = torch.empty(N, device="cuda")
+    st = torch.cuda.current_stream()
+    L = native.lib()
+
+    def launch(i):
+        native.check(L.tf_op_matmul(C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()), native.TF_Q6_K,
+                                    C.c_void_p(W[i % 8].data_ptr()), N, K, 1, C.c_void_p(st.cuda_stream)))
+
+    for i in range(3):
+        launch(i)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(20)]
+    for i, (a, b) in enumerate(evs):
+        a.record(st)
+        launch(i)
+        b.record(st)
+    torch.cuda.synchronize()
+    t = statistics.median(sorted(a.elapsed_time(b) for a, b in evs)) / 1e3
+    alg = raw.nbytes + K * 4 + N * 4
+    peak, kind = peaks()
+    return {"kernel": "gemv_kernel<1, 3> (Q6_K integer path, 16384x2048)", "achieved": round(alg / t / 1e9, 1),
+            "peak": peak, "unit": "GB/s", "frac": round(alg / t / 1e9 / peak, 4), "peak_kind": kind,
+            "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
+
+
 def config_runs():
     """Batch-1 runs of cfg0 / cfg1 / cfg2 as BASELINE states them (prompt, decode tokens): the
     prompt prefill (tf_cuda_prefill: chunked tensor-core GEMM for the Q8_0 / Q4_0 matrices, the
@@ -478,7 +514,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm", "configs"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -490,6 +526,9 @@ def main():
         return
     if args.kernel == "sweep":
         matmul_sweep()
+        return
+    if args.kernel == "q6k":
+        print(json.dumps(q6k_gemv()))
         return
     if args.kernel == "step":
         from tinferno_b200.model import Model, RunConfig
