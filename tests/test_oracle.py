@@ -199,8 +199,9 @@ def test_oracle_against_golden_synthetic(cfg, model_cache):
     orc.close()
 
 
-def test_weight_bytes_match_survey():
-    # GGUF::weight_bytes() of the BASELINE configs (sum of tensor bytes).
+def test_weight_bytes_of_the_configs():
+    # GGUF::weight_bytes() (src/gguf.cpp:219-223, the sum of tensor bytes) of the four
+    # benchmark configurations: the decode roofline's bytes per token.
     assert synth.weight_bytes(synth.CFG0) == 1_313_251_328
     assert synth.weight_bytes(synth.CFG1) == 525_120_000
     assert synth.weight_bytes(synth.CFG2) == 765_194_240
