@@ -935,8 +935,9 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
                        (long long)a.n_items * a.P * a.rb >= q4_int_min_bytes();
     // Q6_K rows (cfg2's 215 MB lm_head) take the integer path at any size: the fp32 dequant
     // of a 256-element super-block is several times the plane build's cost.  K % 512 keeps the
-    // rows (210 bytes per super-block) 4-byte aligned.
-    const bool q6int = (a.wtype == T_Q6_K) && (a.K % 512 == 0) && a.M == 1;
+    // rows (210 bytes per super-block) 4-byte aligned; single-row items only (Q6_K gate/up
+    // pairs stay on the fp32 path).
+    const bool q6int = (a.wtype == T_Q6_K) && (a.K % 512 == 0) && a.M == 1 && a.P == 1;
     int best = -1;
     for (int ks = 1; ks <= warps; ks <<= 1) {
         if (a.K % ks) continue;

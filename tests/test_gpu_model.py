@@ -114,6 +114,43 @@ def test_persistent_mode_matches_reference(cfg, mini_models):
     k.close()
 
 
+def test_q4_integer_path_on_every_matrix(mini_models, tmp_path):
+    """cfg2 with no size threshold for the Q4_0 exact-integer GEMV (TFB200_Q4_INT_MIN_MB=0, read
+    once per process, so in a child process): the 2-4 MB QKV and wo matrices take the integer
+    path that only 32 MB matrices take by default (gate/up pairs and the K = 8192 down rows
+    exceed its 32 units per warp and stay on the fp32 path); the golden stream stays
+    token-exact and the logits within 1e-2 of the oracle."""
+    import subprocess
+    import sys
+    cfg = MINI[2]
+    path = mini_models[cfg.name]
+    gold = os.path.join(GOLDEN, cfg.name + ".npz")
+    out = tmp_path / "q4int.npz"
+    code = (
+        "import numpy as np\n"
+        "from tinferno_b200.model import Model, RunConfig\n"
+        f"g = np.load({gold!r})\n"
+        f"m = Model({path!r}, RunConfig(max_seq={cfg.max_seq}))\n"
+        "lg = m.prefill(g['prompt']); ids, steps = [], []\n"
+        "for _ in range(len(g['tokens'])):\n"
+        "    steps.append(lg.copy()); ids.append(int(np.argmax(lg))); lg = m.decode(ids[-1])\n"
+        f"np.savez({str(out)!r}, ids=np.array(ids), steps=np.stack(steps))\n"
+    )
+    env = dict(os.environ, TFB200_Q4_INT_MIN_MB="0")
+    env["PYTHONPATH"] = os.pathsep.join(sys.path)
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    got = np.load(out)
+    g = np.load(gold)
+    assert got["ids"].tolist() == g["tokens"].tolist()
+    orc = po.OracleModel(gguf.GGUFReader(path), cfg.max_seq)
+    o_ids, o_steps = po.greedy_stream(orc, g["prompt"], len(g["tokens"]), keep_logits=True)
+    assert o_ids == got["ids"].tolist()
+    err = max(np.abs(a - b).max() for a, b in zip(got["steps"], o_steps))
+    assert err < LOGIT_TOL, err
+    orc.close()
+
+
 def test_graph_and_eager_identical(mini_models):
     cfg = MINI[0]
     path = mini_models[cfg.name]
