@@ -308,7 +308,8 @@ def run_ours(args, rank, world, local_rank, dist):
         if not args.no_cpu and world == 1:
             tps, n, threads, kind = cpu_reference_decode(path, prompt, 512, max_seconds=15.0)
             cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": kind,
-                   "sample": f"1 sequence, {PROMPT}-token prompt (untimed prefill), {n} decode steps (~15 s)"}
+                   "sample": f"1 sequence, {PROMPT}-token prompt (untimed prefill), 3 untimed + {n} timed "
+                             "decode steps (~15 s)"}
         wb = synth.weight_bytes(CFG)
         line = {"metric": "decode tok/s (batch 1, cfg0 Llama-3.2-1B Q8_0)", "value": round(value, 2), "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
