@@ -63,6 +63,19 @@ def stage_preset(stage: str) -> RunConfig:
     return RunConfig()
 
 
+_KV_NAMES = {native.TF_KV_F32: "f32", native.TF_KV_F16: "f16", native.TF_KV_BF16: "bf16"}
+
+
+def describe(arch: str, hp: native.HParams, weight_bytes: int, cfg: RunConfig) -> str:
+    """Model::describe (src/model.cpp:91-105): one line of the model's shape and the run
+    configuration, with the GPU stage's own settings in place of threads / SIMD / blocking."""
+    mode = "persistent" if cfg.decode_mode == native.TF_DECODE_PERSISTENT else "kernels"
+    return (f"arch={arch} layers={hp.n_layer} dim={hp.n_embd} heads={hp.n_head}/{hp.n_kv_head} "
+            f"ff={hp.n_ff} vocab={hp.n_vocab} weights={weight_bytes / 1e6:g} MB stage={cfg.stage} "
+            f"device={cfg.device} kv={_KV_NAMES.get(cfg.kv_type, cfg.kv_type)} max_seq={cfg.max_seq} "
+            f"slots={cfg.max_batch} graph={'on' if cfg.use_graph else 'off'} decode={mode}")
+
+
 def hparams_from_gguf(g: GGUFReader) -> native.HParams:
     a = g.arch
     key = lambda f: f"{a}.{f}"
@@ -134,6 +147,10 @@ class Model:
         self.eos = self.hp.eos
         self.weight_bytes = int(self.L.tf_cuda_weight_bytes(self.h))
         self.kernels_per_step = int(self.L.tf_cuda_kernels_per_step(self.h))
+        self.arch = self.gguf.str("general.architecture", "llama")
+
+    def describe(self) -> str:
+        return describe(self.arch, self.hp, self.weight_bytes, self.cfg)
 
     # ---- the reference API ----
     def prefill(self, tokens: Sequence[int], logits: Optional[np.ndarray] = None, seq: int = 0) -> np.ndarray:

@@ -54,3 +54,17 @@ def test_errors_are_status_codes_without_gpu():
     assert L.tf_cuda_n_vocab(None) == -1
     assert L.tf_op_matmul(None, None, 99, None, 4, 32, 1, None) != 0  # unsupported type
     assert L.tf_op_matmul(None, None, 8, None, 4, 48, 1, None) != 0   # K not a block multiple
+
+
+def test_describe_line():
+    """Model::describe (src/model.cpp:91-105) as the host mirror formats it: the model's shape,
+    then the GPU stage's settings."""
+    from tinferno_b200 import synth
+    from tinferno_b200.model import RunConfig, describe
+    hp = native.HParams()
+    c = synth.CFG0
+    hp.n_vocab, hp.n_embd, hp.n_ff, hp.n_layer = c.n_vocab, c.n_embd, c.n_ff, c.n_layer
+    hp.n_head, hp.n_kv_head = c.n_head, c.n_kv_head
+    line = describe("llama", hp, synth.weight_bytes(c), RunConfig(max_seq=2048))
+    assert line == ("arch=llama layers=16 dim=2048 heads=32/8 ff=8192 vocab=128256 weights=1313.25 MB "
+                    "stage=b200 device=0 kv=f32 max_seq=2048 slots=1 graph=on decode=kernels")
