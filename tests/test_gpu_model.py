@@ -281,13 +281,18 @@ def test_reduced_precision_kv_close(kv, mini_models):
     b.close()
 
 
-FULL = [("cfg0", 32, 64)]
+FULL = [("cfg0", 32, 64), ("cfg1", 512, 128), ("cfg2", 128, 128)]
 
 
 @pytest.mark.slow
 @pytest.mark.parametrize("key,n_prompt,n_decode", FULL)
 def test_full_config_stream(key, n_prompt, n_decode, model_cache):
-    """BASELINE-size model: token-exact greedy stream and logits vs the reference."""
+    """BASELINE-size model: token-exact greedy stream and logits vs the reference.  cfg1 (512
+    prompt tokens in tensor-core chunks, decode across the split fused attention) and cfg2
+    (mixed Q4_0 / Q6_K / Q4_1) run when TFB200_FULL_GOLDEN=1: generating their GGUF files takes
+    minutes of host time on a fresh machine."""
+    if key != "cfg0" and os.environ.get("TFB200_FULL_GOLDEN") != "1":
+        pytest.skip("full-size cfg1 / cfg2 streams run with TFB200_FULL_GOLDEN=1")
     cfg = synth.CONFIGS[key]
     gold_path = os.path.join(GOLDEN, cfg.name + ".npz")
     if not os.path.exists(gold_path):

@@ -206,3 +206,23 @@ def test_weight_bytes_of_the_configs():
     assert synth.weight_bytes(synth.CFG1) == 525_120_000
     assert synth.weight_bytes(synth.CFG2) == 765_194_240
     assert synth.weight_bytes(synth.CFG4) == 1_640_622_080
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("key", ["cfg1", "cfg2"])
+def test_oracle_against_golden_full_size(key, model_cache):
+    """The oracle reproduces the reference build's full-size cfg1 (512 + 128 tokens) and cfg2
+    (128 + 128, Q4_0 / Q6_K / Q4_1) streams bit for bit.  Opt-in (TFB200_FULL_GOLDEN=1): the
+    GGUF files take minutes of host time to generate."""
+    if os.environ.get("TFB200_FULL_GOLDEN") != "1":
+        pytest.skip("full-size streams run with TFB200_FULL_GOLDEN=1")
+    cfg = synth.CONFIGS[key]
+    gold = np.load(os.path.join(GOLDEN, cfg.name + ".npz"))
+    path = synth.model_path(cfg, model_cache)
+    assert synth.file_digest(path) == str(gold["sha256"])
+    orc = po.OracleModel(gguf.GGUFReader(path), cfg.max_seq, threads=os.cpu_count() or 1)
+    ids, steps = po.greedy_stream(orc, gold["prompt"], len(gold["tokens"]), keep_logits=True)
+    assert ids == gold["tokens"].tolist()
+    for s, lg in enumerate(steps):
+        assert np.array_equal(lg[gold["topi"][s]], gold["topv"][s])
+    orc.close()
