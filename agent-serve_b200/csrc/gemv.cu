@@ -17,6 +17,14 @@
 // conflict-free shared loads at a 17-word lane stride); int8 -> fp32 conversion uses the
 // exact magic-number construction 0x4B0000xx - (2^23 + 128) (one PRMT + one FADD), which
 // keeps the conversion off the 16/clk conversion pipe.
+//
+// Exact-integer paths (one activation row; dots.cuh): the prologue turns the row into three
+// signed-byte digit planes per 32-element block, each lane keeps its unit's plane words in
+// registers, and the block sums are exact dp4a sums scaled by the block's d (and 2^-sh):
+// Q8_0 rows (INTQ 1; INTQ 4 is the same kernel with the split fused attention), Q4_0 rows of
+// matrices of 32 MB and more (INTQ 2) and Q6_K rows with K % 512 == 0 (INTQ 3).  Each is its
+// own instantiation, so the Q8_0 kernel that a Q8_0 step launches for every GEMV carries no
+// other path's code or registers.
 #include <algorithm>
 #include <cstdlib>
 
