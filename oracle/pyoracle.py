@@ -78,6 +78,7 @@ def oracle_lib():
         lib.tfo_attn_decode.argtypes = [f32p, f32p, f32p, f32p, C.c_int, C.c_int, C.c_int, C.c_int]
         lib.tfo_attn_prefill.argtypes = [f32p, f32p, f32p, f32p, C.c_int, C.c_int, C.c_int, C.c_int]
         lib.tfo_sample_greedy.argtypes = [f32p, C.c_int]
+        lib.tfo_sample_logits.argtypes = [f32p, C.c_int, C.c_float, C.c_float, C.c_float]
         lib.tfo_model_create.restype = C.c_void_p
         lib.tfo_model_create.argtypes = [C.POINTER(TensorDesc), C.c_int, C.POINTER(HParams), C.c_int,
                                          C.c_int]

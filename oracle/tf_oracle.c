@@ -459,6 +459,63 @@ int tfo_sample_greedy(const float* logits, int n) {
     return b;
 }
 
+/* src/sampler.cpp:15-52 with the caller's uniform draw r in [0, 1) (the reference draws it
+ * inside, uniform_real_distribution<float>(0, 1) over its std::mt19937): the candidates in
+ * descending-logit order, p = exp((l - l_max) / temperature) normalised by the running float
+ * sum, the top-p prefix up to and including the first index where the running sum reaches
+ * top_p (renormalised over that prefix), then the first prefix entry whose running sum is at
+ * least r (the last entry if none).  Logits that tie exactly are ordered by index here; the
+ * reference's std::sort leaves their order unspecified.  temperature <= 0 is greedy. */
+static const float* tfo_sort_keys;
+static int tfo_desc_logit(const void* a, const void* b) {
+    const int i = *(const int*)a, j = *(const int*)b;
+    const float x = tfo_sort_keys[i], y = tfo_sort_keys[j];
+    if (x > y) return -1;
+    if (x < y) return 1;
+    return (i > j) - (i < j);
+}
+
+int tfo_sample_logits(const float* logits, int n, float temperature, float top_p, float r) {
+    if (temperature <= 0.0f) return tfo_sample_greedy(logits, n);
+    int* order = (int*)malloc(sizeof(int) * (size_t)n);
+    float* p = (float*)malloc(sizeof(float) * (size_t)n);
+    for (int i = 0; i < n; ++i) order[i] = i;
+    tfo_sort_keys = logits;
+    qsort(order, (size_t)n, sizeof(int), tfo_desc_logit);
+    const float top = logits[order[0]];
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        p[i] = expf((logits[order[i]] - top) / temperature);
+        sum += p[i];
+    }
+    for (int i = 0; i < n; ++i) p[i] /= sum;
+    int keep = n;
+    if (top_p < 1.0f) {
+        float run = 0.0f;
+        keep = 0;
+        while (keep < n) {
+            run += p[keep];
+            ++keep;
+            if (run >= top_p) break;
+        }
+        float z = 0.0f;
+        for (int i = 0; i < keep; ++i) z += p[i];
+        for (int i = 0; i < keep; ++i) p[i] /= z;
+    }
+    int pick = order[keep - 1];
+    float run = 0.0f;
+    for (int i = 0; i < keep; ++i) {
+        run += p[i];
+        if (r <= run) {
+            pick = order[i];
+            break;
+        }
+    }
+    free(order);
+    free(p);
+    return pick;
+}
+
 /* ---- the token loop ------------------------------------------------------------------ */
 
 typedef struct {

@@ -67,6 +67,8 @@ void tfo_attn_decode(float* out, const float* q, const float* k, const float* v,
 void tfo_attn_prefill(float* out, const float* q, const float* k, const float* v, int seq,
                       int n_heads, int n_kv_heads, int head_dim);
 int tfo_sample_greedy(const float* logits, int n);
+/* sample_logits (src/sampler.cpp:15-52) with the caller's uniform draw r in [0, 1). */
+int tfo_sample_logits(const float* logits, int n, float temperature, float top_p, float r);
 
 typedef struct tfo_model tfo_model;
 tfo_model* tfo_model_create(const tfo_tensor* t, int n_tensors, const tfo_hparams* hp,

@@ -226,3 +226,24 @@ def test_oracle_against_golden_full_size(key, model_cache):
     for s, lg in enumerate(steps):
         assert np.array_equal(lg[gold["topi"][s]], gold["topv"][s])
     orc.close()
+
+
+@needs_ref
+@pytest.mark.parametrize("temp,top_p,seed", [(0.8, 0.9, 42), (1.0, 1.0, 7), (0.3, 0.5, 123), (2.0, 0.95, 5),
+                                             (0.0, 0.9, 1)])
+def test_sampler_restatement_matches_reference(temp, top_p, seed):
+    """sample_logits (src/sampler.cpp:15-52): the oracle's restatement fed by the host's
+    std::mt19937 + uniform_real_distribution<float> restatement (tinferno_b200.model.Mt19937Uniform,
+    one draw per step as src/main.cpp:109-114) picks the ids the reference's own sampler picks
+    with the same seed."""
+    from tinferno_b200.model import Mt19937Uniform
+    n, steps = 4096, 64
+    rng = np.random.default_rng(seed)
+    rows = np.ascontiguousarray((rng.standard_normal((steps, n)) * 2.5).astype(np.float32))
+    want = np.zeros(steps, np.int32)
+    po.ref_lib().ref_sample_logits_steps(fp(rows), n, steps, temp, top_p, seed, want.ctypes.data_as(po.i32p))
+    draws = Mt19937Uniform(seed)
+    O = po.oracle_lib()
+    got = [int(O.tfo_sample_logits(fp(rows[i].copy()), n, temp, top_p, draws.next() if temp > 0 else 0.0))
+           for i in range(steps)]
+    assert got == want.tolist()
