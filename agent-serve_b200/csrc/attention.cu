@@ -17,6 +17,8 @@
 // taken from shared memory, never re-read from the cache slot being written.
 #include <cstdlib>
 
+#include <atomic>
+
 #include "attention.cuh"
 
 namespace tfb {
@@ -74,7 +76,7 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int m, int kvh, 
     if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
 }
 
-__global__ void __launch_bounds__(AT_THREADS) attn_decode_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(AT_THREADS) tf_attn_decode_kernel(const AttnArgs a) {
     extern __shared__ float tile[];
     __shared__ float qs[AT_MAX_REP][AT_MAX_HD];
     __shared__ float kn[AT_MAX_HD], vn[AT_MAX_HD];
@@ -259,7 +261,7 @@ static inline size_t attn_stream_smem_bytes(int hd) {
 }
 
 template <int R>  // query heads per kv head
-__global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const AttnArgs a) {
     extern __shared__ __align__(16) float kvt[];
     __shared__ __align__(16) float qs[R][AT_MAX_HD];
     __shared__ float red[AS_THREADS / 32][R][AS_TILE];  // partial scores per dim slice
@@ -478,7 +480,9 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
                 }
             }
         }
-    if (!ok) return;
+    // a CTA whose tile wait gave up (ERR_WAIT_FULL is recorded) still arrives at its head's
+    // counter, so the counter returns to zero; the call's output is then not valid
+    if (!ok && nsp == 1) return;
     // the combine's scratch reuses the tile buffers
     if (nsp > 1) {
         __syncthreads();
@@ -487,7 +491,7 @@ __global__ void __launch_bounds__(AS_THREADS, 2) attn_stream_kernel(const AttnAr
 }
 
 // ---- prefill attention (attn_prefill): one CTA per (query row i, head h) -----------------
-__global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillAttnArgs a) {
+__global__ void __launch_bounds__(AT_THREADS) tf_attn_prefill_kernel(const PrefillAttnArgs a) {
     extern __shared__ float sbuf[];  // [seq] scores
     __shared__ float qs[AT_MAX_HD];
     __shared__ float red[AT_THREADS / 32];
@@ -547,7 +551,7 @@ __global__ void __launch_bounds__(AT_THREADS) attn_prefill_kernel(const PrefillA
 // One CTA per (row, head), a thread per rotation pair; row m is position pos[slot] + m.  The
 // attention of the chunk then runs over the cache alone (fresh == 2), so that every row sees
 // the keys of the rows before it (attn_prefill's causal mask, src/attention.cpp:82-111).
-__global__ void rope_store_kernel(const AttnArgs a) {
+__global__ void tf_rope_store_kernel(const AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     const int m = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
@@ -610,12 +614,14 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
     if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
     if (a.kv_type == KV_F32 && M * a.n_kv >= 16 && a.hd % 32 == 0) {  // many rows: streaming kernel
         static const void* const fns[AT_MAX_REP] = {
-            (const void*)attn_stream_kernel<1>, (const void*)attn_stream_kernel<2>, (const void*)attn_stream_kernel<3>,
-            (const void*)attn_stream_kernel<4>, (const void*)attn_stream_kernel<5>, (const void*)attn_stream_kernel<6>,
-            (const void*)attn_stream_kernel<7>, (const void*)attn_stream_kernel<8>};
+            (const void*)tf_attn_stream_kernel<1>, (const void*)tf_attn_stream_kernel<2>, (const void*)tf_attn_stream_kernel<3>,
+            (const void*)tf_attn_stream_kernel<4>, (const void*)tf_attn_stream_kernel<5>, (const void*)tf_attn_stream_kernel<6>,
+            (const void*)tf_attn_stream_kernel<7>, (const void*)tf_attn_stream_kernel<8>};
         const int R = a.n_head / a.n_kv;
         const void* fn = fns[R - 1];
-        static bool sattr[64][AT_MAX_REP] = {};
+        // set once per device; setting an attribute twice is harmless, so concurrent first
+        // calls only need the flag itself to be race-free
+        static std::atomic<bool> sattr[64][AT_MAX_REP] = {};
         int dev = 0;
         cudaGetDevice(&dev);
         if (dev < 0 || dev >= 64) dev = 0;
@@ -626,7 +632,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
             // two CTAs per SM need the whole shared-memory carve-out
             e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
             if (e != cudaSuccess) return e;
-            sattr[dev][R - 1] = true;
+            sattr[dev][R - 1].store(true);
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(a.n_kv, attn_stream_splits(a, M), M);
@@ -645,18 +651,18 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
     const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;
     if ((max_pos + a.n_split - 1) / a.n_split > AT_CHUNK || a.n_split > AT_MAX_SPLIT) return cudaErrorInvalidValue;
     const size_t smem = attn_smem_bytes(a.hd);
-    static bool attrs[64] = {false};  // set once per device
+    static std::atomic<bool> attrs[64] = {};  // set once per device (see sattr above)
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!attrs[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(tf_attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)attn_smem_bytes(AT_MAX_HD));
         if (e != cudaSuccess) return e;
-        e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+        e = cudaFuncSetAttribute(tf_attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                                  cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
-        attrs[dev] = true;
+        attrs[dev].store(true);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv, a.n_split, M);
@@ -668,7 +674,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attn_decode_kernel, a);
+    return cudaLaunchKernelEx(&cfg, tf_attn_decode_kernel, a);
 }
 
 cudaError_t rope_store_launch(const AttnArgs& a, int M, cudaStream_t st) {
@@ -682,17 +688,17 @@ cudaError_t rope_store_launch(const AttnArgs& a, int M, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, rope_store_kernel, a);
+    return cudaLaunchKernelEx(&cfg, tf_rope_store_kernel, a);
 }
 
 cudaError_t attn_prefill_launch(const PrefillAttnArgs& a, cudaStream_t st) {
     if (a.hd > AT_MAX_HD) return cudaErrorInvalidValue;
     const size_t smem = (size_t)a.seq * sizeof(float);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(tf_attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    attn_prefill_kernel<<<dim3(a.seq, a.n_head), AT_THREADS, smem, st>>>(a);
+    tf_attn_prefill_kernel<<<dim3(a.seq, a.n_head), AT_THREADS, smem, st>>>(a);
     return cudaGetLastError();
 }
 

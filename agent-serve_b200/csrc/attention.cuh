@@ -31,7 +31,7 @@ struct AttnArgs {
     float* out;             // [M][ld_out]
     int ld_out;
     int fresh;              // 1: decode step (rotate + store + attend over [wstart, pos]);
-                            // 2: prefill chunk of one sequence after rope_store_kernel: row m
+                            // 2: prefill chunk of one sequence after tf_rope_store_kernel: row m
                             //    at pos[slot] + m attends over the cache [wstart, pos] as given
     int n_pos_fixed;        // fresh == 0: attend over n_pos_fixed cached positions, q as given
     int* err;

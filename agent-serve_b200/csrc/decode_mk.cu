@@ -469,7 +469,7 @@ __device__ __noinline__ unsigned long long mk_gemv_stages(const MkCtx& c, const 
 }
 
 // All 8 warps are consumers (two per scheduler: up to 255 registers a thread).
-__global__ void __launch_bounds__(MK_THREADS, 1) decode_mk_kernel(const MkArgs a) {
+__global__ void __launch_bounds__(MK_THREADS, 1) tf_decode_mk_kernel(const MkArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ MkShared S;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -672,19 +672,19 @@ size_t mk_smem_bytes(const MkArgs& a) {
 // Resident CTAs per SM for a given dynamic shared-memory size (the cooperative launch needs
 // one per SM); -1 on an error.
 int mk_occupancy(size_t smem) {
-    if (cudaFuncSetAttribute(decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(tf_decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return -1;
-    if (cudaFuncSetAttribute(decode_mk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+    if (cudaFuncSetAttribute(tf_decode_mk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared) != cudaSuccess)
         return -1;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_mk_kernel, MK_THREADS, smem) != cudaSuccess) return -1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tf_decode_mk_kernel, MK_THREADS, smem) != cudaSuccess) return -1;
     return n;
 }
 
 cudaError_t mk_launch(const MkArgs& a, int grid, cudaStream_t st) {
     const size_t smem = mk_smem_bytes(a);
-    cudaError_t e = cudaFuncSetAttribute(decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(tf_decode_mk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -696,7 +696,7 @@ cudaError_t mk_launch(const MkArgs& a, int grid, cudaStream_t st) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_mk_kernel, a);
+    return cudaLaunchKernelEx(&cfg, tf_decode_mk_kernel, a);
 }
 
 }  // namespace tfb

@@ -29,4 +29,8 @@ int attn_pick_split(int cap);
 std::string& last_error_tls();
 int set_error(const std::string& msg);
 
+constexpr int kMaxDevices = 64;
+// The current device's op-level status word (ops.cu): a static device variable, no allocation.
+int op_err_word(int** out);
+
 }  // namespace tfb

@@ -1,11 +1,11 @@
 // Q8_0 / Q4_0 GEMM for M >= 16 activation rows (see gemm.cuh).
 //
-// Default path, gemm_q8_tc_kernel (5th-gen tensor cores): a CTA of 512 threads owns 128
+// Default path, tf_gemm_q8_tc_kernel (5th-gen tensor cores): a CTA of 512 threads owns 128
 // weight rows x NT (128 or 256) activation rows, k in stages of 64, double-buffered in
 // 128-byte swizzled K-major shared memory.  Four threads per weight row dequantise 16-weight
 // pieces from registers (the words of a stage are requested four stages ahead, the first
 // ones before the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw; the activation halves
-// Xh, Xl (prepared once per matmul by xprep_kernel) arrive by cp.async.  Thread 0 issues
+// Xh, Xl (prepared once per matmul by tf_xprep_kernel) arrive by cp.async.  Thread 0 issues
 // tcgen05.mma (kind::f16, fp32 accumulator in TMEM) three times per k step: Wh*Xh, Wh*Xl,
 // Wl*Xh.  The epilogue reads TMEM, scales back by 2^-(sw+sx[m]) (per-column factors computed
 // once), stages the tile in shared memory and, when the k range is split, sums the splits of
@@ -13,7 +13,7 @@
 // then the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
 //
-// Comparison path, gemm_q8_kernel (TFB200_GEMM_TC05=0): the same arithmetic on
+// Comparison path, tf_gemm_q8_kernel (TFB200_GEMM_TC05=0): the same arithmetic on
 // mma.sync.m16n8k16 with 256 threads and a global-workspace split-K reduction.
 #include <cstdlib>
 
@@ -25,7 +25,7 @@ namespace tfb {
 // ---- activation preparation ----------------------------------------------------------------
 // One CTA per activation row: [embedding lookup ->] [RMSNorm (src/layers.cpp:7-12) ->]
 // power-of-two scale to |x| < 2^14 -> f16 halves.
-__global__ void __launch_bounds__(256) xprep_kernel(const XPrepArgs a) {
+__global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
     extern __shared__ __align__(16) float xrow[];  // xpad layout
     __shared__ double redd[8];
     __shared__ float redf[8];
@@ -454,7 +454,7 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
     }
 }
 
-__global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(GM_THREADS, 1) tf_gemm_q8_kernel(const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * GM_BM;
@@ -566,7 +566,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) gemm_q8_kernel(const GemmArgs a
 }
 
 // ---- the GEMM on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) ---------------
-// Same arithmetic and epilogue as gemm_q8_kernel; the products run as tcgen05.mma
+// Same arithmetic and epilogue as tf_gemm_q8_kernel; the products run as tcgen05.mma
 // (kind::f16, M = 128 weight rows, N = NT activation rows, K = 16) issued by one thread, with the
 // fp32 accumulator in tensor memory.  Operands sit in shared memory in the canonical K-major
 // 128-byte-swizzled layout: a row's 64 k values (128 B) form one line of an 8-line, 1024-byte
@@ -615,7 +615,7 @@ constexpr size_t gemm_tc_smem_bytes() {
 
 
 template <int NT, bool Q4>
-__global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the swizzle atoms need 1024-byte aligned stage buffers
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -774,7 +774,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) gemm_q8_tc_kernel(const Gemm
 }
 
 // ---- end of a step at M rows ------------------------------------------------------------------
-__global__ void finish_kernel(const FinishArgs a) {
+__global__ void tf_finish_kernel(const FinishArgs a) {
     __shared__ int gs_s;
     pdl_trigger();
     pdl_wait();
@@ -813,10 +813,10 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     const size_t smem = (size_t)xpad_len(a.K) * 4;
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(xprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(tf_xprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    xprep_kernel<<<a.M, 256, smem, st>>>(a);
+    tf_xprep_kernel<<<a.M, 256, smem, st>>>(a);
     return cudaGetLastError();
 }
 
@@ -849,7 +849,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) dev = 0;
     if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaError_t e = cudaFuncSetAttribute(tf_gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         attr_set[dev] = true;
     }
@@ -861,8 +861,8 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         const bool wide = gemm_tile_rows(a.M) == 256;
         const size_t sm = wide ? gemm_tc_smem_bytes<256>() : gemm_tc_smem_bytes<128>();
         const bool q4 = a.wq4 != 0;
-        const void* fn = q4 ? (wide ? (const void*)gemm_q8_tc_kernel<256, true> : (const void*)gemm_q8_tc_kernel<128, true>)
-                            : (wide ? (const void*)gemm_q8_tc_kernel<256, false> : (const void*)gemm_q8_tc_kernel<128, false>);
+        const void* fn = q4 ? (wide ? (const void*)tf_gemm_q8_tc_kernel<256, true> : (const void*)tf_gemm_q8_tc_kernel<128, true>)
+                            : (wide ? (const void*)tf_gemm_q8_tc_kernel<256, false> : (const void*)tf_gemm_q8_tc_kernel<128, false>);
         static bool tc_attr[64][2][2] = {};
         int dv = 0;
         cudaGetDevice(&dv);
@@ -895,18 +895,18 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
     GemmArgs aa = a;
     void* args[] = {&aa};
-    return launch_pdl((const void*)gemm_q8_kernel, grid, dim3(GM_THREADS), smem, st, args);
+    return launch_pdl((const void*)tf_gemm_q8_kernel, grid, dim3(GM_THREADS), smem, st, args);
 }
 
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {
     FinishArgs aa = a;
     void* args[] = {&aa};
-    return launch_pdl((const void*)finish_kernel, dim3(1), dim3(256), 0, st, args);
+    return launch_pdl((const void*)tf_finish_kernel, dim3(1), dim3(256), 0, st, args);
 }
 
 // Device version of q8_scale_exponent for weights that live only on the device: the largest
 // |d| bits over all blocks (one pass over the scale bytes).
-__global__ void q8_dmax_kernel(const uint8_t* W, long long n_blocks, int block_bytes, unsigned* out) {
+__global__ void tf_q8_dmax_kernel(const uint8_t* W, long long n_blocks, int block_bytes, unsigned* out) {
     unsigned mx = 0;
     for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
         const unsigned d = ((unsigned)W[b * block_bytes] | ((unsigned)W[b * block_bytes + 1] << 8)) & 0x7FFFu;
@@ -926,7 +926,7 @@ cudaError_t q8_scale_exponent_device(const uint8_t* W, long long n_blocks, unsig
                                      int block_bytes) {
     cudaError_t e = cudaMemsetAsync(scratch, 0, sizeof(unsigned), st);
     if (e != cudaSuccess) return e;
-    q8_dmax_kernel<<<296, 256, 0, st>>>(W, n_blocks, block_bytes, scratch);
+    tf_q8_dmax_kernel<<<296, 256, 0, st>>>(W, n_blocks, block_bytes, scratch);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     unsigned h = 0;
     if ((e = cudaMemcpyAsync(&h, scratch, sizeof(unsigned), cudaMemcpyDeviceToHost, st)) != cudaSuccess) return e;

@@ -300,7 +300,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
 // integer path whose fused attention splits each head's positions over several CTAs (each its
 // own function, so the Q8_0 kernel that every GEMV of a Q8_0 step runs carries no other code)
 template <int MAXM, int INTQ>
-__global__ void __launch_bounds__(GV_THREADS, 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int xl = xpad_len(a.K);
@@ -986,11 +986,11 @@ int gemv_max_rows(int K) {
 template <int MAXM, int INTQ>
 static cudaError_t init_one() {
     cudaError_t e =
-        cudaFuncSetAttribute(gemv_kernel<MAXM, INTQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     // every kernel of the step asks for the same (maximal) shared-memory carve-out, so the
     // SMs never have to drain to re-partition L1 / shared memory between kernels
-    return cudaFuncSetAttribute(gemv_kernel<MAXM, INTQ>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    return cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                 cudaSharedmemCarveoutMaxShared);
 }
 
@@ -1019,7 +1019,7 @@ static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemv_kernel<MAXM, INTQ>, a);
+    return cudaLaunchKernelEx(&cfg, tf_gemv_kernel<MAXM, INTQ>, a);
 }
 
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {

@@ -6,7 +6,7 @@
 namespace tfb {
 
 // rmsnorm  src/layers.cpp:7-12 (sum of squares in double; out = (x * inv) * w)
-__global__ void rmsnorm_kernel(float* out, const float* x, const float* w, int n, float eps) {
+__global__ void tf_rmsnorm_kernel(float* out, const float* x, const float* w, int n, float eps) {
     __shared__ double red[32];
     const float* xr = x + (size_t)blockIdx.x * n;
     float* o = out + (size_t)blockIdx.x * n;
@@ -22,7 +22,7 @@ __global__ void rmsnorm_kernel(float* out, const float* x, const float* w, int n
 }
 
 // silu_mul  src/layers.cpp:14-19
-__global__ void silu_mul_kernel(float* g, const float* u, int n) {
+__global__ void tf_silu_mul_kernel(float* g, const float* u, int n) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const float v = g[i];
         g[i] = __fmul_rn(__fdiv_rn(v, 1.0f + expf(-v)), u[i]);
@@ -30,7 +30,7 @@ __global__ void silu_mul_kernel(float* g, const float* u, int n) {
 }
 
 // softmax  src/layers.cpp:25-35 (one block per row)
-__global__ void softmax_kernel(float* x, int n) {
+__global__ void tf_softmax_kernel(float* x, int n) {
     __shared__ float red[32];
     __shared__ float stat;
     float* r = x + (size_t)blockIdx.x * n;
@@ -67,7 +67,7 @@ __global__ void softmax_kernel(float* x, int n) {
 }
 
 // apply_rope_many  src/attention.cpp:31-53 with the reference build's contraction
-__global__ void rope_kernel(float* x, int seq, int n_heads, int hd, int pos0, const float* freq) {
+__global__ void tf_rope_kernel(float* x, int seq, int n_heads, int hd, int pos0, const float* freq) {
     const int d2 = hd / 2;
     const long long total = (long long)seq * n_heads * d2;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -84,7 +84,7 @@ __global__ void rope_kernel(float* x, int seq, int n_heads, int hd, int pos0, co
 }
 
 // sample_greedy  src/sampler.cpp:8-13: single pass, one block per row, u64 key max
-__global__ void argmax_kernel(const float* logits, int n, int* out) {
+__global__ void tf_argmax_kernel(const float* logits, int n, int* out) {
     __shared__ unsigned long long best;
     if (threadIdx.x == 0) best = 0ull;
     __syncthreads();
@@ -102,8 +102,17 @@ __global__ void argmax_kernel(const float* logits, int n, int* out) {
 // dequant_row  src/quant.cpp:133-145 for a list of rows
 __device__ void embed_row_global(float* out, const uint8_t* E, int t, long long rb, int K, long long tok);
 
-__global__ void dequant_rows_kernel(float* out, const uint8_t* W, int t, long long rb, int K, const int* rows) {
-    embed_row_global(out + (size_t)blockIdx.x * K, W, t, rb, K, rows[blockIdx.x]);
+// Row ids outside [0, N) read nothing: the output row is zero and ERR_BAD_TOKEN is recorded.
+__global__ void tf_dequant_rows_kernel(float* out, const uint8_t* W, int t, long long rb, int N, int K, const int* rows,
+                                       int* err) {
+    const int r = rows[blockIdx.x];
+    float* o = out + (size_t)blockIdx.x * K;
+    if (r < 0 || r >= N) {
+        for (int e = threadIdx.x; e < K; e += blockDim.x) o[e] = 0.f;
+        if (threadIdx.x == 0) atomicCAS(err, 0, ERR_BAD_TOKEN);
+        return;
+    }
+    embed_row_global(o, W, t, rb, K, r);
 }
 
 __device__ void embed_row_global(float* out, const uint8_t* E, int t, long long rb, int K, long long tok) {
@@ -144,15 +153,15 @@ __device__ void embed_row_global(float* out, const uint8_t* E, int t, long long 
 }
 
 cudaError_t launch_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, cudaStream_t st) {
-    rmsnorm_kernel<<<rows, 256, 0, st>>>(out, x, w, n, eps);
+    tf_rmsnorm_kernel<<<rows, 256, 0, st>>>(out, x, w, n, eps);
     return cudaGetLastError();
 }
 cudaError_t launch_silu_mul(float* g, const float* u, int n, cudaStream_t st) {
-    silu_mul_kernel<<<(n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096, 256, 0, st>>>(g, u, n);
+    tf_silu_mul_kernel<<<(n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096, 256, 0, st>>>(g, u, n);
     return cudaGetLastError();
 }
 cudaError_t launch_softmax(float* x, int n, int rows, cudaStream_t st) {
-    softmax_kernel<<<rows, 256, 0, st>>>(x, n);
+    tf_softmax_kernel<<<rows, 256, 0, st>>>(x, n);
     return cudaGetLastError();
 }
 cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float* freq, cudaStream_t st) {
@@ -160,15 +169,17 @@ cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float
     int blocks = (int)((total + 255) / 256);
     if (blocks > 4096) blocks = 4096;
     if (blocks < 1) blocks = 1;
-    rope_kernel<<<blocks, 256, 0, st>>>(x, seq, nh, hd, pos0, freq);
+    tf_rope_kernel<<<blocks, 256, 0, st>>>(x, seq, nh, hd, pos0, freq);
     return cudaGetLastError();
 }
 cudaError_t launch_argmax(const float* logits, int n, int rows, int* out, cudaStream_t st) {
-    argmax_kernel<<<rows, 1024, 0, st>>>(logits, n, out);
+    tf_argmax_kernel<<<rows, 1024, 0, st>>>(logits, n, out);
     return cudaGetLastError();
 }
-cudaError_t launch_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, cudaStream_t st) {
-    dequant_rows_kernel<<<n_rows, 256, 0, st>>>(out, static_cast<const uint8_t*>(W), t, row_bytes(t, K), K, rows);
+cudaError_t launch_dequant_rows(float* out, int t, const void* W, int N, int K, const int* rows, int n_rows, int* err,
+                                cudaStream_t st) {
+    tf_dequant_rows_kernel<<<n_rows, 256, 0, st>>>(out, static_cast<const uint8_t*>(W), t, row_bytes(t, K), N, K, rows,
+                                                   err);
     return cudaGetLastError();
 }
 

@@ -36,7 +36,6 @@ cudaError_t launch_silu_mul(float* g, const float* u, int n, cudaStream_t st);
 cudaError_t launch_softmax(float* x, int n, int rows, cudaStream_t st);
 cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float* freq, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int n, int rows, int* out, cudaStream_t st);
-cudaError_t launch_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, cudaStream_t st);
 
 std::string& last_error_tls() {
     static thread_local std::string s;

@@ -1,5 +1,6 @@
 // Op-level C-ABI (tf_op_*): each reference op on device pointers, for the cfg3 kernel sweep
 // and for op-by-op parity against the reference.
+#include <mutex>
 #include <string>
 
 #include "attention.cuh"
@@ -12,7 +13,36 @@ cudaError_t launch_silu_mul(float* g, const float* u, int n, cudaStream_t st);
 cudaError_t launch_softmax(float* x, int n, int rows, cudaStream_t st);
 cudaError_t launch_rope(float* x, int seq, int nh, int hd, int pos0, const float* freq, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int n, int rows, int* out, cudaStream_t st);
-cudaError_t launch_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, cudaStream_t st);
+cudaError_t launch_dequant_rows(float* out, int t, const void* W, int N, int K, const int* rows, int n_rows, int* err,
+                                cudaStream_t st);
+}  // namespace tfb
+
+namespace tfb {
+
+// Status word of the op-level kernels: a __device__ variable has its own instance on every
+// device that loads the module, so each device has one word, and nothing is allocated.
+// Kernels record the first ERR_* code with atomicCAS; tf_op_device_error reads and clears it.
+static __device__ int op_dev_err;
+
+int op_err_word(int** out) {
+    static std::mutex mu;
+    static int* words[kMaxDevices] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return set_error(std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return set_error("device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!words[dev]) {
+        e = cudaGetSymbolAddress((void**)&words[dev], op_dev_err);
+        if (e != cudaSuccess) {
+            words[dev] = nullptr;
+            return set_error(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        }
+    }
+    *out = words[dev];
+    return 0;
+}
+
 }  // namespace tfb
 
 using namespace tfb;
@@ -23,18 +53,7 @@ int op_status(cudaError_t e, const char* what) {
     return 0;
 }
 bool type_ok(int t) { return t == T_F32 || t == T_F16 || t == T_Q4_0 || t == T_Q4_1 || t == T_Q8_0 || t == T_Q6_K; }
-
-int* g_err_word = nullptr;  // device error word for op-level launches (one per process)
-int err_word(int** out) {
-    if (!g_err_word) {
-        cudaError_t e = cudaMalloc(&g_err_word, sizeof(int));
-        if (e != cudaSuccess) return op_status(e, "cudaMalloc");
-        e = cudaMemset(g_err_word, 0, sizeof(int));
-        if (e != cudaSuccess) return op_status(e, "cudaMemset");
-    }
-    *out = g_err_word;
-    return 0;
-}
+int err_word(int** out) { return op_err_word(out); }
 }  // namespace
 
 extern "C" {
@@ -191,10 +210,28 @@ int tf_op_matmul(float* C, const float* A, int t, const void* W, int N, int K, i
     return 0;
 }
 
-int tf_op_dequant_rows(float* out, int t, const void* W, int K, const int* rows, int n_rows, void* stream) {
+int tf_op_dequant_rows(float* out, int t, const void* W, int N, int K, const int* rows, int n_rows, void* stream) {
     if (!type_ok(t)) return set_error("unsupported ggml type");
+    if (N <= 0 || K <= 0 || K % blk_elems(t)) return set_error("bad matrix shape");
     if (n_rows <= 0) return 0;
-    return op_status(launch_dequant_rows(out, t, W, K, rows, n_rows, static_cast<cudaStream_t>(stream)), "dequant_rows");
+    int* err = nullptr;
+    if (err_word(&err)) return -1;
+    return op_status(launch_dequant_rows(out, t, W, N, K, rows, n_rows, err, static_cast<cudaStream_t>(stream)),
+                     "dequant_rows");
+}
+
+int tf_op_device_error(void* stream, int* code) {
+    if (!code) return set_error("code must not be null");
+    *code = 0;
+    int* err = nullptr;
+    if (err_word(&err)) return -1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (op_status(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, st), "cudaMemcpyAsync")) return -1;
+    if (op_status(cudaStreamSynchronize(st), "cudaStreamSynchronize")) return -1;
+    if (h && op_status(cudaMemsetAsync(err, 0, sizeof(int), st), "cudaMemsetAsync")) return -1;
+    *code = h;
+    return 0;
 }
 
 int tf_op_rmsnorm(float* out, const float* x, const float* w, int n, int rows, float eps, void* stream) {
@@ -220,7 +257,9 @@ int tf_op_rope(float* x, int seq, int n_heads, int head_dim, int pos0, const flo
 int tf_op_attn_decode(float* out, const float* q, const void* k_cache, const void* v_cache, int kv_type, int cap,
                       int n_pos, int n_heads, int n_kv_heads, int head_dim, void* stream) {
     if (n_pos <= 0 || n_pos > cap) return set_error("n_pos must be in [1, cap]");
-    if (n_heads % n_kv_heads) return set_error("n_heads must be a multiple of n_kv_heads");
+    if (n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads)
+        return set_error("n_heads must be a positive multiple of n_kv_heads");
+    if (head_dim <= 0 || head_dim % 8) return set_error("head_dim must be a positive multiple of 8");
     int* err = nullptr;
     if (err_word(&err)) return -1;
     const int n_split = attn_pick_split(n_pos);

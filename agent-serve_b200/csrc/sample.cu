@@ -18,7 +18,7 @@ namespace tfb {
 constexpr int SM_THREADS = 1024;
 
 // descending-order radix keys of the logits (monotone map of the float bits, inverted)
-__global__ void sample_keys_kernel(const float* logits, int n, uint32_t* keys, int* vals) {
+__global__ void tf_sample_keys_kernel(const float* logits, int n, uint32_t* keys, int* vals) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const uint32_t u = __float_as_uint(logits[i]);
@@ -55,7 +55,7 @@ __device__ double block_exclusive_scan(double v, double* sh, double& total) {
 }
 
 // One CTA: softmax over the sorted logits, top-p cut, pick with r.
-__global__ void __launch_bounds__(SM_THREADS) sample_pick_kernel(const float* logits, const int* order, int n,
+__global__ void __launch_bounds__(SM_THREADS) tf_sample_pick_kernel(const float* logits, const int* order, int n,
                                                                  float temperature, float top_p, float r, int* out) {
     __shared__ double sh[SM_THREADS / 32];
     __shared__ int found;
@@ -167,13 +167,13 @@ void sample_scratch_destroy(SampleScratch* s) {
 cudaError_t sample_launch(SampleScratch* s, const float* logits, int n, float temperature, float top_p, float r,
                           cudaStream_t st) {
     if (!s || n > s->n || n <= 0) return cudaErrorInvalidValue;
-    sample_keys_kernel<<<(n + 255) / 256, 256, 0, st>>>(logits, n, s->keys_in, s->vals_in);
+    tf_sample_keys_kernel<<<(n + 255) / 256, 256, 0, st>>>(logits, n, s->keys_in, s->vals_in);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     size_t tb = s->temp_bytes;
     e = cub::DeviceRadixSort::SortPairs(s->temp, tb, s->keys_in, s->keys_out, s->vals_in, s->vals_out, n, 0, 32, st);
     if (e != cudaSuccess) return e;
-    sample_pick_kernel<<<1, SM_THREADS, 0, st>>>(logits, s->vals_out, n, temperature, top_p, r, s->out);
+    tf_sample_pick_kernel<<<1, SM_THREADS, 0, st>>>(logits, s->vals_out, n, temperature, top_p, r, s->out);
     return cudaGetLastError();
 }
 

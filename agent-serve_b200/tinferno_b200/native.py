@@ -20,6 +20,8 @@ i32p = C.POINTER(C.c_int)
 TF_F32, TF_F16, TF_Q4_0, TF_Q4_1, TF_Q8_0, TF_Q6_K = 0, 1, 2, 3, 8, 14
 TF_KV_F32, TF_KV_F16, TF_KV_BF16 = 0, 1, 2
 TF_DECODE_KERNELS, TF_DECODE_PERSISTENT = 0, 1
+(TF_DEV_ERR_NONE, TF_DEV_ERR_WAIT_FULL, TF_DEV_ERR_WAIT_EMPTY, TF_DEV_ERR_BAD_INDEX, TF_DEV_ERR_POS,
+ TF_DEV_ERR_GRID_SYNC) = range(6)
 
 
 class TensorDesc(C.Structure):
@@ -61,7 +63,8 @@ SIGNATURES = [
     ("tf_cuda_kernels_per_step", C.c_int, [_V]),
     ("tf_cuda_last_error", C.c_char_p, [_V]),
     ("tf_op_matmul", C.c_int, [_V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V]),
-    ("tf_op_dequant_rows", C.c_int, [_V, C.c_int, _V, C.c_int, _V, C.c_int, _V]),
+    ("tf_op_dequant_rows", C.c_int, [_V, C.c_int, _V, C.c_int, C.c_int, _V, C.c_int, _V]),
+    ("tf_op_device_error", C.c_int, [_V, i32p]),
     ("tf_op_rmsnorm", C.c_int, [_V, _V, _V, C.c_int, C.c_int, C.c_float, _V]),
     ("tf_op_silu_mul", C.c_int, [_V, _V, C.c_int, _V]),
     ("tf_op_softmax", C.c_int, [_V, C.c_int, C.c_int, _V]),

@@ -42,6 +42,7 @@ class ModelConfig:
     etype: int = GGML_Q8_0     # token_embd (= lm_head, tied)
     down_override: Tuple[Tuple[int, int], ...] = ()  # (layer, type) for ffn_down
     bias: bool = False
+    rope_llama3: bool = False  # rope.scaling.type = "llama3" (Llama 3.x frequency smoothing)
     seed: int = 42
     n_prompt: int = 32
     n_decode: int = 64
@@ -71,6 +72,10 @@ CFG4 = ModelConfig("cfg4-qwen25-1.5b-q8_0-bias", "qwen2", 151936, 1536, 28, 12, 
                    bias=True, n_prompt=1024, n_decode=128, max_seq=1152)
 
 CONFIGS: Dict[str, ModelConfig] = {"cfg0": CFG0, "cfg1": CFG1, "cfg2": CFG2, "cfg4": CFG4}
+
+# cfg0 with the llama3 RoPE frequency scaling of real Llama 3.2 files (src/attention.cpp:14-26);
+# a parity case for that branch, not a benchmark configuration
+CFG0_LLAMA3 = replace(CFG0, name="cfg0-llama3rope-q8_0", rope_llama3=True, n_prompt=40, n_decode=24)
 
 
 def mini(cfg: ModelConfig, n_layer: int = 2, n_vocab: int = 4096, **kw) -> ModelConfig:
@@ -114,6 +119,13 @@ def metadata(cfg: ModelConfig):
           f"{a}.attention.head_count": cfg.n_head, f"{a}.attention.head_count_kv": cfg.n_kv_head,
           f"{a}.rope.dimension_count": cfg.head_dim, f"{a}.context_length": cfg.max_seq}
     mf = {f"{a}.rope.freq_base": cfg.rope_theta, f"{a}.attention.layer_norm_rms_epsilon": cfg.rms_eps}
+    if cfg.rope_llama3:
+        # the keys src/model.cpp:28-37 reads, with Llama 3.2's published values
+        ms[f"{a}.rope.scaling.type"] = "llama3"
+        mf[f"{a}.rope.scaling.factor"] = 32.0
+        mf[f"{a}.rope.scaling.low_freq_factor"] = 1.0
+        mf[f"{a}.rope.scaling.high_freq_factor"] = 4.0
+        mu[f"{a}.rope.scaling.original_context_length"] = 8192
     return ms, mu, mf
 
 

@@ -12,8 +12,13 @@ shard: replicas only) and the value is the aggregate tok/s.
   value      tok/s with the token fed back on the device (graph replays, no host round trip)
   e2e        tok/s through the reference-facing call tf_cuda_decode(token -> host logits),
              one host->device token copy and one device->host logits copy per step
-  roofline   the Q8_0 dequant-GEMV kernel (every matmul of the step runs on it) timed alone
-             on the lm_head shape, algorithmic bytes / launch time vs MEASURED_PEAKS.json
+  roofline   the step's kernel (every launch of the decode step runs it): the bytes a step
+             must read (weights + cached K/V) over the CUDA-event time per step, vs
+             MEASURED_PEAKS.json; roofline_lmhead is the same kernel timed alone on the
+             lm_head shape
+  configs    (N = 1) batch-1 prefill + decode of cfg0 / cfg1 / cfg2 at their BASELINE lengths
+  batched    cfg4: 256 sequences sharded over the ranks, with the greedy ids of the golden
+             subset compared against the reference build's (after the timed region)
   cpu_baseline  the reference engine's stage-v2 path (oracle/_ref, built from the reference's
              own sources) on this host's cores, on a bounded sample of the same decode
 
@@ -41,6 +46,11 @@ PROMPT = 32
 # DRAM bytes (read + write) of one lm_head GEMV launch, from an ncu capture of
 # `bench.py --kernel lmhead` (profiles/gemv_q8_0_lmhead_128256x2048.md)
 LMHEAD_TRAFFIC = 283_513_088
+# the kernel every launch of the batch-1 decode step runs, and its DRAM bytes per step (sum
+# over the step's launches of one ncu capture), when measured
+STEP_KERNEL = "tf_gemv_kernel<1, 1> (Q8_0 integer-path GEMV; attention fused into the QKV launches)"
+STEP_TRAFFIC = None
+STEP_TRAFFIC_SOURCE = "not captured"
 
 
 def peaks():
@@ -145,8 +155,10 @@ def run_batched(args, rank, world, local_rank, dist):
     tok = m.prefill_batch(slots, prompts)
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
+    hist = [tok]  # every step's ids come back to the host anyway; kept for the parity check
     for _ in range(warm):
         tok = m.decode_batch(slots, tok.tolist())
+        hist.append(tok)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -154,13 +166,34 @@ def run_batched(args, rank, world, local_rank, dist):
     ev0.record(stream)
     for _ in range(steps):
         tok = m.decode_batch(slots, tok.tolist())
+        hist.append(tok)
     ev1.record(stream)
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
+    # parity (after the timed region): the reference build's greedy ids of the golden subset
+    # of sequences, where this rank holds them
+    checked, failed, compared = 0, 0, 0
+    gold_path = os.path.join(ROOT, "tests", "golden", cfg.name + "-subset.npz")
+    if os.path.exists(gold_path):
+        gold = np.load(gold_path)
+        ids = np.stack(hist)  # [1 + warm + steps][S]
+        for i, g in enumerate(gold["seqs"].tolist()):
+            if s0 <= g < s1:
+                n = min(ids.shape[0], gold["tokens"].shape[1])
+                checked += 1
+                compared = n
+                failed += int(not np.array_equal(ids[:n, g - s0], gold["tokens"][i][:n]))
     t = torch.tensor([ms, prefill_s], device="cuda")
+    pc = torch.tensor([checked, failed, compared], device="cuda", dtype=torch.float64)
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(pc, op=dist.ReduceOp.SUM)
     ms_max, prefill_max = float(t[0].item()), float(t[1].item())
+    n_chk, n_fail = int(pc[0].item()), int(pc[1].item())
+    parity = {"status": ("ok" if n_fail == 0 else "fail") if n_chk else "no golden",
+              "sequences_checked": n_chk, "sequences_failed": n_fail,
+              "ids_per_sequence": compared if n_chk else 0,
+              "against": "greedy ids of the reference build (tests/golden/" + cfg.name + "-subset.npz)"}
     kps = m.kernels_per_step
     m.close()
     cpu = batched_cpu_baseline(cfg) if (rank == 0 and world == 1 and not args.no_cpu) else None
@@ -176,6 +209,7 @@ def run_batched(args, rank, world, local_rank, dist):
             "hbm_roofline": {"bytes_per_step_per_gpu": int(step_bytes),
                              "achieved_gbs": round(step_bytes / (ms_max / steps / 1e3) / 1e9, 1),
                              "frac_of_peak": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / peaks()[0], 4)},
+            "parity": parity,
             "path": "tcgen05 GEMM (f16-split, TMEM accumulator) at >= 16 rows per step, split flash-decode attention",
             "e2e": "every step copies S token ids in and S greedy ids out (host)", "cpu_baseline": cpu}
 
@@ -313,10 +347,10 @@ def run_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e = world * args.steps / float(t.item())
 
-    # ---- roofline: the Q8_0 GEMV kernel alone on the lm_head shape ----
-    roof = None
+    # ---- the lm_head-shape GEMV alone (secondary roofline figure) ----
+    roof_lm = None
     if rank == 0:
-        roof = gemv_roofline(torch, native, m)
+        roof_lm = gemv_roofline(torch, native, m)
     kps = m.kernels_per_step
     m.close()
 
@@ -328,21 +362,35 @@ def run_ours(args, rank, world, local_rank, dist):
                    "sample": f"1 sequence, {PROMPT}-token prompt (untimed prefill), 3 untimed + {n} timed "
                              "decode steps (~15 s)"}
         wb = synth.weight_bytes(CFG)
+        # bytes one decode step reads: every weight (GGUF::weight_bytes, src/gguf.cpp:219-223)
+        # + the fp32 K/V rows of every cached position, at the timed region's mean position
+        kv_pos = 2 * CFG.n_layer * CFG.n_kv_head * CFG.head_dim * 4
+        mean_pos = PROMPT + args.warmup + args.steps / 2
+        step_bytes = wb + kv_pos * mean_pos
+        peak, peak_kind = peaks()
+        ach = step_bytes / (ms_max / args.steps / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": STEP_KERNEL, "scope": "every launch of the decode step (the whole "
+                "step runs on this kernel), timed with CUDA events over the timed region",
+                "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "peak_kind": peak_kind, "traffic": STEP_TRAFFIC, "traffic_source": STEP_TRAFFIC_SOURCE,
+                "algorithmic_bytes_per_step": int(step_bytes)}
         line = {"metric": "decode tok/s (batch 1, cfg0 Llama-3.2-1B Q8_0)", "value": round(value, 2), "unit": "tok/s",
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": {"workload": "cfg0 batch-1 greedy decode after a 32-token prompt (replicas per GPU)",
-                           "model": CFG.name, "global_batch": world, "seq_len": PROMPT + 2 * args.warmup + args.steps,
+                           "model": CFG.name, "global_batch": world, "seq_len": PROMPT + args.warmup + args.steps,
                            "parallelism": f"replicas x{world}", "kv_cache": "f32",
                            "l2": "weights 1.31 GB per step stream through the 126 MB L2 (inputs larger than L2)"},
-                "hbm_roofline": {"bytes_per_token": wb, "achieved_gbs": round(wb * value / world / 1e9, 1),
-                                 "frac_of_peak": round(wb * value / world / 1e9 / peaks()[0], 4),
-                                 "peak_gbs": peaks()[0], "peak_kind": peaks()[1]},
-                "roofline": roof, "cpu_baseline": cpu,
+                "roofline": roof, "roofline_lmhead": roof_lm, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                         "d2h_bytes_per_step": 4 * CFG.n_vocab + 8},
                 "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk}
+        if world == 1 and not args.no_configs:
+            try:
+                line["configs"] = config_runs()
+            except Exception as e:  # never fatal to the headline line
+                line["configs"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     batched = None
     if not args.no_batched:
         batched = run_batched(args, rank, world, local_rank, dist)
@@ -383,7 +431,7 @@ def gemv_roofline(torch, native, m, reps=50, warm=5):
     alg = nbytes + K * 4 + N * 4
     peak, kind = peaks()
     ach = alg / t / 1e9
-    return {"bound": "hbm", "kernel": "gemv_kernel<1> (Q8_0, lm_head 128256x2048)", "achieved": round(ach, 1),
+    return {"bound": "hbm", "kernel": "tf_gemv_kernel<1> (Q8_0, lm_head 128256x2048)", "achieved": round(ach, 1),
             "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "peak_kind": kind,
             "traffic": LMHEAD_TRAFFIC, "traffic_source": "ncu dram__bytes_read+write of one launch, "
             "profiles/gemv_q8_0_lmhead_128256x2048.md", "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
@@ -420,7 +468,7 @@ def q6k_gemv():
     t = statistics.median(sorted(a.elapsed_time(b) for a, b in evs)) / 1e3
     alg = raw.nbytes + K * 4 + N * 4
     peak, kind = peaks()
-    return {"kernel": "gemv_kernel<1, 3> (Q6_K integer path, 16384x2048)", "achieved": round(alg / t / 1e9, 1),
+    return {"kernel": "tf_gemv_kernel<1, 3> (Q6_K integer path, 16384x2048)", "achieved": round(alg / t / 1e9, 1),
             "peak": peak, "unit": "GB/s", "frac": round(alg / t / 1e9 / peak, 4), "peak_kind": kind,
             "algorithmic_bytes": alg, "launch_us": round(t * 1e6, 2)}
 
@@ -531,6 +579,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline sample")
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
+    ap.add_argument("--no-configs", action="store_true", help="skip the cfg1 / cfg2 batch-1 runs (N = 1 only)")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
     ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "

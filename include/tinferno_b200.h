@@ -155,8 +155,9 @@ TF_API int tf_op_matmul_tc(float* C, const float* A, int t, const void* W, int N
                            void* stream);
 
 /* dequant_row(float* out, const Tensor& t, int64_t row)  src/quant.hpp:42: out[i][K] is
- * row rows[i] of W (embedding lookup). */
-TF_API int tf_op_dequant_rows(float* out, int ggml_type, const void* W, int K, const int* rows,
+ * row rows[i] of W[N][K] (embedding lookup).  A row id outside [0, N) reads nothing: its
+ * output row is zero and TF_DEV_ERR_BAD_INDEX is recorded for tf_op_device_error. */
+TF_API int tf_op_dequant_rows(float* out, int ggml_type, const void* W, int N, int K, const int* rows,
                        int n_rows, void* stream);
 
 /* rmsnorm(out, x, weight, n, eps)  src/layers.hpp:7, applied to `rows` rows of length n. */
@@ -198,6 +199,17 @@ TF_API int tf_op_attn_prefill(float* out, const float* q, const float* k, const 
 
 /* sample_greedy(logits, n)  src/sampler.hpp:9: out[r] = first index of the maximum of row r. */
 TF_API int tf_op_argmax(const float* logits, int n, int rows, int* out, void* stream);
+
+/* Device-side status of the op-level calls, no reference counterpart (the reference's ops
+ * throw std::runtime_error on the calling thread, src/model.cpp:185,198).  Kernels cannot
+ * return a status to the call that launched them, so the op-level kernels of a device record
+ * the first problem they meet in one status word of that device: a bounded wait that gave up
+ * (TF_DEV_ERR_WAIT_*), a position beyond the cache, a row id outside its matrix.  This call
+ * waits for `stream`, stores the word in *code (0 = none) and clears it.  The tf_op_* calls
+ * of the current device, tf_op_attn_decode_noalloc included, share the word. */
+enum { TF_DEV_ERR_NONE = 0, TF_DEV_ERR_WAIT_FULL = 1, TF_DEV_ERR_WAIT_EMPTY = 2, TF_DEV_ERR_BAD_INDEX = 3,
+       TF_DEV_ERR_POS = 4, TF_DEV_ERR_GRID_SYNC = 5 };
+TF_API int tf_op_device_error(void* stream, int* code);
 
 #ifdef __cplusplus
 }

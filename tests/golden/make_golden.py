@@ -13,7 +13,13 @@ oracle/_ref/ from them); the fixtures are committed and the GPU tests read only 
                                greedy stream, and per step the top-8 (index, logit) plus the
                                float64 sum and sum of squares of all logits.
 
-usage: python tests/golden/make_golden.py [--full]   (--full adds the BASELINE-size configs)
+  <cfg4 name>-subset.npz       cfg4 (256 sequences x (1024 + 128)): the reference's greedy
+                               streams of 4 of the 256 sequences (the batched benchmark's
+                               sequences 0, 85, 170 and 255, prompt streams 1000 + g), run
+                               one after another as the reference decodes them.
+
+usage: python tests/golden/make_golden.py [--full]   (--full adds the BASELINE-size configs
+       and the cfg4 subset)
 """
 import argparse
 import os
@@ -94,11 +100,38 @@ def synthetic(cfg, n_prompt, n_decode, cache):
     print(f"{name}: {n_prompt}+{n_decode} in {time.time() - t0:.1f}s tokens[:8]={s['tokens'][:8].tolist()}")
 
 
+CFG4_SUBSET = (0, 85, 170, 255)   # sequences of the batched benchmark (prompt stream 1000 + g)
+
+
+def cfg4_subset(cache):
+    cfg = synth.CFG4
+    path = os.path.join(cache, f"{cfg.name}-s{cfg.seed}.gguf")
+    if not os.path.exists(path):
+        synth.write_model(cfg, path)
+    out = {"sha256": synth.file_digest(path), "seqs": np.array(CFG4_SUBSET, np.int32)}
+    per = {k: [] for k in ("prompt", "tokens", "topi", "topv", "lsum", "lsq")}
+    for g in CFG4_SUBSET:
+        t0 = time.time()
+        prompt = synth.prompt_tokens(cfg, cfg.n_prompt, stream=1000 + g)
+        ref = po.RefModel(path, cfg.max_seq, stage="v2")
+        s = stream_summary(ref, prompt, cfg.n_decode)
+        ref.close()
+        per["prompt"].append(prompt)
+        for k in ("tokens", "topi", "topv", "lsum", "lsq"):
+            per[k].append(s[k])
+        print(f"cfg4 seq {g}: {cfg.n_prompt}+{cfg.n_decode} in {time.time() - t0:.1f}s "
+              f"tokens[:8]={s['tokens'][:8].tolist()}", flush=True)
+    for k, v in per.items():
+        out[k] = np.stack(v)
+    np.savez_compressed(os.path.join(HERE, f"{cfg.name}-subset.npz"), **out)
+
+
 MINIS = [
     (synth.mini(synth.CFG0, 2, 4096), 12, 12),
     (synth.mini(synth.CFG1, 2, 4096), 12, 12),
     (synth.mini(synth.CFG2, 2, 4096), 12, 12),
     (synth.mini(synth.CFG4, 2, 4096), 12, 12),
+    (synth.mini(synth.CFG0_LLAMA3, 2, 4096), 40, 24),
 ]
 
 
@@ -119,6 +152,8 @@ def main():
             cfg = synth.CONFIGS[key]
             if not args.only or args.only in cfg.name:
                 synthetic(cfg, n_prompt, n_decode, cache)
+        if not args.only or args.only == "cfg4-subset":
+            cfg4_subset(cache)
 
 
 if __name__ == "__main__":

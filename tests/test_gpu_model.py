@@ -17,7 +17,7 @@ pytestmark = pytest.mark.gpu
 LOGIT_TOL = 1e-2
 
 MINI = [synth.mini(synth.CFG0, 2, 4096), synth.mini(synth.CFG1, 2, 4096), synth.mini(synth.CFG2, 2, 4096),
-        synth.mini(synth.CFG4, 2, 4096)]
+        synth.mini(synth.CFG4, 2, 4096), synth.mini(synth.CFG0_LLAMA3, 2, 4096)]
 
 
 def greedy(model, prompt, n, seq=0):
@@ -287,12 +287,9 @@ FULL = [("cfg0", 32, 64), ("cfg1", 512, 128), ("cfg2", 128, 128)]
 @pytest.mark.slow
 @pytest.mark.parametrize("key,n_prompt,n_decode", FULL)
 def test_full_config_stream(key, n_prompt, n_decode, model_cache):
-    """BASELINE-size model: token-exact greedy stream and logits vs the reference.  cfg1 (512
-    prompt tokens in tensor-core chunks, decode across the split fused attention) and cfg2
-    (mixed Q4_0 / Q6_K / Q4_1) run when TFB200_FULL_GOLDEN=1: generating their GGUF files takes
-    minutes of host time on a fresh machine."""
-    if key != "cfg0" and os.environ.get("TFB200_FULL_GOLDEN") != "1":
-        pytest.skip("full-size cfg1 / cfg2 streams run with TFB200_FULL_GOLDEN=1")
+    """BASELINE-size model: token-exact greedy stream and logits vs the reference: cfg0
+    (32 + 64), cfg1 (512 prompt tokens in tensor-core chunks, decode across the split fused
+    attention, 128 steps) and cfg2 (mixed Q4_0 / Q6_K / Q4_1, 128 + 128)."""
     cfg = synth.CONFIGS[key]
     gold_path = os.path.join(GOLDEN, cfg.name + ".npz")
     if not os.path.exists(gold_path):

@@ -123,8 +123,32 @@ def test_dequant_rows_exact(t):
         po.oracle_lib().tfo_dequant_row(fp(o), t, raw.ctypes.data, k, int(r))
         assert np.array_equal(o, want[i])
     out = torch.zeros((len(rows), k), device="cuda")
-    call(native.lib().tf_op_dequant_rows(ptr(out), t, ptr(dev(raw.reshape(-1))), k, ptr(dev(rows)), len(rows), None))
+    call(native.lib().tf_op_dequant_rows(ptr(out), t, ptr(dev(raw.reshape(-1))), 40, k, ptr(dev(rows)), len(rows), None))
     assert np.array_equal(out.cpu().numpy(), want)
+
+
+def test_device_status_word():
+    """A row id outside the matrix is caught on the device: nothing outside W is read, the row
+    comes back zero, and tf_op_device_error reports TF_DEV_ERR_BAD_INDEX once, then 0."""
+    L = native.lib()
+    k, n = 256, 10
+    rng = np.random.default_rng(5)
+    raw = np.ascontiguousarray(quants.quantize((rng.standard_normal((n, k)) * 0.02).astype(np.float32), native.TF_Q8_0))
+    want = quants.dequant(raw[[3, 9]], native.TF_Q8_0, k)
+    code = C.c_int(-1)
+    call(L.tf_op_device_error(None, C.byref(code)))
+    assert code.value == 0
+    rows = np.array([3, n, -1, 9], np.int32)  # n and -1 are out of range (chosen on the host)
+    out = torch.full((len(rows), k), 7.0, device="cuda")
+    call(L.tf_op_dequant_rows(ptr(out), native.TF_Q8_0, ptr(dev(raw.reshape(-1))), n, k, ptr(dev(rows)), len(rows),
+                              None))
+    call(L.tf_op_device_error(None, C.byref(code)))
+    assert code.value == native.TF_DEV_ERR_BAD_INDEX
+    o = out.cpu().numpy()
+    assert np.all(o[1] == 0) and np.all(o[2] == 0)
+    assert np.array_equal(o[0], want[0]) and np.array_equal(o[3], want[1])
+    call(L.tf_op_device_error(None, C.byref(code)))  # read once: cleared
+    assert code.value == 0
 
 
 def test_rmsnorm_silu_softmax():

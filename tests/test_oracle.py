@@ -180,7 +180,7 @@ def test_oracle_against_golden_ci():
 
 
 MINI = [synth.mini(synth.CFG0, 2, 4096), synth.mini(synth.CFG1, 2, 4096), synth.mini(synth.CFG2, 2, 4096),
-        synth.mini(synth.CFG4, 2, 4096)]
+        synth.mini(synth.CFG4, 2, 4096), synth.mini(synth.CFG0_LLAMA3, 2, 4096)]
 
 
 @pytest.mark.parametrize("cfg", MINI, ids=lambda c: c.name)
@@ -197,6 +197,19 @@ def test_oracle_against_golden_synthetic(cfg, model_cache):
         assert np.array_equal(lg[gold["topi"][s]], gold["topv"][s])
         assert abs(np.sum(lg, dtype=np.float64) - gold["lsum"][s]) < 1e-9 * max(1.0, abs(gold["lsum"][s]))
     orc.close()
+
+
+def test_llama3_rope_branch_matters(model_cache):
+    """The llama3 fixture exercises the frequency-smoothing branch (src/attention.cpp:14-26):
+    the same weights with standard RoPE give different logits on the same prompt."""
+    l3, std = synth.mini(synth.CFG0_LLAMA3, 2, 4096), synth.mini(synth.CFG0, 2, 4096)
+    prompt = np.load(os.path.join(GOLDEN, l3.name + ".npz"))["prompt"]
+    outs = []
+    for cfg in (l3, std):
+        orc = po.OracleModel(gguf.GGUFReader(synth.model_path(cfg, model_cache)), cfg.max_seq)
+        outs.append(orc.prefill(prompt))
+        orc.close()
+    assert np.abs(outs[0] - outs[1]).max() > 1e-4
 
 
 def test_weight_bytes_of_the_configs():

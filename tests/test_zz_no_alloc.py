@@ -41,6 +41,10 @@ SHAPES = [  # (n_pos, H, KV, hd, kv_type): split and unsplit, all cache types
     (300, 14, 2, 64, native.TF_KV_F16),
     (40, 12, 2, 128, native.TF_KV_BF16),
     (2049, 12, 2, 128, native.TF_KV_F32),
+    # F32 caches with >= 16 kv heads and head_dim % 32 == 0 take the streaming kernel (its own
+    # split count, partial layout and combine)
+    (1000, 32, 16, 64, native.TF_KV_F32),
+    (2049, 64, 16, 128, native.TF_KV_F32),
 ]
 
 
@@ -54,6 +58,19 @@ def test_noalloc_matches_allocating_entry_point():
             assert np.isfinite(got).all()
             # same kernel, same split: bit-identical
             np.testing.assert_array_equal(got, want)
+    code = C.c_int(-1)
+    native.check(lib.tf_op_device_error(None, C.byref(code)))
+    assert code.value == 0  # no device-side problem was recorded
+
+
+def test_noalloc_rejects_bad_head_dim():
+    lib = native.lib()
+    q, kc, vc, cap = _case(10, 4, 2, 64, native.TF_KV_F32, seed=5)
+    out = torch.zeros((4, 64), device="cuda")
+    for hd in (0, -2, 12):
+        with pytest.raises(native.TFError, match="head_dim"):
+            native.check(lib.tf_op_attn_decode_noalloc(_ptr(out), _ptr(q), _ptr(kc), _ptr(vc), native.TF_KV_F32, cap,
+                                                       10, 4, 2, hd, None))
 
 
 def test_noalloc_rejects_oversized_scratch():
