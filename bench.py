@@ -581,7 +581,7 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg1 / cfg2 batch-1 runs (N = 1 only)")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "sweep", "bstep", "gemm", "configs", "q6k"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -606,6 +606,25 @@ def main():
             t = int(np.argmax(m.decode(t)))
         m.close()
         print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 4 + 1, "last_token": t}))
+        return
+    if args.kernel == "step0":
+        # one full-size cfg0 batch-1 decode step (the graph of the timed region) between
+        # cudaProfilerStart / Stop, after a 32-token prefill and 3 decode steps, for a launch
+        # list with DRAM bytes under `ncu --profile-from-start off`
+        import torch
+        from tinferno_b200.model import Model, RunConfig
+        m = Model(model_file(), RunConfig(max_seq=CFG.max_seq))
+        t = int(np.argmax(m.prefill(synth.prompt_tokens(CFG, PROMPT))))
+        for _ in range(3):
+            t = m.decode_argmax(t)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        t = m.decode_argmax(t)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
+        kps = m.kernels_per_step
+        m.close()
+        print(json.dumps({"kernel": "step0", "kernels_per_step": kps, "last_token": t}))
         return
     if args.kernel == "gemm":
         # the cfg4 gate/up GEMM of a 256-row batched step (N = 2 x 8960, K = 1536), Q8_0,

@@ -127,3 +127,39 @@ def test_chunked_prefill_matches_oracle(ci, n, paths):
         assert np.abs(got - want).max() < LOGIT_TOL
         t = int(np.argmax(want))
     m.close()
+
+
+@pytest.mark.slow
+def test_cfg4_subset_matches_reference(model_cache):
+    """cfg4 at its BASELINE size (Qwen2.5-1.5B shape, 1024-token prompts, 128 greedy steps): 16
+    of the batched benchmark's sequences, the 4 golden ones among them, through prefill_batch
+    and decode_batch (16 rows: the tcgen05 GEMM and the streaming attention).  The golden
+    sequences' greedy ids must equal the reference build's over all 128 steps, and their
+    top-8 logits agree within the north-star 1e-2."""
+    import os
+    from conftest import GOLDEN
+    cfg = synth.CFG4
+    gold = np.load(os.path.join(GOLDEN, cfg.name + "-subset.npz"))
+    path = synth.model_path(cfg, model_cache)
+    assert synth.file_digest(path) == str(gold["sha256"])
+    golden = gold["seqs"].tolist()
+    seqs = golden + [g for g in range(1, 64) if g not in golden][:16 - len(golden)]
+    prompts = np.stack([synth.prompt_tokens(cfg, cfg.n_prompt, stream=1000 + g) for g in seqs])
+    for i in range(len(golden)):
+        assert np.array_equal(prompts[i], gold["prompt"][i])
+    B, n = len(seqs), gold["tokens"].shape[1]
+    m = Model(path, RunConfig(max_seq=cfg.max_seq, max_batch=B))
+    tok = m.prefill_batch(list(range(B)), prompts)
+    ids = [tok.copy()]
+    err = 0.0
+    for s in range(n - 1):
+        tok, lg = m.decode_batch(list(range(B)), tok.tolist(), want_logits=True)
+        ids.append(tok.copy())
+        for i in range(len(golden)):
+            err = max(err, float(np.abs(lg[i][gold["topi"][i][s + 1]] - gold["topv"][i][s + 1]).max()))
+    m.close()
+    ids = np.stack(ids)
+    for i in range(len(golden)):
+        assert ids[:, i].tolist() == gold["tokens"][i].tolist(), f"sequence {golden[i]}"
+    assert err < 1e-2, err
+    print(f"cfg4 subset: {len(golden)} sequences token-exact over {n} ids, top-8 max |diff| {err:.2e}")
