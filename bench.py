@@ -49,8 +49,9 @@ LMHEAD_TRAFFIC = 283_513_088
 # the kernel every launch of the batch-1 decode step runs, and its DRAM bytes per step (sum
 # over the step's launches of one ncu capture), when measured
 STEP_KERNEL = "tf_gemv_kernel<1, 1> (Q8_0 integer-path GEMV; attention fused into the QKV launches)"
-STEP_TRAFFIC = None
-STEP_TRAFFIC_SOURCE = "not captured"
+STEP_TRAFFIC = 1_323_928_576
+STEP_TRAFFIC_SOURCE = ("ncu dram__bytes_read+write summed over the 65 launches of one step at position 35, "
+                       "profiles/decode_step_cfg0_dram.md")
 
 
 def peaks():
