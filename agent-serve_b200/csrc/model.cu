@@ -26,7 +26,7 @@
 #include "dots.cuh"
 #include "gemm.cuh"
 #include "sample.cuh"
-#include "decode_mk.cuh"
+#include "persist.cuh"
 #include "engine.cuh"
 
 namespace tfb {
@@ -134,10 +134,14 @@ struct tf_model {
     std::map<long long, cudaGraphExec_t> graphs;
     int kernels_per_step = 0;
     // persistent decode kernel (batch 1)
-    bool mk = false;
-    MkPhase* d_phases = nullptr;
-    int n_phases = 0, mk_slot_bytes = 0, mk_slots = 0, mk_xfloats = 0, mk_grid = 0;
-    unsigned* d_bar = nullptr;
+    bool pk = false;
+    PkPlan pk_plan{};
+    int pk_grid = 0, pk_ctl_words = 0;
+    PkMat* d_pkmats = nullptr;
+    unsigned* d_pkctl = nullptr;
+    unsigned long long* d_pkkeys = nullptr;
+    float* d_pkpart = nullptr;
+    unsigned* d_pktickets = nullptr;
     std::string err;
 };
 
@@ -601,158 +605,110 @@ int run_step(tf_model* m, int M, bool head, int fused, bool chunk = false) {
     return 0;
 }
 
-// Phase table of one decode step for the persistent kernel (batch 1): per layer
-// QKV (RMSNorm [+ embedding] + GEMV + bias) | attention | wo (+ residual) |
-// gate/up (RMSNorm + GEMV + SwiGLU) | down (+ residual); then the lm_head (RMSNorm +
-// GEMV + greedy argmax).  Returns the shared-memory plan in m.
-int build_mk_plan(tf_model* m) {
-    std::vector<MkPhase> ph;
-    // Each consumer warp takes 2 rows of a stage, split along K into KS segments (KS divides
-    // MK_WARPS).  Q8_0 rows whose K splits into 2048-element segments use the register
-    // path (one 64-element unit per lane); other shapes use the shared-memory dot.
-    auto gemv_phase = [&](const WeightRef& w, int n_items, int P) {
-        const bool aligned4 = (reinterpret_cast<uintptr_t>(w.p) & 3) == 0;
-        const bool q8fast = w.type == T_Q8_0 && w.K % 64 == 0 && aligned4;
-        const int be = blk_elems(w.type) == 1 ? 32 : blk_elems(w.type);
-        int ks = 0, reg = 0;
-        if (q8fast && w.K % 2048 == 0 && MK_WARPS % (w.K / 2048) == 0) {
-            ks = w.K / 2048;
-            reg = 1;
-        } else {
-            for (int d = 1; d <= MK_WARPS; ++d) {
-                if (MK_WARPS % d || w.K % d) continue;
-                const int seg = w.K / d;
-                if (seg % be || (q8fast && seg % 64)) continue;
-                ks = d;
-                if ((long long)(MK_WARPS / d) * 2 * w.rb <= MK_STAGE_BUDGET) break;
-            }
-            if (!ks) ks = 1;
+// Matrix table of the persistent kernel (batch 1): per layer QKV (rows q | k | v), wo,
+// gate/up (row pairs), down, then the lm_head.  Every matrix must be Q8_0 with rows that split
+// into 64-element units, at most 32 per warp lane set (16 for row pairs) for KS | PK_WARPS;
+// the KV cache must be fp32.  Returns 1 (and leaves m->pk false) when the model does not fit.
+int build_pk_plan(tf_model* m) {
+    std::vector<PkMat> mats;
+    int slot = 0, max_k = m->D;
+    auto add = [&](const WeightRef& w, int n_items, int P, const float* norm_w, const float* bias) -> bool {
+        if (w.type != T_Q8_0 || w.K % 64 || (reinterpret_cast<uintptr_t>(w.p) & 3) || w.K > PK_MAX_K) return false;
+        int ks = 0;
+        for (int k = 1; k <= PK_WARPS; k <<= 1) {
+            if ((w.K / 64) % k || (w.K / 64 / k) * P > 32) continue;
+            ks = k;
+            if ((long long)(PK_WARPS / k) * P * w.rb <= PK_SLOT_BUDGET) break;
         }
-        MkPhase p;
-        memset(&p, 0, sizeof(p));
-        p.kind = PH_GEMV;
-        p.W = w.p;
-        p.rb = w.rb;
-        p.wtype = w.type;
-        p.K = w.K;
-        p.n_items = n_items;
-        p.P = P;
-        p.KS = ks;
-        p.fast = q8fast && (w.K / ks) % 64 == 0;
-        p.reg = reg;
-        p.ri = (MK_WARPS / ks) * (2 / P);
-        return p;
+        if (!ks) return false;
+        PkMat t;
+        t.W = w.p;
+        t.rb = w.rb;
+        t.K = w.K;
+        t.n_items = n_items;
+        t.P = P;
+        t.KS = ks;
+        t.RI = PK_WARPS / ks;
+        t.norm_w = norm_w;
+        t.bias = bias;
+        mats.push_back(t);
+        slot = std::max(slot, (int)(((long long)t.RI * P * w.rb + 32 + 15) & ~15LL));
+        max_k = std::max(max_k, w.K);
+        return true;
     };
     for (int li = 0; li < m->hp.n_layer; ++li) {
         const LayerDev& Ld = m->L[li];
-        MkPhase q = gemv_phase(Ld.qkv, m->H + 2 * m->KV, 1);
-        q.pro = li == 0 ? PRO_EMBED_RMSNORM : PRO_RMSNORM;
-        q.x = m->x;
-        q.norm_w = Ld.attn_norm;
-        q.epi = EPI_STORE;
-        q.y = m->qkv;
-        q.bias = Ld.bqkv;
-        ph.push_back(q);
-        MkPhase at;
-        memset(&at, 0, sizeof(at));
-        at.kind = PH_ATTN;
-        at.layer = li;
-        ph.push_back(at);
-        MkPhase o = gemv_phase(Ld.wo, m->D, 1);
-        o.pro = PRO_COPY;
-        o.x = m->attn;
-        o.epi = EPI_RESID;
-        o.resid = m->x;
-        ph.push_back(o);
-        MkPhase gu = gemv_phase(Ld.gateup, m->FF, 2);
-        gu.pro = PRO_RMSNORM;
-        gu.x = m->x;
-        gu.norm_w = Ld.ffn_norm;
-        gu.epi = EPI_SWIGLU;
-        gu.y = m->h;
-        ph.push_back(gu);
-        MkPhase dn = gemv_phase(Ld.down, m->D, 1);
-        dn.pro = PRO_COPY;
-        dn.x = m->h;
-        dn.epi = EPI_RESID;
-        dn.resid = m->x;
-        ph.push_back(dn);
+        if (!add(Ld.qkv, m->H + 2 * m->KV, 1, Ld.attn_norm, Ld.bqkv) || !add(Ld.wo, m->D, 1, nullptr, nullptr) ||
+            !add(Ld.gateup, m->FF, 2, Ld.ffn_norm, nullptr) || !add(Ld.down, m->D, 1, nullptr, nullptr))
+            return 1;
     }
-    MkPhase lm = gemv_phase(m->outw, m->V, 1);
-    lm.pro = PRO_RMSNORM;
-    lm.x = m->x;
-    lm.norm_w = m->out_norm;
-    lm.epi = EPI_ARGMAX;
-    lm.y = m->logits;
-    ph.push_back(lm);
-
-    int slot = 0, xf = 8 * (2 * m->hd + 1);
-    for (const MkPhase& p : ph) {
-        if (p.kind != PH_GEMV) continue;
-        const long long payload = (long long)p.ri * p.P * p.rb;
-        slot = std::max(slot, (int)((payload + 32 + 15) & ~15LL));
-        xf = std::max(xf, xpad_len(p.K));
-    }
-    xf = (xf + 3) & ~3;
-    MkArgs probe;
-    memset(&probe, 0, sizeof(probe));
-    probe.xfloats = xf;
-    probe.slot_bytes = slot;
-    probe.n_slots = 0;
-    const size_t fixed = mk_smem_bytes(probe);
-    int n_slots = (int)((MK_SMEM_LIMIT - (long long)fixed) / slot);
-    if (n_slots > MK_MAX_SLOTS) n_slots = MK_MAX_SLOTS;
-    if (n_slots < 2) return 1;  // shapes too large for the persistent kernel
-    m->mk_slot_bytes = slot;
-    m->mk_slots = n_slots;
-    m->mk_xfloats = xf;
-    m->n_phases = (int)ph.size();
-    CK(cudaMalloc(&m->d_phases, sizeof(MkPhase) * ph.size()));
-    CK(cudaMemcpy(m->d_phases, ph.data(), sizeof(MkPhase) * ph.size(), cudaMemcpyHostToDevice));
-    CK(cudaMalloc(&m->d_bar, 2 * sizeof(unsigned)));
-    CK(cudaMemset(m->d_bar, 0, 2 * sizeof(unsigned)));
-    // one CTA per SM, all co-resident (cooperative launch); if the kernel cannot be resident
-    // on an SM the engine keeps the per-kernel path
-    MkArgs full;
-    memset(&full, 0, sizeof(full));
-    full.xfloats = xf;
-    full.slot_bytes = slot;
-    full.n_slots = n_slots;
-    const int occ = mk_occupancy(mk_smem_bytes(full));
-    if (occ < 1) {
+    if (!add(m->outw, m->V, 1, m->out_norm, nullptr)) return 1;
+    // fp32 cache (the reference's type): the attention tiles arrive as bulk copies of cache rows
+    if (m->opt.kv_type != TF_KV_F32 || m->hd % 4 || m->hd > 256 || m->D % 4) return 1;
+    if (m->hp.n_head > m->num_sms) return 1;
+    PkPlan plan;
+    if (!pk_plan(slot, max_k, m->hd, plan) || plan.attn_tp < 16) return 1;
+    if (pk_occupancy(plan.smem) < 1) {
         cudaGetLastError();
         return 1;
     }
-    m->mk_grid = m->num_sms;
-    m->mk = true;
+    m->pk_plan = plan;
+    m->pk_grid = m->num_sms;
+    const int L = m->hp.n_layer;
+    CK(cudaMalloc(&m->d_pkmats, sizeof(PkMat) * mats.size()));
+    CK(cudaMemcpy(m->d_pkmats, mats.data(), sizeof(PkMat) * mats.size(), cudaMemcpyHostToDevice));
+    // counters [PC_PER_LAYER * L + 1] + the abort word, then the per-step greedy keys
+    m->pk_ctl_words = PC_PER_LAYER * L + 2;
+    CK(cudaMalloc(&m->d_pkctl, sizeof(unsigned) * m->pk_ctl_words));
+    CK(cudaMalloc(&m->d_pkkeys, sizeof(unsigned long long) * (size_t)m->opt.max_seq));
+    const int max_nsf = std::max(1, m->pk_grid / m->hp.n_head);
+    CK(cudaMalloc(&m->d_pkpart, sizeof(float) * (size_t)m->hp.n_head * max_nsf * (m->hd + 2)));
+    CK(cudaMalloc(&m->d_pktickets, sizeof(unsigned) * m->hp.n_head));
+    CK(cudaMemset(m->d_pktickets, 0, sizeof(unsigned) * m->hp.n_head));
+    m->pk = true;
     return 0;
 }
 
 // Run `n_steps` batch-1 steps of slot `seq` in one persistent launch: the first n_prompt
-// steps consume prompt[] (device), later ones their own argmax; the lm_head runs from step
-// first_head on; during prompt steps attention starts at ws_prompt.
-int run_mk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps, int first_head, int ws_prompt,
+// steps consume prompt[] (device), later ones the previous step's argmax; the lm_head runs
+// from step first_head on; during prompt steps attention starts at ws_prompt.
+int run_pk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps, int first_head, int ws_prompt,
            int hist_cap) {
-    MkArgs a;
+    const PkPlan& p = m->pk_plan;
+    PkArgs a;
     memset(&a, 0, sizeof(a));
-    a.ph = m->d_phases;
-    a.n_ph = m->n_phases;
+    a.mats = m->d_pkmats;
+    a.n_layer = m->hp.n_layer;
     a.n_steps = n_steps;
     a.n_prompt = n_prompt;
     a.prompt = d_prompt;
     a.first_head = first_head;
     a.ws_prompt = ws_prompt;
+    a.pos0 = m->hpos[seq];
     a.slot = seq;
-    a.slot_bytes = m->mk_slot_bytes;
-    a.n_slots = m->mk_slots;
-    a.xfloats = m->mk_xfloats;
+    a.slot_bytes = p.slot_bytes;
+    a.n_slots = p.n_slots;
+    a.reg_off = p.reg_off;
+    a.misc_off = p.misc_off;
+    a.attn_tp = p.attn_tp;
+    // position splits per query head: one tile per split while the grid has room
+    const int span = m->hpos[seq] + n_steps - (n_prompt >= n_steps ? ws_prompt : 0);
+    const int max_nsf = std::max(1, m->pk_grid / m->hp.n_head);
+    a.nsf = std::max(1, std::min(max_nsf, (span + p.attn_tp - 1) / p.attn_tp));
     a.eps = m->hp.rms_eps;
     a.embd = m->embd.p;
     a.embd_type = m->embd.type;
     a.embd_rb = m->embd.rb;
     a.n_vocab = m->V;
-    a.x_resid = m->x;
+    a.x = m->x;
+    a.qkv = m->qkv;
+    a.attn = m->attn;
+    a.h = m->h;
+    a.logits = m->logits;
     a.D = m->D;
+    a.H = m->H;
+    a.KVd = m->KV;
+    a.FF = m->FF;
     a.kc = m->kc;
     a.vc = m->vc;
     a.layer_elems = m->layer_elems;
@@ -764,16 +720,19 @@ int run_mk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps,
     a.n_head = m->hp.n_head;
     a.n_kv = m->hp.n_kv_head;
     a.hd = m->hd;
-    a.qkv = m->qkv;
-    a.attn_out = m->attn;
+    a.part = m->d_pkpart;
+    a.tickets = m->d_pktickets;
     a.tok = m->d_tokens;
     a.pos = m->d_pos;
     a.hist = m->d_hist;
     a.hist_cap = hist_cap;
-    a.keys = m->keys;
-    a.bar = m->d_bar;
+    a.keys = m->d_pkkeys;
+    a.cnt = m->d_pkctl;
+    a.abort_g = reinterpret_cast<int*>(m->d_pkctl + m->pk_ctl_words - 1);
     a.err = m->d_err;
-    CK(mk_launch(a, m->mk_grid, m->stream));
+    CK(cudaMemsetAsync(m->d_pkctl, 0, sizeof(unsigned) * m->pk_ctl_words, m->stream));
+    CK(cudaMemsetAsync(m->d_pkkeys, 0, sizeof(unsigned long long) * n_steps, m->stream));
+    CK(pk_launch(a, m->pk_grid, p.smem, m->stream));
     return 0;
 }
 
@@ -789,6 +748,7 @@ int finish_call(tf_model* m) {
         cudaMemsetAsync(m->ctl, 0, sizeof(unsigned), m->stream);
         cudaMemsetAsync(m->keys, 0, sizeof(unsigned long long) * T, m->stream);
         cudaMemsetAsync(m->d_async, 0, sizeof(unsigned) * (2 * m->hp.n_layer + m->hp.n_head), m->stream);
+        if (m->pk) cudaMemsetAsync(m->d_pktickets, 0, sizeof(unsigned) * m->hp.n_head, m->stream);
         cudaStreamSynchronize(m->stream);
         return fail(m, err_code_text(c));
     }
@@ -847,7 +807,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_phases, m->d_bar, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
+                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkpart, m->d_pktickets, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
                    m->xplanes};
     for (void* p : dev)
         if (p) cudaFree(p);
@@ -1171,7 +1131,11 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     if (!m->smp) BAD("sampler scratch allocation failed");
     CKD(cudaMallocHost(&m->hlog, sizeof(float) * (size_t)T * m->V));
     m->hpos.assign(o.max_batch, 0);
-    if (o.decode_mode == TF_DECODE_PERSISTENT && build_mk_plan(m) < 0) BAD(m->err);
+    if (o.decode_mode != TF_DECODE_KERNELS) {
+        const int rc = build_pk_plan(m);
+        if (rc < 0) BAD(m->err);
+        if (rc > 0 && o.decode_mode == TF_DECODE_PERSISTENT) BAD("the persistent decode kernel does not take this model");
+    }
     {   // positions per tile of the attention fused into the QKV kernel (same for every layer)
         const GemvArgs q = gemv_base(m, m->L[0].qkv, m->H + 2 * m->KV, 1, 1);
         m->attn_tile = (q.intq && !q.q4 && !q.q6) ? fused_attn_tile(q, m->hd) : 0;
@@ -1186,7 +1150,7 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         cudaStreamEndCapture(m->stream, &g);
         if (g) cudaGraphDestroy(g);
         if (rc) BAD(m->err);
-        m->kernels_per_step = n;
+        m->kernels_per_step = m->pk ? 1 : n;
     }
     *out = m;
     return 0;
@@ -1220,8 +1184,8 @@ int tf_cuda_decode(tf_model* m, int seq, int token, float* logits, int* argmax_o
     if (m->hpos[seq] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
     if (token < 0 || token >= m->V) return fail(m, "token id out of range");
     if (set_slot_row(m, 0, seq, token)) return -1;
-    if (m->mk) {
-        if (run_mk(m, seq, m->d_tokens, 1, 1, 0, 0, 0)) return -1;
+    if (m->pk) {
+        if (run_pk(m, seq, m->d_tokens, 1, 1, 0, 0, 0)) return -1;
     } else if (run_step(m, 1, true, fuse_attn_ok(m, m->hpos[seq] + 1))) {
         return -1;
     }
@@ -1241,10 +1205,11 @@ int tf_cuda_prefill(tf_model* m, int seq, const int* tokens, int n, float* logit
     int* stage = m->hi + 64;
     memcpy(stage, tokens, sizeof(int) * n);
     CK(cudaMemcpyAsync(m->d_prompt, stage, sizeof(int) * n, cudaMemcpyHostToDevice, m->stream));
-    if (m->mk) {
-        // all n prompt steps in one persistent launch; attention inside the chunk sees the
-        // chunk alone, from its first position; the lm_head runs for the last token only
-        if (run_mk(m, seq, m->d_prompt, n, n, n - 1, m->hpos[seq], 0)) return -1;
+    if (m->pk && !(m->ptile && n >= GM_MIN_M)) {
+        // short prompts: all n token steps in one persistent launch; attention inside the
+        // chunk sees the chunk alone, from its first position; the lm_head runs for the last
+        // token only (prompts of >= 16 tokens take the tensor-core chunks below)
+        if (run_pk(m, seq, m->d_prompt, n, n, n - 1, m->hpos[seq], 0)) return -1;
         m->hpos[seq] += n;
         return read_outputs(m, 1, logits, argmax_out);
     }
@@ -1289,8 +1254,8 @@ int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eo
     if (m->hpos[seq] + n > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
     if (first_token < 0 || first_token >= m->V) return fail(m, "token id out of range");
     if (set_slot_row(m, 0, seq, first_token)) return -1;
-    if (m->mk) {
-        if (run_mk(m, seq, m->d_tokens, 1, n, 0, 0, n)) return -1;
+    if (m->pk) {
+        if (run_pk(m, seq, m->d_tokens, 1, n, 0, 0, n)) return -1;
     } else {
         StepCtl c = {0u, 0, n, 0};
         memcpy(m->hi + 4, &c, sizeof(c));
