@@ -1,5 +1,5 @@
-// Row-dot routines shared by the GEMV kernel (gemv.cu) and the decode megakernel
-// (decode_mk.cu): fp32 activations (shared memory, xpad layout) times GGUF block weights
+// Row-dot routines shared by the GEMV kernel (gemv.cu) and the persistent decode kernel
+// (persist.cu): fp32 activations (shared memory, xpad layout) times GGUF block weights
 // (shared memory, native layout), fp32 accumulation.
 #pragma once
 

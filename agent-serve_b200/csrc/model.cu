@@ -645,7 +645,10 @@ int build_pk_plan(tf_model* m) {
     if (!add(m->outw, m->V, 1, m->out_norm, nullptr)) return 1;
     // fp32 cache (the reference's type): the attention tiles arrive as bulk copies of cache rows
     if (m->opt.kv_type != TF_KV_F32 || m->hd % 4 || m->hd > 256 || m->D % 4) return 1;
-    if (m->hp.n_head > m->num_sms) return 1;
+    if (m->hp.n_head > m->num_sms || m->hd / 2 > PK_MAX_D2) return 1;
+    // rows a CTA owns: its residual rows and QKV rows stay in shared memory
+    if ((m->D + m->num_sms - 1) / m->num_sms > PK_ROWS || (m->H + 2 * m->KV + m->num_sms - 1) / m->num_sms > PK_ROWS)
+        return 1;
     PkPlan plan;
     if (!pk_plan(slot, max_k, m->hd, plan) || plan.attn_tp < 16) return 1;
     if (pk_occupancy(plan.smem) < 1) {

@@ -19,7 +19,9 @@
 // Arrival counters only grow during a launch (the host zeroes them before it): a CTA arrives
 // once per phase per step, so phase p of step s is complete when its counter reaches
 // (steps that ran p up to s) * grid.  Cross-CTA data is written with plain stores, published
-// by a CTA barrier + fence + release add, and read with ld.global.cg after an acquire load.
+// by a CTA barrier + release add, and read with ld.global.cg after an acquire load.  A CTA
+// keeps on chip what only it updates (its rows of the residual stream) and what it reads at
+// every layer (its QKV bias rows, the step's RoPE row).
 // Every wait is bounded; a CTA that gives up records the error code, raises the launch's
 // abort word (every other wait checks it) and leaves after its copies in flight have landed.
 #include <algorithm>
@@ -37,6 +39,10 @@ struct PkMisc {
     uint64_t abar;  // attention K / V tile copies
     double redd[PK_WARPS];
     float red[2][PK_WARPS][4];
+    float xo[PK_ROWS];        // this CTA's rows of the residual stream (it alone updates them)
+    float pre[PK_ROWS];       // this CTA's QKV bias rows
+    float cs[PK_MAX_D2];      // RoPE cos / sin of this step's position (attention CTAs)
+    float sn[PK_MAX_D2];
     unsigned long long ckey;
     int ok;
     int abort;  // this CTA gave up: its producer stops, its waits return at once
@@ -148,13 +154,12 @@ __device__ bool pk_verdict(PkCtx& c, bool ok) {
     return *reinterpret_cast<volatile int*>(&c.S->ok) != 0;
 }
 
-// Publish this CTA's phase results and count its arrival.
+// Publish this CTA's phase results and count its arrival: the CTA barrier orders every
+// thread's stores before thread 0's release add (release is cumulative), so the consumers'
+// acquire load of the counter makes them visible.
 __device__ __forceinline__ void pk_arrive(unsigned* cnt) {
     cbar();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        red_release_gpu_add(cnt, 1u);
-    }
+    if (threadIdx.x == 0) red_release_gpu_add(cnt, 1u);
 }
 
 // Attention tile: cached K rows [p0, p0 + n) of one head into ks (row stride kst floats,
@@ -193,8 +198,11 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
     const int K = mt.K, nq = K >> 2;
     const bool norm = kind == PK_QKV || kind == PK_GU || kind == PK_HEAD;
     const bool embed = kind == PK_QKV && token != -1;
+    const int i0 = item_begin(mt.n_items, c.cta, c.G), i1 = item_begin(mt.n_items, c.cta + 1, c.G);
+    if (kind == PK_QKV)  // static operands first: this CTA's bias rows (zero without bias)
+        for (int r = tid; r < i1 - i0; r += PK_CONS) c.S->pre[r] = mt.bias ? __ldg(mt.bias + i0 + r) : 0.f;
     float4 wn[PK_PRO_U];
-    if (norm) {  // static operands first: the RMSNorm weights of this thread's chunks
+    if (norm) {  // and the RMSNorm weights of this thread's chunks
 #pragma unroll
         for (int u = 0; u < PK_PRO_U; ++u) {
             const int q = tid + u * PK_CONS;
@@ -222,7 +230,11 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
         cbar();
         // this CTA's rows of the residual stream: the rows its wo / down epilogues update
         const int r0 = item_begin(a.D, c.cta, c.G), r1 = item_begin(a.D, c.cta + 1, c.G);
-        for (int e = r0 + tid; e < r1; e += PK_CONS) a.x[e] = xs[xpad(e)];
+        for (int e = r0 + tid; e < r1; e += PK_CONS) {
+            const float xv = xs[xpad(e)];
+            a.x[e] = xv;
+            c.S->xo[e - r0] = xv;
+        }
 #pragma unroll
         for (int u = 0; u < PK_PRO_U; ++u) {
             const int q = tid + u * PK_CONS;
@@ -292,7 +304,6 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
     }
 
     // ---- main loop: two stages per iteration (two independent dp4a chains per warp)
-    const int i0 = item_begin(mt.n_items, c.cta, c.G), i1 = item_begin(mt.n_items, c.cta + 1, c.G);
     const int n_stages = (i1 - i0 + RI - 1) / RI;
     const long long rb = mt.rb;
     const int lane_off = (my_item * P + prow) * (int)rb + (my_ks * U + (pact ? pu : 0)) * 68;
@@ -355,9 +366,12 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
         if (mine && leader && first_row && okr) {
             const int row = rsel ? item1 : item0;
             if (kind == PK_QKV) {
-                a.qkv[row] = keep + (mt.bias ? __ldg(mt.bias + row) : 0.f);
+                a.qkv[row] = keep + c.S->pre[row - i0];
             } else if (kind == PK_WO || kind == PK_DOWN) {
-                a.x[row] = __ldcg(a.x + row) + keep;
+                // wo / down rows are the CTA's residual rows (both partition D the same way)
+                const float xv = c.S->xo[row - i0] + keep;
+                c.S->xo[row - i0] = xv;
+                a.x[row] = xv;
             } else if (kind == PK_GU) {
                 a.h[row] = __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other);
             } else {
@@ -381,7 +395,6 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
             if (k && cta_ok) atomicMax(a.keys + step, k);
         }
         if (cta_ok) {
-            __threadfence();
             red_release_gpu_add(arr, 1u);
         } else {
             atomicExch(a.abort_g, 1);
@@ -411,9 +424,9 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, con
     float* qs = f;                   // [hd]
     float* kn = qs + hd;             // [hd]
     float* vn = kn + hd;             // [hd]
-    float* cs = vn + hd;             // [d2]
-    float* sn = cs + d2;             // [d2]
-    float* red = sn + d2;            // [2][32]
+    const float* cs = c.S->cs;       // [d2], loaded at the start of the step
+    const float* sn = c.S->sn;
+    float* red = vn + 2 * hd;        // [2][32] (after a gap of hd floats: the layout of pk_plan)
     float* pacc = red + 64;          // [ng][hd]
     float* sc = pacc + ng * hd;      // [tp]
     float* ks = sc + tp;             // [tp][kst]
@@ -430,10 +443,6 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, con
         const int np = min(s1, s0 + tp) - s0;
         const int npc = (s0 + np == pos + 1) ? np - 1 : np;
         pk_issue_tile(c, ks, vs, kst, hd, kcf + (size_t)s0 * hd, vcf + (size_t)s0 * hd, npc);
-    }
-    for (int i = tid; i < d2; i += PK_CONS) {
-        cs[i] = __ldg(a.cosb + (size_t)pos * d2 + i);
-        sn[i] = __ldg(a.sinb + (size_t)pos * d2 + i);
     }
     if (!pk_wait(c, dep, target)) {
         if (s0 < s1) {  // the tile's copies land before the CTA unwinds
@@ -627,6 +636,11 @@ __global__ void __launch_bounds__(PK_THREADS, 1) tf_decode_persistent_kernel(con
             }
         }
         const int token = s < a.n_prompt ? a.prompt[s] : -2;
+        if (cta < a.n_head * a.nsf)  // the step's RoPE row, read at every layer's attention
+            for (int i = tid; i < a.hd / 2; i += PK_CONS) {
+                S->cs[i] = __ldg(a.cosb + (size_t)pos * (a.hd / 2) + i);
+                S->sn[i] = __ldg(a.sinb + (size_t)pos * (a.hd / 2) + i);
+            }
         for (int l = 0; l < L && ok; ++l) {
             unsigned* cl = a.cnt + PC_PER_LAYER * l;
             const PkMat* ml = a.mats + PK_MATS * l;

@@ -26,6 +26,8 @@ constexpr int PK_SMEM_LIMIT = 227 * 1024;     // dynamic shared memory per CTA
 constexpr int PK_PRO_U = 4;                   // float4 activation chunks per consumer thread
 constexpr int PK_MAX_K = PK_CONS * 4 * PK_PRO_U;  // longest row (8192 elements)
 constexpr int PK_MAX_TP = PK_CONS;            // attention positions per tile (one per thread)
+constexpr int PK_ROWS = 64;                   // residual rows / QKV rows a CTA may own
+constexpr int PK_MAX_D2 = 128;                // head_dim / 2 of the RoPE table row kept on chip
 
 // matrices per layer in the table: QKV (rows q | k | v), wo, gate/up (row pairs), down; the
 // lm_head follows the last layer's

@@ -93,7 +93,19 @@ def test_long_context_crosses_fused_attention_limit(ci, n_prompt, n_decode, mini
     orc.close()
 
 
-@pytest.mark.parametrize("cfg", MINI, ids=lambda c: c.name)
+# the persistent kernel takes models whose matrices are all Q8_0 with rows of 64-element
+# units that fit its lanes (cfg0, cfg1, llama3 RoPE); cfg2's Q4_0 / Q6_K / Q4_1 matrices and
+# cfg4's K = 8960 down rows stay on the per-kernel path
+PERSISTENT = [MINI[0], MINI[1], MINI[4]]
+
+
+def test_persistent_mode_rejects_other_models(mini_models):
+    for cfg in (MINI[2], MINI[3]):
+        with pytest.raises(native.TFError, match="persistent decode kernel does not take"):
+            Model(mini_models[cfg.name], RunConfig(max_seq=cfg.max_seq, decode_mode=native.TF_DECODE_PERSISTENT))
+
+
+@pytest.mark.parametrize("cfg", PERSISTENT, ids=lambda c: c.name)
 def test_persistent_mode_matches_reference(cfg, mini_models):
     """The one-launch-per-call persistent kernel: same golden stream, logits within
     tolerance of the per-kernel path, and its fused prefill + greedy generation."""
