@@ -140,6 +140,9 @@ struct tf_model {
     PkMat* d_pkmats = nullptr;
     unsigned* d_pkctl = nullptr;
     unsigned long long* d_pkkeys = nullptr;
+    uint2* d_pkll = nullptr;
+    size_t pk_ll_pairs = 0;
+    unsigned pk_ep = 1;
     float* d_pkpart = nullptr;
     unsigned* d_pktickets = nullptr;
     std::string err;
@@ -657,11 +660,14 @@ int build_pk_plan(tf_model* m) {
     }
     m->pk_plan = plan;
     m->pk_grid = m->num_sms;
-    const int L = m->hp.n_layer;
     CK(cudaMalloc(&m->d_pkmats, sizeof(PkMat) * mats.size()));
     CK(cudaMemcpy(m->d_pkmats, mats.data(), sizeof(PkMat) * mats.size(), cudaMemcpyHostToDevice));
-    // counters [PC_PER_LAYER * L + 1] + the abort word, then the per-step greedy keys
-    m->pk_ctl_words = PC_PER_LAYER * L + 2;
+    // the step counter and the abort word; the per-step greedy keys; the LL activation pairs
+    m->pk_ctl_words = 2;
+    m->pk_ll_pairs = (size_t)(m->H + 2 * m->KV) + m->H + m->D + m->FF;
+    CK(cudaMalloc(&m->d_pkll, sizeof(uint2) * m->pk_ll_pairs));
+    CK(cudaMemset(m->d_pkll, 0, sizeof(uint2) * m->pk_ll_pairs));  // epoch 0 is never expected
+    m->pk_ep = 1;
     CK(cudaMalloc(&m->d_pkctl, sizeof(unsigned) * m->pk_ctl_words));
     CK(cudaMalloc(&m->d_pkkeys, sizeof(unsigned long long) * (size_t)m->opt.max_seq));
     const int max_nsf = std::max(1, m->pk_grid / m->hp.n_head);
@@ -703,10 +709,14 @@ int run_pk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps,
     a.embd_type = m->embd.type;
     a.embd_rb = m->embd.rb;
     a.n_vocab = m->V;
-    a.x = m->x;
-    a.qkv = m->qkv;
-    a.attn = m->attn;
-    a.h = m->h;
+    a.llq = m->d_pkll;
+    a.lla = a.llq + (m->H + 2 * m->KV);
+    a.llx = a.lla + m->H;
+    a.llh = a.llx + m->D;
+    // epochs of this launch follow the last one's, so no pair left by an earlier launch can
+    // carry an epoch this launch waits for
+    a.ep0 = m->pk_ep;
+    m->pk_ep += (unsigned)(n_steps + 1) * (unsigned)m->hp.n_layer * PK_EPS;
     a.logits = m->logits;
     a.D = m->D;
     a.H = m->H;
@@ -810,7 +820,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkpart, m->d_pktickets, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
+                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
                    m->xplanes};
     for (void* p : dev)
         if (p) cudaFree(p);

@@ -16,14 +16,17 @@
 //              (and one position split), its first K/V tile requested (bulk copies) before
 //              the q/k/v exist.
 //
-// Arrival counters only grow during a launch (the host zeroes them before it): a CTA arrives
-// once per phase per step, so phase p of step s is complete when its counter reaches
-// (steps that ran p up to s) * grid.  Cross-CTA data is written with plain stores, published
-// by a CTA barrier + release add, and read with ld.global.cg after an acquire load.  A CTA
-// keeps on chip what only it updates (its rows of the residual stream) and what it reads at
-// every layer (its QKV bias rows, the step's RoPE row).
-// Every wait is bounded; a CTA that gives up records the error code, raises the launch's
-// abort word (every other wait checks it) and leaves after its copies in flight have landed.
+// Inside a step the phases hand their outputs over as flag-in-data pairs {value, epoch}
+// (one 8-byte store per value, persist.cuh): a consumer polls exactly the pairs it needs, so
+// a phase boundary costs the store's propagation and one poll, with no fence and no counter.
+// Every phase needs all of the previous phase's outputs (directly, or for the attention
+// through the heads that cover every QKV row), so no CTA can overwrite a buffer that another
+// CTA has still to read.  Between steps the CTAs meet at one counter (fence, release add,
+// acquire), which also orders each step's KV-cache stores before the next step's reads.  A
+// CTA keeps on chip what only it updates (its rows of the residual stream) and what it reads
+// at every layer (its QKV bias rows, the step's RoPE row).  Every wait is bounded; a CTA that
+// gives up records the error code, raises the launch's abort word (every other wait checks
+// it) and leaves after its copies in flight have landed.
 #include <algorithm>
 #include <cstdlib>
 
@@ -52,6 +55,24 @@ struct PkMisc {
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(PK_CONS) : "memory"); }
 __device__ __forceinline__ int ld_vol(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// flag-in-data pairs: {value bits, epoch}, each pair one naturally aligned 8-byte access
+__device__ __forceinline__ void st_ll(uint2* p, float v, unsigned ep) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(ep) : "memory");
+}
+__device__ __forceinline__ uint4 ld_ll2(const uint2* p) {  // two pairs (16-byte aligned)
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ uint2 ld_ll1(const uint2* p) {
+    uint2 r;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
 
 struct PkRing {
     uint8_t* base;
@@ -154,12 +175,36 @@ __device__ bool pk_verdict(PkCtx& c, bool ok) {
     return *reinterpret_cast<volatile int*>(&c.S->ok) != 0;
 }
 
-// Publish this CTA's phase results and count its arrival: the CTA barrier orders every
-// thread's stores before thread 0's release add (release is cumulative), so the consumers'
-// acquire load of the counter makes them visible.
-__device__ __forceinline__ void pk_arrive(unsigned* cnt) {
-    cbar();
-    if (threadIdx.x == 0) red_release_gpu_add(cnt, 1u);
+// Poll this thread's float4 chunks q = tid + u * PK_CONS (< nq) of an LL vector until every
+// pair carries epoch ep; the values land in v.  Bounded; false on a timeout or an abort.
+__device__ bool ll_read(PkCtx& c, const uint2* src, int nq, unsigned ep, float4 (&v)[PK_PRO_U]) {
+    unsigned todo = 0;
+#pragma unroll
+    for (int u = 0; u < PK_PRO_U; ++u) {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if ((int)threadIdx.x + u * PK_CONS < nq) todo |= 1u << u;
+    }
+    for (int i = 0; i < kGridPolls && todo; ++i) {
+#pragma unroll
+        for (int u = 0; u < PK_PRO_U; ++u) {
+            if (!(todo >> u & 1u)) continue;
+            const int q = (int)threadIdx.x + u * PK_CONS;
+            const uint4 lo = ld_ll2(src + 4 * q), hi = ld_ll2(src + 4 * q + 2);
+            if (lo.y == ep && lo.w == ep && hi.y == ep && hi.w == ep) {
+                v[u] = make_float4(__uint_as_float(lo.x), __uint_as_float(lo.z), __uint_as_float(hi.x),
+                                   __uint_as_float(hi.z));
+                todo &= ~(1u << u);
+            }
+        }
+        if (!todo) break;
+        if ((i & 15) == 15 && (ld_vol(&c.S->abort) || ld_vol(c.a->abort_g))) return false;
+        if (i > 8) __nanosleep(i > 65536 ? 1024 : 64);
+    }
+    if (todo) {
+        atomicCAS(c.a->err, 0, ERR_GRID_SYNC);
+        return false;
+    }
+    return true;
 }
 
 // Attention tile: cached K rows [p0, p0 + n) of one head into ks (row stride kst floats,
@@ -170,12 +215,7 @@ __device__ __forceinline__ void pk_issue_tile(PkCtx& c, float* ks, float* vs, in
                                               const float* vc, int n) {
     const int lane = threadIdx.x & 31;
     if (threadIdx.x < 32) {
-        if (lane == 0) {
-            // order earlier generic accesses (this region's previous use, other CTAs' cache
-            // stores seen through the phase counters) before the async-proxy copies
-            asm volatile("fence.proxy.async;" ::: "memory");
-            mbar_expect_tx(&c.S->abar, (uint32_t)(2 * n * hd * 4));
-        }
+        if (lane == 0) mbar_expect_tx(&c.S->abar, (uint32_t)(2 * n * hd * 4));
         __syncwarp();
         for (int r = lane; r < n; r += 32) bulk_g2s(ks + (size_t)r * kst, kc + (size_t)r * hd, (uint32_t)hd * 4, &c.S->abar);
         if (lane == 0 && n) bulk_g2s(vs, vc, (uint32_t)(n * hd * 4), &c.S->abar);
@@ -189,9 +229,13 @@ __device__ __forceinline__ void pk_issue_tile(PkCtx& c, float* ks, float* vs, in
 //      PK_DOWN: h -> x += W h
 //      PK_HEAD: RMSNorm(x) -> logits, greedy key of the step
 // token >= 0: embed that token (layer-0 QKV); token == -2: embed the argmax of step - 1.
-template <int kind>
-__device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigned target, unsigned* arr, int token,
-                        int step) {
+// src / ep_in: the LL vector the activation is read from and its epoch (unused when
+// embedding); ep_out: the epoch of this phase's outputs.
+// One copy of this code serves every GEMV phase (kind is a run-time value and the kernel calls
+// it from one place): the phases run one after another, so a single copy stays in the
+// instruction cache where five specialised ones would evict each other at every layer.
+__device__ __forceinline__ bool pk_gemv(PkCtx& c, const PkMat& mat, int kind, const uint2* src, unsigned ep_in,
+                                        unsigned ep_out, int token, int step) {
     const PkArgs& a = *c.a;
     const PkMat mt = mat;  // the plan in registers (the table is in global memory)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -209,7 +253,6 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
             wn[u] = q < nq ? __ldg(reinterpret_cast<const float4*>(mt.norm_w) + q) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
-    if (!pk_wait(c, dep, target)) return false;
 
     // ---- prologue: the activation as digit planes in the region, the lane's unit in registers
     float4 v[PK_PRO_U];
@@ -230,23 +273,15 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
         cbar();
         // this CTA's rows of the residual stream: the rows its wo / down epilogues update
         const int r0 = item_begin(a.D, c.cta, c.G), r1 = item_begin(a.D, c.cta + 1, c.G);
-        for (int e = r0 + tid; e < r1; e += PK_CONS) {
-            const float xv = xs[xpad(e)];
-            a.x[e] = xv;
-            c.S->xo[e - r0] = xv;
-        }
+        for (int e = r0 + tid; e < r1; e += PK_CONS) c.S->xo[e - r0] = xs[xpad(e)];
 #pragma unroll
         for (int u = 0; u < PK_PRO_U; ++u) {
             const int q = tid + u * PK_CONS;
             v[u] = q < nq ? *reinterpret_cast<const float4*>(xs + xpad(4 * q)) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     } else {
-        const float4* src = reinterpret_cast<const float4*>(kind == PK_WO ? a.attn : kind == PK_DOWN ? a.h : a.x);
-#pragma unroll
-        for (int u = 0; u < PK_PRO_U; ++u) {
-            const int q = tid + u * PK_CONS;
-            v[u] = q < nq ? __ldcg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+        const bool got = ll_read(c, src, nq, ep_in, v);
+        if (!pk_verdict(c, got)) return false;
     }
     if (norm) {
         // rmsnorm (src/layers.cpp:7-12): sum of squares in double, inv in float, (x * inv) * w
@@ -366,14 +401,14 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
         if (mine && leader && first_row && okr) {
             const int row = rsel ? item1 : item0;
             if (kind == PK_QKV) {
-                a.qkv[row] = keep + c.S->pre[row - i0];
+                st_ll(a.llq + row, keep + c.S->pre[row - i0], ep_out);
             } else if (kind == PK_WO || kind == PK_DOWN) {
                 // wo / down rows are the CTA's residual rows (both partition D the same way)
                 const float xv = c.S->xo[row - i0] + keep;
                 c.S->xo[row - i0] = xv;
-                a.x[row] = xv;
+                st_ll(a.llx + row, xv, ep_out);
             } else if (kind == PK_GU) {
-                a.h[row] = __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other);
+                st_ll(a.llh + row, __fmul_rn(__fdiv_rn(keep, 1.0f + expf(-keep)), other), ep_out);
             } else {
                 a.logits[row] = keep;
                 const unsigned long long k = argmax_key(keep, (uint32_t)row);
@@ -394,9 +429,7 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
             c.S->ckey = 0ull;
             if (k && cta_ok) atomicMax(a.keys + step, k);
         }
-        if (cta_ok) {
-            red_release_gpu_add(arr, 1u);
-        } else {
+        if (!cta_ok) {
             atomicExch(a.abort_g, 1);
             *reinterpret_cast<volatile int*>(&c.S->abort) = 1;
         }
@@ -413,7 +446,7 @@ __device__ bool pk_gemv(PkCtx& c, const PkMat& mat, const unsigned* dep, unsigne
 // hd + 4 floats), CTA-wide max / sum, ng groups of hd threads for the weighted V sum; with
 // nsf > 1 each split leaves (max, sum, weighted V) and the last of the head's CTAs combines
 // the splits in split order.
-__device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, const unsigned* dep, unsigned target) {
+__device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, unsigned ep_qkv, unsigned ep_att) {
     const PkArgs& a = *c.a;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int hd = a.hd, d2 = hd / 2, n_rep = a.n_head / a.n_kv;
@@ -444,17 +477,29 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, con
         const int npc = (s0 + np == pos + 1) ? np - 1 : np;
         pk_issue_tile(c, ks, vs, kst, hd, kcf + (size_t)s0 * hd, vcf + (size_t)s0 * hd, npc);
     }
-    if (!pk_wait(c, dep, target)) {
-        if (s0 < s1) {  // the tile's copies land before the CTA unwinds
-            mbar_wait(&c.S->abar, c.tiles & 1, nullptr, 0, nullptr);
-            ++c.tiles;
+    {   // this head's q and its kv head's k, v: one LL pair per thread, polled
+        bool got = true;
+        if (tid < 3 * hd) {
+            const int part = tid / hd, i = tid % hd;
+            const size_t off = part == 0 ? (size_t)qh * hd : (size_t)a.H + (part == 2 ? a.KVd : 0) + (size_t)kvh * hd;
+            int n = 0;
+            uint2 pr = ld_ll1(a.llq + off + i);
+            for (; pr.y != ep_qkv && n < kGridPolls; ++n) {
+                if ((n & 15) == 15 && (ld_vol(&c.S->abort) || ld_vol(a.abort_g))) break;
+                if (n > 8) __nanosleep(n > 65536 ? 1024 : 64);
+                pr = ld_ll1(a.llq + off + i);
+            }
+            got = pr.y == ep_qkv;
+            if (!got && n == kGridPolls) atomicCAS(a.err, 0, ERR_GRID_SYNC);
+            (part == 0 ? qs : part == 1 ? kn : vn)[i] = __uint_as_float(pr.x);
         }
-        return false;
-    }
-    for (int i = tid; i < hd; i += PK_CONS) {
-        qs[i] = __ldcg(a.qkv + (size_t)qh * hd + i);
-        kn[i] = __ldcg(a.qkv + (size_t)a.H + (size_t)kvh * hd + i);
-        vn[i] = __ldcg(a.qkv + (size_t)a.H + a.KVd + (size_t)kvh * hd + i);
+        if (!pk_verdict(c, got)) {
+            if (s0 < s1) {  // the tile's copies land before the CTA unwinds
+                mbar_wait(&c.S->abar, c.tiles & 1, nullptr, 0, nullptr);
+                ++c.tiles;
+            }
+            return false;
+        }
     }
     cbar();
     for (int i = tid; i < hd; i += PK_CONS) {
@@ -539,7 +584,7 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, con
         for (int d = tid; d < hd; d += PK_CONS) {
             float o = 0.f;
             for (int g = 0; g < ng; ++g) o += pacc[g * hd + d];
-            a.attn[(size_t)qh * hd + d] = o / l_run;
+            st_ll(a.lla + (size_t)qh * hd + d, o / l_run, ep_att);
         }
         return true;
     }
@@ -576,7 +621,7 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, con
     for (int d = tid; d < hd; d += PK_CONS) {
         float num = 0.f;
         for (int q = 0; q < nsf; ++q) num = fmaf(cm[2 * nsf + q], __ldcg(pb + (size_t)q * (hd + 2) + 2 + d), num);
-        a.attn[(size_t)qh * hd + d] = num / den;
+        st_ll(a.lla + (size_t)qh * hd + d, num / den, ep_att);
     }
     if (tid == 0) a.tickets[qh] = 0u;
     return true;
@@ -607,8 +652,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) tf_decode_persistent_kernel(con
     PkCtx c{&a, rg, S, smem + a.reg_off, cta, G, 0, 0};
     const int L = a.n_layer;
     const unsigned uG = (unsigned)G;
-    unsigned* cnt_head = a.cnt + PC_PER_LAYER * L;
-    const unsigned* last_down = a.cnt + PC_PER_LAYER * (L - 1) + PC_DOWN;
+    const int n_att = a.n_head * a.nsf;
     bool ok = true;
     for (int s = 0; s < a.n_steps && ok; ++s) {
         const int pos = a.pos0 + s;
@@ -621,49 +665,53 @@ __global__ void __launch_bounds__(PK_THREADS, 1) tf_decode_persistent_kernel(con
             ok = false;
             break;
         }
-        const int ws = s < a.n_prompt ? min(max(a.ws_prompt, 0), pos) : 0;
-        const unsigned tl = (unsigned)(s + 1) * uG;  // layer phases of this step complete
-        // QKV of layer 0 follows the previous step's last phase
-        const unsigned* dep0 = nullptr;
-        unsigned t0 = 0;
-        if (s > 0) {
-            if (s - 1 >= a.first_head) {
-                dep0 = cnt_head;
-                t0 = (unsigned)(s - a.first_head) * uG;
-            } else {
-                dep0 = last_down;
-                t0 = (unsigned)s * uG;
-            }
+        // every CTA has finished the previous step: its KV-cache stores and greedy key are out
+        if (s > 0 && !pk_wait(c, a.cnt, (unsigned)s * uG)) {
+            ok = false;
+            break;
         }
+        // the cache rows other CTAs stored (generic proxy) are read by bulk copies (async proxy)
+        if (tid < 32 && cta < n_att) asm volatile("fence.proxy.async;" ::: "memory");
+        const int ws = s < a.n_prompt ? min(max(a.ws_prompt, 0), pos) : 0;
         const int token = s < a.n_prompt ? a.prompt[s] : -2;
-        if (cta < a.n_head * a.nsf)  // the step's RoPE row, read at every layer's attention
+        if (cta < n_att)  // the step's RoPE row, read at every layer's attention
             for (int i = tid; i < a.hd / 2; i += PK_CONS) {
                 S->cs[i] = __ldg(a.cosb + (size_t)pos * (a.hd / 2) + i);
                 S->sn[i] = __ldg(a.sinb + (size_t)pos * (a.hd / 2) + i);
             }
-        for (int l = 0; l < L && ok; ++l) {
-            unsigned* cl = a.cnt + PC_PER_LAYER * l;
-            const PkMat* ml = a.mats + PK_MATS * l;
-            ok = pk_gemv<PK_QKV>(c, ml[PK_QKV], l == 0 ? dep0 : cl - PC_PER_LAYER + PC_DOWN, l == 0 ? t0 : tl,
-                                 cl + PC_QKV, l == 0 ? token : -1, s);
-            if (!ok) break;
-            if (cta < a.n_head * a.nsf) ok = pk_attention(c, l, cta, pos, ws, cl + PC_QKV, tl);
-            if (!ok) break;
-            pk_arrive(cl + PC_ATT);
-            ok = pk_gemv<PK_WO>(c, ml[PK_WO], cl + PC_ATT, tl, cl + PC_WO, -1, s);
-            if (ok) ok = pk_gemv<PK_GU>(c, ml[PK_GU], cl + PC_WO, tl, cl + PC_GU, -1, s);
-            if (ok) ok = pk_gemv<PK_DOWN>(c, ml[PK_DOWN], cl + PC_GU, tl, cl + PC_DOWN, -1, s);
+        const unsigned eb = a.ep0 + (unsigned)s * (unsigned)L * PK_EPS;  // epochs of this step
+        // phases of the step in order: per layer QKV, attention, wo, gate/up, down; then the
+        // lm_head (one call site for every GEMV phase)
+        const int n_ph = L * 5 + (s >= a.first_head ? 1 : 0);
+        for (int ph = 0; ph < n_ph && ok; ++ph) {
+            const int l = ph / 5, k = ph % 5;
+            const unsigned e = eb + (unsigned)l * PK_EPS;
+            if (k == 1) {
+                if (cta < n_att) ok = pk_attention(c, l, cta, pos, ws, e + PE_QKV, e + PE_ATT);
+                continue;
+            }
+            const int kind = l == L ? PK_HEAD : k == 0 ? PK_QKV : k == 2 ? PK_WO : k == 3 ? PK_GU : PK_DOWN;
+            const PkMat& mt = l == L ? a.mats[PK_MATS * L] : a.mats[PK_MATS * l + (k == 0 ? 0 : k - 1)];
+            const uint2* src = k == 2 ? a.lla : k == 4 ? a.llh : a.llx;
+            const unsigned ep_in = l == L || k == 0 ? e - PK_EPS + PE_DOWN : k == 2 ? e + PE_ATT : k == 3 ? e + PE_WO
+                                                                                                   : e + PE_GU;
+            const unsigned ep_out = k == 0 ? e + PE_QKV : k == 2 ? e + PE_WO : k == 3 ? e + PE_GU : e + PE_DOWN;
+            ok = pk_gemv(c, mt, kind, src, ep_in, ep_out, (l == 0 && k == 0) ? token : -1, s);
         }
-        if (ok && s >= a.first_head) ok = pk_gemv<PK_HEAD>(c, a.mats[PK_MATS * L], last_down, tl, cnt_head, -1, s);
+        if (ok) {  // step done: fence (cumulative over the CTA's stores), then count the arrival
+            cbar();
+            if (tid == 0) {
+                __threadfence();
+                red_release_gpu_add(a.cnt, 1u);
+            }
+        }
     }
     if (!ok || cta != 0) return;
     // CTA 0 publishes the last step's argmax and the new position once every CTA is done
-    const int sl = a.n_steps - 1;
-    const bool head = sl >= a.first_head;
-    if (!pk_wait(c, head ? cnt_head : last_down, head ? (unsigned)(sl - a.first_head + 1) * uG : (unsigned)a.n_steps * uG))
-        return;
+    if (!pk_wait(c, a.cnt, (unsigned)a.n_steps * uG)) return;
     if (tid == 0) {
-        if (head) {
+        const int sl = a.n_steps - 1;
+        if (sl >= a.first_head) {
             const int tok = (int)key_index(__ldcg(a.keys + sl));
             a.tok[0] = tok;
             if (sl - a.first_head < a.hist_cap) a.hist[sl - a.first_head] = tok;

@@ -32,8 +32,11 @@ constexpr int PK_MAX_D2 = 128;                // head_dim / 2 of the RoPE table 
 // matrices per layer in the table: QKV (rows q | k | v), wo, gate/up (row pairs), down; the
 // lm_head follows the last layer's
 enum : int { PK_QKV = 0, PK_WO = 1, PK_GU = 2, PK_DOWN = 3, PK_MATS = 4, PK_HEAD = 5 };
-// arrival counters per layer (QKV, attention, wo, gate/up, down), then the lm_head's
-enum : int { PC_QKV = 0, PC_ATT = 1, PC_WO = 2, PC_GU = 3, PC_DOWN = 4, PC_PER_LAYER = 5 };
+// Inside a step, activations cross CTAs as flag-in-data pairs {value bits, epoch} written with
+// one 8-byte store: a reader polls the pairs it needs until every epoch is the one it expects,
+// so no fence or counter round trip sits between a phase and the next.  Epoch of buffer k
+// written at (step s, layer l): ep0 + (s * n_layer + l) * PK_EPS + k.
+enum : int { PE_QKV = 1, PE_ATT = 2, PE_WO = 3, PE_GU = 4, PE_DOWN = 5, PK_EPS = 8 };
 
 // One GEMV phase: a Q8_0 matrix and its plan.  A CTA owns items [n_items*c/G,
 // n_items*(c+1)/G); an item is one row (P = 1) or a gate/up row pair (P = 2); a stage holds
@@ -69,11 +72,12 @@ struct PkArgs {
     int embd_type;
     long long embd_rb;
     int n_vocab;
-    // activations (global, written and read across CTAs with ld.global.cg)
-    float* x;              // residual [D]
-    float* qkv;            // [H + 2 KV]
-    float* attn;           // [H]
-    float* h;              // [FF]
+    // activations crossing CTAs: {value bits, epoch} pairs
+    uint2* llq;            // q | k | v [H + 2 KV]
+    uint2* lla;            // attention output [H]
+    uint2* llx;            // residual stream [D] (after wo, after down)
+    uint2* llh;            // SwiGLU output [FF]
+    unsigned ep0;          // epoch base of this launch
     float* logits;         // [V]
     int D, H, KVd, FF;
     // fp32 KV cache and RoPE table
@@ -92,7 +96,7 @@ struct PkArgs {
     int* hist;             // generated ids, hist[s - first_head]
     int hist_cap;
     unsigned long long* keys;  // [n_steps] greedy keys (zero at launch)
-    unsigned* cnt;             // [PC_PER_LAYER * n_layer + 1] arrival counters (zero at launch)
+    unsigned* cnt;             // [1] step arrivals (zero at launch)
     int* abort_g;              // raised by any CTA that gives up (zero at launch)
     int* err;
 };

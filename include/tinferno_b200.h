@@ -62,10 +62,12 @@ typedef struct tf_options {
     int device;
     int kv_type;   /* TF_KV_* */
     int use_graph; /* per-kernel path: 1 = capture the decode step in a CUDA graph (default) */
-    int decode_mode; /* batch-1 decode/prefill/generate: TF_DECODE_KERNELS (default, 0)
+    int decode_mode; /* batch-1 decode / short prefill / generate: TF_DECODE_KERNELS (default, 0)
                         launches one kernel per phase under programmatic dependent launch,
                         captured in a CUDA graph (also the path of batched decode);
-                        TF_DECODE_PERSISTENT runs whole steps in one cooperative kernel */
+                        TF_DECODE_PERSISTENT runs whole token steps in one cooperative kernel
+                        (all layer matrices and the lm_head Q8_0, fp32 KV cache; tf_cuda_create
+                        fails for other models) */
 } tf_options;
 
 enum { TF_DECODE_KERNELS = 0, TF_DECODE_PERSISTENT = 1 };
