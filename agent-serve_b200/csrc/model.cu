@@ -15,11 +15,13 @@
 //   (+ end-of-step bookkeeping: next token, history, position), all launched with
 //   programmatic dependent launch and captured once per row count into a CUDA graph.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <map>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "attention.cuh"
@@ -27,6 +29,7 @@
 #include "gemm.cuh"
 #include "sample.cuh"
 #include "persist.cuh"
+#include "upload.cuh"
 #include "engine.cuh"
 
 namespace tfb {
@@ -145,6 +148,7 @@ struct tf_model {
     unsigned pk_ep = 1;
     float* d_pkpart = nullptr;
     unsigned* d_pktickets = nullptr;
+    double upload_s = 0.0;  // seconds tf_cuda_create spent moving the weights into HBM
     std::string err;
 };
 
@@ -1007,42 +1011,59 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
         if (t->ggml_type == T_Q4_0) return q8_scale_exponent(b, t->nbytes, 18);
         return 0;
     };
+    // every tensor goes through the pinned, double-buffered uploader (TFB200_UPLOAD_SYNC=1: one
+    // synchronous pageable cudaMemcpy per tensor instead, for comparison)
+    Uploader up;
+    const char* usync = getenv("TFB200_UPLOAD_SYNC");
+    const bool streamed = !(usync && usync[0] == '1');
+    if (streamed) {
+        const unsigned hc = std::thread::hardware_concurrency();
+        CKD(up.init((size_t)32 << 20, 3, (int)std::min(8u, std::max(1u, hc / 2))));
+    }
+    auto put = [&](void* dst, const void* src, size_t n) -> cudaError_t {
+        return streamed ? up.copy(dst, src, n) : cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
+    };
+    auto put_rows = [&](void* dst, size_t dpitch, const void* src, size_t width, size_t rows) -> cudaError_t {
+        return streamed ? up.copy_rows(dst, dpitch, src, width, rows)
+                        : cudaMemcpy2D(dst, dpitch, src, width, width, rows, cudaMemcpyHostToDevice);
+    };
+    const auto t_up = std::chrono::steady_clock::now();
     m->L.resize(hp.n_layer);
     for (int i = 0; i < hp.n_layer; ++i) {
         LDesc& L = ld[i];
         LayerDev& Ld = m->L[i];
-        CKD(cudaMemcpy(A + pl[i].an, L.an->data, L.an->nbytes, cudaMemcpyHostToDevice));
+        CKD(put(A + pl[i].an, L.an->data, L.an->nbytes));
         Ld.attn_norm = reinterpret_cast<const float*>(A + pl[i].an);
-        CKD(cudaMemcpy(A + pl[i].qkv, L.q->data, L.q->nbytes, cudaMemcpyHostToDevice));
-        CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes, L.k->data, L.k->nbytes, cudaMemcpyHostToDevice));
-        CKD(cudaMemcpy(A + pl[i].qkv + L.q->nbytes + L.k->nbytes, L.v->data, L.v->nbytes, cudaMemcpyHostToDevice));
+        CKD(put(A + pl[i].qkv, L.q->data, L.q->nbytes));
+        CKD(put(A + pl[i].qkv + L.q->nbytes, L.k->data, L.k->nbytes));
+        CKD(put(A + pl[i].qkv + L.q->nbytes + L.k->nbytes, L.v->data, L.v->nbytes));
         Ld.qkv = wref(A + pl[i].qkv, L.q->ggml_type, m->D, m->H + 2 * m->KV);
         Ld.qkv.sw = std::min({wscale(L.q), wscale(L.k), wscale(L.v)});
         Ld.bqkv = nullptr;
         if (L.bq) {
             float* b = reinterpret_cast<float*>(A + pl[i].b);
-            CKD(cudaMemcpy(b, L.bq->data, (size_t)m->H * 4, cudaMemcpyHostToDevice));
-            CKD(cudaMemcpy(b + m->H, L.bk->data, (size_t)m->KV * 4, cudaMemcpyHostToDevice));
-            CKD(cudaMemcpy(b + m->H + m->KV, L.bv->data, (size_t)m->KV * 4, cudaMemcpyHostToDevice));
+            CKD(put(b, L.bq->data, (size_t)m->H * 4));
+            CKD(put(b + m->H, L.bk->data, (size_t)m->KV * 4));
+            CKD(put(b + m->H + m->KV, L.bv->data, (size_t)m->KV * 4));
             Ld.bqkv = b;
         }
-        CKD(cudaMemcpy(A + pl[i].o, L.o->data, L.o->nbytes, cudaMemcpyHostToDevice));
+        CKD(put(A + pl[i].o, L.o->data, L.o->nbytes));
         Ld.wo = wref(A + pl[i].o, L.o->ggml_type, m->H, m->D);
         Ld.wo.sw = wscale(L.o);
-        CKD(cudaMemcpy(A + pl[i].fn, L.fn->data, L.fn->nbytes, cudaMemcpyHostToDevice));
+        CKD(put(A + pl[i].fn, L.fn->data, L.fn->nbytes));
         Ld.ffn_norm = reinterpret_cast<const float*>(A + pl[i].fn);
         const size_t grb = (size_t)row_bytes(L.g->ggml_type, m->D);
-        CKD(cudaMemcpy2D(A + pl[i].gu, 2 * grb, L.g->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
-        CKD(cudaMemcpy2D(A + pl[i].gu + grb, 2 * grb, L.u->data, grb, grb, m->FF, cudaMemcpyHostToDevice));
+        CKD(put_rows(A + pl[i].gu, 2 * grb, L.g->data, grb, m->FF));
+        CKD(put_rows(A + pl[i].gu + grb, 2 * grb, L.u->data, grb, m->FF));
         Ld.gateup = wref(A + pl[i].gu, L.g->ggml_type, m->D, 2 * m->FF);
         Ld.gateup.sw = std::min(wscale(L.g), wscale(L.u));
-        CKD(cudaMemcpy(A + pl[i].d, L.d->data, L.d->nbytes, cudaMemcpyHostToDevice));
+        CKD(put(A + pl[i].d, L.d->data, L.d->nbytes));
         Ld.down = wref(A + pl[i].d, L.d->ggml_type, m->FF, m->D);
         Ld.down.sw = wscale(L.d);
     }
-    CKD(cudaMemcpy(A + p_embd, te->data, te->nbytes, cudaMemcpyHostToDevice));
+    CKD(put(A + p_embd, te->data, te->nbytes));
     m->embd = wref(A + p_embd, te->ggml_type, m->D, (int)te->ne[1]);
-    if (ow != te) CKD(cudaMemcpy(A + p_out, ow->data, ow->nbytes, cudaMemcpyHostToDevice));
+    if (ow != te) CKD(put(A + p_out, ow->data, ow->nbytes));
     m->outw = wref(A + p_out, ow->ggml_type, m->D, (int)ow->ne[1]);
     m->outw.sw = wscale(ow);
     {
@@ -1058,7 +1079,9 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
             }
         m->gemm_ok = all > 0 && 2 * tc >= all;
     }
-    CKD(cudaMemcpy(A + p_onorm, on->data, on->nbytes, cudaMemcpyHostToDevice));
+    CKD(put(A + p_onorm, on->data, on->nbytes));
+    if (streamed) CKD(up.finish());
+    m->upload_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_up).count();
     m->out_norm = reinterpret_cast<const float*>(A + p_onorm);
 
     // ---- KV cache: per layer [slot][kv_head][cap][hd] ----

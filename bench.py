@@ -354,6 +354,7 @@ def run_ours(args, rank, world, local_rank, dist):
         roof_lm = gemv_roofline(torch, native, m)
     kps = m.kernels_per_step
     m.close()
+    upload = upload_timing(path, local_rank) if rank == 0 else None
 
     if rank == 0:
         cpu = None
@@ -386,7 +387,7 @@ def run_ours(args, rank, world, local_rank, dist):
                 "roofline": roof, "roofline_lmhead": roof_lm, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                         "d2h_bytes_per_step": 4 * CFG.n_vocab + 8},
-                "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk}
+                "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk, "upload": upload}
         if world == 1 and not args.no_configs:
             try:
                 line["configs"] = config_runs()
@@ -398,6 +399,28 @@ def run_ours(args, rank, world, local_rank, dist):
     if rank == 0:
         line["batched"] = batched
         print(json.dumps(line), flush=True)
+
+
+def upload_timing(path, device):
+    """Seconds tf_cuda_create takes for the cfg0 model (1.31 GB, file pages already cached by
+    the earlier load), with the pinned double-buffered upload and with one synchronous
+    pageable cudaMemcpy per tensor (TFB200_UPLOAD_SYNC=1)."""
+    from tinferno_b200.model import Model, RunConfig
+    out = {}
+    for name, env in (("streamed", None), ("synchronous", "1")):
+        if env:
+            os.environ["TFB200_UPLOAD_SYNC"] = env
+        else:
+            os.environ.pop("TFB200_UPLOAD_SYNC", None)
+        t0 = time.perf_counter()
+        m = Model(path, RunConfig(max_seq=64, device=device))
+        out[name + "_s"] = round(time.perf_counter() - t0, 3)
+        m.close()
+    os.environ.pop("TFB200_UPLOAD_SYNC", None)
+    out["bytes"] = synth.weight_bytes(CFG)
+    out["streamed_GB_s"] = round(out["bytes"] / out["streamed_s"] / 1e9, 2)
+    out["scope"] = "tf_cuda_create wall time (upload, KV cache, tables, graph-free set-up)"
+    return out
 
 
 def gemv_roofline(torch, native, m, reps=50, warm=5):
