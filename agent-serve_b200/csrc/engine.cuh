@@ -20,6 +20,7 @@ int gemv_slots(int num_sms);  // resident GEMV CTAs the device holds (SMs x CTAs
 int gemv_max_rows(int K);
 int fused_attn_tile(const GemvArgs& a, int hd);  // positions per fused-attention tile of a QKV launch
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl);
+cudaError_t key_apply_launch(const long long* key, int* tok, int* hist, const StepCtl* ctl, cudaStream_t st);
 cudaError_t gemv_init_attrs();
 
 struct AttnArgs;

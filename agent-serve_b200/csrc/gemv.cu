@@ -742,7 +742,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
                     if (a.yplanes) pre[row - i0] = hv;
                 } else {  // EPI_ARGMAX
                     a.y[row] = keep;
-                    const unsigned long long k = argmax_key(keep, (uint32_t)row);
+                    const unsigned long long k = argmax_key(keep, (uint32_t)(row + a.row_base));
                     best[0] = k > best[0] ? k : best[0];
                 }
             }
@@ -828,7 +828,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
                 } else {  // EPI_ARGMAX
                     const float v = acc0[m];
                     a.y[(size_t)m * a.ldy + row] = v;
-                    const unsigned long long k = argmax_key(v, (uint32_t)row);
+                    const unsigned long long k = argmax_key(v, (uint32_t)(row + a.row_base));
                     best[m] = k > best[m] ? k : best[m];
                 }
             }
@@ -864,6 +864,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
                         const int tok = (int)key_index(k);
                         a.tok_next[m] = tok;
                         if (a.hist && gs < a.ctl->hist_cap) a.hist[(size_t)gs * a.M + m] = tok;
+                    } else if (a.fin == FIN_KEY) {
+                        const unsigned long long k = atomicExch(&a.keys[m], 0ull);
+                        a.key_out[m] = (long long)(k ^ 0x8000000000000000ull);
                     }
                     a.pos[a.slots[m]] += 1;
                 }
@@ -873,6 +876,30 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
             }
         }
     }
+}
+
+// Vocab-split lm_head: the token of the next step from the key reduced across GPUs (max of
+// the flipped keys; the reference's first-index tie rule survives the reduction because the
+// key orders equal logits by descending 0xFFFFFFFF - index), and its history entry.
+__global__ void tf_key_apply_kernel(const long long* key, int* tok, int* hist, const StepCtl* ctl) {
+    const unsigned long long k = (unsigned long long)key[0] ^ 0x8000000000000000ull;
+    const int t = (int)key_index(k);
+    tok[0] = t;
+    const int gs = ctl->gen_step - 1;
+    if (hist && gs >= 0 && gs < ctl->hist_cap) hist[gs] = t;
+}
+
+cudaError_t key_apply_launch(const long long* key, int* tok, int* hist, const StepCtl* ctl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tf_key_apply_kernel, key, tok, hist, ctl);
 }
 
 // ---- host side --------------------------------------------------------------------------

@@ -23,7 +23,10 @@ constexpr int GV_PRO_UNROLL = 8;                 // float4 activation loads in f
 // previous kernel (xplanes); no activation load, norm or plane build in the prologue
 enum : int { PRO_COPY = 0, PRO_RMSNORM = 1, PRO_EMBED_RMSNORM = 2, PRO_PLANES = 3 };
 enum : int { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
-enum : int { FIN_NONE = 0, FIN_ADVANCE = 1, FIN_ARGMAX = 2 };
+// FIN_KEY (vocab-split lm_head): the step's greedy key over this GPU's rows goes to key_out,
+// order-flipped to a signed 64-bit value (key ^ 2^63) for a max all-reduce across GPUs; the
+// next token comes from the reduced key (tf_key_apply_kernel)
+enum : int { FIN_NONE = 0, FIN_ADVANCE = 1, FIN_ARGMAX = 2, FIN_KEY = 3 };
 
 // Per-step control words in device memory (one set per engine).
 struct StepCtl {
@@ -67,6 +70,8 @@ struct GemvArgs {
     float* resid;        // EPI_RESID
     int ldr;
     unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
+    int row_base;        // EPI_ARGMAX: vocabulary index of row 0 of W (vocab-split lm_head)
+    long long* key_out;  // FIN_KEY: the step's key, order-flipped for a signed max reduction
     // end of step
     int fin;
     StepCtl* ctl;

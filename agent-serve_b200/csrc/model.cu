@@ -149,6 +149,12 @@ struct tf_model {
     float* d_pkpart = nullptr;
     unsigned* d_pktickets = nullptr;
     double upload_s = 0.0;  // seconds tf_cuda_create spent moving the weights into HBM
+    // vocab-split lm_head (batch 1): this GPU's rows [vs_row0, vs_row1) of the output matrix;
+    // the step's key leaves in d_keyred for a max all-reduce across the GPUs
+    bool vsplit = false;
+    bool split_step = false;  // set only while tf_cuda_decode_shard enqueues its step
+    int vs_row0 = 0, vs_row1 = 0;
+    long long* d_keyred = nullptr;
     std::string err;
 };
 
@@ -450,12 +456,17 @@ int enqueue_step_gemm(tf_model* m, int M, bool head, int* n_launch, bool chunk) 
 }
 
 // fused: CTAs per query head of the attention fused into the QKV kernel (0: separate kernel)
-int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fused, bool chunk = false) {
+int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fused, bool chunk = false,
+                 bool from_key = false) {
     if (chunk) return enqueue_step_gemm(m, M, head, n_launch, true);
     if (M >= GM_MIN_M && m->gtile >= M) return enqueue_step_gemm(m, M, head, n_launch, false);
     const int D = m->D, H = m->H, KV = m->KV, FF = m->FF, V = m->V;
     const int ldq = H + 2 * KV;
     int launches = 0;
+    if (from_key) {  // vocab split: this step's token is the argmax of the reduced key
+        CK(key_apply_launch(m->d_keyred, m->d_tokens, m->d_hist, m->ctl, m->stream));
+        ++launches;
+    }
     bool fuse = false, planes_wo = false, planes_down = false;
     for (int li = 0; li < m->hp.n_layer; ++li) {
         const LayerDev& Ld = m->L[li];
@@ -564,17 +575,23 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
         }
     }
     if (head) {  // rmsnorm + lm_head GEMV + logits + greedy argmax + end of step
-        GemvArgs a = gemv_base(m, m->outw, V, 1, M);
+        const bool split = m->split_step && M == 1;
+        const int r0 = split ? m->vs_row0 : 0, nr = split ? m->vs_row1 - m->vs_row0 : V;
+        WeightRef ow = m->outw;
+        ow.p += (size_t)r0 * ow.rb;
+        GemvArgs a = gemv_base(m, ow, nr, 1, M);
         a.pro = PRO_RMSNORM;
         a.x = m->x;
         a.ldx = D;
         a.norm_w = m->out_norm;
         a.eps = m->hp.rms_eps;
         a.epi = EPI_ARGMAX;
-        a.y = m->logits;
+        a.y = m->logits + r0;
         a.ldy = V;
         a.keys = m->keys;
-        a.fin = FIN_ARGMAX;
+        a.row_base = r0;
+        a.fin = split ? FIN_KEY : FIN_ARGMAX;
+        a.key_out = m->d_keyred;
         a.ctl = m->ctl;
         a.tok_next = m->d_tokens;
         a.pos = m->d_pos;
@@ -588,14 +605,17 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
 }
 
 // Run one step for M rows (tokens in d_tokens[0..M), slots in d_slots[0..M)).
-int run_step(tf_model* m, int M, bool head, int fused, bool chunk = false) {
-    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused, chunk);
-    const long long key = ((long long)fused << 40) + (long long)M * 8 + (head ? 1 : 0) + (chunk ? 4 : 0);
+int run_step(tf_model* m, int M, bool head, int fused, bool chunk = false, bool from_key = false) {
+    if (!m->opt.use_graph) return enqueue_step(m, M, head, true, nullptr, fused, chunk, from_key);
+    // graphs are keyed by everything that changes the launch sequence or its arguments
+    const bool split = head && m->split_step && M == 1;
+    const long long key = ((long long)fused << 40) + ((long long)(split ? 1 + m->vs_row0 : 0) << 20) +
+                          (long long)M * 32 + (head ? 1 : 0) + (chunk ? 4 : 0) + (from_key ? 8 : 0);
     auto it = m->graphs.find(key);
     if (it == m->graphs.end()) {
         cudaGraph_t g = nullptr;
         CK(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-        int rc = enqueue_step(m, M, head, true, nullptr, fused, chunk);
+        int rc = enqueue_step(m, M, head, true, nullptr, fused, chunk, from_key);
         cudaError_t e = cudaStreamEndCapture(m->stream, &g);
         if (rc) {
             if (g) cudaGraphDestroy(g);
@@ -824,7 +844,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
+                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_keyred, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
                    m->xplanes};
     for (void* p : dev)
         if (p) cudaFree(p);
@@ -1323,6 +1343,72 @@ int tf_cuda_generate_greedy(tf_model* m, int seq, int first_token, int n, int eo
         CK(cudaStreamSynchronize(m->stream));
     }
     if (n_out) *n_out = j;
+    return 0;
+}
+
+int tf_cuda_set_vocab_shard(tf_model* m, int rank, int world) {
+    if (!m) return set_error("null model");
+    if (world < 1 || rank < 0 || rank >= world || world > m->V) return fail(m, "bad vocab shard (rank, world)");
+    CK(cudaSetDevice(m->device));
+    if (!m->d_keyred) CK(cudaMalloc(&m->d_keyred, sizeof(long long)));
+    const int r0 = (int)((long long)m->V * rank / world), r1 = (int)((long long)m->V * (rank + 1) / world);
+    if (r0 != m->vs_row0 || r1 != m->vs_row1 || (world > 1) != m->vsplit) {
+        // captured steps hold the old rows: capture again
+        for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+        m->graphs.clear();
+    }
+    m->vs_row0 = r0;
+    m->vs_row1 = r1;
+    m->vsplit = world > 1;
+    return 0;
+}
+
+void* tf_cuda_shard_key(tf_model* m) { return m ? static_cast<void*>(m->d_keyred) : nullptr; }
+
+int tf_cuda_decode_shard(tf_model* m, int seq, int token) {
+    if (!m) return set_error("null model");
+    if (!m->d_keyred) return fail(m, "tf_cuda_set_vocab_shard was not called");
+    CK(cudaSetDevice(m->device));
+    if (check_seq(m, seq)) return -1;
+    if (m->hpos[seq] + 1 > m->opt.max_seq) return fail(m, "decode exceeds max_seq");
+    if (token >= m->V) return fail(m, "token id out of range");
+    const bool from_key = token < 0;
+    if (!from_key) {  // the first step of a run: host token, fresh step counter and history
+        if (set_slot_row(m, 0, seq, token)) return -1;
+        StepCtl c = {0u, 0, m->opt.max_seq, 0};
+        memcpy(m->hi + 4, &c, sizeof(c));
+        CK(cudaMemcpyAsync(m->ctl, m->hi + 4, sizeof(StepCtl), cudaMemcpyHostToDevice, m->stream));
+    }
+    m->split_step = m->vsplit;
+    const int rc = run_step(m, 1, true, fuse_attn_ok(m, m->hpos[seq] + 1), false, from_key);
+    m->split_step = false;
+    if (rc) return -1;
+    m->hpos[seq] += 1;
+    return 0;
+}
+
+int tf_cuda_shard_token(tf_model* m, int seq, int* token) {
+    if (!m) return set_error("null model");
+    if (!m->d_keyred || !token) return fail(m, "no vocab shard, or token is null");
+    CK(cudaSetDevice(m->device));
+    if (check_seq(m, seq)) return -1;
+    CK(key_apply_launch(m->d_keyred, m->d_tokens, m->d_hist, m->ctl, m->stream));
+    CK(cudaMemcpyAsync(m->hb, m->d_tokens, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    const int rc = finish_call(m);
+    if (rc) return rc;
+    *token = m->hb[0];
+    return 0;
+}
+
+int tf_cuda_history(tf_model* m, int n, int* out) {
+    if (!m) return set_error("null model");
+    if (n < 0 || n > m->opt.max_seq || (n && !out)) return fail(m, "bad history request");
+    if (!n) return 0;
+    CK(cudaSetDevice(m->device));
+    CK(cudaMemcpyAsync(m->hi + 64, m->d_hist, sizeof(int) * n, cudaMemcpyDeviceToHost, m->stream));
+    const int rc = finish_call(m);
+    if (rc) return rc;
+    memcpy(out, m->hi + 64, sizeof(int) * n);
     return 0;
 }
 

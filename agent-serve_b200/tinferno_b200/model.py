@@ -234,6 +234,30 @@ class Model:
             self.decode(t)
         return out
 
+    # ---- vocab-split lm_head (include/tinferno_b200.h, tf_cuda_set_vocab_shard) ----
+    def set_vocab_shard(self, rank: int, world: int):
+        native.check(self.L.tf_cuda_set_vocab_shard(self.h, int(rank), int(world)), self.h)
+
+    @property
+    def shard_key_ptr(self) -> int:
+        """Device address of this GPU's order-flipped greedy key (one int64)."""
+        return int(self.L.tf_cuda_shard_key(self.h) or 0)
+
+    def decode_shard(self, token: int = -1, seq: int = 0):
+        """One asynchronous step with the split lm_head; token < 0 continues from the reduced key."""
+        native.check(self.L.tf_cuda_decode_shard(self.h, seq, int(token)), self.h)
+
+    def shard_token(self, seq: int = 0) -> int:
+        out = C.c_int(0)
+        native.check(self.L.tf_cuda_shard_token(self.h, seq, C.byref(out)), self.h)
+        return out.value
+
+    def history(self, n: int) -> list:
+        """The first n ids of the last device-side greedy run (tf_cuda_history)."""
+        out = np.zeros(max(1, n), np.int32)
+        native.check(self.L.tf_cuda_history(self.h, int(n), out.ctypes.data_as(native.i32p)), self.h)
+        return out[:n].tolist()
+
     @property
     def stream(self) -> int:
         return int(self.L.tf_cuda_stream(self.h) or 0)

@@ -55,6 +55,11 @@ SIGNATURES = [
     ("tf_cuda_decode_batch", C.c_int, [_V, i32p, i32p, C.c_int, i32p, f32p]),
     ("tf_cuda_prefill_batch", C.c_int, [_V, i32p, i32p, C.c_int, C.c_int, i32p]),
     ("tf_cuda_sample", C.c_int, [_V, C.c_int, C.c_float, C.c_float, C.c_float, i32p]),
+    ("tf_cuda_set_vocab_shard", C.c_int, [_V, C.c_int, C.c_int]),
+    ("tf_cuda_shard_key", C.c_void_p, [_V]),
+    ("tf_cuda_decode_shard", C.c_int, [_V, C.c_int, C.c_int]),
+    ("tf_cuda_shard_token", C.c_int, [_V, C.c_int, i32p]),
+    ("tf_cuda_history", C.c_int, [_V, C.c_int, i32p]),
     ("tf_cuda_reset", C.c_int, [_V, C.c_int]),
     ("tf_cuda_n_pos", C.c_int, [_V, C.c_int]),
     ("tf_cuda_n_vocab", C.c_int, [_V]),

@@ -308,6 +308,7 @@ def run_ours(args, rank, world, local_rank, dist):
     first = prefill()
     ids = m.generate_greedy(first, args.warmup)  # W untimed steps (graph captured and warm)
     nxt = ids[-1]  # the timed steps continue the stream at positions 32+W ..
+    replica_ids = list(ids)
     clocks = ClockSampler(local_rank)
     if dist:
         dist.barrier()
@@ -321,6 +322,7 @@ def run_ours(args, rank, world, local_rank, dist):
     torch.cuda.synchronize()
     ms = ev0.elapsed_time(ev1)
     clk = clocks.stop()
+    replica_ids += [int(v) for v in out[1:n_out.value]]
     if dist:
         dist.barrier()
     t = torch.tensor([ms], device="cuda")
@@ -347,6 +349,40 @@ def run_ours(args, rank, world, local_rank, dist):
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e = world * args.steps / float(t.item())
+
+    # ---- vocab-split lm_head (N > 1): every rank decodes the same sequence and computes V/N of
+    # the lm_head rows; one NCCL int64 max all-reduce of the greedy key per step ----
+    vsplit = None
+    if dist and world > 1:
+        from tinferno_b200 import shard
+        first = prefill()
+        m.set_vocab_shard(rank, world)
+        red = shard.nccl_key_reducer(m, dist)
+        ids_w = shard.split_greedy(m, first, args.warmup, red)
+        dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for i in range(args.steps):
+            m.decode_shard(ids_w[-1] if i == 0 else -1)
+            red()
+        ev1.record(stream)
+        m.shard_token()
+        torch.cuda.synchronize()
+        ids_k = [ids_w[-1]] + m.history(args.steps - 1)
+        t = torch.tensor([ev0.elapsed_time(ev1)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_split = float(t.item())
+        # the same stream as the replica leg (value): [first, W warm-up ids] then the timed ids
+        same = ids_w == replica_ids[:len(ids_w)] and ids_k == replica_ids[len(ids_w) - 1:len(ids_w) - 1 + len(ids_k)]
+        ok = torch.tensor([1 if same else 0], device="cuda")
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        m.set_vocab_shard(0, 1)
+        vsplit = {"metric": "batch-1 decode tok/s of ONE sequence with the lm_head split over the GPUs",
+                  "tok_s": round(args.steps / (ms_split / 1e3), 1), "ms_per_step": round(ms_split / args.steps, 4),
+                  "n_gpus": world, "lm_head_rows_per_gpu": CFG.n_vocab // world,
+                  "collective": "NCCL int64 max all-reduce of the greedy key, one per step, on the model's stream",
+                  "ids_equal_replica_stream": bool(ok.item())}
 
     # ---- the lm_head-shape GEMV alone (secondary roofline figure) ----
     roof_lm = None
@@ -387,7 +423,8 @@ def run_ours(args, rank, world, local_rank, dist):
                 "roofline": roof, "roofline_lmhead": roof_lm, "cpu_baseline": cpu,
                 "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
                         "d2h_bytes_per_step": 4 * CFG.n_vocab + 8},
-                "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk, "upload": upload}
+                "gpu_launches": kps * args.steps, "kernels_per_step": kps, "clocks": clk, "upload": upload,
+                "vocab_split": vsplit}
         if world == 1 and not args.no_configs:
             try:
                 line["configs"] = config_runs()

@@ -121,6 +121,30 @@ TF_API int tf_cuda_prefill_batch(tf_model* m, const int* seq_ids, const int* tok
  * temperature <= 0 is sample_greedy. */
 TF_API int tf_cuda_sample(tf_model* m, int row, float temperature, float top_p, float r, int* out_id);
 
+/* Vocab-split lm_head for batch-1 latency on several GPUs (each GPU runs the same sequence,
+ * the 279 MB cfg0 lm_head is split), no reference counterpart (the reference's lm_head is one
+ * matmul, src/model.cpp:205, and sample_greedy, src/sampler.cpp:8-13):
+ *   tf_cuda_set_vocab_shard  this handle computes logits rows [V*rank/world, V*(rank+1)/world)
+ *                            only (world == 1: the whole vocabulary again);
+ *   tf_cuda_shard_key        device address of one int64: after each tf_cuda_decode_shard,
+ *                            this GPU's greedy key (value, then first index on ties),
+ *                            order-flipped so that a signed max all-reduce across the GPUs
+ *                            (ncclAllReduce ncclInt64 ncclMax on the model's stream) leaves the
+ *                            key of the whole vocabulary's argmax in every copy;
+ *   tf_cuda_decode_shard     one decode step of `seq` with the split lm_head, asynchronous (no
+ *                            synchronisation); token >= 0 starts a run from a host token,
+ *                            token < 0 takes the argmax of the reduced key on the device;
+ *   tf_cuda_shard_token      the argmax of the reduced key (host), synchronising the stream.
+ * The logits of a shard step are valid for the shard's rows only. */
+TF_API int tf_cuda_set_vocab_shard(tf_model* m, int rank, int world);
+TF_API void* tf_cuda_shard_key(tf_model* m);
+TF_API int tf_cuda_decode_shard(tf_model* m, int seq, int token);
+TF_API int tf_cuda_shard_token(tf_model* m, int seq, int* token);
+/* The first n greedy ids of the last device-side run (tf_cuda_generate_greedy's, or the shard
+ * steps' since the last tf_cuda_decode_shard with a host token), synchronising the stream.
+ * No reference counterpart (the CLI collects ids on the host, src/main.cpp:112-122). */
+TF_API int tf_cuda_history(tf_model* m, int n, int* out);
+
 /* Model::reset()  src/model.cpp:80-83 (one slot; seq < 0 resets every slot). */
 TF_API int tf_cuda_reset(tf_model* m, int seq);
 
