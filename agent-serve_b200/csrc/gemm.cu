@@ -12,9 +12,7 @@
 // the tile through distributed shared memory of their thread-block cluster in split order;
 // then the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
-//
-// Comparison path, tf_gemm_q8_kernel (TFB200_GEMM_TC05=0): the same arithmetic on
-// mma.sync.m16n8k16 with 256 threads and a global-workspace split-K reduction.
+
 #include <cstdlib>
 
 #include "dots.cuh"
@@ -85,39 +83,22 @@ __global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
     int sx = 140 - be;
     sx = sx > 100 ? 100 : (sx < -100 ? -100 : sx);
     const float S = ldexpf(1.0f, sx);
-    __half* xh = a.xh + (size_t)m * K;
-    __half* xl = a.xl + (size_t)m * K;
     for (int e = tid; e < K; e += nth) {
         const float v = xrow[xpad(e)] * S;  // exact: a power-of-two scale
         const __half h = __float2half_rn(v);
-        xh[e] = h;
-        xl[e] = __float2half_rn(v - __half2float(h));
+        a.xh[(size_t)m * K + e] = h;
+        a.xl[(size_t)m * K + e] = __float2half_rn(v - __half2float(h));
     }
     if (tid == 0) a.sx[m] = sx;
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------
-__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
-                 : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// shared memory of one stage: Wh, Wl [BN][LDS], Xh, Xl [BM][LDS] halves
-constexpr int GM_TILE_H = GM_BN * GM_LDS;  // halves per operand tile
-constexpr size_t GM_STAGE_BYTES = (size_t)4 * GM_TILE_H * 2;
 constexpr int GM_EPI_LD = GM_BN + 4;         // epilogue tile row stride (floats)
 
 // The 9 words of weight row r, k-stage kc, block half j (j = 0: bytes 0..35 of the stage's
@@ -351,7 +332,7 @@ __device__ __forceinline__ float4 ld_cluster_v4(uint32_t local_addr, int rank) {
 // each split reduces its slice of rows by reading the other splits' tiles straight from their
 // shared memory; otherwise the splits meet through the global workspace and tile counters.
 // Either way the splits are summed in split order (deterministic).
-template <int BMT, bool CLUSTER = false, int NTH = GM_THREADS>
+template <int BMT, bool CLUSTER, int NTH>
 __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, int m0, int n0, bool ok_in = true) {
     const int tid = threadIdx.x;
     const int rv = min(BMT, a.M - m0);  // valid activation rows of the tile
@@ -454,119 +435,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
     }
 }
 
-__global__ void __launch_bounds__(GM_THREADS, 1) tf_gemm_q8_kernel(const GemmArgs a) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * GM_BM;
-    const int wn = warp & 3, wm = warp >> 2;
-    const int nk_all = a.K / GM_BK;
-    // this split's k stages [kb, kb + nk)
-    const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
-    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
-    const float wscale = ldexpf(1.0f, a.sw);
-
-    auto stage_ptr = [&](int s, int which) {  // which: 0 Wh, 1 Wl, 2 Xh, 3 Xl
-        return reinterpret_cast<__half*>(smem + (size_t)s * GM_STAGE_BYTES) + (size_t)which * GM_TILE_H;
-    };
-    const int wr = tid >> 1, wj = tid & 1;  // this thread's weight row and block half
-    auto load_x = [&](int s, int kc) {
-        // 128 rows x 64 halves per plane = 8 chunks of 16 B per row
-        for (int i = tid; i < 2 * GM_BM * 8; i += GM_THREADS) {
-            const int pl = i / (GM_BM * 8), r = (i / 8) % GM_BM, c = i % 8;
-            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + r) * a.K + (size_t)kc * GM_BK + 8 * c;
-            cp_async16(stage_ptr(s, 2 + pl) + r * GM_LDS + 8 * c, src);
-        }
-        cp_async_commit();
-    };
-
-    uint32_t wv[9];
-    pdl_trigger();
-    pdl_wait();
-    // prologue: stage 0
-    load_x(0, kb);
-    gm_load_w(wv, a, n0 + wr, kb, wj);
-    gm_dequant(wv, wj, wscale, stage_ptr(0, 0) + wr * GM_LDS + 32 * wj, stage_ptr(0, 1) + wr * GM_LDS + 32 * wj);
-    cp_async_wait_all();
-    __syncthreads();
-
-    float acc[2][8][4];
-#pragma unroll
-    for (int i = 0; i < 2; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[i][j][c] = 0.f;
-
-    for (int kc = 0; kc < nk; ++kc) {
-        const int s = kc & 1;
-        const bool more = kc + 1 < nk;
-        if (more) {
-            load_x(s ^ 1, kb + kc + 1);
-            gm_load_w(wv, a, n0 + wr, kb + kc + 1, wj);
-        }
-        const __half* sWh = stage_ptr(s, 0);
-        const __half* sWl = stage_ptr(s, 1);
-        const __half* sXh = stage_ptr(s, 2);
-        const __half* sXl = stage_ptr(s, 3);
-#pragma unroll
-        for (int k16 = 0; k16 < GM_BK / 16; ++k16) {
-            uint32_t ah[2][4], al[2][4];
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int row = wn * 32 + 16 * i + (lane & 15), col = 16 * k16 + 8 * (lane >> 4);
-                ldsm_x4(ah[i], sWh + row * GM_LDS + col);
-                ldsm_x4(al[i], sWl + row * GM_LDS + col);
-            }
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                uint32_t bh[4], bl[4];
-                const int q = lane >> 3;
-                const int row = wm * 64 + 8 * (2 * jj + (q >> 1)) + (lane & 7), col = 16 * k16 + 8 * (q & 1);
-                ldsm_x4(bh, sXh + row * GM_LDS + col);
-                ldsm_x4(bl, sXl + row * GM_LDS + col);
-#pragma unroll
-                for (int i = 0; i < 2; ++i) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int j = 2 * jj + h;
-                        mma16816(acc[i][j], ah[i], bh[2 * h], bh[2 * h + 1]);
-                        mma16816(acc[i][j], ah[i], bl[2 * h], bl[2 * h + 1]);
-                        mma16816(acc[i][j], al[i], bh[2 * h], bh[2 * h + 1]);
-                    }
-                }
-            }
-        }
-        if (more)
-            gm_dequant(wv, wj, wscale, stage_ptr(s ^ 1, 0) + wr * GM_LDS + 32 * wj,
-                       stage_ptr(s ^ 1, 1) + wr * GM_LDS + 32 * wj);
-        cp_async_wait_all();
-        __syncthreads();
-    }
-
-    // ---- epilogue: scale back, stage [m][n] in shared memory, apply ----
-    float* tile = reinterpret_cast<float*>(smem);  // [GM_BM][GM_EPI_LD]
-    const int g = lane >> 2, t4 = lane & 3;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-            const int mm = wm * 64 + 8 * j + 2 * t4 + cc;
-            const int m = m0 + mm;
-            const float sc = m < a.M ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int nn = wn * 32 + 16 * i + g;
-                tile[mm * GM_EPI_LD + nn] = acc[i][j][cc] * sc;
-                tile[mm * GM_EPI_LD + nn + 8] = acc[i][j][2 + cc] * sc;
-            }
-        }
-    }
-    __syncthreads();
-    gemm_epilogue<GM_BM>(a, tile, m0, n0);
-}
-
 // ---- the GEMM on the 5th-generation tensor cores (tcgen05, accumulators in TMEM) ---------------
-// Same arithmetic and epilogue as tf_gemm_q8_kernel; the products run as tcgen05.mma
+// The products run as tcgen05.mma
 // (kind::f16, M = 128 weight rows, N = NT activation rows, K = 16) issued by one thread, with the
 // fp32 accumulator in tensor memory.  Operands sit in shared memory in the canonical K-major
 // 128-byte-swizzled layout: a row's 64 k values (128 B) form one line of an 8-line, 1024-byte
@@ -829,33 +699,14 @@ int gemm_tile_rows(int M) {
     return (M > 128 && v == 256) ? 256 : 128;
 }
 
-// tcgen05 path (default) or the mma.sync path (TFB200_GEMM_TC05=0)
-static bool gemm_use_tc05() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("TFB200_GEMM_TC05");
-        v = (e && e[0] == '0') ? 0 : 1;
-    }
-    return v != 0;
-}
+bool gemm_takes_q4() { return true; }
 
-bool gemm_takes_q4() { return gemm_use_tc05(); }
 
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
-    const size_t smem = 2 * GM_STAGE_BYTES;
-    static bool attr_set[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64) dev = 0;
-    if (!attr_set[dev]) {
-        cudaError_t e = cudaFuncSetAttribute(tf_gemm_q8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set[dev] = true;
-    }
     const int ks = a.ksplit > 1 ? a.ksplit : 1;
     if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
-    if (gemm_use_tc05()) {
+    {
         GemmArgs aa = a;
         void* args[] = {&aa};
         const bool wide = gemm_tile_rows(a.M) == 256;
@@ -891,11 +742,6 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
         cfg.numAttrs = 2;
         return cudaLaunchKernelExC(&cfg, fn, args);
     }
-    if (a.wq4) return cudaErrorInvalidValue;  // the mma.sync kernel reads Q8_0 blocks only
-    dim3 grid((a.N + GM_BN - 1) / GM_BN, (a.M + GM_BM - 1) / GM_BM, ks);
-    GemmArgs aa = a;
-    void* args[] = {&aa};
-    return launch_pdl((const void*)tf_gemm_q8_kernel, grid, dim3(GM_THREADS), smem, st, args);
 }
 
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {

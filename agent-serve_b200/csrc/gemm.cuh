@@ -19,9 +19,7 @@ namespace tfb {
 constexpr int GM_BN = 128;      // weight rows per CTA
 constexpr int GM_BM = 128;      // activation rows per CTA
 constexpr int GM_BK = 64;       // k per pipeline stage (two Q8_0 blocks)
-constexpr int GM_THREADS = 256; // 8 warps: 4 along n x 2 along m (warp tile 32 n x 64 m)
 constexpr int GM_TC_THREADS = 512;  // tcgen05 kernel: 4 threads per weight row (16 weights each)
-constexpr int GM_LDS = GM_BK + 8;  // shared row stride in halves (144 B: ldmatrix conflict-free)
 constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
 constexpr int GM_WPF = 4;       // tcgen05 GEMM: weight stages in flight per thread (registers)
 
@@ -62,9 +60,9 @@ struct GemmArgs {
     int ldr;
     unsigned long long* keys;  // EPI_ARGMAX: one key per activation row
     int store_logits;          // EPI_ARGMAX: also store the logits in y
-    // split-K (grid.z = ksplit > 1): on the tcgen05 path the splits of a tile are one cluster
-    // and sum through distributed shared memory; on the mma.sync path each split writes its
-    // scaled tile to ws[z][M][N] and the splits meet through tile_cnt (arrivals, departures)
+    // split-K (grid.z = ksplit > 1): the splits of a tile are one thread-block cluster and sum
+    // through distributed shared memory; ws / tile_cnt serve the non-cluster reduction of
+    // gemm_epilogue (global workspace, tile arrivals)
     int ksplit;
     float* ws;
     unsigned* tile_cnt;
@@ -105,11 +103,12 @@ struct FinishArgs {
 };
 
 cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st);
+
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st);
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st);
 // per-matrix sw of host-resident blocks (block_bytes 34 for Q8_0, 18 for Q4_0)
 int q8_scale_exponent(const uint8_t* host_blocks, size_t nbytes, int block_bytes = 34);
-// whether gemm_launch takes Q4_0 weights (the tcgen05 kernel; the mma.sync one reads Q8_0 only)
+// whether gemm_launch takes Q4_0 weights (the tcgen05 kernel does)
 bool gemm_takes_q4();
 int q8_exponent_from_dbits(unsigned max_abs_d_bits);
 // sw of device-resident Q8_0 blocks (synchronises `st`); scratch: one device unsigned

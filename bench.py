@@ -642,6 +642,8 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg1 / cfg2 batch-1 runs (N = 1 only)")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
+    ap.add_argument("--rows", type=int, default=128, help="--kernel bstep: rows of the batched step")
+    ap.add_argument("--ctx", type=int, default=512, help="--kernel bstep: prompt length before the step")
     ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
@@ -721,11 +723,11 @@ def main():
             print(json.dumps(line), flush=True)
         return
     if args.kernel == "bstep":
-        # one cfg4 batched decode step (128 rows at context ~530) between cudaProfilerStart /
+        # one cfg4 batched decode step (--rows rows at context --ctx) between cudaProfilerStart /
         # Stop, for a launch list under `ncu --profile-from-start off`
         import torch
         from tinferno_b200.model import Model, RunConfig
-        S, P = 128, 512
+        S, P = args.rows, args.ctx
         m = Model(synth.model_path(synth.CFG4), RunConfig(max_seq=P + 16, max_batch=S))
         prompts = np.stack([synth.prompt_tokens(synth.CFG4, P, stream=1000 + g) for g in range(S)])
         tok = m.prefill_batch(list(range(S)), prompts)
@@ -735,8 +737,16 @@ def main():
         tok = m.decode_batch(list(range(S)), tok.tolist())
         torch.cuda.synchronize()
         torch.cuda.profiler.stop()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        st = torch.cuda.ExternalStream(m.stream)
+        ev[0].record(st)
+        for _ in range(5):
+            tok = m.decode_batch(list(range(S)), tok.tolist())
+        ev[1].record(st)
+        torch.cuda.synchronize()
         m.close()
-        print(json.dumps({"kernel": "bstep", "rows": S, "context": P + 2, "first_ids": [int(v) for v in tok[:4]]}))
+        print(json.dumps({"kernel": "bstep", "rows": S, "context": P + 2, "ms_per_step": round(ev[0].elapsed_time(ev[1]) / 5, 3),
+                          "first_ids": [int(v) for v in tok[:4]]}))
         return
     if args.warmup < 3:
         args.warmup = 3
