@@ -148,6 +148,9 @@ struct tf_model {
     unsigned pk_ep = 1;
     float* d_pkpart = nullptr;
     unsigned* d_pktickets = nullptr;
+    unsigned long long* d_pktrace = nullptr;  // phase trace (TFB200_PK_TRACE=1 at creation)
+    int* d_pktrace_n = nullptr;
+    int pk_trace_cap = 0;
     double upload_s = 0.0;  // seconds tf_cuda_create spent moving the weights into HBM
     // vocab-split lm_head (batch 1): this GPU's rows [vs_row0, vs_row1) of the output matrix;
     // the step's key leaves in d_keyred for a max all-reduce across the GPUs
@@ -698,6 +701,11 @@ int build_pk_plan(tf_model* m) {
     CK(cudaMalloc(&m->d_pkpart, sizeof(float) * (size_t)m->hp.n_head * max_nsf * (m->hd + 2)));
     CK(cudaMalloc(&m->d_pktickets, sizeof(unsigned) * m->hp.n_head));
     CK(cudaMemset(m->d_pktickets, 0, sizeof(unsigned) * m->hp.n_head));
+    if (const char* tr = getenv("TFB200_PK_TRACE"); tr && tr[0] == '1') {
+        m->pk_trace_cap = 1 << 16;
+        CK(cudaMalloc(&m->d_pktrace, sizeof(unsigned long long) * 2 * m->pk_trace_cap));
+        CK(cudaMalloc(&m->d_pktrace_n, sizeof(int) * 2));
+    }
     m->pk = true;
     return 0;
 }
@@ -769,6 +777,12 @@ int run_pk(tf_model* m, int seq, const int* d_prompt, int n_prompt, int n_steps,
     a.err = m->d_err;
     CK(cudaMemsetAsync(m->d_pkctl, 0, sizeof(unsigned) * m->pk_ctl_words, m->stream));
     CK(cudaMemsetAsync(m->d_pkkeys, 0, sizeof(unsigned long long) * n_steps, m->stream));
+    if (m->d_pktrace) {
+        a.trace = m->d_pktrace;
+        a.trace_cap = m->pk_trace_cap;
+        a.trace_n = m->d_pktrace_n;
+        CK(cudaMemsetAsync(m->d_pktrace_n, 0, sizeof(int) * 2, m->stream));
+    }
     CK(pk_launch(a, m->pk_grid, p.smem, m->stream));
     return 0;
 }
@@ -844,7 +858,7 @@ int tf_cuda_destroy(tf_model* m) {
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
-                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_keyred, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
+                   m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_keyred, m->d_pktrace, m->d_pktrace_n, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
                    m->xplanes};
     for (void* p : dev)
         if (p) cudaFree(p);
@@ -1397,6 +1411,23 @@ int tf_cuda_shard_token(tf_model* m, int seq, int* token) {
     const int rc = finish_call(m);
     if (rc) return rc;
     *token = m->hb[0];
+    return 0;
+}
+
+int tf_cuda_trace_read(tf_model* m, unsigned long long* out, int cap, int* n_out) {
+    if (!m) return set_error("null model");
+    if (!m->d_pktrace) return fail(m, "no phase trace (persistent kernel created with TFB200_PK_TRACE=1)");
+    if (!out || !n_out || cap < 1) return fail(m, "bad trace buffer");
+    CK(cudaSetDevice(m->device));
+    int n[2] = {0, 0};
+    CK(cudaStreamSynchronize(m->stream));
+    CK(cudaMemcpy(n, m->d_pktrace_n, sizeof(n), cudaMemcpyDeviceToHost));
+    for (int w = 0; w < 2; ++w) {
+        const int k = std::min(std::min(n[w], m->pk_trace_cap), cap);
+        if (k) CK(cudaMemcpy(out + (size_t)w * cap, m->d_pktrace + (size_t)w * m->pk_trace_cap, sizeof(unsigned long long) * k,
+                             cudaMemcpyDeviceToHost));
+        n_out[w] = k;
+    }
     return 0;
 }
 

@@ -50,7 +50,7 @@ struct PkMisc {
     int ok;
     int abort;  // this CTA gave up: its producer stops, its waits return at once
     int flag;
-    int pad;
+    int trace_i;  // phase-trace entries written by this CTA
 };
 
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(PK_CONS) : "memory"); }
@@ -92,6 +92,19 @@ struct PkCtx {
 };
 
 __device__ __forceinline__ int item_begin(int n, int c, int G) { return (int)((long long)n * c / G); }
+
+// Phase trace (PkArgs::trace): thread 0 of CTA 0 and of the last CTA stamp the global timer.
+__device__ __forceinline__ void pk_trace(const PkCtx& c, int tag) {
+    const PkArgs& a = *c.a;
+    if (!a.trace || threadIdx.x != 0) return;
+    const int w = c.cta == 0 ? 0 : (c.cta == c.G - 1 ? 1 : -1);
+    if (w < 0) return;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    const int i = c.S->trace_i++;
+    if (i < a.trace_cap) a.trace[(size_t)w * a.trace_cap + i] = (t << 8) | (unsigned)tag;
+    a.trace_n[w] = i + 1;
+}
 
 // ---- producer -----------------------------------------------------------------------------
 __device__ void pk_produce(const PkArgs& a, const PkRing& rg, PkMisc* S, int cta, int G) {
@@ -254,6 +267,7 @@ __device__ __forceinline__ bool pk_gemv(PkCtx& c, const PkMat& mat, int kind, co
         }
     }
 
+    pk_trace(c, PT_START + kind);
     // ---- prologue: the activation as digit planes in the region, the lane's unit in registers
     float4 v[PK_PRO_U];
     float* xs = reinterpret_cast<float*>(c.reg);
@@ -282,6 +296,7 @@ __device__ __forceinline__ bool pk_gemv(PkCtx& c, const PkMat& mat, int kind, co
     } else {
         const bool got = ll_read(c, src, nq, ep_in, v);
         if (!pk_verdict(c, got)) return false;
+        pk_trace(c, PT_READ + kind);
     }
     if (norm) {
         // rmsnorm (src/layers.cpp:7-12): sum of squares in double, inv in float, (x * inv) * w
@@ -338,6 +353,7 @@ __device__ __forceinline__ bool pk_gemv(PkCtx& c, const PkMat& mat, int kind, co
         invB = pinv[2 * unit + 1];
     }
 
+    pk_trace(c, PT_PRO + kind);
     // ---- main loop: two stages per iteration (two independent dp4a chains per warp)
     const int n_stages = (i1 - i0 + RI - 1) / RI;
     const long long rb = mt.rb;
@@ -418,6 +434,7 @@ __device__ __forceinline__ bool pk_gemv(PkCtx& c, const PkMat& mat, int kind, co
         // a failed wait does not leave the loop: every warp takes the same barriers; once the
         // abort flag is up the remaining waits return at once
     }
+    pk_trace(c, PT_LOOP + kind);
     c.cs += n_stages;
     if (kind == PK_HEAD && best) atomicMax(&c.S->ckey, best);
     if (!ok) *reinterpret_cast<volatile int*>(&c.S->abort) = 1;
@@ -477,6 +494,7 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, uns
         const int npc = (s0 + np == pos + 1) ? np - 1 : np;
         pk_issue_tile(c, ks, vs, kst, hd, kcf + (size_t)s0 * hd, vcf + (size_t)s0 * hd, npc);
     }
+    pk_trace(c, PT_ATT0);
     {   // this head's q and its kv head's k, v: one LL pair per thread, polled
         bool got = true;
         if (tid < 3 * hd) {
@@ -513,6 +531,7 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, uns
             kc[cache_off + (size_t)pos * hd + i] = kn[i];
             vc[cache_off + (size_t)pos * hd + i] = vn[i];
         }
+    pk_trace(c, PT_QKV);
     const float scale = 1.0f / sqrtf((float)hd);
     const int pg = tid / hd, pd = tid % hd;
     const bool pv_thread = tid < ng * hd;
@@ -577,6 +596,7 @@ __device__ bool pk_attention(PkCtx& c, int layer, int item, int pos, int ws, uns
         }
         cbar();
     }
+    pk_trace(c, PT_ATT1);
     if (!pk_verdict(c, tile_ok)) return false;
     if (pv_thread) pacc[tid] = acc;
     cbar();
@@ -640,6 +660,7 @@ __global__ void __launch_bounds__(PK_THREADS, 1) tf_decode_persistent_kernel(con
             mbar_init(&S->empty[s], PK_WARPS);
         }
         mbar_init(&S->abar, 1);
+        S->trace_i = 0;
         S->abort = 0;
         S->ckey = 0ull;
         mbar_fence_init();

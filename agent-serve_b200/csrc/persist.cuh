@@ -99,7 +99,17 @@ struct PkArgs {
     unsigned* cnt;             // [1] step arrivals (zero at launch)
     int* abort_g;              // raised by any CTA that gives up (zero at launch)
     int* err;
+    // optional phase trace (nullptr: off): CTA 0 and the last CTA record (globaltimer << 8 |
+    // tag) at every phase boundary, trace[w * trace_cap + i], w = 0 / 1; tags in PkTrace
+    unsigned long long* trace;
+    int trace_cap;
+    int* trace_n;              // [2] entries written
 };
+
+// trace tags: phase start 10 + kind, activation read 20 + kind, prologue done 30 + kind, rows
+// done 40 + kind (kind: PK_QKV / WO / GU / DOWN / HEAD); attention start 50, q / k / v read
+// 53, attention done 51
+enum : int { PT_START = 10, PT_READ = 20, PT_PRO = 30, PT_LOOP = 40, PT_ATT0 = 50, PT_ATT1 = 51, PT_QKV = 53 };
 
 // Shared-memory plan: ring slots, then the region (activation planes or attention tiles),
 // then the control block.

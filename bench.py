@@ -644,7 +644,7 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
     ap.add_argument("--rows", type=int, default=128, help="--kernel bstep: rows of the batched step")
     ap.add_argument("--ctx", type=int, default=512, help="--kernel bstep: prompt length before the step")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "sweep", "bstep", "gemm", "configs", "q6k"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -669,6 +669,43 @@ def main():
             t = int(np.argmax(m.decode(t)))
         m.close()
         print(json.dumps({"kernel": "step", "kernels_per_step": 2 * 4 + 1, "last_token": t}))
+        return
+    if args.kernel == "pktrace":
+        # per-phase breakdown of one cfg0 decode step on the persistent kernel (phase trace of
+        # the first CTA: the time between consecutive trace points, averaged over the layers)
+        import ctypes as C
+        from tinferno_b200 import native
+        from tinferno_b200.model import Model, RunConfig
+        os.environ["TFB200_PK_TRACE"] = "1"
+        m = Model(model_file(), RunConfig(max_seq=CFG.max_seq, decode_mode=native.TF_DECODE_PERSISTENT))
+        t = int(np.argmax(m.prefill(synth.prompt_tokens(CFG, PROMPT))))
+        for _ in range(6):
+            t = m.decode_argmax(t)
+        cap = 8192
+        buf = np.zeros(2 * cap, np.uint64)
+        n = np.zeros(2, np.int32)
+        t = m.decode_argmax(t)
+        native.check(m.L.tf_cuda_trace_read(m.h, buf.ctypes.data_as(C.POINTER(C.c_ulonglong)), cap,
+                                            n.ctypes.data_as(native.i32p)), m.h)
+        m.close()
+        names = {0: "qkv", 1: "wo", 2: "gate/up", 3: "down", 5: "lm_head"}
+        stage = {10: "start", 20: "read", 30: "prologue", 40: "rows", 50: "attn_start", 53: "attn_qkv_read",
+                 51: "attn_done"}
+        out = {}
+        for w, who in ((0, "cta0 (attention + GEMV rows)"), (1, "last cta (GEMV rows only)")):
+            ev = buf[w * cap:w * cap + n[w]]
+            ts = (ev >> np.uint64(8)).astype(np.int64)
+            tags = (ev & np.uint64(255)).astype(np.int64)
+            def lab(g):
+                g = int(g)
+                return f"{stage.get(g - g % 10, '?')}/{names.get(g % 10, '?')}" if g < 50 else stage.get(g, "?")
+            seg = {}
+            for t0, g0, t1, g1 in zip(ts, tags, ts[1:], tags[1:]):
+                seg.setdefault(f"{lab(g0)} -> {lab(g1)}", []).append((t1 - t0) / 1e3)
+            out[who] = {"step_us": round((ts[-1] - ts[0]) / 1e3, 1),
+                        "segments_us": {k: {"n": len(v), "mean": round(float(np.mean(v)), 3), "sum": round(float(np.sum(v)), 1)}
+                                        for k, v in sorted(seg.items(), key=lambda kv: -sum(kv[1]))}}
+        print(json.dumps(out, indent=1))
         return
     if args.kernel == "step0":
         # one full-size cfg0 batch-1 decode step (the graph of the timed region) between

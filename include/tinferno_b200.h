@@ -145,6 +145,15 @@ TF_API int tf_cuda_shard_token(tf_model* m, int seq, int* token);
  * No reference counterpart (the CLI collects ids on the host, src/main.cpp:112-122). */
 TF_API int tf_cuda_history(tf_model* m, int n, int* out);
 
+/* Phase trace of the persistent decode kernel, the B200 counterpart of the reference's Timings /
+ * --profile (src/common.hpp:118-134, src/main.cpp:132-141): with TFB200_PK_TRACE=1 in the
+ * environment at tf_cuda_create, thread 0 of the first and of the last CTA stamp the GPU's
+ * global timer at every phase boundary of the last launch.  out receives two rows of `cap`
+ * entries (first CTA, last CTA), each (nanoseconds << 8 | tag); n_out[2] their counts.  Tags:
+ * 10 + k phase start, 20 + k activation read, 30 + k prologue done, 40 + k rows done (k: 0 QKV,
+ * 1 wo, 2 gate/up, 3 down, 5 lm_head); 50 attention start, 53 q / k / v read, 51 attention done. */
+TF_API int tf_cuda_trace_read(tf_model* m, unsigned long long* out, int cap, int* n_out);
+
 /* Model::reset()  src/model.cpp:80-83 (one slot; seq < 0 resets every slot). */
 TF_API int tf_cuda_reset(tf_model* m, int seq);
 
