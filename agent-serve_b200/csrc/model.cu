@@ -1051,8 +1051,14 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     const char* usync = getenv("TFB200_UPLOAD_SYNC");
     const bool streamed = !(usync && usync[0] == '1');
     if (streamed) {
-        const unsigned hc = std::thread::hardware_concurrency();
-        CKD(up.init((size_t)32 << 20, 3, (int)std::min(8u, std::max(1u, hc / 2))));
+        // staging: TFB200_UPLOAD_CHUNK_MB per buffer (default 2: measured fastest of 2 / 8 / 32 MB
+        // with the file in the page cache), 4 buffers, host copies on TFB200_UPLOAD_THREADS
+        // threads (default 1: more threads measured no faster)
+        const char* ce = getenv("TFB200_UPLOAD_CHUNK_MB");
+        const char* te = getenv("TFB200_UPLOAD_THREADS");
+        const size_t chunk = (size_t)std::max(1, ce ? atoi(ce) : 2) << 20;
+        const int threads = std::max(1, std::min(32, te ? atoi(te) : 1));
+        CKD(up.init(chunk, 4, threads));
     }
     auto put = [&](void* dst, const void* src, size_t n) -> cudaError_t {
         return streamed ? up.copy(dst, src, n) : cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
