@@ -819,26 +819,40 @@ int set_slot_row(tf_model* m, int row, int seq, int token) {
     return 0;
 }
 
+// Whether host memory is page-locked (tf_host_alloc, cudaMallocHost, cudaHostRegister): the
+// DMA then writes the caller's buffer directly, with no staging copy on the host.
+bool host_pinned(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
 int read_outputs(tf_model* m, int M, float* logits, int* argmax_out) {
+    const bool direct = logits && host_pinned(logits);
     if (logits)
-        CK(cudaMemcpyAsync(m->hlog, m->logits, sizeof(float) * (size_t)M * m->V, cudaMemcpyDeviceToHost, m->stream));
+        CK(cudaMemcpyAsync(direct ? logits : m->hlog, m->logits, sizeof(float) * (size_t)M * m->V, cudaMemcpyDeviceToHost,
+                           m->stream));
     if (argmax_out) CK(cudaMemcpyAsync(m->hb, m->d_tokens, sizeof(int) * M, cudaMemcpyDeviceToHost, m->stream));
     int rc = finish_call(m);
     if (rc) return rc;
-    if (logits) memcpy(logits, m->hlog, sizeof(float) * (size_t)M * m->V);
+    if (logits && !direct) memcpy(logits, m->hlog, sizeof(float) * (size_t)M * m->V);
     if (argmax_out) memcpy(argmax_out, m->hb, sizeof(int) * M);
     return 0;
 }
 
 // Outputs of row `row` of the last step (a prefill chunk's last prompt token).
 int read_outputs_row(tf_model* m, int row, float* logits, int* argmax_out) {
+    const bool direct = logits && host_pinned(logits);
     if (logits)
-        CK(cudaMemcpyAsync(m->hlog, m->logits + (size_t)row * m->V, sizeof(float) * m->V, cudaMemcpyDeviceToHost,
-                           m->stream));
+        CK(cudaMemcpyAsync(direct ? logits : m->hlog, m->logits + (size_t)row * m->V, sizeof(float) * m->V,
+                           cudaMemcpyDeviceToHost, m->stream));
     if (argmax_out) CK(cudaMemcpyAsync(m->hb, m->d_tokens + row, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
     int rc = finish_call(m);
     if (rc) return rc;
-    if (logits) memcpy(logits, m->hlog, sizeof(float) * m->V);
+    if (logits && !direct) memcpy(logits, m->hlog, sizeof(float) * m->V);
     if (argmax_out) *argmax_out = m->hb[0];
     return 0;
 }
@@ -850,6 +864,22 @@ int read_outputs_row(tf_model* m, int row, float* logits, int* argmax_out) {
 extern "C" {
 
 const char* tf_cuda_last_error(tf_model* m) { return m && !m->err.empty() ? m->err.c_str() : last_error_tls().c_str(); }
+
+int tf_host_alloc(size_t bytes, void** out) {
+    if (!out) return set_error("out is null");
+    *out = nullptr;
+    if (!bytes) return 0;
+    const cudaError_t e = cudaMallocHost(out, bytes);
+    if (e != cudaSuccess) return set_error(std::string("cudaMallocHost: ") + cudaGetErrorString(e));
+    return 0;
+}
+
+int tf_host_free(void* p) {
+    if (!p) return 0;
+    const cudaError_t e = cudaFreeHost(p);
+    if (e != cudaSuccess) return set_error(std::string("cudaFreeHost: ") + cudaGetErrorString(e));
+    return 0;
+}
 
 int tf_cuda_destroy(tf_model* m) {
     if (!m) return 0;

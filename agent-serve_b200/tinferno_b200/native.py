@@ -68,6 +68,8 @@ SIGNATURES = [
     ("tf_cuda_stream", C.c_void_p, [_V]),
     ("tf_cuda_kernels_per_step", C.c_int, [_V]),
     ("tf_cuda_last_error", C.c_char_p, [_V]),
+    ("tf_host_alloc", C.c_int, [C.c_size_t, C.POINTER(C.c_void_p)]),
+    ("tf_host_free", C.c_int, [_V]),
     ("tf_op_matmul", C.c_int, [_V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_dequant_rows", C.c_int, [_V, C.c_int, _V, C.c_int, C.c_int, _V, C.c_int, _V]),
     ("tf_op_device_error", C.c_int, [_V, i32p]),
@@ -118,3 +120,29 @@ def check(rc: int, handle=None):
     if rc != 0:
         msg = lib().tf_cuda_last_error(handle)
         raise TFError(msg.decode() if msg else f"status {rc}")
+
+
+class HostArray:
+    """A page-locked host buffer (tf_host_alloc) viewed as a numpy array: logits written into
+    it by the engine arrive by DMA with no staging copy.  Keep the object alive while the
+    array is in use; close() (or garbage collection) frees it."""
+
+    def __init__(self, n: int, dtype=None):
+        import numpy as np
+        dtype = np.dtype(dtype or np.float32)
+        self._p = C.c_void_p()
+        check(lib().tf_host_alloc(int(n) * dtype.itemsize, C.byref(self._p)))
+        buf = (C.c_byte * (int(n) * dtype.itemsize)).from_address(self._p.value)
+        self.array = np.frombuffer(buf, dtype=dtype, count=int(n))
+
+    def close(self):
+        if self._p:
+            self.array = None
+            lib().tf_host_free(self._p)
+            self._p = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -334,7 +334,10 @@ def run_ours(args, rank, world, local_rank, dist):
     # ---- e2e: the reference-facing call with host token in and host logits out ----
     first = prefill()
     tok = first
-    logits = np.empty(m.n_vocab, np.float32)
+    # the caller's logits buffer in page-locked memory (tf_host_alloc): the D2H copy lands in
+    # it directly
+    host_logits = native.HostArray(m.n_vocab)
+    logits = host_logits.array
     for _ in range(args.warmup):
         m.decode(tok, logits)
         tok = m.last_argmax
@@ -349,6 +352,7 @@ def run_ours(args, rank, world, local_rank, dist):
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e = world * args.steps / float(t.item())
+    host_logits.close()
 
     # ---- vocab-split lm_head (N > 1): every rank decodes the same sequence and computes V/N of
     # the lm_head rows; one NCCL int64 max all-reduce of the greedy key per step ----

@@ -166,6 +166,14 @@ TF_API void* tf_cuda_stream(tf_model* m);
 /* Kernels launched per decode step (for launch accounting). */
 TF_API int tf_cuda_kernels_per_step(tf_model* m);
 
+/* Page-locked host memory for output buffers, no reference counterpart (the reference's
+ * logits buffer is ordinary memory, src/main.cpp:103): logits written by tf_cuda_prefill /
+ * tf_cuda_decode / tf_cuda_decode_batch into a buffer from tf_host_alloc (or any page-locked
+ * memory) arrive by DMA directly, without the staging copy on the host that ordinary memory
+ * needs.  Free with tf_host_free. */
+TF_API int tf_host_alloc(size_t bytes, void** out);
+TF_API int tf_host_free(void* p);
+
 /* Message of the last failure on this thread (m may be NULL). */
 TF_API const char* tf_cuda_last_error(tf_model* m);
 

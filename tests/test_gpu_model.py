@@ -336,3 +336,26 @@ def test_streamed_upload_matches_synchronous(cfg, mini_models, monkeypatch):
     lb = b.prefill(prompt)
     b.close()
     assert np.array_equal(la, lb)
+
+
+def test_page_locked_logits_buffer(mini_models):
+    """Logits into a tf_host_alloc buffer (direct DMA, no host staging copy) equal those into
+    ordinary memory, for prefill and decode."""
+    cfg = MINI[0]
+    path = mini_models[cfg.name]
+    prompt = synth.prompt_tokens(cfg, 20, stream=41)  # >= 16: the tensor-core prefill chunk
+    a = Model(path, RunConfig(max_seq=64))
+    b = Model(path, RunConfig(max_seq=64))
+    pin = native.HostArray(a.n_vocab)
+    la = a.prefill(prompt)
+    b.prefill(prompt, logits=pin.array)
+    assert np.array_equal(la, pin.array)
+    t = int(np.argmax(la))
+    for _ in range(3):
+        la = a.decode(t)
+        b.decode(t, logits=pin.array)
+        assert np.array_equal(la, pin.array)
+        t = int(np.argmax(la))
+    pin.close()
+    a.close()
+    b.close()
