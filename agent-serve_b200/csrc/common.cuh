@@ -103,6 +103,36 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (TMA engine; a hint, no completion to wait on).
+// src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// flag-in-data pairs: {value bits, epoch}, each pair one naturally aligned 8-byte access
+__device__ __forceinline__ void st_ll(uint2* p, float v, unsigned ep) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(ep) : "memory");
+}
+__device__ __forceinline__ uint4 ld_ll2(const uint2* p) {  // two pairs (16-byte aligned)
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+__device__ __forceinline__ uint2 ld_ll1(const uint2* p) {
+    uint2 r;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
+
 // ---- programmatic dependent launch -----------------------------------------------------
 // Every kernel calls pdl_wait() before it reads anything an earlier kernel of the step
 // wrote, and calls it unconditionally, so completion is transitive along the chain.

@@ -36,6 +36,17 @@ namespace tfb {
 // floats of the cross-warp reduction buffer: two parities x warps x (2 rows x max(M, 2))
 __host__ __device__ constexpr int gv_red_floats(int maxm) { return 2 * GV_WARPS * 2 * (maxm < 2 ? 2 : maxm); }
 
+// launch trace: this CTA's stamp k (see GemvArgs::trace)
+__device__ __noinline__ void gv_stamp(unsigned long long* trace, int k) {
+    trace[(size_t)blockIdx.x * GV_TRACE_SLOTS + k] = global_ns();
+}
+// the same, taken once `dep` has been computed
+__device__ __noinline__ void gv_stamp_after(unsigned long long* trace, int k, double dep) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t) : "d"(dep));
+    trace[(size_t)blockIdx.x * GV_TRACE_SLOTS + k] = t;
+}
+
 __device__ __forceinline__ void named_bar_compute() {
     asm volatile("bar.sync 1, %0;" ::"n"(GV_WARPS * 32) : "memory");
 }
@@ -106,7 +117,7 @@ __device__ __noinline__ void fused_attn_split_out(float* part, int n_split, unsi
 // groups of hd threads for the weighted V sum (group g takes positions g, g + ng, ...).
 // SPLIT (its own kernel instantiation, launched only when a head's positions are split):
 // CTA cta owns query head cta % n_head and position split cta / n_head of attn_nsf.
-template <bool SPLIT>
+template <bool SPLIT, bool TR>
 __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem, size_t avail, int cta, int G) {
     const AttnArgs& t = a.at;
     const int tid = threadIdx.x, nth = blockDim.x, warp = tid >> 5, lane = tid & 31, nw = nth >> 5;
@@ -134,6 +145,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
 
     pdl_trigger();
     pdl_wait();
+    if (TR && tid == 0) gv_stamp(a.trace, 1);
     const int slot = t.slots ? t.slots[0] : 0;
     const int pos = t.pos[slot];
     const bool pos_ok = pos >= 0 && pos < t.cap && tp >= 4;
@@ -176,6 +188,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
             }
         }
         *flag = ok;
+        if (TR) gv_stamp(a.trace, 2);
     }
     __syncthreads();
     float m_run = -INFINITY, l_run = 0.f, acc = 0.f;
@@ -188,6 +201,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
             vn[i] = __ldcg(row + (size_t)(t.n_head + t.n_kv) * hd + (size_t)kvh * hd + i);
         }
         __syncthreads();
+        if (TR && tid == 0) gv_stamp(a.trace, 5);
         for (int i = tid; i < hd; i += nth) {
             const int j = i % d2;
             if (i < d2) rope_pair(qs[j], qs[j + d2], cs[j], sn[j]);
@@ -263,6 +277,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
             }
             __syncthreads();
         }
+        if (TR && tid == 0) gv_stamp(a.trace, 6);
         if constexpr (!SPLIT) {
             if (pv_thread) pacc[tid] = acc;
             __syncthreads();
@@ -288,18 +303,21 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
     // leave; the last attention CTA out clears the counters for this layer's next step
     __syncthreads();
     if (tid == 0) {
+        if (TR) gv_stamp(a.trace, 3);
         const unsigned d = atomicAdd(a.sync + 1, 1u);
         if (d == (unsigned)a.attn_ctas - 1) {
             a.sync[0] = 0u;
             a.sync[1] = 0u;
         }
+        if (TR) gv_stamp(a.trace, 4);
     }
 }
 
 // INTQ: 0 fp32 dots, 1 Q8_0 integer path, 2 Q4_0 integer path, 3 Q6_K integer path, 4 the Q8_0
 // integer path whose fused attention splits each head's positions over several CTAs (each its
 // own function, so the Q8_0 kernel that every GEMV of a Q8_0 step runs carries no other code)
-template <int MAXM, int INTQ>
+// TR: the launch-trace instantiation (stamps into a.trace; see GemvArgs::trace)
+template <int MAXM, int INTQ, bool TR>
 __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -319,9 +337,10 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
     // their K/V rows while the GEMV CTAs work); GEMV CTA gb = blockIdx.x - attn_ctas
     const int G = (int)gridDim.x - a.attn_ctas;
     const int gb = (int)blockIdx.x - a.attn_ctas;
+    if (TR && tid == 0) gv_stamp(a.trace, 0);
     if constexpr (INTQ == 1 || INTQ == 4) {  // the attention fuses into Q8_0 QKV launches only
         if (gb < 0) {
-            fused_attention<INTQ == 4>(a, smem, (size_t)xbytes + (size_t)GV_STAGES * a.stage_bytes, (int)blockIdx.x, G);
+            fused_attention<INTQ == 4, TR>(a, smem, (size_t)xbytes + (size_t)GV_STAGES * a.stage_bytes, (int)blockIdx.x, G);
             return;
         }
     }
@@ -392,7 +411,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
             wn[u] = c < nq ? reinterpret_cast<const float4*>(a.norm_w)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     }
+    if (TR && tid == 0) gv_stamp(a.trace, 5);
     pdl_wait();
+    if (TR && tid == 0) gv_stamp(a.trace, 1);
     if (prefetched && a.epi == EPI_RESID)
         for (int i = tid; i < (i1 - i0) * a.M; i += nth) {
             const int m = i / (i1 - i0), r = i % (i1 - i0);
@@ -432,7 +453,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
             }
             for (int i = 4 * n16 + tid; i < nw4; i += nth)
                 reinterpret_cast<uint32_t*>(xs)[i] = __ldcg(reinterpret_cast<const uint32_t*>(a.xplanes) + i);
+            if (TR && tid == 0) gv_stamp(a.trace, 6);
             named_bar_compute();
+            if (TR && tid == 0) gv_stamp(a.trace, 7);
             const uint8_t* planes = reinterpret_cast<const uint8_t*>(xs);
             const float* pinv = reinterpret_cast<const float*>(planes + 3 * pstride);
             const int unit = (warp % a.KS) * U + pu;
@@ -486,9 +509,11 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
                         ss = fma((double)v[u].w, (double)v[u].w, ss);
                     }
                 }
+                if (TR && tid == 0) gv_stamp_after(a.trace, 6, ss);
                 ss = warp_sum_d(ss);
                 if (lane == 0) redd[warp] = ss;
                 named_bar_compute();
+                if (TR && tid == 0) gv_stamp(a.trace, 7);
                 double tot = 0.0;
                 for (int w = 0; w < GV_WARPS; ++w) tot += redd[w];
                 const float inv = 1.0f / sqrtf((float)(tot / a.K) + a.eps);
@@ -646,6 +671,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
     if (!use_int) named_bar_compute();
 
     // ---------------- consumers: main loop ----------------
+    if (TR && tid == 0) gv_stamp(a.trace, 2);
     const int kseg = a.K / a.KS;
     const int my_item = warp / a.KS, my_ks = warp % a.KS;
     unsigned long long best[MAXM];
@@ -835,6 +861,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
         }
     }
 
+    if (TR && tid == 0) gv_stamp(a.trace, 3);
     if (a.epi == EPI_ARGMAX)  // the lanes that ran argmax epilogues
         for (int m = 0; m < a.M; ++m)
             if (best[m]) atomicMax(&ckey[m], best[m]);
@@ -875,6 +902,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2) tf_gemv_kernel(const GemvArgs a
                 __threadfence();
             }
         }
+        if (TR) gv_stamp(a.trace, 4);
     }
 }
 
@@ -1000,7 +1028,6 @@ void gemv_plan_w(GemvArgs& a, int warps, int budget) {
     const long long payload = (long long)(warps / best) * a.P * a.rb;
     a.stage_bytes = (int)((payload + 32 + 15) & ~15LL);
 }
-
 void gemv_plan(GemvArgs& a) { gemv_plan_w(a, GV_WARPS, GV_STAGE_BUDGET); }
 
 int gemv_max_rows(int K) {
@@ -1010,14 +1037,14 @@ int gemv_max_rows(int K) {
     return m < 1 ? 1 : (m > GV_MAXM ? GV_MAXM : m);
 }
 
-template <int MAXM, int INTQ>
+template <int MAXM, int INTQ, bool TR = false>
 static cudaError_t init_one() {
     cudaError_t e =
-        cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     // every kernel of the step asks for the same (maximal) shared-memory carve-out, so the
     // SMs never have to drain to re-partition L1 / shared memory between kernels
-    return cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    return cudaFuncSetAttribute(tf_gemv_kernel<MAXM, INTQ, TR>, cudaFuncAttributePreferredSharedMemoryCarveout,
                                 cudaSharedmemCarveoutMaxShared);
 }
 
@@ -1028,12 +1055,14 @@ cudaError_t gemv_init_attrs() {
     if ((e = init_one<1, 2>())) return e;
     if ((e = init_one<1, 3>())) return e;
     if ((e = init_one<1, 4>())) return e;
+    if ((e = init_one<1, 1, true>())) return e;
+    if ((e = init_one<1, 4, true>())) return e;
     if ((e = init_one<2, 0>())) return e;
     if ((e = init_one<4, 0>())) return e;
     return init_one<8, 0>();
 }
 
-template <int MAXM, int INTQ>
+template <int MAXM, int INTQ, bool TR = false>
 static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     const size_t smem = gemv_smem_bytes(a.M, a.K, a.stage_bytes, MAXM);
     cudaLaunchConfig_t cfg = {};
@@ -1046,7 +1075,7 @@ static cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tf_gemv_kernel<MAXM, INTQ>, a);
+    return cudaLaunchKernelEx(&cfg, tf_gemv_kernel<MAXM, INTQ, TR>, a);
 }
 
 cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
@@ -1055,6 +1084,8 @@ cudaError_t gemv_launch(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) 
             if (!a.intq) return launch_t<1, 0>(a, grid, st, pdl);
             if (a.q6) return launch_t<1, 3>(a, grid, st, pdl);
             if (a.q4) return launch_t<1, 2>(a, grid, st, pdl);
+            if (a.trace)  // the launch-trace instantiations (Q8_0 integer path only)
+                return a.attn_nsf > 1 ? launch_t<1, 4, true>(a, grid, st, pdl) : launch_t<1, 1, true>(a, grid, st, pdl);
             return a.attn_nsf > 1 ? launch_t<1, 4>(a, grid, st, pdl) : launch_t<1, 1>(a, grid, st, pdl);
         case 2: return launch_t<2, 0>(a, grid, st, pdl);
         case 4: return launch_t<4, 0>(a, grid, st, pdl);

@@ -158,6 +158,11 @@ struct tf_model {
     bool split_step = false;  // set only while tf_cuda_decode_shard enqueues its step
     int vs_row0 = 0, vs_row1 = 0;
     long long* d_keyred = nullptr;
+    // GEMV launch trace (TFB200_GV_TRACE=1 at creation): [GV_TRACE_LAUNCHES][GV_TRACE_CTAS]
+    // [GV_TRACE_SLOTS] stamps of the last step run, and per launch {grid, attention CTAs, kind}
+    // of the last step enqueued
+    unsigned long long* d_gvtrace = nullptr;
+    std::vector<int> gvt_meta;
     std::string err;
 };
 
@@ -471,6 +476,14 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
         ++launches;
     }
     bool fuse = false, planes_wo = false, planes_down = false;
+    if (m->d_gvtrace) m->gvt_meta.clear();
+    // trace slots of the next GEMV launch (kind: 0 QKV, 1 wo, 2 gate/up, 3 down, 4 lm_head)
+    auto trace = [&](GemvArgs& a, int grid, int kind) {
+        const int li = (int)m->gvt_meta.size() / 3;
+        if (!m->d_gvtrace || li >= GV_TRACE_LAUNCHES || grid > GV_TRACE_CTAS) return;
+        a.trace = m->d_gvtrace + (size_t)li * GV_TRACE_CTAS * GV_TRACE_SLOTS;
+        m->gvt_meta.insert(m->gvt_meta.end(), {grid, a.attn_ctas, kind});
+    };
     for (int li = 0; li < m->hp.n_layer; ++li) {
         const LayerDev& Ld = m->L[li];
         {   // [embedding +] rmsnorm + fused QKV GEMV + bias
@@ -508,6 +521,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
                 grid = std::max(1, std::min(grid, gemv_slots(m->num_sms) - a.attn_ctas));
                 if (planes_wo) a.yplanes = m->xplanes;
             }
+            trace(a, grid + a.attn_ctas, 0);
             CK(gemv_launch(a, grid + a.attn_ctas, m->stream, pdl));
             ++launches;
         }
@@ -525,6 +539,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
             a.epi = EPI_RESID;
             a.resid = m->x;
             a.ldr = D;
+            trace(a, gemv_grid(a, m->num_sms), 1);
             CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
             ++launches;
         }
@@ -555,6 +570,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
             } else {
                 grid = gemv_grid(a, m->num_sms);
             }
+            trace(a, grid, 2);
             CK(gemv_launch(a, grid, m->stream, pdl));
             ++launches;
         }
@@ -573,6 +589,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
                 a.pos = m->d_pos;
                 a.slots = m->d_slots;
             }
+            trace(a, gemv_grid(a, m->num_sms), 3);
             CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
             ++launches;
         }
@@ -600,6 +617,7 @@ int enqueue_step(tf_model* m, int M, bool head, bool pdl, int* n_launch, int fus
         a.pos = m->d_pos;
         a.slots = m->d_slots;
         a.hist = m->d_hist;
+        trace(a, gemv_grid(a, m->num_sms), 4);
         CK(gemv_launch(a, gemv_grid(a, m->num_sms), m->stream, pdl));
         ++launches;
     }
@@ -889,7 +907,7 @@ int tf_cuda_destroy(tf_model* m) {
     void* dev[] = {m->arena, m->kc, m->vc, m->cosb, m->sinb, m->x, m->qkv, m->attn, m->h, m->logits, m->part,
                    m->counters, m->keys, m->d_tokens, m->d_slots, m->d_pos, m->d_wstart, m->d_hist, m->d_prompt,
                    m->d_err, m->ctl, m->d_pkmats, m->d_pkctl, m->d_pkkeys, m->d_pkll, m->d_pkpart, m->d_pktickets, m->d_keyred, m->d_pktrace, m->d_pktrace_n, m->d_async, m->xh, m->xl, m->d_sx, m->gws, m->gcnt,
-                   m->xplanes};
+                   m->xplanes, m->d_gvtrace};
     for (void* p : dev)
         if (p) cudaFree(p);
     sample_scratch_destroy(m->smp);
@@ -1152,6 +1170,11 @@ int tf_cuda_create(const tf_tensor_desc* t, int nt, const tf_hparams* hp_in, con
     CKD(put(A + p_onorm, on->data, on->nbytes));
     if (streamed) CKD(up.finish());
     m->upload_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_up).count();
+    if (const char* e = getenv("TFB200_GV_TRACE"); e && e[0] == '1') {
+        const size_t n = (size_t)GV_TRACE_LAUNCHES * GV_TRACE_CTAS * GV_TRACE_SLOTS;
+        CKD(cudaMalloc(&m->d_gvtrace, n * sizeof(unsigned long long)));
+        CKD(cudaMemset(m->d_gvtrace, 0, n * sizeof(unsigned long long)));
+    }
     m->out_norm = reinterpret_cast<const float*>(A + p_onorm);
 
     // ---- KV cache: per layer [slot][kv_head][cap][hd] ----
@@ -1464,6 +1487,20 @@ int tf_cuda_trace_read(tf_model* m, unsigned long long* out, int cap, int* n_out
                              cudaMemcpyDeviceToHost));
         n_out[w] = k;
     }
+    return 0;
+}
+
+int tf_cuda_launch_trace(tf_model* m, unsigned long long* out, int max_launches, int* meta, int* n_launch) {
+    if (!m) return set_error("null model");
+    if (!m->d_gvtrace) return fail(m, "no launch trace (model created with TFB200_GV_TRACE=1)");
+    if (!out || !meta || !n_launch || max_launches < 1) return fail(m, "bad trace buffer");
+    CK(cudaSetDevice(m->device));
+    const int n = std::min((int)m->gvt_meta.size() / 3, max_launches);
+    CK(cudaStreamSynchronize(m->stream));
+    CK(cudaMemcpy(out, m->d_gvtrace, sizeof(unsigned long long) * (size_t)n * GV_TRACE_CTAS * GV_TRACE_SLOTS,
+                  cudaMemcpyDeviceToHost));
+    memcpy(meta, m->gvt_meta.data(), sizeof(int) * 3 * (size_t)n);
+    *n_launch = n;
     return 0;
 }
 

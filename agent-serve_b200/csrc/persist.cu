@@ -56,24 +56,6 @@ struct PkMisc {
 __device__ __forceinline__ void cbar() { asm volatile("bar.sync 1, %0;" ::"n"(PK_CONS) : "memory"); }
 __device__ __forceinline__ int ld_vol(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
-// flag-in-data pairs: {value bits, epoch}, each pair one naturally aligned 8-byte access
-__device__ __forceinline__ void st_ll(uint2* p, float v, unsigned ep) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(ep) : "memory");
-}
-__device__ __forceinline__ uint4 ld_ll2(const uint2* p) {  // two pairs (16-byte aligned)
-    uint4 r;
-    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p)
-                 : "memory");
-    return r;
-}
-__device__ __forceinline__ uint2 ld_ll1(const uint2* p) {
-    uint2 r;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
-    return r;
-}
-
 struct PkRing {
     uint8_t* base;
     int slot_bytes, n_slots;

@@ -61,6 +61,7 @@ SIGNATURES = [
     ("tf_cuda_shard_token", C.c_int, [_V, C.c_int, i32p]),
     ("tf_cuda_history", C.c_int, [_V, C.c_int, i32p]),
     ("tf_cuda_trace_read", C.c_int, [_V, C.POINTER(C.c_ulonglong), C.c_int, i32p]),
+    ("tf_cuda_launch_trace", C.c_int, [_V, C.POINTER(C.c_ulonglong), C.c_int, i32p, i32p]),
     ("tf_cuda_reset", C.c_int, [_V, C.c_int]),
     ("tf_cuda_n_pos", C.c_int, [_V, C.c_int]),
     ("tf_cuda_n_vocab", C.c_int, [_V]),

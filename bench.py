@@ -579,6 +579,73 @@ def config_runs():
     return out
 
 
+def launch_trace(steps=6, model_path=None):
+    """Per-launch breakdown of one cfg0 decode step on the per-kernel path: every CTA of every
+    GEMV launch stamps %globaltimer at entry, after griddepcontrol.wait, prologue done, rows
+    done and exit (TFB200_GV_TRACE=1, tf_cuda_launch_trace); the chain per launch kind is
+    averaged over the layers (times in us, relative to the previous launch's last exit)."""
+    import ctypes as C
+    from tinferno_b200 import native
+    from tinferno_b200.model import Model, RunConfig
+    os.environ["TFB200_GV_TRACE"] = "1"
+    try:
+        m = Model(model_path or model_file(), RunConfig(max_seq=CFG.max_seq))
+    finally:
+        del os.environ["TFB200_GV_TRACE"]
+    t = int(np.argmax(m.prefill(synth.prompt_tokens(CFG, PROMPT))))
+    for _ in range(steps):
+        t = m.decode_argmax(t)
+    ML, CT, SL = 192, 512, 8
+    buf = np.zeros(ML * CT * SL, np.uint64)
+    meta = np.zeros(ML * 3, np.int32)
+    nl = np.zeros(1, np.int32)
+    native.check(m.L.tf_cuda_launch_trace(m.h, buf.ctypes.data_as(C.POINTER(C.c_ulonglong)), ML,
+                                          meta.ctypes.data_as(native.i32p), nl.ctypes.data_as(native.i32p)), m.h)
+    m.close()
+    n = int(nl[0])
+    tr = buf.reshape(ML, CT, SL)[:n].astype(np.int64)
+    meta = meta.reshape(ML, 3)[:n]
+    kinds = {0: "qkv+attention", 1: "wo", 2: "gate/up", 3: "down", 4: "lm_head"}
+    seg, prev_exit, t0 = {}, None, None
+    for i in range(n):
+        grid, na, kind = (int(v) for v in meta[i])
+        g, at = tr[i, na:grid], tr[i, :na]
+        ex = max(int(g[:, 4].max()), int(at[:, 4].max()) if na else 0)
+        t0 = int(g[:, 0].min()) if t0 is None else t0
+        if prev_exit is not None:
+            d = seg.setdefault(kinds[kind], {})
+            wf = int(g[:, 1].min())
+            vals = [("first entry", int(g[:, 0].min()) - prev_exit),
+                    ("last entry", int(g[:, 0].max()) - prev_exit),
+                    ("first wait release", wf - prev_exit),
+                    ("last wait release", int(g[:, 1].max()) - prev_exit),
+                    ("longest prologue", int((g[:, 2] - g[:, 1]).max())),
+                    ("last prologue done", int(g[:, 2].max()) - prev_exit),
+                    ("last rows done", int(g[:, 3].max()) - prev_exit),
+                    ("last GEMV exit", int(g[:, 4].max()) - prev_exit)]
+            # the GEMV CTA whose wait released last, stamp by stamp
+            lc = g[int(np.argmax(g[:, 1]))]
+            vals += [("latest CTA: entry", int(lc[0]) - prev_exit), ("latest CTA: before wait", int(lc[5]) - prev_exit),
+                     ("latest CTA: wait release", int(lc[1]) - prev_exit)]
+            if kind != 4 and int(g[:, 6].min()) > 0:
+                vals += [("longest: wait release -> activation loaded", int((g[:, 6] - g[:, 1]).max())),
+                         ("longest: activation loaded -> first barrier", int((g[:, 7] - g[:, 6]).max())),
+                         ("longest: first barrier -> prologue done", int((g[:, 2] - g[:, 7]).max()))]
+            if na:
+                vals += [("attention, longest: q/k/v ready -> loaded", int((at[:, 5] - at[:, 2]).max())),
+                         ("attention, longest: loaded -> tiles done", int((at[:, 6] - at[:, 5]).max())),
+                         ("attention, longest: tiles done -> output written", int((at[:, 3] - at[:, 6]).max()))]
+                vals += [("attention: last q/k/v ready", int(at[:, 2].max()) - prev_exit),
+                         ("attention: last done", int(at[:, 3].max()) - prev_exit)]
+            vals.append(("launch exit (chain)", ex - prev_exit))
+            for name, v in vals:
+                d.setdefault(name, []).append(v / 1e3)
+        prev_exit = ex
+    return {"kernel": "gvtrace", "step_us": round((prev_exit - t0) / 1e3, 1), "launches": n,
+            "per_kind_mean_us_after_previous_exit": {k: {s: round(float(np.mean(v)), 2) for s, v in d.items()}
+                                                     for k, d in seg.items()}}
+
+
 def matmul_sweep():
     """BASELINE cfg3: Y[M,N] = X[M,K] W[N,K]^T for Q8_0 and Q4_0 weights (N(0, 0.02) quantised),
     X ~ N(0, 1); K=2048 with N in {512, 2048, 8192, 128256}, K=8192 with N=2048; M in
@@ -648,7 +715,7 @@ def main():
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
     ap.add_argument("--rows", type=int, default=128, help="--kernel bstep: rows of the batched step")
     ap.add_argument("--ctx", type=int, default=512, help="--kernel bstep: prompt length before the step")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "sweep", "bstep", "gemm", "configs", "q6k"],
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "gvtrace", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -710,6 +777,9 @@ def main():
                         "segments_us": {k: {"n": len(v), "mean": round(float(np.mean(v)), 3), "sum": round(float(np.sum(v)), 1)}
                                         for k, v in sorted(seg.items(), key=lambda kv: -sum(kv[1]))}}
         print(json.dumps(out, indent=1))
+        return
+    if args.kernel == "gvtrace":
+        print(json.dumps(launch_trace(), indent=1))
         return
     if args.kernel == "step0":
         # one full-size cfg0 batch-1 decode step (the graph of the timed region) between

@@ -154,6 +154,13 @@ TF_API int tf_cuda_history(tf_model* m, int n, int* out);
  * 1 wo, 2 gate/up, 3 down, 5 lm_head); 50 attention start, 53 q / k / v read, 51 attention done. */
 TF_API int tf_cuda_trace_read(tf_model* m, unsigned long long* out, int cap, int* n_out);
 
+/* Launch trace of the per-kernel decode step (a model created with TFB200_GV_TRACE=1): for each
+ * GEMV launch of the last step enqueued, GV_TRACE_CTAS (512) CTAs x 8 %globaltimer stamps (ns):
+ * entry, after griddepcontrol.wait, prologue done (attention CTAs: q/k/v ready), rows done
+ * (attention done), exit; out holds max_launches x 512 x 8 values, meta max_launches x 3 ints
+ * {grid, attention CTAs, kind: 0 QKV, 1 wo, 2 gate/up, 3 down, 4 lm_head}.  Diagnostic only. */
+TF_API int tf_cuda_launch_trace(tf_model* m, unsigned long long* out, int max_launches, int* meta, int* n_launch);
+
 /* Model::reset()  src/model.cpp:80-83 (one slot; seq < 0 resets every slot). */
 TF_API int tf_cuda_reset(tf_model* m, int seq);
 
