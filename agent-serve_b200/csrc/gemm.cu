@@ -1,7 +1,7 @@
 // Q8_0 / Q4_0 GEMM for M >= 16 activation rows (see gemm.cuh).
 //
 // Default path, tf_gemm_q8_tc_kernel (5th-gen tensor cores): a CTA of 512 threads owns 128
-// weight rows x NT (128 or 256) activation rows, k in stages of 64, double-buffered in
+// weight rows x NT (32, 64, 128 or 256) activation rows, k in stages of 64, double-buffered in
 // 128-byte swizzled K-major shared memory.  Four threads per weight row dequantise 16-weight
 // pieces from registers (the words of a stage are requested four stages ahead, the first
 // ones before the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw; the activation halves
@@ -464,6 +464,11 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                  : "memory");
 }
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -472,13 +477,22 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
+// Shared memory of the tcgen05 GEMM: two weight stages (Wh, Wl: the tensor cores read one
+// while the threads dequantise the next) and a ring of gemm_x_stages activation stages (Xh, Xl),
+// whose cp.async copies run that many stages ahead of the MMAs: the activations come from L2,
+// whose latency one stage of lookahead leaves exposed at few rows.
+constexpr size_t GM_WSTAGE = (size_t)2 * GM_BN * GM_BK * 2;
 template <int NT>
-constexpr size_t gemm_tc_stage_bytes() {
-    return (size_t)2 * GM_BN * GM_BK * 2 + (size_t)2 * NT * GM_BK * 2;  // Wh, Wl, Xh, Xl
+constexpr size_t gemm_x_stage_bytes() {
+    return (size_t)2 * NT * GM_BK * 2;
+}
+template <int NT>
+constexpr int gemm_x_stages() {
+    return NT <= 32 ? 8 : NT <= 64 ? 6 : NT <= 128 ? 4 : 2;
 }
 template <int NT>
 constexpr size_t gemm_tc_smem_bytes() {
-    const size_t pipe = 2 * gemm_tc_stage_bytes<NT>();
+    const size_t pipe = 2 * GM_WSTAGE + (size_t)gemm_x_stages<NT>() * gemm_x_stage_bytes<NT>();
     const size_t epi = (size_t)NT * GM_EPI_LD * 4 + (size_t)NT * 4;  // tile + column scales
     return (pipe > epi ? pipe : epi) + 64 + 1024;  // + mbarriers, the TMEM address, 1024-B alignment
 }
@@ -495,15 +509,16 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
-    constexpr size_t SB = gemm_tc_stage_bytes<NT>();
+    constexpr size_t XB = gemm_x_stage_bytes<NT>();
+    constexpr int XS = gemm_x_stages<NT>();
     uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - 64 - 1024;
     uint64_t* done = reinterpret_cast<uint64_t*>(tail);            // [2] MMAs of a stage completed
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail + 32);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 40);
-    auto wh = [&](int s) { return smem + (size_t)s * SB; };
-    auto wl = [&](int s) { return smem + (size_t)s * SB + GM_BN * GM_BK * 2; };
-    auto xh = [&](int s) { return smem + (size_t)s * SB + 2 * GM_BN * GM_BK * 2; };
-    auto xl = [&](int s) { return smem + (size_t)s * SB + 2 * GM_BN * GM_BK * 2 + NT * GM_BK * 2; };
+    auto wh = [&](int s) { return smem + (size_t)s * GM_WSTAGE; };
+    auto wl = [&](int s) { return smem + (size_t)s * GM_WSTAGE + GM_BN * GM_BK * 2; };
+    auto xh = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * XB; };
+    auto xl = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * XB + NT * GM_BK * 2; };
 
     if (warp == 0) {  // TMEM for the NT x 128 fp32 accumulator (NT columns)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -539,25 +554,32 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     // and destination advance by constant strides.
     const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0 + 64 i
     const uint32_t xdst0 = kint_off(xr0, 8 * xc);
-    auto load_x = [&](int s, int kc) {
-        static_assert(NT % 64 == 0, "rows per copy pass");
+    auto load_x = [&](int s, int kc) {  // s: activation ring slot; one cp.async group per call
+        static_assert(NT % 64 == 0 || NT == 32, "rows per copy pass");
+        if (NT >= 64 || xr0 < NT) {  // NT = 32: half the threads copy
 #pragma unroll
-        for (int pl = 0; pl < 2; ++pl) {
-            const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + xr0) * a.K + (size_t)kc * GM_BK + 8 * xc;
-            uint8_t* dst = (pl ? xl(s) : xh(s)) + xdst0;
+            for (int pl = 0; pl < 2; ++pl) {
+                const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + xr0) * a.K + (size_t)kc * GM_BK + 8 * xc;
+                uint8_t* dst = (pl ? xl(s) : xh(s)) + xdst0;
 #pragma unroll 4
-            for (int i = 0; i < NT / 64; ++i) cp_async16(dst + 8192 * i, src + (size_t)64 * i * a.K);
+                for (int i = 0; i < (NT < 64 ? 1 : NT / 64); ++i) cp_async16(dst + 8192 * i, src + (size_t)64 * i * a.K);
+            }
         }
         cp_async_commit();
     };
 
     // Software pipeline: the weight words of the next GM_WPF stages are in flight in registers
     // (a stage's 68-byte row pieces come from HBM, so one stage of lookahead leaves the loads
-    // latency-bound), and the activations of stage kc + 1 are requested as soon as the MMAs of
-    // stage kc - 1 (the previous user of that buffer) have completed.
+    // latency-bound), and the activations of stage kc + XS - 1 are requested as soon as the
+    // MMAs of stage kc - 1 (the previous user of that ring slot) have completed.  Every
+    // iteration commits one cp.async group (empty past the last stage), so that "stage kc has
+    // landed" is always "at most XS - 2 younger groups pending".
     bool ok = true;
     int last_kc = -1;  // the last stage whose MMAs were issued
-    if (nk > 0) load_x(0, kb);
+    for (int i = 0; i < XS - 1; ++i) {
+        if (i < nk) load_x(i, kb + i);
+        else cp_async_commit();
+    }
     // Stage kc's weight words sit in slot kc % PF: the k loop is unrolled by PF so every slot
     // index is static (registers) and a slot is refilled right after its dequantisation, PF
     // stages ahead of its use (a shift of the slots would wait on the newest load every stage).
@@ -579,14 +601,15 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                     else gm_dequant16_t<1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
                 }
                 if (kc + PF < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
-                cp_async_wait_all();
+                asm volatile("cp.async.wait_group %0;" ::"n"(XS - 2) : "memory");  // stage kc's activations
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
                 __syncthreads();
                 last_kc = kc;
+                const int xb = kc % XS;
                 if (tid == 0) {
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(s)),
-                                   bl = smem_u32(xl(s));
+                    const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(xb)),
+                                   bl = smem_u32(xl(xb));
 #pragma unroll
                     for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
                         const uint32_t o = 32u * j;
@@ -598,13 +621,17 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                     umma_commit(&done[s]);
                 }
                 if (kc + 1 < nk) {
-                    // stage s ^ 1 was last read by the MMAs of stage kc - 1
+                    // weight stage s ^ 1 and activation slot (kc - 1) % XS were last read by the
+                    // MMAs of stage kc - 1
                     if (kc >= 1) ok = mbar_wait(&done[s ^ 1], ((kc - 1) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
-                    if (ok) load_x(s ^ 1, kb + kc + 1);
                 }
+                // (slot (kc + XS - 1) % XS: at kc = 0 the one slot the prologue left unused)
+                if (ok && kc + XS - 1 < nk) load_x((kc + XS - 1) % XS, kb + kc + XS - 1);
+                else cp_async_commit();
             }
         }
     }
+    cp_async_wait_all();  // no copy may still land in the buffers the epilogue reuses
     // the last stage's commit covers every MMA issued before it
     if (last_kc >= 0 && !mbar_wait(&done[last_kc & 1], (last_kc >> 1) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -623,15 +650,23 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     {
         const int row = 32 * (warp & 3) + lane;           // weight row of this thread's TMEM lane
         const int c0 = (warp >> 2) * (NT / 4);             // four column groups of warps
-        for (int c = c0; c < c0 + NT / 4; c += 16) {
-            uint32_t r[16];
-            tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
+        if constexpr (NT / 4 >= 16) {
+            for (int c = c0; c < c0 + NT / 4; c += 16) {
+                uint32_t r[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int mm = c + u;
+                    tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[mm];
+                }
+            }
+        } else {  // NT = 32: eight columns per warp
+            uint32_t r[8];
+            tmem_ld8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c0, r);
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int u = 0; u < 16; ++u) {
-                const int mm = c + u;
-                tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[mm];
-            }
+            for (int u = 0; u < 8; ++u) tile[(c0 + u) * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[c0 + u];
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -691,12 +726,18 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
 }
 
 int gemm_tile_rows(int M) {
+    // the MMA's N is the tile's activation rows: a tile no wider than the rows present keeps
+    // the tensor-core time of a few-row step down (TFB200_GEMM_NT=128: at least 128 rows, at
+    // most 128; =256: at least 128 rows)
     static int v = -1;
     if (v < 0) {
         const char* e = getenv("TFB200_GEMM_NT");
-        v = (e && atoi(e) == 128) ? 128 : 256;
+        v = e ? atoi(e) : 0;
     }
-    return (M > 128 && v == 256) ? 256 : 128;
+    if (v == 128) return 128;
+    if (M > 128) return 256;
+    if (v == 256 || M > 64) return 128;
+    return M > 32 ? 64 : 32;
 }
 
 bool gemm_takes_q4() { return true; }
@@ -709,21 +750,27 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     {
         GemmArgs aa = a;
         void* args[] = {&aa};
-        const bool wide = gemm_tile_rows(a.M) == 256;
-        const size_t sm = wide ? gemm_tc_smem_bytes<256>() : gemm_tc_smem_bytes<128>();
+        const int nt = gemm_tile_rows(a.M);
+        const int wi = nt == 256 ? 3 : nt == 128 ? 2 : nt == 64 ? 1 : 0;
         const bool q4 = a.wq4 != 0;
-        const void* fn = q4 ? (wide ? (const void*)tf_gemm_q8_tc_kernel<256, true> : (const void*)tf_gemm_q8_tc_kernel<128, true>)
-                            : (wide ? (const void*)tf_gemm_q8_tc_kernel<256, false> : (const void*)tf_gemm_q8_tc_kernel<128, false>);
-        static bool tc_attr[64][2][2] = {};
+        static const size_t sms[4] = {gemm_tc_smem_bytes<32>(), gemm_tc_smem_bytes<64>(), gemm_tc_smem_bytes<128>(),
+                                      gemm_tc_smem_bytes<256>()};
+        static const void* fns[4][2] = {
+            {(const void*)tf_gemm_q8_tc_kernel<32, false>, (const void*)tf_gemm_q8_tc_kernel<32, true>},
+            {(const void*)tf_gemm_q8_tc_kernel<64, false>, (const void*)tf_gemm_q8_tc_kernel<64, true>},
+            {(const void*)tf_gemm_q8_tc_kernel<128, false>, (const void*)tf_gemm_q8_tc_kernel<128, true>},
+            {(const void*)tf_gemm_q8_tc_kernel<256, false>, (const void*)tf_gemm_q8_tc_kernel<256, true>}};
+        const size_t sm = sms[wi];
+        const void* fn = fns[wi][q4];
+        static bool tc_attr[64][4][2] = {};
         int dv = 0;
         cudaGetDevice(&dv);
         if (dv < 0 || dv >= 64) dv = 0;
-        if (!tc_attr[dv][wide][q4]) {
+        if (!tc_attr[dv][wi][q4]) {
             cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
             if (e != cudaSuccess) return e;
-            tc_attr[dv][wide][q4] = true;
+            tc_attr[dv][wi][q4] = true;
         }
-        const int nt = wide ? 256 : 128;
         // the k splits of a tile form one cluster (their reduction goes through distributed
         // shared memory)
         cudaLaunchConfig_t cfg = {};

@@ -75,8 +75,8 @@ constexpr int GM_MAX_SPLIT = 8;
 // workspace floats / tile counters the split-K path needs for `num_sms` SMs
 inline size_t gemm_ws_floats(int num_sms) { return (size_t)GM_MAX_SPLIT * num_sms * GM_BN * GM_ROW_PAD; }
 inline int gemm_tile_counters(int num_sms) { return 2 * num_sms; }  // arrivals, departures per tile
-// activation rows per tcgen05 CTA tile for an M-row GEMM (128 or 256; TFB200_GEMM_NT=128
-// keeps 128-row tiles at every M)
+// activation rows per tcgen05 CTA tile for an M-row GEMM (32, 64, 128 or 256: the smallest
+// that holds M up to 128 rows, 256 above; TFB200_GEMM_NT=128 keeps 128-row tiles at every M)
 int gemm_tile_rows(int M);
 // k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
 inline int gemm_pick_split(int N, int M, int K, int num_sms) {

@@ -713,7 +713,8 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the cfg4 batched-decode measurement")
     ap.add_argument("--no-configs", action="store_true", help="skip the cfg1 / cfg2 batch-1 runs (N = 1 only)")
     ap.add_argument("--batched-steps", type=int, default=128, help="timed cfg4 batched decode steps")
-    ap.add_argument("--rows", type=int, default=128, help="--kernel bstep: rows of the batched step")
+    ap.add_argument("--rows", type=int, default=None,
+                    help="--kernel bstep: rows of the batched step (128); --kernel gemm: activation rows (256)")
     ap.add_argument("--ctx", type=int, default=512, help="--kernel bstep: prompt length before the step")
     ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "gvtrace", "sweep", "bstep", "gemm", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
@@ -801,12 +802,12 @@ def main():
         print(json.dumps({"kernel": "step0", "kernels_per_step": kps, "last_token": t}))
         return
     if args.kernel == "gemm":
-        # the cfg4 gate/up GEMM of a 256-row batched step (N = 2 x 8960, K = 1536), Q8_0,
+        # the cfg4 gate/up GEMM of a batched step (N = 2 x 8960, K = 1536; 256 rows unless --rows), Q8_0,
         # 1 warm-up + 3 launches through tf_op_matmul_tc (for an ncu capture of launch 2)
         import torch
         from tinferno_b200 import gguf, native, quants
         L = native.lib()
-        N, K, M = 17920, 1536, 256
+        N, K, M = 17920, 1536, args.rows or 256
         rng = np.random.default_rng(7)
         raw = np.ascontiguousarray(quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
                                                    gguf.GGML_Q8_0)).reshape(-1)
@@ -838,7 +839,7 @@ def main():
         # Stop, for a launch list under `ncu --profile-from-start off`
         import torch
         from tinferno_b200.model import Model, RunConfig
-        S, P = args.rows, args.ctx
+        S, P = args.rows or 128, args.ctx
         m = Model(synth.model_path(synth.CFG4), RunConfig(max_seq=P + 16, max_batch=S))
         prompts = np.stack([synth.prompt_tokens(synth.CFG4, P, stream=1000 + g) for g in range(S)])
         tok = m.prefill_batch(list(range(S)), prompts)

@@ -91,7 +91,7 @@ def test_matmul_integer_path_large(t, shape):
 
 @pytest.mark.parametrize("t", [gguf.GGML_Q8_0, gguf.GGML_Q4_0])
 @pytest.mark.parametrize("shape", [(256, 2048, 16), (1000, 2048, 64), (130, 896, 130), (96, 4864, 33),
-                                   (2048, 8192, 40), (515, 1536, 300)])
+                                   (2048, 8192, 40), (515, 1536, 300), (384, 1536, 32)])
 def test_matmul_tensor_core(shape, t):
     """Q8_0 and Q4_0 at M >= 16 run the tensor-core GEMM (f16-split products, fp32
     accumulation, split-K clusters when the tiles do not cover the SMs)."""
