@@ -20,6 +20,12 @@
 
 namespace tfb {
 
+// byte offset of element (row, k) of a [rows][64] f16 operand tile in the 128-byte swizzled
+// K-major layout: 8-row atoms of 1024 B, the 16-byte chunk c of line r stored at chunk c ^ r
+__host__ __device__ __forceinline__ uint32_t gm_kint_off(int row, int k) {
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
+}
+
 // ---- activation preparation ----------------------------------------------------------------
 // One CTA per activation row: [embedding lookup ->] [RMSNorm (src/layers.cpp:7-12) ->]
 // power-of-two scale to |x| < 2^14 -> f16 halves.
@@ -83,11 +89,21 @@ __global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
     int sx = 140 - be;
     sx = sx > 100 ? 100 : (sx < -100 ? -100 : sx);
     const float S = ldexpf(1.0f, sx);
-    for (int e = tid; e < K; e += nth) {
-        const float v = xrow[xpad(e)] * S;  // exact: a power-of-two scale
-        const __half h = __float2half_rn(v);
-        a.xh[(size_t)m * K + e] = h;
-        a.xl[(size_t)m * K + e] = __float2half_rn(v - __half2float(h));
+    // 8-element chunks into the GEMM's operand layout (gemm.cuh, XPrepArgs::mp)
+    for (int c = tid; c < K / 8; c += nth) {
+        const int e0 = 8 * c;
+        uint32_t hv[4], lv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float v0 = xrow[xpad(e0 + 2 * i)] * S, v1 = xrow[xpad(e0 + 2 * i + 1)] * S;  // exact scaling
+            const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+            const __half l0 = __float2half_rn(v0 - __half2float(h0)), l1 = __float2half_rn(v1 - __half2float(h1));
+            hv[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lv[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        const size_t off = (size_t)(e0 >> 6) * a.mp * (GM_BK * 2) + gm_kint_off(m, e0 & 63);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.xh) + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.xl) + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
     }
     if (tid == 0) a.sx[m] = sx;
 }
@@ -136,10 +152,7 @@ __device__ __forceinline__ void gm_load_w16(uint32_t (&w)[6], const GemmArgs& a,
     }
 }
 
-// byte offset of element (row, k) of a [rows][64] f16 operand tile in the swizzled layout
-__device__ __forceinline__ uint32_t kint_off(int row, int k) {
-    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7)) & 7) << 4) + (k & 7) * 2);
-}
+__device__ __forceinline__ uint32_t kint_off(int row, int k) { return gm_kint_off(row, k); }
 
 // offsets of the 8-half groups of one weight row's block in the swizzled layout
 struct KintRow {
@@ -549,21 +562,16 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
 
     // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
-    // activations of stage kc: 16-byte cp.async chunks.  Thread t copies chunk c = t % 8 of
-    // rows r = t / 8 + 32 i; r % 8 (its swizzle row) and c are fixed per thread, so source
-    // and destination advance by constant strides.
-    const int xc = tid & 7, xr0 = tid >> 3;  // rows xr0 + 64 i
-    const uint32_t xdst0 = kint_off(xr0, 8 * xc);
+    // activations of stage kc: the tile's NT rows are one contiguous NT * 128-byte block of
+    // each half in the operand layout xprep writes; 16-byte cp.async chunks
     auto load_x = [&](int s, int kc) {  // s: activation ring slot; one cp.async group per call
-        static_assert(NT % 64 == 0 || NT == 32, "rows per copy pass");
-        if (NT >= 64 || xr0 < NT) {  // NT = 32: half the threads copy
+        const size_t src0 = (size_t)kc * a.mp * (GM_BK * 2) + (size_t)m0 * (GM_BK * 2);
 #pragma unroll
-            for (int pl = 0; pl < 2; ++pl) {
-                const __half* src = (pl ? a.xl : a.xh) + (size_t)(m0 + xr0) * a.K + (size_t)kc * GM_BK + 8 * xc;
-                uint8_t* dst = (pl ? xl(s) : xh(s)) + xdst0;
-#pragma unroll 4
-                for (int i = 0; i < (NT < 64 ? 1 : NT / 64); ++i) cp_async16(dst + 8192 * i, src + (size_t)64 * i * a.K);
-            }
+        for (int pl = 0; pl < 2; ++pl) {
+            const uint8_t* src = reinterpret_cast<const uint8_t*>(pl ? a.xl : a.xh) + src0;
+            uint8_t* dst = pl ? xl(s) : xh(s);
+#pragma unroll
+            for (int i = tid; i < NT * 8; i += GM_TC_THREADS) cp_async16(dst + 16 * i, src + 16 * i);
         }
         cp_async_commit();
     };
@@ -716,13 +724,21 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 }
 
 cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
+    if (a.K % GM_BK) return cudaErrorInvalidValue;
     const size_t smem = (size_t)xpad_len(a.K) * 4;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(tf_xprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    tf_xprep_kernel<<<a.M, 256, smem, st>>>(a);
+    XPrepArgs aa = a;
+    aa.mp = gemm_x_rows(a.M);
+    tf_xprep_kernel<<<a.M, 256, smem, st>>>(aa);
     return cudaGetLastError();
+}
+
+int gemm_x_rows(int M) {
+    const int nt = gemm_tile_rows(M);
+    return (M + nt - 1) / nt * nt;
 }
 
 int gemm_tile_rows(int M) {
@@ -749,6 +765,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
     {
         GemmArgs aa = a;
+        aa.mp = gemm_x_rows(a.M);
         void* args[] = {&aa};
         const int nt = gemm_tile_rows(a.M);
         const int wi = nt == 256 ? 3 : nt == 128 ? 2 : nt == 64 ? 1 : 0;

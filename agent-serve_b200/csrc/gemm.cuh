@@ -36,10 +36,16 @@ struct XPrepArgs {
     const int* tokens;
     float* x_out;         // [M][ldx]: the embedded rows (the residual stream)
     int K, M;
-    __half* xh;           // [M][K]
+    // xh / xl: the halves in the GEMM's operand layout: k-stage kc (64 columns) of rows
+    // [0, mp) is one block of mp * 128 bytes at kc * mp * 128, row r of it at the 128-byte
+    // swizzled K-major offsets of an 8-row atom (r / 8) * 1024 (gm_kint_off), so the NT rows
+    // of a tile are one contiguous NT * 128-byte block per stage; mp = gemm_x_rows(M) (set
+    // by xprep_launch)
+    __half* xh;
     __half* xl;
     int* sx;              // [M] scale exponents
     int* err;
+    int mp;
 };
 
 struct GemmArgs {
@@ -48,9 +54,10 @@ struct GemmArgs {
     long long rb;
     int N, K, M;
     int sw;               // weight scale exponent
-    const __half* xh;     // [>= ceil(M/GM_ROW_PAD)*GM_ROW_PAD][K]
+    const __half* xh;     // XPrepArgs' operand layout (mp = gemm_x_rows(M), set by gemm_launch)
     const __half* xl;
     const int* sx;        // [M]
+    int mp;
     // epilogue (GemvArgs conventions)
     int epi;              // EPI_STORE / EPI_RESID / EPI_SWIGLU (interleaved gate/up rows) / EPI_ARGMAX
     float* y;
@@ -78,6 +85,8 @@ inline int gemm_tile_counters(int num_sms) { return 2 * num_sms; }  // arrivals,
 // activation rows per tcgen05 CTA tile for an M-row GEMM (32, 64, 128 or 256: the smallest
 // that holds M up to 128 rows, 256 above; TFB200_GEMM_NT=128 keeps 128-row tiles at every M)
 int gemm_tile_rows(int M);
+// rows per k-stage block of the activation operand layout for an M-row GEMM
+int gemm_x_rows(int M);
 // k splits for an N x M GEMM: enough CTAs to cover the SMs once when the tiles alone do not
 inline int gemm_pick_split(int N, int M, int K, int num_sms) {
     const int mt = gemm_tile_rows(M);  // activation rows per CTA tile

@@ -584,7 +584,6 @@ def launch_trace(steps=6, model_path=None):
     GEMV launch stamps %globaltimer at entry, after griddepcontrol.wait, prologue done, rows
     done and exit (TFB200_GV_TRACE=1, tf_cuda_launch_trace); the chain per launch kind is
     averaged over the layers (times in us, relative to the previous launch's last exit)."""
-    import ctypes as C
     from tinferno_b200 import native
     from tinferno_b200.model import Model, RunConfig
     os.environ["TFB200_GV_TRACE"] = "1"
@@ -745,7 +744,6 @@ def main():
     if args.kernel == "pktrace":
         # per-phase breakdown of one cfg0 decode step on the persistent kernel (phase trace of
         # the first CTA: the time between consecutive trace points, averaged over the layers)
-        import ctypes as C
         from tinferno_b200 import native
         from tinferno_b200.model import Model, RunConfig
         os.environ["TFB200_PK_TRACE"] = "1"
