@@ -1,15 +1,18 @@
 // Q8_0 / Q4_0 GEMM for M >= 16 activation rows (see gemm.cuh).
 //
-// Default path, tf_gemm_q8_tc_kernel (5th-gen tensor cores): a CTA of 512 threads owns 128
-// weight rows x NT (32, 64, 128 or 256) activation rows, k in stages of 64, double-buffered in
-// 128-byte swizzled K-major shared memory.  Four threads per weight row dequantise 16-weight
-// pieces from registers (the words of a stage are requested four stages ahead, the first
-// ones before the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw; the activation halves
-// Xh, Xl (prepared once per matmul by tf_xprep_kernel) arrive by cp.async.  Thread 0 issues
-// tcgen05.mma (kind::f16, fp32 accumulator in TMEM) three times per k step: Wh*Xh, Wh*Xl,
-// Wl*Xh.  The epilogue reads TMEM, scales back by 2^-(sw+sx[m]) (per-column factors computed
-// once), stages the tile in shared memory and, when the k range is split, sums the splits of
-// the tile through distributed shared memory of their thread-block cluster in split order;
+// Default path, tf_gemm_q8_tc_kernel (5th-gen tensor cores): a CTA owns 128 weight rows x NT
+// (32, 64, 128 or 256) activation rows, k in stages of 64, in 128-byte swizzled K-major shared
+// memory, with its warps in three roles synchronised by mbarriers (no CTA-wide barrier per
+// stage).  Sixteen dequantising warps, four threads per weight row, turn 16-weight pieces held
+// in registers (the words of a stage are requested four stages ahead, the first ones before
+// the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw in one of two weight buffers; one
+// warp bulk-copies the activation halves Xh, Xl (prepared once per matmul by tf_xprep_kernel
+// in the operand layout) into a ring of stages; one thread issues tcgen05.mma (kind::f16, fp32
+// accumulator in TMEM) three times per k step: Wh*Xh, Wh*Xl, Wl*Xh, and commits each stage to
+// the barriers that free its buffers.  The epilogue reads TMEM, scales back by 2^-(sw+sx[m])
+// (per-column factors computed once), stages the tile in shared memory and, when the k range
+// is split, sums the splits of the tile through distributed shared memory of their
+// thread-block cluster in split order;
 // then the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
 
@@ -109,28 +112,10 @@ __global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 constexpr int GM_EPI_LD = GM_BN + 4;         // epilogue tile row stride (floats)
 
-// The 9 words of weight row r, k-stage kc, block half j (j = 0: bytes 0..35 of the stage's
-// 68-byte unit, j = 1: bytes 32..67).
-__device__ __forceinline__ void gm_load_w(uint32_t (&w)[9], const GemmArgs& a, int n, int kc, int j) {
-    if (n < a.N) {
-        const uint32_t* p = reinterpret_cast<const uint32_t*>(a.W + (long long)n * a.rb + (long long)kc * 68) + 8 * j;
-#pragma unroll
-        for (int i = 0; i < 9; ++i) w[i] = __ldg(p + i);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 9; ++i) w[i] = 0u;
-    }
-}
-
-// The weight words a thread of the 512-thread tcgen05 kernel needs for weight row r, k-stage
+// The weight words a dequantising thread of the tcgen05 kernel needs for weight row r, k-stage
 // kc, 16-weight piece jh = 2 * block + half: w[0] holds the block's fp16 scale (word 0 or 8 of
 // the stage's 68-byte unit), w[1..5] the five words 4*jh .. 4*jh + 4 (bytes 16*jh .. 16*jh +
 // 19), whose bytes 2 * block + 2 .. + 17 are the piece's 16 quants.
@@ -154,169 +139,44 @@ __device__ __forceinline__ void gm_load_w16(uint32_t (&w)[6], const GemmArgs& a,
 
 __device__ __forceinline__ uint32_t kint_off(int row, int k) { return gm_kint_off(row, k); }
 
-// offsets of the 8-half groups of one weight row's block in the swizzled layout
-struct KintRow {
-    int row, k0;
-    __device__ __forceinline__ uint32_t operator()(int c) const { return kint_off(row, k0 + 8 * c); }
-};
-
-// The same split with packed half2 arithmetic and no per-element conversion: q is made exact
-// in f16 from its byte (0x6400 | (q + 128) is 1024 + q + 128), Wh = q * dh rounds the exact
-// 19-bit product once (dh = d * 2^sw, an f16 value), and Wl = fma(q, dh, -Wh) is the exact
-// remainder (at most 8 significant bits).  Equal to gm_dequant_to's Wh, Wl.
-template <int J, class Off>
-__device__ __forceinline__ void gm_dequant_h2_t(const uint32_t (&w)[9], float wscale, uint8_t* dh, uint8_t* dl,
-                                                Off hoff) {
-    constexpr int j = J;  // compile-time, so the word indices below are static (registers)
-    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
+// One 16-weight piece of gm_load_w16's words into the exact f16 split, with packed half2
+// arithmetic and no per-element conversion: q is made exact in f16 from its byte (0x6400 |
+// (q + 128) is 1024 + q + 128; Q4_0: (0x6400 | nibble) - 1032 is nibble - 8), Wh = q * dh rounds
+// the exact product once (dh = d * 2^sw, an f16 value; at most 19 significant bits for Q8_0, 15
+// for Q4_0), and Wl = fma(q, dh, -Wh) is the exact remainder.  One instruction stream for every
+// lane of a warp (the lanes hold pieces of both blocks of a stage, and of both nibble halves
+// for Q4_0): the pieces of block 1 start two bytes later in their five window words, so a
+// funnel shift by 16 bits (0 for block 0) aligns both, and the nibble half is a shift by
+// 4 * half.  off0 / off1: the byte offsets of the piece's two 8-half groups.
+template <bool Q4>
+__device__ __forceinline__ void gm_dequant16_u(const uint32_t (&w)[6], uint32_t blk, uint32_t half, float wscale,
+                                               uint8_t* dh, uint8_t* dl, uint32_t off0, uint32_t off1) {
+    const uint32_t sh = blk << 4;
+    const uint32_t dbits = (w[0] >> sh) & 0xFFFFu;
     const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
     const __half2 d2 = __halves2half2(dsc, dsc);
-    const __half2 k1152 = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
-    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words (even: pairs stay in one word)
+    const unsigned short kb = Q4 ? 0x6408u : 0x6480u;  // 1032 (nibble - 8) or 1152 (byte ^ 0x80 - 128)
+    const __half2 kq = __halves2half2(__ushort_as_half(kb), __ushort_as_half(kb));
+    uint32_t q[5];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const int b = b0 + 8 * c + e;
-            const uint32_t wd = w[b >> 2] ^ 0x80808080u;
-            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
-            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
-            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
-            const __half2 hi = __hmul2(q2, d2);
-            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
-            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
-            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
-        }
-        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-    }
-}
-
-// gm_dequant_h2_t for one 16-weight piece (gm_load_w16's words, block J): the two 8-half
-// groups go to dh / dl + hoff(0), hoff(1).
-template <int J, class Off>
-__device__ __forceinline__ void gm_dequant16_t(const uint32_t (&w)[6], float wscale, uint8_t* dh, uint8_t* dl,
-                                               Off hoff) {
-    const uint32_t dbits = J == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
-    const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
-    const __half2 d2 = __halves2half2(dsc, dsc);
-    const __half2 k1152 = __halves2half2(__ushort_as_half((unsigned short)0x6480u), __ushort_as_half((unsigned short)0x6480u));
-    constexpr int b0 = 2 * J + 2;  // first quant byte within the five window words (even)
+    for (int i = 0; i < 5; ++i) q[i] = __funnelshift_r(w[1 + i], i < 4 ? w[2 + i] : 0u, sh);
 #pragma unroll
     for (int c = 0; c < 2; ++c) {
         uint32_t hv[4], lv[4];
 #pragma unroll
         for (int e = 0; e < 8; e += 2) {
-            const int b = b0 + 8 * c + e;
-            const uint32_t wd = w[1 + (b >> 2)] ^ 0x80808080u;
+            const int b = 2 + 8 * c + e;  // the piece's bytes are 2 .. 17 of the aligned window
+            const uint32_t wd = Q4 ? ((q[b >> 2] >> (half << 2)) & 0x0F0F0F0Fu) : (q[b >> 2] ^ 0x80808080u);
             const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
             const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
-            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1152);
+            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), kq);
             const __half2 hi = __hmul2(q2, d2);
             const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
             hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
             lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
         }
-        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-    }
-}
-
-// Q4_0 piece (block J, nibble half H) from gm_load_w16<true>'s words: q = nibble - 8 made
-// exact in f16 as (0x6400 | nibble) - 1032, then the same exact Wh / Wl split (|q| <= 8, so
-// q * dh has at most 15 significant bits and Wl at most 4).
-template <int J, int H, class Off>
-__device__ __forceinline__ void gm_dequant16_q4_t(const uint32_t (&w)[6], float wscale, uint8_t* dh, uint8_t* dl,
-                                                  Off hoff) {
-    const uint32_t dbits = J == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
-    const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
-    const __half2 d2 = __halves2half2(dsc, dsc);
-    const __half2 k1032 = __halves2half2(__ushort_as_half((unsigned short)0x6408u), __ushort_as_half((unsigned short)0x6408u));
-    constexpr int b0 = 2 * J + 2;  // first quant byte within the five window words (even)
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const int b = b0 + 8 * c + e;
-            const uint32_t wd = H ? ((w[1 + (b >> 2)] >> 4) & 0x0F0F0F0Fu) : (w[1 + (b >> 2)] & 0x0F0F0F0Fu);
-            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
-            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
-            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), k1032);
-            const __half2 hi = __hmul2(q2, d2);
-            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
-            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
-            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
-        }
-        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-    }
-}
-
-template <class Off>
-__device__ __forceinline__ void gm_dequant_h2(const uint32_t (&w)[9], int j, float wscale, uint8_t* dh, uint8_t* dl,
-                                              Off hoff) {
-    if (j == 0) gm_dequant_h2_t<0>(w, wscale, dh, dl, hoff);
-    else gm_dequant_h2_t<1>(w, wscale, dh, dl, hoff);
-}
-
-// Dequantise one Q8_0 block (from the 9 words) into 32 f16 halves Wh, Wl; the 8-half group c
-// goes to dh + hoff(c) / dl + hoff(c) (bytes).
-template <class Off>
-__device__ __forceinline__ void gm_dequant_to(const uint32_t (&w)[9], int j, float wscale, uint8_t* dh, uint8_t* dl,
-                                              Off hoff) {
-    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
-    const float d = __half2float(__ushort_as_half((unsigned short)dbits)) * wscale;  // exact
-    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 8 elements per 16-byte store
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            float v2[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int b = b0 + 8 * c + e + u;
-                const int q = (int)(int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
-                v2[u] = (float)q * d;  // exact: 8-bit integer times an 11-bit mantissa
-            }
-            const __half h0 = __float2half_rn(v2[0]), h1 = __float2half_rn(v2[1]);
-            const __half l0 = __float2half_rn(v2[0] - __half2float(h0));
-            const __half l1 = __float2half_rn(v2[1] - __half2float(h1));
-            hv[e >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            lv[e >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        }
-        *reinterpret_cast<uint4*>(dh + hoff(c)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(dl + hoff(c)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-    }
-}
-
-// Dequantise one Q8_0 block (from the 9 words) into 32 f16 halves Wh, Wl at dh / dl.
-__device__ __forceinline__ void gm_dequant(const uint32_t (&w)[9], int j, float wscale, __half* dh, __half* dl) {
-    const uint32_t dbits = j == 0 ? (w[0] & 0xFFFFu) : (w[0] >> 16);
-    const float d = __half2float(__ushort_as_half((unsigned short)dbits)) * wscale;  // exact
-    const int b0 = j == 0 ? 2 : 4;  // first quant byte within the 9 words
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 8 elements per 16-byte store
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            float v2[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int b = b0 + 8 * c + e + u;
-                const int q = (int)(int8_t)((w[b >> 2] >> (8 * (b & 3))) & 0xFFu);
-                v2[u] = (float)q * d;  // exact: 8-bit integer times an 11-bit mantissa
-            }
-            const __half h0 = __float2half_rn(v2[0]), h1 = __float2half_rn(v2[1]);
-            const __half l0 = __float2half_rn(v2[0] - __half2float(h0));
-            const __half l1 = __float2half_rn(v2[1] - __half2float(h1));
-            hv[e >> 1] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            lv[e >> 1] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
-        }
-        reinterpret_cast<uint4*>(dh)[c] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        reinterpret_cast<uint4*>(dl)[c] = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        *reinterpret_cast<uint4*>(dh + (c ? off1 : off0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(dl + (c ? off1 : off0)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
     }
 }
 
@@ -456,9 +316,8 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
 // atom, and the 16-byte chunk c of line r is stored at chunk c ^ r, so that the tensor cores'
 // reads of eight lines spread over all banks; atoms of 8 rows are SBO = 1024 B apart, and the
 // 16-element k steps of the stage are 32 B apart within the lines.
-// Two stages: while the tensor cores consume stage s, all threads dequantise the weights and
-// copy the activations of the next stage into s ^ 1; a tcgen05.commit per stage arrives on
-// that stage's mbarrier when its MMAs have read it.
+// A tcgen05.commit per stage arrives on the barriers of the buffers it read once its MMAs
+// have completed.
 __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
     // start >> 4 [0,14), LBO [16,30) (1: unused by swizzled K-major), SBO >> 4 [32,46),
     // version 1 [46,48), base offset 0, layout 2 = 128-byte swizzle [61,64)
@@ -491,9 +350,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 
 // Shared memory of the tcgen05 GEMM: two weight stages (Wh, Wl: the tensor cores read one
-// while the threads dequantise the next) and a ring of gemm_x_stages activation stages (Xh, Xl),
-// whose cp.async copies run that many stages ahead of the MMAs: the activations come from L2,
-// whose latency one stage of lookahead leaves exposed at few rows.
+// while the dequantising warps write the next) and a ring of gemm_x_stages activation stages
+// (Xh, Xl), whose bulk copies run that many stages ahead of the MMAs.
 constexpr size_t GM_WSTAGE = (size_t)2 * GM_BN * GM_BK * 2;
 template <int NT>
 constexpr size_t gemm_x_stage_bytes() {
@@ -507,9 +365,8 @@ template <int NT>
 constexpr size_t gemm_tc_smem_bytes() {
     const size_t pipe = 2 * GM_WSTAGE + (size_t)gemm_x_stages<NT>() * gemm_x_stage_bytes<NT>();
     const size_t epi = (size_t)NT * GM_EPI_LD * 4 + (size_t)NT * 4;  // tile + column scales
-    return (pipe > epi ? pipe : epi) + 64 + 1024;  // + mbarriers, the TMEM address, 1024-B alignment
+    return (pipe > epi ? pipe : epi) + GM_TC_TAIL + 1024;  // + mbarriers, TMEM address, 1024-B alignment
 }
-
 
 template <int NT, bool Q4>
 __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const GemmArgs a) {
@@ -522,25 +379,35 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
     const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
-    constexpr size_t XB = gemm_x_stage_bytes<NT>();
     constexpr int XS = gemm_x_stages<NT>();
-    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - 64 - 1024;
-    uint64_t* done = reinterpret_cast<uint64_t*>(tail);            // [2] MMAs of a stage completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail + 32);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tail + 40);
+    constexpr uint32_t XH = NT * GM_BK * 2;  // bytes of one activation half of a stage
+    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - GM_TC_TAIL - 1024;
+    uint64_t* wready = reinterpret_cast<uint64_t*>(tail);  // [2] weight stage written (dequant warps)
+    uint64_t* wfree = wready + 2;                          // [2] its MMAs completed
+    uint64_t* xfull = wfree + 2;                           // [XS] activation stage landed
+    uint64_t* xempty = xfull + XS;                         // [XS] its MMAs completed
+    uint64_t* mma_done = xempty + XS;                      // every MMA completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     auto wh = [&](int s) { return smem + (size_t)s * GM_WSTAGE; };
     auto wl = [&](int s) { return smem + (size_t)s * GM_WSTAGE + GM_BN * GM_BK * 2; };
-    auto xh = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * XB; };
-    auto xl = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * XB + NT * GM_BK * 2; };
+    auto xh = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * 2 * XH; };
 
     if (warp == 0) {  // TMEM for the NT x 128 fp32 accumulator (NT columns)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(NT));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
-    if (tid == 0) {
-        mbar_init(&done[0], 1);
-        mbar_init(&done[1], 1);
+    if (tid == GM_DQ_THREADS) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&wready[i], GM_DQ_THREADS / 32);
+            mbar_init(&wfree[i], 1);
+        }
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xempty[i], 1);
+        }
+        mbar_init(mma_done, 1);
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -548,102 +415,97 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    // the weight words of the first PF stages do not depend on earlier kernels: request them
-    // before waiting for the previous kernel of the step
-    constexpr int PF = GM_WPF;
-    // thread: weight row wr, 16-weight piece wjh (block wjh >> 1, half wjh & 1) of each stage
-    const int wr = tid >> 2, wjh = tid & 3;
-    uint32_t wbuf[PF][6];  // weight words of stage kc in slot kc % PF
-#pragma unroll
-    for (int u = 0; u < PF; ++u)
-        if (u < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + u, wjh);
-    pdl_trigger();
-    pdl_wait();
 
-    // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
-    const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
-    // activations of stage kc: the tile's NT rows are one contiguous NT * 128-byte block of
-    // each half in the operand layout xprep writes; 16-byte cp.async chunks
-    auto load_x = [&](int s, int kc) {  // s: activation ring slot; one cp.async group per call
-        const size_t src0 = (size_t)kc * a.mp * (GM_BK * 2) + (size_t)m0 * (GM_BK * 2);
+    if (warp < GM_DQ_THREADS / 32) {
+        // ---- dequantising warps: stage kc's weights into weight buffer kc & 1 ----
+        // The weight words of the next GM_WPF stages are in flight in registers (a stage's
+        // 68-byte row pieces come from HBM); the first ones are requested before the PDL wait.
+        constexpr int PF = GM_WPF;
+        const int wr = tid >> 2, wjh = tid & 3;  // weight row, 16-weight piece (block, half)
+        const uint32_t off0 = kint_off(wr, 16 * wjh), off1 = kint_off(wr, 16 * wjh + 8);
+        uint32_t wbuf[PF][6];                    // weight words of stage kc in slot kc % PF
 #pragma unroll
-        for (int pl = 0; pl < 2; ++pl) {
-            const uint8_t* src = reinterpret_cast<const uint8_t*>(pl ? a.xl : a.xh) + src0;
-            uint8_t* dst = pl ? xl(s) : xh(s);
+        for (int u = 0; u < PF; ++u)
+            if (u < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + u, wjh);
+        pdl_trigger();
+        pdl_wait();
+        bool ok = true;
+        // unrolled by PF so that every register slot index is static
+        for (int kc0 = 0; kc0 < nk && ok; kc0 += PF) {
 #pragma unroll
-            for (int i = tid; i < NT * 8; i += GM_TC_THREADS) cp_async16(dst + 16 * i, src + 16 * i);
-        }
-        cp_async_commit();
-    };
-
-    // Software pipeline: the weight words of the next GM_WPF stages are in flight in registers
-    // (a stage's 68-byte row pieces come from HBM, so one stage of lookahead leaves the loads
-    // latency-bound), and the activations of stage kc + XS - 1 are requested as soon as the
-    // MMAs of stage kc - 1 (the previous user of that ring slot) have completed.  Every
-    // iteration commits one cp.async group (empty past the last stage), so that "stage kc has
-    // landed" is always "at most XS - 2 younger groups pending".
-    bool ok = true;
-    int last_kc = -1;  // the last stage whose MMAs were issued
-    for (int i = 0; i < XS - 1; ++i) {
-        if (i < nk) load_x(i, kb + i);
-        else cp_async_commit();
-    }
-    // Stage kc's weight words sit in slot kc % PF: the k loop is unrolled by PF so every slot
-    // index is static (registers) and a slot is refilled right after its dequantisation, PF
-    // stages ahead of its use (a shift of the slots would wait on the newest load every stage).
-    for (int kc0 = 0; kc0 < nk && ok; kc0 += PF) {
-#pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int kc = kc0 + u;
-            if (kc < nk && ok) {
-                const int s = kc & 1;
-                // dequantise the held weight words into stage s (free: its previous MMAs
-                // completed before load_x refilled it)
-                if constexpr (Q4) {
-                    if (wjh == 0) gm_dequant16_q4_t<0, 0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 0});
-                    else if (wjh == 1) gm_dequant16_q4_t<0, 1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16});
-                    else if (wjh == 2) gm_dequant16_q4_t<1, 0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 32});
-                    else gm_dequant16_q4_t<1, 1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 48});
-                } else {
-                    if (wjh < 2) gm_dequant16_t<0>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
-                    else gm_dequant16_t<1>(wbuf[u], wscale, wh(s), wl(s), KintRow{wr, 16 * wjh});
-                }
-                if (kc + PF < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
-                asm volatile("cp.async.wait_group %0;" ::"n"(XS - 2) : "memory");  // stage kc's activations
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // visible to the tensor cores
-                __syncthreads();
-                last_kc = kc;
-                const int xb = kc % XS;
-                if (tid == 0) {
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(xb)),
-                                   bl = smem_u32(xl(xb));
-#pragma unroll
-                    for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
-                        const uint32_t o = 32u * j;
-                        umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
-                                 (kc > 0 || j > 0) ? 1u : 0u);
-                        umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
-                        umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
+            for (int u = 0; u < PF; ++u) {
+                const int kc = kc0 + u;
+                if (kc < nk && ok) {
+                    const int s = kc & 1;
+                    // buffer s was last read by the MMAs of stage kc - 2
+                    if (kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+                    if (ok) {
+                        gm_dequant16_u<Q4>(wbuf[u], (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, wh(s), wl(s),
+                                           off0, off1);
+                        if (kc + PF < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
+                        // the stores become visible to the tensor cores' reads, then the warp arrives
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&wready[s]);
                     }
-                    umma_commit(&done[s]);
                 }
-                if (kc + 1 < nk) {
-                    // weight stage s ^ 1 and activation slot (kc - 1) % XS were last read by the
-                    // MMAs of stage kc - 1
-                    if (kc >= 1) ok = mbar_wait(&done[s ^ 1], ((kc - 1) >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag);
-                }
-                // (slot (kc + XS - 1) % XS: at kc = 0 the one slot the prologue left unused)
-                if (ok && kc + XS - 1 < nk) load_x((kc + XS - 1) % XS, kb + kc + XS - 1);
-                else cp_async_commit();
             }
         }
+    } else if (warp == GM_DQ_THREADS / 32) {
+        // ---- activation copies: stage kc into ring slot kc % XS (two bulk copies) ----
+        pdl_trigger();
+        pdl_wait();
+        if (lane == 0) {
+            const size_t xstride = (size_t)a.mp * (GM_BK * 2);
+            const uint8_t* xhs = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
+            const uint8_t* xls = reinterpret_cast<const uint8_t*>(a.xl) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
+            int issued = 0;
+            for (int kc = 0; kc < nk; ++kc) {
+                const int b = kc % XS;
+                if (kc >= XS && !mbar_wait(&xempty[b], ((kc / XS) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
+                mbar_expect_tx(&xfull[b], 2 * XH);
+                bulk_g2s(xh(b), xhs + (size_t)kc * xstride, XH, &xfull[b]);
+                bulk_g2s(xh(b) + XH, xls + (size_t)kc * xstride, XH, &xfull[b]);
+                ++issued;
+            }
+            // copies in flight land before the buffers are reused (only pending after an abort)
+            for (int kc = issued > XS ? issued - XS : 0; kc < issued; ++kc)
+                mbar_wait(&xfull[kc % XS], (kc / XS) & 1, nullptr, 0, nullptr);
+        }
+        __syncwarp();  // the other lanes wait here without issuing, not in a polling loop
+    } else {
+        // ---- MMA issue: one thread ----
+        pdl_trigger();
+        pdl_wait();
+        if (lane == 0) {
+            // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
+            const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
+            for (int kc = 0; kc < nk; ++kc) {
+                const int s = kc & 1, b = kc % XS;
+                if (!mbar_wait(&wready[s], (kc >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
+                if (!mbar_wait(&xfull[b], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(b)), bl = bh + XH;
+#pragma unroll
+                for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
+                    const uint32_t o = 32u * j;
+                    umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
+                             (kc > 0 || j > 0) ? 1u : 0u);
+                    umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
+                    umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
+                }
+                umma_commit(&wfree[s]);
+                umma_commit(&xempty[b]);
+            }
+            umma_commit(mma_done);  // arrives once every MMA issued above has completed
+        }
+        __syncwarp();
     }
-    cp_async_wait_all();  // no copy may still land in the buffers the epilogue reuses
-    // the last stage's commit covers every MMA issued before it
-    if (last_kc >= 0 && !mbar_wait(&done[last_kc & 1], (last_kc >> 1) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
+    // (not cut short by an abort: TMEM stays allocated until every issued MMA has completed)
+    if (!mbar_wait(mma_done, 0, a.err, ERR_WAIT_FULL, nullptr)) *abort_flag = 1;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     __syncthreads();
+    const bool ok = *abort_flag == 0 && nk > 0;
 
     // ---- epilogue: TMEM -> registers -> scaled tile[m][n] in shared memory ----
     float* tile = reinterpret_cast<float*>(smem);  // [NT][GM_EPI_LD], the pipeline buffers are free
@@ -655,19 +517,16 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
         colsc[tid] = (ok && m < a.M) ? ldexpf(1.0f, -(a.sw + a.sx[m])) : 0.f;
     }
     __syncthreads();
-    {
-        const int row = 32 * (warp & 3) + lane;           // weight row of this thread's TMEM lane
-        const int c0 = (warp >> 2) * (NT / 4);             // four column groups of warps
+    if (warp < 16) {  // sixteen warps: four TMEM lane quarters x four column groups
+        const int row = 32 * (warp & 3) + lane;  // weight row of this thread's TMEM lane
+        const int c0 = (warp >> 2) * (NT / 4);
         if constexpr (NT / 4 >= 16) {
             for (int c = c0; c < c0 + NT / 4; c += 16) {
                 uint32_t r[16];
                 tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    const int mm = c + u;
-                    tile[mm * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[mm];
-                }
+                for (int u = 0; u < 16; ++u) tile[(c + u) * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[c + u];
             }
         } else {  // NT = 32: eight columns per warp
             uint32_t r[8];

@@ -19,7 +19,9 @@ namespace tfb {
 constexpr int GM_BN = 128;      // weight rows per CTA
 constexpr int GM_BM = 128;      // activation rows per CTA
 constexpr int GM_BK = 64;       // k per pipeline stage (two Q8_0 blocks)
-constexpr int GM_TC_THREADS = 512;  // tcgen05 kernel: 4 threads per weight row (16 weights each)
+constexpr int GM_DQ_THREADS = 512;  // tcgen05 kernel: dequantising threads, 4 per weight row
+constexpr int GM_TC_THREADS = GM_DQ_THREADS + 64;  // + an activation-copy warp and an MMA warp
+constexpr int GM_TC_TAIL = 256;     // tcgen05 kernel: shared bytes of barriers and flags
 constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
 constexpr int GM_WPF = 4;       // tcgen05 GEMM: weight stages in flight per thread (registers)
 
