@@ -3,18 +3,22 @@
 // Default path, tf_gemm_q8_tc_kernel (5th-gen tensor cores): a CTA owns 128 weight rows x NT
 // (32, 64, 128 or 256) activation rows, k in stages of 64, in 128-byte swizzled K-major shared
 // memory, with its warps in three roles synchronised by mbarriers (no CTA-wide barrier per
-// stage).  Sixteen dequantising warps, four threads per weight row, turn 16-weight pieces held
-// in registers (the words of a stage are requested four stages ahead, the first ones before
-// the PDL wait) into exact f16 halves Wh, Wl of q*d*2^sw in one of two weight buffers; one
-// warp bulk-copies the activation halves Xh, Xl (prepared once per matmul by tf_xprep_kernel
-// in the operand layout) into a ring of stages; one thread issues tcgen05.mma (kind::f16, fp32
-// accumulator in TMEM) three times per k step: Wh*Xh, Wh*Xl, Wl*Xh, and commits each stage to
-// the barriers that free its buffers.  The epilogue reads TMEM, scales back by 2^-(sw+sx[m])
-// (per-column factors computed once), stages the tile in shared memory and, when the k range
-// is split, sums the splits of the tile through distributed shared memory of their
-// thread-block cluster in split order;
+// stage).  Sixteen dequantising warps, four threads per weight row, turn 16-weight pieces into
+// exact f16 halves Wh, Wl of q*d*2^sw in one of two weight buffers; their quantised words come
+// either (WT: K a multiple of 256, tiles up to 128 rows) from a ring of chunks of four stages,
+// each one 2-D tensor-map copy of the tile's 128 rows, or from global memory into registers
+// four stages ahead.  One warp issues those copies and the bulk copies of the activation halves
+// Xh, Xl (prepared once per matmul by tf_xprep_kernel in the operand layout); one thread
+// issues tcgen05.mma (kind::f16, fp32 accumulator in TMEM) three times per k step: Wh*Xh,
+// Wh*Xl, Wl*Xh, and commits each stage to the barriers that free its buffers.  The epilogue
+// reads TMEM, scales back by 2^-(sw+sx[m]) (per-column factors computed once), stages the tile
+// in shared memory and, when the k range is split, sums the splits of the tile through
+// distributed shared memory of their thread-block cluster in split order;
 // then the fused epilogue (bias, residual add, SwiGLU on interleaved gate/up rows, logits +
 // greedy argmax keys).
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <cstdlib>
 
@@ -357,41 +361,65 @@ template <int NT>
 constexpr size_t gemm_x_stage_bytes() {
     return (size_t)2 * NT * GM_BK * 2;
 }
-template <int NT>
-constexpr int gemm_x_stages() {
-    return NT <= 32 ? 8 : NT <= 64 ? 6 : NT <= 128 ? 4 : 2;
+// WT (weights by tensor-map copy, K % 256 == 0): the quantised rows arrive in chunks of GM_WCH
+// stages (4 x 68 = 272 bytes of a Q8_0 row, 4 x 36 = 144 of a Q4_0 row: 16-byte multiples), one
+// 2-D copy of 128 rows per chunk, into a ring of gemm_raw_chunks chunks; without WT every
+// dequantising thread loads its words from global memory into registers.
+constexpr int GM_WCH = 4;
+template <bool Q4>
+constexpr uint32_t gemm_chunk_bytes() {
+    return (uint32_t)GM_BN * GM_WCH * (Q4 ? 36 : 68);
 }
-template <int NT>
+template <int NT, bool WT>
+constexpr int gemm_x_stages() {
+    return WT ? (NT <= 32 ? 4 : NT <= 64 ? 3 : 2) : (NT <= 32 ? 8 : NT <= 64 ? 6 : NT <= 128 ? 4 : 2);
+}
+template <int NT, bool Q4, bool WT>
+constexpr int gemm_raw_chunks() {
+    return !WT ? 0 : Q4 ? (NT <= 64 ? 4 : 3) : (NT <= 64 ? 3 : 2);
+}
+template <int NT, bool Q4, bool WT>
 constexpr size_t gemm_tc_smem_bytes() {
-    const size_t pipe = 2 * GM_WSTAGE + (size_t)gemm_x_stages<NT>() * gemm_x_stage_bytes<NT>();
+    const size_t pipe = 2 * GM_WSTAGE + (size_t)gemm_x_stages<NT, WT>() * gemm_x_stage_bytes<NT>() +
+                        (size_t)gemm_raw_chunks<NT, Q4, WT>() * gemm_chunk_bytes<Q4>();
     const size_t epi = (size_t)NT * GM_EPI_LD * 4 + (size_t)NT * 4;  // tile + column scales
     return (pipe > epi ? pipe : epi) + GM_TC_TAIL + 1024;  // + mbarriers, TMEM address, 1024-B alignment
 }
 
-template <int NT, bool Q4>
-__global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const GemmArgs a) {
+template <int NT, bool Q4, bool WT>
+__global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const GemmArgs a,
+                                                                         const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // the swizzle atoms need 1024-byte aligned stage buffers
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * GM_BN, m0 = blockIdx.y * NT;
     const int nk_all = a.K / GM_BK;
-    const int kb = (int)((long long)nk_all * blockIdx.z / gridDim.z);
-    const int nk = (int)((long long)nk_all * (blockIdx.z + 1) / gridDim.z) - kb;
+    // the k range of this split (whole chunks with WT)
+    const int ku = WT ? GM_WCH : 1, nu = nk_all / ku;
+    const int kb = ku * (int)((long long)nu * blockIdx.z / gridDim.z);
+    const int nk = ku * (int)((long long)nu * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
-    constexpr int XS = gemm_x_stages<NT>();
+    constexpr int XS = gemm_x_stages<NT, WT>();
+    constexpr int RC = gemm_raw_chunks<NT, Q4, WT>();
+    constexpr int RCd = RC > 0 ? RC : 1;  // (divisor in code only the WT instantiations run)
+    constexpr int UB = Q4 ? 36 : 68;               // bytes of a row's 64-weight stage
+    constexpr uint32_t RB = GM_WCH * UB;           // bytes of a row's chunk
     constexpr uint32_t XH = NT * GM_BK * 2;  // bytes of one activation half of a stage
-    uint8_t* tail = smem + gemm_tc_smem_bytes<NT>() - GM_TC_TAIL - 1024;
+    uint8_t* tail = smem + gemm_tc_smem_bytes<NT, Q4, WT>() - GM_TC_TAIL - 1024;
     uint64_t* wready = reinterpret_cast<uint64_t*>(tail);  // [2] weight stage written (dequant warps)
     uint64_t* wfree = wready + 2;                          // [2] its MMAs completed
     uint64_t* xfull = wfree + 2;                           // [XS] activation stage landed
     uint64_t* xempty = xfull + XS;                         // [XS] its MMAs completed
     uint64_t* mma_done = xempty + XS;                      // every MMA completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+    uint64_t* rfull = mma_done + 1;                        // [RC] weight chunk landed (WT)
+    uint64_t* rempty = rfull + RC;                         // [RC] chunk read by the dequantising warps
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     auto wh = [&](int s) { return smem + (size_t)s * GM_WSTAGE; };
     auto wl = [&](int s) { return smem + (size_t)s * GM_WSTAGE + GM_BN * GM_BK * 2; };
     auto xh = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * 2 * XH; };
+    auto raw = [&](int c) { return smem + 2 * GM_WSTAGE + (size_t)XS * 2 * XH + (size_t)c * gemm_chunk_bytes<Q4>(); };
 
     if (warp == 0) {  // TMEM for the NT x 128 fp32 accumulator (NT columns)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -408,6 +436,10 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
             mbar_init(&xempty[i], 1);
         }
         mbar_init(mma_done, 1);
+        for (int i = 0; i < RC; ++i) {
+            mbar_init(&rfull[i], 1);
+            mbar_init(&rempty[i], GM_DQ_THREADS / 32);
+        }
         *abort_flag = 0;
         mbar_fence_init();
     }
@@ -416,7 +448,35 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
 
-    if (warp < GM_DQ_THREADS / 32) {
+    if (WT && warp < GM_DQ_THREADS / 32) {
+        // ---- dequantising warps (WT): stage kc's words from the chunk ring ----
+        const int wr = tid >> 2, wjh = tid & 3;  // weight row, 16-weight piece (block, half)
+        const uint32_t off0 = kint_off(wr, 16 * wjh), off1 = kint_off(wr, 16 * wjh + 8);
+        const int sw0 = Q4 ? 4 * (wjh >> 1) : 8 * (wjh >> 1);  // word of the block's scale
+        const int ww0 = Q4 ? 4 * (wjh >> 1) : 4 * wjh;         // first of the piece's five words
+        pdl_trigger();
+        pdl_wait();
+        bool ok = true;
+        for (int kc = 0; kc < nk && ok; ++kc) {
+            const int s = kc & 1, ci = kc / GM_WCH, j = kc % GM_WCH, slot = ci % RCd;
+            if (j == 0) ok = mbar_wait(&rfull[slot], (ci / RCd) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            // buffer s was last read by the MMAs of stage kc - 2
+            if (ok && kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+            if (!ok) break;
+            const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw(slot) + wr * RB + j * UB);
+            uint32_t w[6];
+            w[0] = rw[sw0];
+#pragma unroll
+            for (int i = 0; i < 5; ++i) w[1 + i] = rw[ww0 + i];
+            gm_dequant16_u<Q4>(w, (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, wh(s), wl(s), off0, off1);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&wready[s]);
+                if (j == GM_WCH - 1) mbar_arrive(&rempty[slot]);  // the chunk's last stage is read
+            }
+        }
+    } else if (warp < GM_DQ_THREADS / 32) {
         // ---- dequantising warps: stage kc's weights into weight buffer kc & 1 ----
         // The weight words of the next GM_WPF stages are in flight in registers (a stage's
         // 68-byte row pieces come from HBM); the first ones are requested before the PDL wait.
@@ -451,6 +511,57 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                 }
             }
         }
+    } else if (WT && warp == GM_DQ_THREADS / 32) {
+        // ---- copies (WT): weight chunks (one 2-D tensor copy of the tile's 128 rows x RB bytes,
+        // rows past N filled with zeros; the first RC chunks before the PDL wait) and activation
+        // stages, issued by lane 0 ----
+        const int nch = nk / GM_WCH;
+        auto issue_chunk = [&](int c) {
+            if (lane != 0) return;
+            const int slot = c % RCd;
+            mbar_expect_tx(&rfull[slot], gemm_chunk_bytes<Q4>());
+            // x: the chunk's first 16-bit element of the row (a multiple of 8: 16-byte aligned)
+            const int x = (kb + c * GM_WCH) * UB / 2;
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    smem_u32(raw(slot))),
+                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(n0), "r"(smem_u32(&rfull[slot]))
+                : "memory");
+        };
+        const int pre = nch < RC ? nch : RC;
+        for (int c = 0; c < pre; ++c) issue_chunk(c);
+        int issued_c = pre;
+        pdl_trigger();
+        pdl_wait();
+        const size_t xstride = (size_t)a.mp * (GM_BK * 2);
+        const uint8_t* xhs = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
+        const uint8_t* xls = reinterpret_cast<const uint8_t*>(a.xl) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
+        int issued_x = 0;
+        for (int kc = 0; kc < nk; ++kc) {
+            if (kc > 0 && kc % GM_WCH == 0) {
+                // entering chunk ci: chunk ci + RC - 1 takes the slot that chunk ci - 1 held
+                const int cn = kc / GM_WCH + RC - 1;
+                if (cn < nch) {
+                    if (!mbar_wait(&rempty[cn % RCd], ((cn / RCd) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
+                    issue_chunk(cn);
+                    ++issued_c;
+                }
+            }
+            const int b = kc % XS;
+            if (kc >= XS && !mbar_wait(&xempty[b], ((kc / XS) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
+            if (lane == 0) {
+                mbar_expect_tx(&xfull[b], 2 * XH);
+                bulk_g2s(xh(b), xhs + (size_t)kc * xstride, XH, &xfull[b]);
+                bulk_g2s(xh(b) + XH, xls + (size_t)kc * xstride, XH, &xfull[b]);
+            }
+            ++issued_x;
+        }
+        // copies in flight land before the buffers are reused (only pending after an abort)
+        for (int kc = issued_x > XS ? issued_x - XS : 0; kc < issued_x; ++kc)
+            mbar_wait(&xfull[kc % XS], (kc / XS) & 1, nullptr, 0, nullptr);
+        for (int c = issued_c > RC ? issued_c - RC : 0; c < issued_c; ++c)
+            mbar_wait(&rfull[c % RCd], (c / RCd) & 1, nullptr, 0, nullptr);
+        __syncwarp();
     } else if (warp == GM_DQ_THREADS / 32) {
         // ---- activation copies: stage kc into ring slot kc % XS (two bulk copies) ----
         pdl_trigger();
@@ -618,53 +729,102 @@ int gemm_tile_rows(int M) {
 bool gemm_takes_q4() { return true; }
 
 
+// The tensor map of a weight matrix for the WT path: 16-bit elements, rows of rb / 2 elements
+// rb bytes apart, boxes of one chunk (GM_WCH stages) x 128 rows; rows past N read as zeros.
+static bool gemm_weight_map(CUtensorMap* m, const GemmArgs& a) {
+    static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    if (!enc) return false;
+    const int ub = a.wq4 ? 36 : 68;
+    const cuuint64_t dims[2] = {(cuuint64_t)(a.rb / 2), (cuuint64_t)a.N};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.rb};
+    const cuuint32_t box[2] = {(cuuint32_t)(GM_WCH * ub / 2), (cuuint32_t)GM_BN};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<uint8_t*>(a.W), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool gemm_wt_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("TFB200_GEMM_WT");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v != 0;
+}
+
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
-    const int ks = a.ksplit > 1 ? a.ksplit : 1;
+    int ks = a.ksplit > 1 ? a.ksplit : 1;
     if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
-    {
-        GemmArgs aa = a;
-        aa.mp = gemm_x_rows(a.M);
-        void* args[] = {&aa};
-        const int nt = gemm_tile_rows(a.M);
-        const int wi = nt == 256 ? 3 : nt == 128 ? 2 : nt == 64 ? 1 : 0;
-        const bool q4 = a.wq4 != 0;
-        static const size_t sms[4] = {gemm_tc_smem_bytes<32>(), gemm_tc_smem_bytes<64>(), gemm_tc_smem_bytes<128>(),
-                                      gemm_tc_smem_bytes<256>()};
-        static const void* fns[4][2] = {
-            {(const void*)tf_gemm_q8_tc_kernel<32, false>, (const void*)tf_gemm_q8_tc_kernel<32, true>},
-            {(const void*)tf_gemm_q8_tc_kernel<64, false>, (const void*)tf_gemm_q8_tc_kernel<64, true>},
-            {(const void*)tf_gemm_q8_tc_kernel<128, false>, (const void*)tf_gemm_q8_tc_kernel<128, true>},
-            {(const void*)tf_gemm_q8_tc_kernel<256, false>, (const void*)tf_gemm_q8_tc_kernel<256, true>}};
-        const size_t sm = sms[wi];
-        const void* fn = fns[wi][q4];
-        static bool tc_attr[64][4][2] = {};
-        int dv = 0;
-        cudaGetDevice(&dv);
-        if (dv < 0 || dv >= 64) dv = 0;
-        if (!tc_attr[dv][wi][q4]) {
-            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-            if (e != cudaSuccess) return e;
-            tc_attr[dv][wi][q4] = true;
-        }
-        // the k splits of a tile form one cluster (their reduction goes through distributed
-        // shared memory)
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks);
-        cfg.blockDim = dim3(GM_TC_THREADS);
-        cfg.dynamicSmemBytes = sm;
-        cfg.stream = st;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        attr[1].id = cudaLaunchAttributeClusterDimension;
-        attr[1].val.clusterDim.x = 1;
-        attr[1].val.clusterDim.y = 1;
-        attr[1].val.clusterDim.z = (unsigned)ks;
-        cfg.attrs = attr;
-        cfg.numAttrs = 2;
-        return cudaLaunchKernelExC(&cfg, fn, args);
+    GemmArgs aa = a;
+    aa.mp = gemm_x_rows(a.M);
+    alignas(64) CUtensorMap wmap;
+    memset(&wmap, 0, sizeof(wmap));
+    void* args[] = {&aa, &wmap};
+    const int nt = gemm_tile_rows(a.M);
+    const int wi = nt == 256 ? 3 : nt == 128 ? 2 : nt == 64 ? 1 : 0;
+    const bool q4 = a.wq4 != 0;
+    // weights by bulk copy: rows 16-byte aligned, whole chunks per split (tiles up to 128 rows:
+    // the 256-row tile's activation stages leave no room for the chunk ring)
+    const int nch = a.K / (GM_BK * GM_WCH);
+    const bool wt = gemm_wt_enabled() && nt <= 128 && a.K % (GM_BK * GM_WCH) == 0 && a.rb % 16 == 0 &&
+                    (reinterpret_cast<uintptr_t>(a.W) & 15) == 0 && nch > 0 && gemm_weight_map(&wmap, a);
+    if (wt && ks > nch) ks = nch;
+    static const size_t sms[4][2][2] = {
+        {{gemm_tc_smem_bytes<32, false, false>(), gemm_tc_smem_bytes<32, false, true>()},
+         {gemm_tc_smem_bytes<32, true, false>(), gemm_tc_smem_bytes<32, true, true>()}},
+        {{gemm_tc_smem_bytes<64, false, false>(), gemm_tc_smem_bytes<64, false, true>()},
+         {gemm_tc_smem_bytes<64, true, false>(), gemm_tc_smem_bytes<64, true, true>()}},
+        {{gemm_tc_smem_bytes<128, false, false>(), gemm_tc_smem_bytes<128, false, true>()},
+         {gemm_tc_smem_bytes<128, true, false>(), gemm_tc_smem_bytes<128, true, true>()}},
+        {{gemm_tc_smem_bytes<256, false, false>(), 0}, {gemm_tc_smem_bytes<256, true, false>(), 0}}};
+    static const void* fns[4][2][2] = {
+        {{(const void*)tf_gemm_q8_tc_kernel<32, false, false>, (const void*)tf_gemm_q8_tc_kernel<32, false, true>},
+         {(const void*)tf_gemm_q8_tc_kernel<32, true, false>, (const void*)tf_gemm_q8_tc_kernel<32, true, true>}},
+        {{(const void*)tf_gemm_q8_tc_kernel<64, false, false>, (const void*)tf_gemm_q8_tc_kernel<64, false, true>},
+         {(const void*)tf_gemm_q8_tc_kernel<64, true, false>, (const void*)tf_gemm_q8_tc_kernel<64, true, true>}},
+        {{(const void*)tf_gemm_q8_tc_kernel<128, false, false>, (const void*)tf_gemm_q8_tc_kernel<128, false, true>},
+         {(const void*)tf_gemm_q8_tc_kernel<128, true, false>, (const void*)tf_gemm_q8_tc_kernel<128, true, true>}},
+        {{(const void*)tf_gemm_q8_tc_kernel<256, false, false>, nullptr},
+         {(const void*)tf_gemm_q8_tc_kernel<256, true, false>, nullptr}}};
+    const size_t sm = sms[wi][q4][wt];
+    const void* fn = fns[wi][q4][wt];
+    static bool tc_attr[64][4][2][2] = {};
+    int dv = 0;
+    cudaGetDevice(&dv);
+    if (dv < 0 || dv >= 64) dv = 0;
+    if (!tc_attr[dv][wi][q4][wt]) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) return e;
+        tc_attr[dv][wi][q4][wt] = true;
     }
+    // the k splits of a tile form one cluster (their reduction goes through distributed
+    // shared memory)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((a.N + GM_BN - 1) / GM_BN, (a.M + nt - 1) / nt, ks);
+    cfg.blockDim = dim3(GM_TC_THREADS);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = (unsigned)ks;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
 cudaError_t finish_launch(const FinishArgs& a, cudaStream_t st) {
