@@ -605,8 +605,10 @@ static int attn_stream_splits(const AttnArgs& a, int M) {
         waves = e ? atoi(e) : 1;
         if (waves < 1) waves = 1;
     }
+    // rounded down: a split count that leaves a partial second wave doubles the kernel's time
+    // (cfg4 at 32 rows x 1026 positions: 5 splits = 320 CTAs for 296 slots)
     const int pairs = M * a.n_kv;
-    int s = (waves * 2 * sms + pairs - 1) / pairs;
+    int s = waves * 2 * sms / pairs;
     return s < 1 ? 1 : (s > a.n_split ? a.n_split : s);
 }
 

@@ -42,6 +42,10 @@ __global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
     __shared__ float redf[8];
     const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nth = blockDim.x;
     const int K = a.K, nq = K >> 2;
+    // the GEMM that reads these operands may start its set-up and weight prefetch now; every
+    // read below waits for the kernel that wrote the input row
+    pdl_trigger();
+    pdl_wait();
     if (a.embd) {
         int tok = a.tokens[m];
         if (tok < 0 || tok >= a.n_vocab) {
@@ -702,8 +706,18 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     }
     XPrepArgs aa = a;
     aa.mp = gemm_x_rows(a.M);
-    tf_xprep_kernel<<<a.M, 256, smem, st>>>(aa);
-    return cudaGetLastError();
+    // programmatic dependent launch: the CTAs become resident while the previous kernel drains
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.M);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, tf_xprep_kernel, aa);
 }
 
 int gemm_x_rows(int M) {
