@@ -145,20 +145,19 @@ __device__ __forceinline__ void gm_load_w16(uint32_t (&w)[6], const GemmArgs& a,
     }
 }
 
-__device__ __forceinline__ uint32_t kint_off(int row, int k) { return gm_kint_off(row, k); }
 
 // One 16-weight piece of gm_load_w16's words into the exact f16 split, with packed half2
 // arithmetic and no per-element conversion: q is made exact in f16 from its byte (0x6400 |
 // (q + 128) is 1024 + q + 128; Q4_0: (0x6400 | nibble) - 1032 is nibble - 8), Wh = q * dh rounds
 // the exact product once (dh = d * 2^sw, an f16 value; at most 19 significant bits for Q8_0, 15
 // for Q4_0), and Wl = fma(q, dh, -Wh) is the exact remainder.  One instruction stream for every
-// lane of a warp (the lanes hold pieces of both blocks of a stage, and of both nibble halves
+// lane of a warp (the lanes hold pieces of either block of a stage, and of either nibble half
 // for Q4_0): the pieces of block 1 start two bytes later in their five window words, so a
 // funnel shift by 16 bits (0 for block 0) aligns both, and the nibble half is a shift by
-// 4 * half.  off0 / off1: the byte offsets of the piece's two 8-half groups.
+// 4 * half.  hv / lv: the piece's 16 halves in k order, two per word (even k in the low half).
 template <bool Q4>
-__device__ __forceinline__ void gm_dequant16_u(const uint32_t (&w)[6], uint32_t blk, uint32_t half, float wscale,
-                                               uint8_t* dh, uint8_t* dl, uint32_t off0, uint32_t off1) {
+__device__ __forceinline__ void gm_dequant16_r(const uint32_t (&w)[6], uint32_t blk, uint32_t half, float wscale,
+                                               uint32_t (&hv)[8], uint32_t (&lv)[8]) {
     const uint32_t sh = blk << 4;
     const uint32_t dbits = (w[0] >> sh) & 0xFFFFu;
     const __half dsc = __float2half_rn(__half2float(__ushort_as_half((unsigned short)dbits)) * wscale);
@@ -169,23 +168,24 @@ __device__ __forceinline__ void gm_dequant16_u(const uint32_t (&w)[6], uint32_t 
 #pragma unroll
     for (int i = 0; i < 5; ++i) q[i] = __funnelshift_r(w[1 + i], i < 4 ? w[2 + i] : 0u, sh);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        uint32_t hv[4], lv[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const int b = 2 + 8 * c + e;  // the piece's bytes are 2 .. 17 of the aligned window
-            const uint32_t wd = Q4 ? ((q[b >> 2] >> (half << 2)) & 0x0F0F0F0Fu) : (q[b >> 2] ^ 0x80808080u);
-            const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
-            const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
-            const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), kq);
-            const __half2 hi = __hmul2(q2, d2);
-            const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
-            hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
-            lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
-        }
-        *reinterpret_cast<uint4*>(dh + (c ? off1 : off0)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(dl + (c ? off1 : off0)) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+    for (int e = 0; e < 16; e += 2) {
+        const int b = 2 + e;  // the piece's bytes are 2 .. 17 of the aligned window
+        const uint32_t wd = Q4 ? ((q[b >> 2] >> (half << 2)) & 0x0F0F0F0Fu) : (q[b >> 2] ^ 0x80808080u);
+        const uint32_t sel = (uint32_t)(b & 3) | (4u << 4) | ((uint32_t)((b & 3) + 1) << 8) | (4u << 12);
+        const uint32_t qb = __byte_perm(wd, 0x64646464u, sel);
+        const __half2 q2 = __hsub2(*reinterpret_cast<const __half2*>(&qb), kq);
+        const __half2 hi = __hmul2(q2, d2);
+        const __half2 lo = __hfma2(q2, d2, __hneg2(hi));
+        hv[e >> 1] = *reinterpret_cast<const uint32_t*>(&hi);
+        lv[e >> 1] = *reinterpret_cast<const uint32_t*>(&lo);
     }
+}
+
+// eight consecutive 32-bit tensor-memory columns of this thread's lane (the warp's lane quarter)
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 
 // Split-K reduction and the fused epilogue over a CTA tile staged in shared memory as
@@ -332,13 +332,16 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t saddr) {
     return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc) {
+// the same with the A operand (the weights) in tensor memory: lane r holds row r, column c the
+// k pair (2c, 2c + 1) of the instruction's 16 k values
+__device__ __forceinline__ void umma_f16_ta(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n"
         :
-        : "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+        : "r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -357,10 +360,31 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr));
 }
 
-// Shared memory of the tcgen05 GEMM: two weight stages (Wh, Wl: the tensor cores read one
-// while the dequantising warps write the next) and a ring of gemm_x_stages activation stages
-// (Xh, Xl), whose bulk copies run that many stages ahead of the MMAs.
-constexpr size_t GM_WSTAGE = (size_t)2 * GM_BN * GM_BK * 2;
+// Shared memory of the tcgen05 GEMM: a ring of gemm_x_stages activation stages (Xh, Xl), whose
+// bulk copies run that many stages ahead of the MMAs, and (WT) the ring of quantised weight
+// chunks.  The dequantised weights (Wh, Wl of two k stages: the tensor cores read one while the
+// dequantising warps write the next) live in tensor memory beside the accumulator, so the
+// tensor cores' reads of the A operand and the dequantising warps' writes take no
+// shared-memory bandwidth.
+// Accumulators: for tiles up to 128 rows one per product of the split, Wh*Xh, Wh*Xl and Wl*Xh,
+// side by side, so that the first two come from one MMA whose B operand is the stage's Xh and Xl
+// halves together (2 NT rows, contiguous in shared memory): two MMAs per k step instead of three
+// (at a few rows an MMA's cost barely depends on its N).  The 256-row tile keeps one
+// accumulator and three MMAs (N is at its limit).  The epilogue sums the accumulators.
+template <int NT>
+constexpr int gemm_n_acc() {
+    return NT <= 128 ? 3 : 1;
+}
+// tensor-memory columns: the accumulators' NT columns each, then per weight buffer Wh (32
+// columns: 128 rows x 64 halves) and Wl (32); allocated as a power of two
+template <int NT>
+constexpr uint32_t gemm_acc_cols() {
+    return (uint32_t)(gemm_n_acc<NT>() * NT);
+}
+template <int NT>
+constexpr uint32_t gemm_tmem_cols() {
+    return gemm_acc_cols<NT>() + 2 * 64 <= 256 ? 256u : 512u;
+}
 template <int NT>
 constexpr size_t gemm_x_stage_bytes() {
     return (size_t)2 * NT * GM_BK * 2;
@@ -384,10 +408,15 @@ constexpr int gemm_raw_chunks() {
 }
 template <int NT, bool Q4, bool WT>
 constexpr size_t gemm_tc_smem_bytes() {
-    const size_t pipe = 2 * GM_WSTAGE + (size_t)gemm_x_stages<NT, WT>() * gemm_x_stage_bytes<NT>() +
+    const size_t pipe = (size_t)gemm_x_stages<NT, WT>() * gemm_x_stage_bytes<NT>() +
                         (size_t)gemm_raw_chunks<NT, Q4, WT>() * gemm_chunk_bytes<Q4>();
     const size_t epi = (size_t)NT * GM_EPI_LD * 4 + (size_t)NT * 4;  // tile + column scales
-    return (pipe > epi ? pipe : epi) + GM_TC_TAIL + 1024;  // + mbarriers, TMEM address, 1024-B alignment
+    // at least enough to keep a third CTA (a second with 512 columns) off the SM: tcgen05.alloc
+    // waits while the SM's 512 columns are taken, and a waiting CTA must not hold up the other
+    // k splits of its cluster
+    const size_t floor = gemm_tmem_cols<NT>() > 256 ? (size_t)120 * 1024 : (size_t)80 * 1024;
+    const size_t need = (pipe > epi ? pipe : epi) + GM_TC_TAIL + 1024;  // + mbarriers, TMEM address, alignment
+    return need > floor ? need : floor;
 }
 
 template <int NT, bool Q4, bool WT>
@@ -411,7 +440,9 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     constexpr uint32_t RB = GM_WCH * UB;           // bytes of a row's chunk
     constexpr uint32_t XH = NT * GM_BK * 2;  // bytes of one activation half of a stage
     uint8_t* tail = smem + gemm_tc_smem_bytes<NT, Q4, WT>() - GM_TC_TAIL - 1024;
-    uint64_t* wready = reinterpret_cast<uint64_t*>(tail);  // [2] weight stage written (dequant warps)
+    // [2] weight stage written (dequant warps; warp 0 arrives only once it has also seen the
+    // stage's activations land, so this one barrier is all the MMA thread waits on)
+    uint64_t* wready = reinterpret_cast<uint64_t*>(tail);
     uint64_t* wfree = wready + 2;                          // [2] its MMAs completed
     uint64_t* xfull = wfree + 2;                           // [XS] activation stage landed
     uint64_t* xempty = xfull + XS;                         // [XS] its MMAs completed
@@ -420,14 +451,18 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     uint64_t* rempty = rfull + RC;                         // [RC] chunk read by the dequantising warps
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rempty + RC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    auto wh = [&](int s) { return smem + (size_t)s * GM_WSTAGE; };
-    auto wl = [&](int s) { return smem + (size_t)s * GM_WSTAGE + GM_BN * GM_BK * 2; };
-    auto xh = [&](int b) { return smem + 2 * GM_WSTAGE + (size_t)b * 2 * XH; };
-    auto raw = [&](int c) { return smem + 2 * GM_WSTAGE + (size_t)XS * 2 * XH + (size_t)c * gemm_chunk_bytes<Q4>(); };
+    const bool trc = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+    auto stamp = [&](int i) {
+        if (trc) a.trace[i] = (unsigned long long)clock64();
+    };
+    if (tid == 0) stamp(0);
+    auto xh = [&](int b) { return smem + (size_t)b * 2 * XH; };
+    auto raw = [&](int c) { return smem + (size_t)XS * 2 * XH + (size_t)c * gemm_chunk_bytes<Q4>(); };
+    constexpr uint32_t TCOLS = gemm_tmem_cols<NT>();
 
-    if (warp == 0) {  // TMEM for the NT x 128 fp32 accumulator (NT columns)
+    if (warp == 0) {  // TMEM: the NT x 128 fp32 accumulator (NT columns) and the two weight buffers
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(NT));
+                     "r"(TCOLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     if (tid == GM_DQ_THREADS) {
@@ -451,11 +486,16 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    if (tid == 0) stamp(1);
 
+    // dequantising warp w: weight rows 32 (w % 4) + lane (its tensor-memory lane quarter), the
+    // stage's 16-weight piece w / 4 (block, half: the MMA k step it feeds); its Wh / Wl words go to
+    // tensor-memory columns AC + 64 s + (0 | 32) + 8 * piece of weight buffer s
+    constexpr uint32_t AC = gemm_acc_cols<NT>();  // first column of the weight buffers
+    const uint32_t tq = tmem + ((uint32_t)(32 * (warp & 3)) << 16) + AC + 8u * (uint32_t)(warp >> 2);
     if (WT && warp < GM_DQ_THREADS / 32) {
         // ---- dequantising warps (WT): stage kc's words from the chunk ring ----
-        const int wr = tid >> 2, wjh = tid & 3;  // weight row, 16-weight piece (block, half)
-        const uint32_t off0 = kint_off(wr, 16 * wjh), off1 = kint_off(wr, 16 * wjh + 8);
+        const int wr = 32 * (warp & 3) + lane, wjh = warp >> 2;  // weight row, 16-weight piece (block, half)
         const int sw0 = Q4 ? 4 * (wjh >> 1) : 8 * (wjh >> 1);  // word of the block's scale
         const int ww0 = Q4 ? 4 * (wjh >> 1) : 4 * wjh;         // first of the piece's five words
         pdl_trigger();
@@ -464,20 +504,34 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
         for (int kc = 0; kc < nk && ok; ++kc) {
             const int s = kc & 1, ci = kc / GM_WCH, j = kc % GM_WCH, slot = ci % RCd;
             if (j == 0) ok = mbar_wait(&rfull[slot], (ci / RCd) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            const bool tk = tid == 0 && kc < GM_TR_MAXK;
+            if (tk) stamp(GM_TR_DQ + 4 * kc);
             // buffer s was last read by the MMAs of stage kc - 2
             if (ok && kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+            if (ok && warp == 0) ok = mbar_wait(&xfull[kc % XS], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+            if (tk) stamp(GM_TR_DQ + 4 * kc + 1);
+            ok = __all_sync(0xffffffffu, ok);  // the tensor-memory stores below are warp-wide
             if (!ok) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t* rw = reinterpret_cast<const uint32_t*>(raw(slot) + wr * RB + j * UB);
-            uint32_t w[6];
+            uint32_t w[6], hv[8], lv[8];
             w[0] = rw[sw0];
 #pragma unroll
             for (int i = 0; i < 5; ++i) w[1 + i] = rw[ww0 + i];
-            gm_dequant16_u<Q4>(w, (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, wh(s), wl(s), off0, off1);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            gm_dequant16_r<Q4>(w, (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, hv, lv);
+            tmem_st8(tq + 64u * (uint32_t)s, hv);
+            tmem_st8(tq + 64u * (uint32_t)s + 32u, lv);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&wready[s]);
                 if (j == GM_WCH - 1) mbar_arrive(&rempty[slot]);  // the chunk's last stage is read
+                if (trc && kc < GM_TR_MAXK) {  // warp 0's arrival; the last arrival and its warp
+                    const unsigned long long t = (unsigned long long)clock64();
+                    if (warp == 0) a.trace[GM_TR_DQ + 4 * kc + 2] = t;
+                    atomicMax(&a.trace[GM_TR_DQ + 4 * kc + 3], (t << 5) | (unsigned long long)warp);
+                }
             }
         }
     } else if (warp < GM_DQ_THREADS / 32) {
@@ -485,8 +539,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
         // The weight words of the next GM_WPF stages are in flight in registers (a stage's
         // 68-byte row pieces come from HBM); the first ones are requested before the PDL wait.
         constexpr int PF = GM_WPF;
-        const int wr = tid >> 2, wjh = tid & 3;  // weight row, 16-weight piece (block, half)
-        const uint32_t off0 = kint_off(wr, 16 * wjh), off1 = kint_off(wr, 16 * wjh + 8);
+        const int wr = 32 * (warp & 3) + lane, wjh = warp >> 2;  // weight row, 16-weight piece (block, half)
         uint32_t wbuf[PF][6];                    // weight words of stage kc in slot kc % PF
 #pragma unroll
         for (int u = 0; u < PF; ++u)
@@ -503,74 +556,31 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                     const int s = kc & 1;
                     // buffer s was last read by the MMAs of stage kc - 2
                     if (kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+                    if (ok && warp == 0)
+                        ok = mbar_wait(&xfull[kc % XS], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+                    ok = __all_sync(0xffffffffu, ok);  // the tensor-memory stores below are warp-wide
                     if (ok) {
-                        gm_dequant16_u<Q4>(wbuf[u], (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, wh(s), wl(s),
-                                           off0, off1);
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        uint32_t hv[8], lv[8];
+                        gm_dequant16_r<Q4>(wbuf[u], (uint32_t)(wjh >> 1), (uint32_t)(wjh & 1), wscale, hv, lv);
                         if (kc + PF < nk) gm_load_w16<Q4>(wbuf[u], a, n0 + wr, kb + kc + PF, wjh);
-                        // the stores become visible to the tensor cores' reads, then the warp arrives
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        tmem_st8(tq + 64u * (uint32_t)s, hv);
+                        tmem_st8(tq + 64u * (uint32_t)s + 32u, lv);
+                        // the stores complete before the tensor cores read them, then the warp arrives
+                        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&wready[s]);
                     }
                 }
             }
         }
-    } else if (WT && warp == GM_DQ_THREADS / 32) {
-        // ---- copies (WT): weight chunks (one 2-D tensor copy of the tile's 128 rows x RB bytes,
-        // rows past N filled with zeros; the first RC chunks before the PDL wait) and activation
-        // stages, issued by lane 0 ----
-        const int nch = nk / GM_WCH;
-        auto issue_chunk = [&](int c) {
-            if (lane != 0) return;
-            const int slot = c % RCd;
-            mbar_expect_tx(&rfull[slot], gemm_chunk_bytes<Q4>());
-            // x: the chunk's first 16-bit element of the row (a multiple of 8: 16-byte aligned)
-            const int x = (kb + c * GM_WCH) * UB / 2;
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                    smem_u32(raw(slot))),
-                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(n0), "r"(smem_u32(&rfull[slot]))
-                : "memory");
-        };
-        const int pre = nch < RC ? nch : RC;
-        for (int c = 0; c < pre; ++c) issue_chunk(c);
-        int issued_c = pre;
-        pdl_trigger();
-        pdl_wait();
-        const size_t xstride = (size_t)a.mp * (GM_BK * 2);
-        const uint8_t* xhs = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
-        const uint8_t* xls = reinterpret_cast<const uint8_t*>(a.xl) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
-        int issued_x = 0;
-        for (int kc = 0; kc < nk; ++kc) {
-            if (kc > 0 && kc % GM_WCH == 0) {
-                // entering chunk ci: chunk ci + RC - 1 takes the slot that chunk ci - 1 held
-                const int cn = kc / GM_WCH + RC - 1;
-                if (cn < nch) {
-                    if (!mbar_wait(&rempty[cn % RCd], ((cn / RCd) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
-                    issue_chunk(cn);
-                    ++issued_c;
-                }
-            }
-            const int b = kc % XS;
-            if (kc >= XS && !mbar_wait(&xempty[b], ((kc / XS) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
-            if (lane == 0) {
-                mbar_expect_tx(&xfull[b], 2 * XH);
-                bulk_g2s(xh(b), xhs + (size_t)kc * xstride, XH, &xfull[b]);
-                bulk_g2s(xh(b) + XH, xls + (size_t)kc * xstride, XH, &xfull[b]);
-            }
-            ++issued_x;
-        }
-        // copies in flight land before the buffers are reused (only pending after an abort)
-        for (int kc = issued_x > XS ? issued_x - XS : 0; kc < issued_x; ++kc)
-            mbar_wait(&xfull[kc % XS], (kc / XS) & 1, nullptr, 0, nullptr);
-        for (int c = issued_c > RC ? issued_c - RC : 0; c < issued_c; ++c)
-            mbar_wait(&rfull[c % RCd], (c / RCd) & 1, nullptr, 0, nullptr);
-        __syncwarp();
-    } else if (warp == GM_DQ_THREADS / 32) {
+    } else if (warp == GM_X_WARP) {
         // ---- activation copies: stage kc into ring slot kc % XS (two bulk copies) ----
         pdl_trigger();
         pdl_wait();
         if (lane == 0) {
+            stamp(2);
             const size_t xstride = (size_t)a.mp * (GM_BK * 2);
             const uint8_t* xhs = reinterpret_cast<const uint8_t*>(a.xh) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
             const uint8_t* xls = reinterpret_cast<const uint8_t*>(a.xl) + (size_t)kb * xstride + (size_t)m0 * (GM_BK * 2);
@@ -578,6 +588,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
             for (int kc = 0; kc < nk; ++kc) {
                 const int b = kc % XS;
                 if (kc >= XS && !mbar_wait(&xempty[b], ((kc / XS) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
+                if (kc < GM_TR_MAXK) stamp(GM_TR_X + kc);
                 mbar_expect_tx(&xfull[b], 2 * XH);
                 bulk_g2s(xh(b), xhs + (size_t)kc * xstride, XH, &xfull[b]);
                 bulk_g2s(xh(b) + XH, xls + (size_t)kc * xstride, XH, &xfull[b]);
@@ -588,29 +599,79 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                 mbar_wait(&xfull[kc % XS], (kc / XS) & 1, nullptr, 0, nullptr);
         }
         __syncwarp();  // the other lanes wait here without issuing, not in a polling loop
-    } else {
+    } else if (warp == GM_W_WARP) {
+        // ---- weight chunks (WT): one 2-D tensor copy of the tile's 128 rows x RB bytes per chunk
+        // (rows past N filled with zeros) into ring slot c % RC, the first RC before the PDL wait;
+        // chunk c takes the slot once the dequantising warps have read chunk c - RC ----
+        if (WT && lane == 0) {
+            const int nch = nk / GM_WCH;
+            auto issue_chunk = [&](int c) {
+                const int slot = c % RCd;
+                if (c < GM_TR_DQ - GM_TR_CHUNK) stamp(GM_TR_CHUNK + c);
+                mbar_expect_tx(&rfull[slot], gemm_chunk_bytes<Q4>());
+                // x: the chunk's first 16-bit element of the row (a multiple of 8: 16-byte aligned)
+                const int x = (kb + c * GM_WCH) * UB / 2;
+                asm volatile(
+                    "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                        smem_u32(raw(slot))),
+                    "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(x), "r"(n0), "r"(smem_u32(&rfull[slot]))
+                    : "memory");
+            };
+            const int pre = nch < RC ? nch : RC;
+            for (int c = 0; c < pre; ++c) issue_chunk(c);
+            int issued = pre;
+            pdl_trigger();
+            pdl_wait();
+            for (int c = pre; c < nch; ++c) {
+                if (!mbar_wait(&rempty[c % RCd], ((c / RCd) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag)) break;
+                issue_chunk(c);
+                ++issued;
+            }
+            // copies in flight land before the buffers are reused (only pending after an abort)
+            for (int c = issued > RC ? issued - RC : 0; c < issued; ++c)
+                mbar_wait(&rfull[c % RCd], (c / RCd) & 1, nullptr, 0, nullptr);
+        } else {
+            pdl_trigger();
+            pdl_wait();
+        }
+        __syncwarp();
+    } else {  // warp == GM_MMA_WARP
         // ---- MMA issue: one thread ----
         pdl_trigger();
         pdl_wait();
         if (lane == 0) {
-            // instruction descriptor: D f32, A/B f16, both K-major, N = NT, M = 128
+            // instruction descriptors: D f32, A/B f16, both K-major, M = 128, N = NT (and 2 NT)
             const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
+            const uint32_t idesc2 = (1u << 4) | ((uint32_t)((2 * NT) >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
             for (int kc = 0; kc < nk; ++kc) {
                 const int s = kc & 1, b = kc % XS;
+                // the weights of stage kc are in buffer s, and (dequantising warp 0 saw it before
+                // it arrived) its activations in ring slot b
                 if (!mbar_wait(&wready[s], (kc >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
-                if (!mbar_wait(&xfull[b], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
+                if (kc < GM_TR_MAXK) stamp(GM_TR_MMA + 2 * kc);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t ah = smem_u32(wh(s)), al = smem_u32(wl(s)), bh = smem_u32(xh(b)), bl = bh + XH;
+                // Wh / Wl of buffer s in tensor memory (8 columns per k step), Xh / Xl in shared memory
+                // (a k step is 32 bytes along the lines: 2 in the descriptor's start-address field,
+                // which holds address >> 4 < 2^14 with room for the steps)
+                const uint32_t ah = tmem + AC + 64u * (uint32_t)s, al = ah + 32u;
+                const uint64_t dh = umma_desc_k_sw128(smem_u32(xh(b))), dl = umma_desc_k_sw128(smem_u32(xh(b)) + XH);
 #pragma unroll
-                for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps: 32 bytes along the lines
-                    const uint32_t o = 32u * j;
-                    umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bh + o), idesc,
-                             (kc > 0 || j > 0) ? 1u : 0u);
-                    umma_f16(tmem, umma_desc_k_sw128(ah + o), umma_desc_k_sw128(bl + o), idesc, 1u);
-                    umma_f16(tmem, umma_desc_k_sw128(al + o), umma_desc_k_sw128(bh + o), idesc, 1u);
+                for (int j = 0; j < GM_BK / 16; ++j) {  // 16-element k steps
+                    const uint32_t c = 8u * j;
+                    const uint32_t first = (kc > 0 || j > 0) ? 1u : 0u;
+                    if constexpr (gemm_n_acc<NT>() > 1) {
+                        // Wh * [Xh; Xl] into columns [0, 2 NT), Wl * Xh into [2 NT, 3 NT)
+                        umma_f16_ta(tmem, ah + c, dh + 2u * j, idesc2, first);
+                        umma_f16_ta(tmem + 2u * NT, al + c, dh + 2u * j, idesc, first);
+                    } else {
+                        umma_f16_ta(tmem, ah + c, dh + 2u * j, idesc, first);
+                        umma_f16_ta(tmem, ah + c, dl + 2u * j, idesc, 1u);
+                        umma_f16_ta(tmem, al + c, dh + 2u * j, idesc, 1u);
+                    }
                 }
                 umma_commit(&wfree[s]);
                 umma_commit(&xempty[b]);
+                if (kc < GM_TR_MAXK) stamp(GM_TR_MMA + 2 * kc + 1);
             }
             umma_commit(mma_done);  // arrives once every MMA issued above has completed
         }
@@ -618,6 +679,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     }
     // (not cut short by an abort: TMEM stays allocated until every issued MMA has completed)
     if (!mbar_wait(mma_done, 0, a.err, ERR_WAIT_FULL, nullptr)) *abort_flag = 1;
+    if (tid == 0) stamp(3);
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     __syncthreads();
     const bool ok = *abort_flag == 0 && nk > 0;
@@ -635,29 +697,40 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     if (warp < 16) {  // sixteen warps: four TMEM lane quarters x four column groups
         const int row = 32 * (warp & 3) + lane;  // weight row of this thread's TMEM lane
         const int c0 = (warp >> 2) * (NT / 4);
-        if constexpr (NT / 4 >= 16) {
+        const uint32_t tl = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+        if constexpr (gemm_n_acc<NT>() == 1) {
             for (int c = c0; c < c0 + NT / 4; c += 16) {
                 uint32_t r[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c, r);
+                tmem_ld16(tl + (uint32_t)c, r);
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
                 for (int u = 0; u < 16; ++u) tile[(c + u) * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[c + u];
             }
-        } else {  // NT = 32: eight columns per warp
-            uint32_t r[8];
-            tmem_ld8(tmem + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)c0, r);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        } else {  // the three accumulators: main product plus the sum of the two corrections
+            for (int c = c0; c < c0 + NT / 4; c += 8) {
+                uint32_t r0[8], r1[8], r2[8];
+                tmem_ld8(tl + (uint32_t)c, r0);
+                tmem_ld8(tl + (uint32_t)(NT + c), r1);
+                tmem_ld8(tl + (uint32_t)(2 * NT + c), r2);
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int u = 0; u < 8; ++u) tile[(c0 + u) * GM_EPI_LD + row] = __uint_as_float(r[u]) * colsc[c0 + u];
+                for (int u = 0; u < 8; ++u)
+                    tile[(c + u) * GM_EPI_LD + row] =
+                        (__uint_as_float(r0[u]) + (__uint_as_float(r1[u]) + __uint_as_float(r2[u]))) * colsc[c + u];
+            }
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT));
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS));
     // with k splits the cluster's barriers are kept even after an error (gemm_epilogue returns
     // after them); without, the error word holds the failure
     if (!ok && gridDim.z == 1) return;
     gemm_epilogue<NT, true, GM_TC_THREADS>(a, tile, m0, n0, ok);
+    if (trc) {
+        __syncthreads();
+        if (tid == 0) stamp(4);
+    }
 }
 
 // ---- end of a step at M rows ------------------------------------------------------------------
@@ -776,11 +849,15 @@ static bool gemm_wt_enabled() {
     return v != 0;
 }
 
+static unsigned long long* g_gemm_trace = nullptr;
+void gemm_set_trace(unsigned long long* buf) { g_gemm_trace = buf; }
+
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t st) {
     if (a.K % GM_BK || a.M <= 0 || a.N <= 0) return cudaErrorInvalidValue;
     int ks = a.ksplit > 1 ? a.ksplit : 1;
     if (ks > 1 && (!a.ws || !a.tile_cnt || ks > GM_MAX_SPLIT)) return cudaErrorInvalidValue;
     GemmArgs aa = a;
+    if (!aa.trace) aa.trace = g_gemm_trace;
     aa.mp = gemm_x_rows(a.M);
     alignas(64) CUtensorMap wmap;
     memset(&wmap, 0, sizeof(wmap));

@@ -20,7 +20,10 @@ constexpr int GM_BN = 128;      // weight rows per CTA
 constexpr int GM_BM = 128;      // activation rows per CTA
 constexpr int GM_BK = 64;       // k per pipeline stage (two Q8_0 blocks)
 constexpr int GM_DQ_THREADS = 512;  // tcgen05 kernel: dequantising threads, 4 per weight row
-constexpr int GM_TC_THREADS = GM_DQ_THREADS + 64;  // + an activation-copy warp and an MMA warp
+constexpr int GM_TC_THREADS = GM_DQ_THREADS + 96;  // + an activation-copy warp, an MMA warp, a weight-copy warp
+constexpr int GM_X_WARP = GM_DQ_THREADS / 32;      // warp roles after the dequantising warps
+constexpr int GM_MMA_WARP = GM_X_WARP + 1;
+constexpr int GM_W_WARP = GM_X_WARP + 2;
 constexpr int GM_TC_TAIL = 256;     // tcgen05 kernel: shared bytes of barriers and flags
 constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
 constexpr int GM_WPF = 4;       // tcgen05 GEMM: weight stages in flight per thread (registers)
@@ -76,7 +79,18 @@ struct GemmArgs {
     float* ws;
     unsigned* tile_cnt;
     int* err;
+    // optional pipeline trace of CTA (0, 0, 0) of the tcgen05 kernel (nullptr: off): clock64()
+    // stamps at the GM_TR_* slots below (gemm_set_trace)
+    unsigned long long* trace;
 };
+
+// trace slots: kernel entry, set-up done, copy warp past its wait, every MMA completed, epilogue
+// done; per weight chunk c its copy issue; per k stage kc: dequantising warp 0 past the chunk wait,
+// past its waits and arrived, the last dequantising warp's arrival (stamp << 5 | warp); the MMA
+// thread past its wait and committed; the activation stage's copy issue
+constexpr int GM_TR_CHUNK = 8, GM_TR_DQ = 72, GM_TR_MMA = 584, GM_TR_X = 840, GM_TR_SLOTS = 968, GM_TR_MAXK = 128;
+// every later gemm_launch of this process traces into buf (device memory, GM_TR_SLOTS words; nullptr: off)
+void gemm_set_trace(unsigned long long* buf);
 
 constexpr int GM_ROW_PAD = 256;  // activation buffers hold a multiple of this many rows
 

@@ -220,6 +220,11 @@ int tf_op_dequant_rows(float* out, int t, const void* W, int N, int K, const int
                      "dequant_rows");
 }
 
+int tf_op_gemm_trace(unsigned long long* buf) {
+    gemm_set_trace(buf);
+    return 0;
+}
+
 int tf_op_device_error(void* stream, int* code) {
     if (!code) return set_error("code must not be null");
     *code = 0;

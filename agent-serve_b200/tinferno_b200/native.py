@@ -73,6 +73,7 @@ SIGNATURES = [
     ("tf_host_free", C.c_int, [_V]),
     ("tf_op_matmul", C.c_int, [_V, _V, C.c_int, _V, C.c_int, C.c_int, C.c_int, _V]),
     ("tf_op_dequant_rows", C.c_int, [_V, C.c_int, _V, C.c_int, C.c_int, _V, C.c_int, _V]),
+    ("tf_op_gemm_trace", C.c_int, [_V]),
     ("tf_op_device_error", C.c_int, [_V, i32p]),
     ("tf_op_rmsnorm", C.c_int, [_V, _V, _V, C.c_int, C.c_int, C.c_float, _V]),
     ("tf_op_silu_mul", C.c_int, [_V, _V, C.c_int, _V]),

@@ -715,7 +715,8 @@ def main():
     ap.add_argument("--rows", type=int, default=None,
                     help="--kernel bstep: rows of the batched step (128); --kernel gemm: activation rows (256)")
     ap.add_argument("--ctx", type=int, default=512, help="--kernel bstep: prompt length before the step")
-    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "gvtrace", "sweep", "bstep", "gemm", "configs", "q6k"],
+    ap.add_argument("--trace-k", dest="trace_k", type=int, default=0, help="--kernel gemmtrace: K of the traced GEMM (1536)")
+    ap.add_argument("--kernel", default="", choices=["", "lmhead", "step", "step0", "pktrace", "gvtrace", "sweep", "bstep", "gemm", "gemmtrace", "configs", "q6k"],
                     help="profiling cases: 'lmhead' = only the dequant-GEMV on the lm_head shape (1 warm-up + "
                          "3 launches); 'step' = the cfg0 layer shapes on a 2-layer model, 4-token prefill + 2 "
                          "eager decode steps")
@@ -827,6 +828,49 @@ def main():
         us = ev[0].elapsed_time(ev[1]) * 1e3
         print(json.dumps({"kernel": "gemm", "N": N, "K": K, "M": M, "us_incl_prep": round(us, 2),
                           "TFLOP_s": round(2 * N * K * M / us / 1e6, 1)}))
+        return
+    if args.kernel == "gemmtrace":
+        # the --kernel gemm launch with the pipeline trace of its first CTA (tf_op_gemm_trace):
+        # per k stage, in SM cycles from the kernel's entry, when dequantising warp 0 passed its
+        # chunk and buffer waits and arrived, when warp 15 arrived, when the MMA thread passed its
+        # waits and committed, and when the copy warp issued the chunk and activation copies
+        import torch
+        from tinferno_b200 import gguf, native, quants
+        L = native.lib()
+        N, K, M = 17920, args.trace_k or 1536, args.rows or 32
+        rng = np.random.default_rng(7)
+        raw = np.ascontiguousarray(quants.quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32),
+                                                   gguf.GGML_Q8_0)).reshape(-1)
+        W = torch.from_numpy(raw).cuda()
+        X = torch.randn(M, K, device="cuda")
+        Y = torch.empty(M, N, device="cuda")
+        st = torch.cuda.current_stream()
+        sw = C.c_int(0)
+        native.check(L.tf_op_weight_scale(C.c_void_p(W.data_ptr()), gguf.GGML_Q8_0, N, K, C.byref(sw),
+                                          C.c_void_p(st.cuda_stream)))
+        tr = torch.zeros(968, dtype=torch.int64, device="cuda")
+        for i in range(4):
+            if i == 3:
+                torch.cuda.synchronize()
+                native.check(L.tf_op_gemm_trace(C.c_void_p(tr.data_ptr())))
+            native.check(L.tf_op_matmul_tc(C.c_void_p(Y.data_ptr()), C.c_void_p(X.data_ptr()), gguf.GGML_Q8_0,
+                                           C.c_void_p(W.data_ptr()), N, K, M, sw.value, C.c_void_p(st.cuda_stream)))
+        torch.cuda.synchronize()
+        native.check(L.tf_op_gemm_trace(None))
+        t = tr.cpu().numpy().astype(np.int64)
+        t0 = int(t[0])
+        rel = lambda v: int(v) - t0 if v else None
+        nk = K // 64
+        stages = []
+        for k in range(min(nk, 128)):
+            last = int(t[75 + 4 * k])
+            stages.append({"k": k, "dq0_chunk": rel(t[72 + 4 * k]), "dq0_buf": rel(t[73 + 4 * k]),
+                           "dq0_arr": rel(t[74 + 4 * k]), "dq_last_arr": rel(last >> 5), "dq_last_warp": last & 31,
+                           "mma_go": rel(t[584 + 2 * k]), "mma_cmt": rel(t[585 + 2 * k]),
+                           "x_iss": rel(t[840 + k])})
+        print(json.dumps({"kernel": "gemmtrace", "N": N, "K": K, "M": M, "setup": rel(t[1]), "copy_wait_done": rel(t[2]),
+                          "mma_all_done": rel(t[3]), "epilogue_done": rel(t[4]),
+                          "chunks_issued": [rel(v) for v in t[8:8 + nk // 4]], "stages": stages}))
         return
     if args.kernel == "configs":
         for line in config_runs():

@@ -250,6 +250,17 @@ TF_API int tf_op_attn_prefill(float* out, const float* q, const float* k, const 
 /* sample_greedy(logits, n)  src/sampler.hpp:9: out[r] = first index of the maximum of row r. */
 TF_API int tf_op_argmax(const float* logits, int n, int rows, int* out, void* stream);
 
+/* Pipeline trace of the tensor-core GEMM, no reference counterpart (a finer-grained companion
+ * of the reference's --profile timings, src/main.cpp): while `buf` (device memory, 968
+ * unsigned 64-bit words, zeroed) is set, every tensor-core GEMM launch of this process has its
+ * first CTA write clock64() stamps into it: [0] entry, [1] set-up done, [2] activation-copy warp
+ * past its dependency wait, [3] every MMA completed, [4] epilogue done; [8 + c] weight chunk c
+ * issued; [72 + 4k + i] k-stage k: dequantising warp 0 past the chunk wait (i = 0), past the
+ * buffer wait (1), arrived (2), the last dequantising warp's arrival as stamp << 5 | warp (3);
+ * [584 + 2k + i] the MMA thread past its wait (0), committed (1); [840 + k] activation stage k
+ * issued.  nullptr switches it off. */
+TF_API int tf_op_gemm_trace(unsigned long long* buf);
+
 /* Device-side status of the op-level calls, no reference counterpart (the reference's ops
  * throw std::runtime_error on the calling thread, src/model.cpp:185,198).  Kernels cannot
  * return a status to the call that launched them, so the op-level kernels of a device record
