@@ -376,14 +376,20 @@ constexpr int gemm_n_acc() {
     return NT <= 128 ? 3 : 1;
 }
 // tensor-memory columns: the accumulators' NT columns each, then per weight buffer Wh (32
-// columns: 128 rows x 64 halves) and Wl (32); allocated as a power of two
+// columns: 128 rows x 64 halves) and Wl (32); allocated as a power of two.  Weight buffers: as
+// many as the 512 columns hold (up to four), so that the dequantising warps run that many stages
+// ahead of the MMAs (an MMA batch completes ~1000 cycles after it is issued)
 template <int NT>
 constexpr uint32_t gemm_acc_cols() {
     return (uint32_t)(gemm_n_acc<NT>() * NT);
 }
 template <int NT>
+constexpr int gemm_w_bufs() {
+    return (512 - (int)gemm_acc_cols<NT>()) / 64 > 4 ? 4 : (512 - (int)gemm_acc_cols<NT>()) / 64;
+}
+template <int NT>
 constexpr uint32_t gemm_tmem_cols() {
-    return gemm_acc_cols<NT>() + 2 * 64 <= 256 ? 256u : 512u;
+    return gemm_acc_cols<NT>() + 64u * gemm_w_bufs<NT>() <= 256 ? 256u : 512u;
 }
 template <int NT>
 constexpr size_t gemm_x_stage_bytes() {
@@ -400,11 +406,12 @@ constexpr uint32_t gemm_chunk_bytes() {
 }
 template <int NT, bool WT>
 constexpr int gemm_x_stages() {
-    return WT ? (NT <= 32 ? 4 : NT <= 64 ? 3 : 2) : (NT <= 32 ? 8 : NT <= 64 ? 6 : NT <= 128 ? 4 : 2);
+    // deep enough to cover a bulk copy's latency under the weight stream (~2000 cycles, two stages)
+    return NT <= 32 ? 8 : NT <= 64 ? 6 : NT <= 128 ? 4 : 3;
 }
 template <int NT, bool Q4, bool WT>
 constexpr int gemm_raw_chunks() {
-    return !WT ? 0 : Q4 ? (NT <= 64 ? 4 : 3) : (NT <= 64 ? 3 : 2);
+    return !WT ? 0 : Q4 ? (NT <= 64 ? 4 : 3) : (NT <= 32 ? 4 : NT <= 64 ? 3 : 2);
 }
 template <int NT, bool Q4, bool WT>
 constexpr size_t gemm_tc_smem_bytes() {
@@ -434,17 +441,18 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
     const int nk = ku * (int)((long long)nu * (blockIdx.z + 1) / gridDim.z) - kb;
     const float wscale = ldexpf(1.0f, a.sw);
     constexpr int XS = gemm_x_stages<NT, WT>();
+    constexpr int WB = gemm_w_bufs<NT>();
     constexpr int RC = gemm_raw_chunks<NT, Q4, WT>();
     constexpr int RCd = RC > 0 ? RC : 1;  // (divisor in code only the WT instantiations run)
     constexpr int UB = Q4 ? 36 : 68;               // bytes of a row's 64-weight stage
     constexpr uint32_t RB = GM_WCH * UB;           // bytes of a row's chunk
     constexpr uint32_t XH = NT * GM_BK * 2;  // bytes of one activation half of a stage
     uint8_t* tail = smem + gemm_tc_smem_bytes<NT, Q4, WT>() - GM_TC_TAIL - 1024;
-    // [2] weight stage written (dequant warps; warp 0 arrives only once it has also seen the
+    // [WB] weight stage written (dequant warps; warp 0 arrives only once it has also seen the
     // stage's activations land, so this one barrier is all the MMA thread waits on)
     uint64_t* wready = reinterpret_cast<uint64_t*>(tail);
-    uint64_t* wfree = wready + 2;                          // [2] its MMAs completed
-    uint64_t* xfull = wfree + 2;                           // [XS] activation stage landed
+    uint64_t* wfree = wready + WB;                         // [WB] its MMAs completed
+    uint64_t* xfull = wfree + WB;                          // [XS] activation stage landed
     uint64_t* xempty = xfull + XS;                         // [XS] its MMAs completed
     uint64_t* mma_done = xempty + XS;                      // every MMA completed
     uint64_t* rfull = mma_done + 1;                        // [RC] weight chunk landed (WT)
@@ -466,7 +474,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
     }
     if (tid == GM_DQ_THREADS) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < WB; ++i) {
             mbar_init(&wready[i], GM_DQ_THREADS / 32);
             mbar_init(&wfree[i], 1);
         }
@@ -502,12 +510,12 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
         pdl_wait();
         bool ok = true;
         for (int kc = 0; kc < nk && ok; ++kc) {
-            const int s = kc & 1, ci = kc / GM_WCH, j = kc % GM_WCH, slot = ci % RCd;
+            const int s = kc % WB, ci = kc / GM_WCH, j = kc % GM_WCH, slot = ci % RCd;
             if (j == 0) ok = mbar_wait(&rfull[slot], (ci / RCd) & 1, a.err, ERR_WAIT_FULL, abort_flag);
             const bool tk = tid == 0 && kc < GM_TR_MAXK;
             if (tk) stamp(GM_TR_DQ + 4 * kc);
-            // buffer s was last read by the MMAs of stage kc - 2
-            if (ok && kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+            // buffer s was last read by the MMAs of stage kc - WB
+            if (ok && kc >= WB) ok = mbar_wait(&wfree[s], ((kc / WB) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
             if (ok && warp == 0) ok = mbar_wait(&xfull[kc % XS], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag);
             if (tk) stamp(GM_TR_DQ + 4 * kc + 1);
             ok = __all_sync(0xffffffffu, ok);  // the tensor-memory stores below are warp-wide
@@ -535,7 +543,7 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
             }
         }
     } else if (warp < GM_DQ_THREADS / 32) {
-        // ---- dequantising warps: stage kc's weights into weight buffer kc & 1 ----
+        // ---- dequantising warps: stage kc's weights into weight buffer kc % WB ----
         // The weight words of the next GM_WPF stages are in flight in registers (a stage's
         // 68-byte row pieces come from HBM); the first ones are requested before the PDL wait.
         constexpr int PF = GM_WPF;
@@ -553,9 +561,9 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
             for (int u = 0; u < PF; ++u) {
                 const int kc = kc0 + u;
                 if (kc < nk && ok) {
-                    const int s = kc & 1;
-                    // buffer s was last read by the MMAs of stage kc - 2
-                    if (kc >= 2) ok = mbar_wait(&wfree[s], ((kc - 2) >> 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
+                    const int s = kc % WB;
+                    // buffer s was last read by the MMAs of stage kc - WB
+                    if (kc >= WB) ok = mbar_wait(&wfree[s], ((kc / WB) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
                     if (ok && warp == 0)
                         ok = mbar_wait(&xfull[kc % XS], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag);
                     ok = __all_sync(0xffffffffu, ok);  // the tensor-memory stores below are warp-wide
@@ -644,10 +652,10 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
             const uint32_t idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
             const uint32_t idesc2 = (1u << 4) | ((uint32_t)((2 * NT) >> 3) << 17) | ((uint32_t)(GM_BN >> 4) << 24);
             for (int kc = 0; kc < nk; ++kc) {
-                const int s = kc & 1, b = kc % XS;
+                const int s = kc % WB, b = kc % XS;
                 // the weights of stage kc are in buffer s, and (dequantising warp 0 saw it before
                 // it arrived) its activations in ring slot b
-                if (!mbar_wait(&wready[s], (kc >> 1) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
+                if (!mbar_wait(&wready[s], (kc / WB) & 1, a.err, ERR_WAIT_FULL, abort_flag)) break;
                 if (kc < GM_TR_MAXK) stamp(GM_TR_MMA + 2 * kc);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 // Wh / Wl of buffer s in tensor memory (8 columns per k step), Xh / Xl in shared memory

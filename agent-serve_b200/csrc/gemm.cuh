@@ -24,7 +24,7 @@ constexpr int GM_TC_THREADS = GM_DQ_THREADS + 96;  // + an activation-copy warp,
 constexpr int GM_X_WARP = GM_DQ_THREADS / 32;      // warp roles after the dequantising warps
 constexpr int GM_MMA_WARP = GM_X_WARP + 1;
 constexpr int GM_W_WARP = GM_X_WARP + 2;
-constexpr int GM_TC_TAIL = 256;     // tcgen05 kernel: shared bytes of barriers and flags
+constexpr int GM_TC_TAIL = 512;     // tcgen05 kernel: shared bytes of barriers and flags
 constexpr int GM_MIN_M = 16;    // below this the GEMV kernel runs
 constexpr int GM_WPF = 4;       // tcgen05 GEMM: weight stages in flight per thread (registers)
 
