@@ -213,6 +213,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
                 kv_store(t.kc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, kn[i]);
                 kv_store(t.vc, (long long)(cache_off + (size_t)pos * hd + i), t.kv_type, vn[i]);
             }
+        if (TR && tid == 0) gv_stamp(a.trace, 8);
         const float scale = 1.0f / sqrtf((float)hd);
         const int pg = tid / hd, pd = tid % hd;
         for (int t0 = s0; t0 < s1; t0 += tp) {
@@ -246,6 +247,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
                 }
                 sv = scale * ((s0 + s1) + (s2 + s3));
             }
+            if (TR && tid == 0 && t0 == s0) gv_stamp(a.trace, 9);
             float tm = warp_max(sv);
             if (lane == 0) red[warp] = tm;
             __syncthreads();
@@ -262,6 +264,7 @@ __device__ __forceinline__ void fused_attention(const GemvArgs& a, uint8_t* smem
             __syncthreads();
             float lt = 0.f;
             for (int w = 0; w < nw; ++w) lt += red[32 + w];
+            if (TR && tid == 0 && t0 == s0) gv_stamp(a.trace, 7);
             const float alpha = expf(m_run - mnew);  // 0 on the first tile
             l_run = fmaf(l_run, alpha, lt);
             m_run = mnew;

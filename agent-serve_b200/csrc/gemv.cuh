@@ -102,11 +102,13 @@ struct GemvArgs {
     // trace[c * GV_TRACE_SLOTS + k] at entry (0), after griddepcontrol.wait (1), prologue done
     // (2; attention CTAs: q/k/v ready), rows done (3; attention done) and exit (4); inside
     // the Q8_0 integer prologue: before griddepcontrol.wait (5), activation loaded (6), after
-    // the first barrier that follows (7); attention CTAs: q/k/v loaded (5), tiles done (6)
+    // the first barrier that follows (7); attention CTAs: q/k/v loaded (5), tiles done (6),
+    // the first tile's scores and softmax sums done (7), rotation and cache store done (8), the
+    // first tile's scores done (9)
     unsigned long long* trace;
 };
 
-constexpr int GV_TRACE_SLOTS = 8;
+constexpr int GV_TRACE_SLOTS = 10;
 constexpr int GV_TRACE_CTAS = 512;     // CTAs per launch the trace buffer holds
 constexpr int GV_TRACE_LAUNCHES = 192; // launches per step the trace buffer holds
 

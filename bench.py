@@ -594,7 +594,7 @@ def launch_trace(steps=6, model_path=None):
     t = int(np.argmax(m.prefill(synth.prompt_tokens(CFG, PROMPT))))
     for _ in range(steps):
         t = m.decode_argmax(t)
-    ML, CT, SL = 192, 512, 8
+    ML, CT, SL = 192, 512, 10
     buf = np.zeros(ML * CT * SL, np.uint64)
     meta = np.zeros(ML * 3, np.int32)
     nl = np.zeros(1, np.int32)
@@ -633,6 +633,11 @@ def launch_trace(steps=6, model_path=None):
             if na:
                 vals += [("attention, longest: q/k/v ready -> loaded", int((at[:, 5] - at[:, 2]).max())),
                          ("attention, longest: loaded -> tiles done", int((at[:, 6] - at[:, 5]).max())),
+                         ("attention, longest: loaded -> rotated and stored", int((at[:, 8] - at[:, 5]).max())),
+                         ("attention, longest: rotated and stored -> first tile's scores", int((at[:, 9] - at[:, 8]).max())),
+                         ("attention, longest: first tile's scores -> softmax sums", int((at[:, 7] - at[:, 9]).max())),
+                         ("attention, longest: first tile's softmax sums -> tiles done", int((at[:, 6] - at[:, 7]).max())),
+                         ("attention, mean: loaded -> tiles done", float((at[:, 6] - at[:, 5]).mean())),
                          ("attention, longest: tiles done -> output written", int((at[:, 3] - at[:, 6]).max()))]
                 vals += [("attention: last q/k/v ready", int(at[:, 2].max()) - prev_exit),
                          ("attention: last done", int(at[:, 3].max()) - prev_exit)]

@@ -155,9 +155,10 @@ TF_API int tf_cuda_history(tf_model* m, int n, int* out);
 TF_API int tf_cuda_trace_read(tf_model* m, unsigned long long* out, int cap, int* n_out);
 
 /* Launch trace of the per-kernel decode step (a model created with TFB200_GV_TRACE=1): for each
- * GEMV launch of the last step enqueued, GV_TRACE_CTAS (512) CTAs x 8 %globaltimer stamps (ns):
+ * GEMV launch of the last step enqueued, GV_TRACE_CTAS (512) CTAs x 10 %globaltimer stamps (ns):
  * entry, after griddepcontrol.wait, prologue done (attention CTAs: q/k/v ready), rows done
- * (attention done), exit; out holds max_launches x 512 x 8 values, meta max_launches x 3 ints
+ * (attention done), exit, and finer stamps inside the prologue and the fused attention; out
+ * holds max_launches x 512 x 10 values, meta max_launches x 3 ints
  * {grid, attention CTAs, kind: 0 QKV, 1 wo, 2 gate/up, 3 down, 4 lm_head}.  Diagnostic only. */
 TF_API int tf_cuda_launch_trace(tf_model* m, unsigned long long* out, int max_launches, int* meta, int* n_launch);
 
