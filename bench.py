@@ -434,6 +434,13 @@ def run_ours(args, rank, world, local_rank, dist):
                 line["configs"] = config_runs()
             except Exception as e:  # never fatal to the headline line
                 line["configs"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+            try:  # BASELINE cfg3, the isolated dequant-matmul sweep (bounded in time)
+                sw = matmul_sweep(quiet=True, max_seconds=60)
+                line["cfg3_sweep"] = {"columns": ["type", "N", "K", "M", "path", "us", "GB_s", "hbm_frac", "TFLOP_s"],
+                                      "rows": [[r["type"], r["N"], r["K"], r["M"], r["path"], r["us"], r["GB_s"],
+                                                r["hbm_frac"], r["TFLOP_s"]] for r in sw]}
+            except Exception as e:  # never fatal to the headline line
+                line["cfg3_sweep"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
     batched = None
     if not args.no_batched:
         batched = run_batched(args, rank, world, local_rank, dist)
@@ -650,20 +657,24 @@ def launch_trace(steps=6, model_path=None):
                                                      for k, d in seg.items()}}
 
 
-def matmul_sweep():
+def matmul_sweep(quiet=False, max_seconds=None):
     """BASELINE cfg3: Y[M,N] = X[M,K] W[N,K]^T for Q8_0 and Q4_0 weights (N(0, 0.02) quantised),
     X ~ N(0, 1); K=2048 with N in {512, 2048, 8192, 128256}, K=8192 with N=2048; M in
     {1, 8, 64, 512}.  Weight copies rotate so that every timed launch reads its weights from
     HBM (the rotation exceeds the 126 MB L2).  M <= 8 runs the dequant-GEMV, M >= 16 the
-    tensor-core GEMM for both types (timed without the one-off scale pass of the matrix)."""
+    tensor-core GEMM for both types (timed without the one-off scale pass of the matrix).
+    quiet: no per-shape lines on stdout; max_seconds: stop after the shape that passes it."""
     import torch
     from tinferno_b200 import gguf, native, quants
     L = native.lib()
     st = torch.cuda.current_stream()
     rows = []
     peak = peaks()[0]
+    t_start = time.perf_counter()
     for t, tname in ((gguf.GGML_Q8_0, "Q8_0"), (gguf.GGML_Q4_0, "Q4_0")):
         for K, N in ((2048, 512), (2048, 2048), (2048, 8192), (2048, 128256), (8192, 2048)):
+            if max_seconds and time.perf_counter() - t_start > max_seconds:
+                break
             rng = np.random.default_rng(K + N)
             w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
             raw = np.ascontiguousarray(quants.quantize(w, t)).reshape(-1)
@@ -701,7 +712,8 @@ def matmul_sweep():
                              "us": round(ms * 1e3, 2), "GB_s": round(alg / (ms / 1e3) / 1e9, 1),
                              "hbm_frac": round(alg / (ms / 1e3) / 1e9 / peak, 3),
                              "TFLOP_s": round(fl / (ms / 1e3) / 1e12, 2)})
-                print(json.dumps(rows[-1]), flush=True)
+                if not quiet:
+                    print(json.dumps(rows[-1]), flush=True)
             del W
             torch.cuda.empty_cache()
     return rows
