@@ -15,6 +15,9 @@
 // and the V-weighted sum over its positions.  The last CTA of a (row, kv head) combines the
 // split partials (max, sum, acc) into the normalised output.  The new position's k/v are
 // taken from shared memory, never re-read from the cache slot being written.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <cstdlib>
 
 #include <atomic>
@@ -237,12 +240,14 @@ __global__ void __launch_bounds__(AT_THREADS) tf_attn_decode_kernel(const AttnAr
 
 // ---- streaming decode attention (fp32 caches, many rows) -------------------------------------
 // One CTA per (row, kv head, position split) walks its positions in tiles of AS_TILE held in
-// a ring of AS_NB shared-memory buffers filled by 1-D bulk copies (TMA engine): the K rows one
-// copy each into rows padded to hd + 4 floats, the V rows in one copy.  Per tile, with the
-// whole group of query heads of the kv head (GQA) sharing the tile:
-//   scores   lane = position, warp = a slice of hd/8 dims: float4 K reads (the padding puts
-//            consecutive positions on distinct banks), q read as warp-wide broadcasts, the 8
-//            slices' partial dots summed in a fixed order through shared memory;
+// a ring of AS_NB shared-memory buffers filled by the TMA engine: the K rows as hd/32 boxes of
+// 32 positions x 32 floats through a 2-D tensor map with the 128-byte swizzle (16-byte chunk c
+// of row r stored at chunk c ^ (r % 8) of its 128-byte line), the V rows by one 1-D bulk copy.
+// Per tile, with the whole group of query heads of the kv head (GQA) sharing the tile:
+//   scores   lane = position, warp = a slice of hd/8 dims: float4 K reads at the swizzled
+//            chunk (the 8 lanes of a quarter-warp meet 8 distinct chunks: no bank conflicts),
+//            q read as warp-wide broadcasts, the 8 slices' partial dots summed in a fixed
+//            order through shared memory;
 //   softmax  warp = query head, lane = position: running max / sum (attn_decode's softmax,
 //            src/attention.cpp:63-72, as an online softmax over tiles);
 //   P.V      warp = positions p = warp (mod 8), lane = 4 dims, every head of the group held
@@ -253,16 +258,27 @@ constexpr int AS_THREADS = 256;
 constexpr int AS_TILE = 32;
 constexpr int AS_NB = 3;
 static inline size_t attn_stream_smem_bytes(int hd) {
-    const size_t tiles = (size_t)AS_NB * AS_TILE * (2 * hd + 4) * sizeof(float);
+    // + 1 KB: the swizzled K boxes start on 1024-byte boundaries
+    const size_t tiles = (size_t)AS_NB * AS_TILE * 2 * hd * sizeof(float) + 1024;
     const size_t fin = (size_t)(AS_THREADS / 32) * AT_MAX_REP * hd * sizeof(float);  // final sums
     const size_t comb = (size_t)(AT_MAX_REP * AT_MAX_SPLIT + AT_MAX_SPLIT) * sizeof(float);
     size_t m = tiles > fin ? tiles : fin;
     return m > comb ? m : comb;
 }
 
+// byte offset of element d of position r in a tile of swizzled K boxes (box d / 32, line r,
+// chunk (d % 32) / 4 at chunk ^ (r % 8))
+__device__ __forceinline__ uint32_t as_koff(int r, int d) {
+    return (uint32_t)((d >> 5) * (AS_TILE * 128) + r * 128 + ((((d >> 2) & 7) ^ (r & 7)) << 4) + (d & 3) * 4);
+}
+
 template <int R>  // query heads per kv head
-__global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const AttnArgs a) {
-    extern __shared__ __align__(16) float kvt[];
+__global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const AttnArgs a,
+                                                                        const __grid_constant__ CUtensorMap kmap) {
+    extern __shared__ __align__(16) float kvt_raw[];
+    // the swizzled K boxes need 1024-byte aligned buffers
+    float* kvt = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(kvt_raw) +
+                                          ((1024u - (smem_u32(kvt_raw) & 1023u)) & 1023u));
     __shared__ __align__(16) float qs[R][AT_MAX_HD];
     __shared__ float red[AS_THREADS / 32][R][AS_TILE];  // partial scores per dim slice
     __shared__ __align__(16) float ep[AS_TILE][8];       // exp(score - max), [position][head]
@@ -286,7 +302,7 @@ __global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const Att
     __syncthreads();
     pdl_trigger();
     pdl_wait();
-    const int hd = a.hd, d2 = hd / 2, kst = hd + 4, cpw = hd / 32;
+    const int hd = a.hd, d2 = hd / 2, cpw = hd / 32;
     const int slot = a.slots ? a.slots[m] : 0;
     const int pos = a.fresh == 2 ? a.pos[slot] + m : (a.fresh ? a.pos[slot] : a.n_pos_fixed - 1);
     if (a.fresh && (pos < 0 || pos >= a.cap)) {
@@ -303,24 +319,29 @@ __global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const Att
     const int n_tiles = (p1 - p0 + AS_TILE - 1) / AS_TILE;
     const float* row = a.qkv + (size_t)m * a.ld_qkv;
     const size_t cache_off = (size_t)slot * a.slot_stride + (size_t)kvh * a.cap * hd;
-    const float* kc = static_cast<const float*>(a.kc) + cache_off;
     const float* vc = static_cast<const float*>(a.vc) + cache_off;
+    const int krow0 = (int)(cache_off / hd);                // the pair's first row in the K tensor map
     const bool fresh_last = a.fresh == 1 && p1 == n_pos;  // this split holds the new position
-    float* kbuf = kvt;                                     // [AS_NB][AS_TILE][kst]
-    float* vbuf = kvt + (size_t)AS_NB * AS_TILE * kst;     // [AS_NB][AS_TILE][hd]
+    float* kbuf = kvt;                                     // [AS_NB][hd / 32 boxes][AS_TILE][32], swizzled
+    float* vbuf = kvt + (size_t)AS_NB * AS_TILE * hd;      // [AS_NB][AS_TILE][hd]
 
-    // tile t into buffer t % AS_NB, issued by the last warp: lane r copies K row r
+    // tile t into buffer t % AS_NB, issued by lane 0 of the last warp: the K boxes always carry
+    // 32 positions (rows past the cache read as zeros, rows past the split are not used), the
+    // V copy the tile's cached rows
     constexpr int IW = AS_THREADS / 32 - 1;
     auto issue = [&](int t) {
+        if (lane != 0) return;
         const int b = t % AS_NB, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
         const int qc = (fresh_last && q0 + qn == n_pos) ? qn - 1 : qn;  // cached rows of the tile
-        if (lane == 0) mbar_expect_tx(&full[b], (uint32_t)(2 * qc * hd * 4));
-        __syncwarp();
-        if (lane < qc)
-            bulk_g2s(kbuf + ((size_t)b * AS_TILE + lane) * kst, kc + (size_t)(q0 + lane) * hd, (uint32_t)hd * 4,
-                     &full[b]);
-        if (lane == 0 && qc)
-            bulk_g2s(vbuf + (size_t)b * AS_TILE * hd, vc + (size_t)q0 * hd, (uint32_t)(qc * hd * 4), &full[b]);
+        mbar_expect_tx(&full[b], (uint32_t)(AS_TILE * hd * 4 + qc * hd * 4));
+        uint8_t* kb = reinterpret_cast<uint8_t*>(kbuf + (size_t)b * AS_TILE * hd);
+        for (int bx = 0; bx < cpw; ++bx)
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    smem_u32(kb + bx * AS_TILE * 128)),
+                "l"(reinterpret_cast<uint64_t>(&kmap)), "r"(32 * bx), "r"(krow0 + q0), "r"(smem_u32(&full[b]))
+                : "memory");
+        if (qc) bulk_g2s(vbuf + (size_t)b * AS_TILE * hd, vc + (size_t)q0 * hd, (uint32_t)(qc * hd * 4), &full[b]);
     };
     if (warp == IW) {
         issue(0);
@@ -363,12 +384,12 @@ __global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const Att
     bool ok = true;
     for (int t = 0; t < n_tiles; ++t) {
         const int b = t % AS_NB, q0 = p0 + t * AS_TILE, qn = min(AS_TILE, p1 - q0);
-        float* ks = kbuf + (size_t)b * AS_TILE * kst;
+        uint8_t* ks = reinterpret_cast<uint8_t*>(kbuf + (size_t)b * AS_TILE * hd);
         float* vs = vbuf + (size_t)b * AS_TILE * hd;
         if (!mbar_wait(&full[b], (t / AS_NB) & 1, a.err, ERR_WAIT_FULL, nullptr)) ok = false;
         if (fresh_last && q0 + qn == n_pos) {  // uniform: the new key / value enter the tile
             for (int i = tid; i < hd; i += AS_THREADS) {
-                ks[(size_t)(qn - 1) * kst + i] = kn[i];  // fp32 cache: stored exactly
+                *reinterpret_cast<float*>(ks + as_koff(qn - 1, i)) = kn[i];  // fp32 cache: stored exactly
                 vs[(size_t)(qn - 1) * hd + i] = vn[i];
             }
             __syncthreads();
@@ -379,9 +400,8 @@ __global__ void __launch_bounds__(AS_THREADS, 2) tf_attn_stream_kernel(const Att
 #pragma unroll
             for (int h = 0; h < R; ++h) sp[h] = make_float2(0.f, 0.f);
             if (lane < qn) {
-                const float4* kr = reinterpret_cast<const float4*>(ks + (size_t)lane * kst) + warp * cpw;
                 for (int c = 0; c < cpw; ++c) {
-                    const float4 k4 = kr[c];
+                    const float4 k4 = *reinterpret_cast<const float4*>(ks + as_koff(lane, 4 * (warp * cpw + c)));
                     const float2 k01 = make_float2(k4.x, k4.y), k23 = make_float2(k4.z, k4.w);
 #pragma unroll
                     for (int h = 0; h < R; ++h) {
@@ -612,9 +632,36 @@ static int attn_stream_splits(const AttnArgs& a, int M) {
     return s < 1 ? 1 : (s > a.n_split ? a.n_split : s);
 }
 
+// The K cache of one layer as a 2-D tensor map: n_rows rows of hd floats, boxes of 32 rows x 32
+// floats (128 bytes: the 128-byte swizzle's line), rows past n_rows read as zeros.
+static bool attn_k_map(CUtensorMap* m, const AttnArgs& a) {
+    static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+    static std::atomic<bool> tried{false};
+    if (!tried.load()) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        tried.store(true);
+    }
+    if (!enc || (reinterpret_cast<uintptr_t>(a.kc) & 15)) return false;
+    const long long rows = a.n_rows > 0 ? a.n_rows : (long long)a.n_kv * a.cap;
+    const cuuint64_t dims[2] = {(cuuint64_t)a.hd, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)a.hd * 4};
+    const cuuint32_t box[2] = {32, (cuuint32_t)AS_TILE};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.kc, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool pdl) {
     if (a.hd > AT_MAX_HD || a.hd % 8 || a.n_head / a.n_kv > AT_MAX_REP) return cudaErrorInvalidValue;
-    if (a.kv_type == KV_F32 && M * a.n_kv >= 16 && a.hd % 32 == 0) {  // many rows: streaming kernel
+    alignas(64) CUtensorMap kmap;
+    memset(&kmap, 0, sizeof(kmap));
+    // many rows: the streaming kernel (fp32 cache, K boxes through the tensor map)
+    if (a.kv_type == KV_F32 && M * a.n_kv >= 16 && a.hd % 32 == 0 && attn_k_map(&kmap, a)) {
         static const void* const fns[AT_MAX_REP] = {
             (const void*)tf_attn_stream_kernel<1>, (const void*)tf_attn_stream_kernel<2>, (const void*)tf_attn_stream_kernel<3>,
             (const void*)tf_attn_stream_kernel<4>, (const void*)tf_attn_stream_kernel<5>, (const void*)tf_attn_stream_kernel<6>,
@@ -647,7 +694,7 @@ cudaError_t attn_decode_launch(const AttnArgs& a, int M, cudaStream_t st, bool p
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         AttnArgs aa = a;
-        void* args[] = {&aa};
+        void* args[] = {&aa, &kmap};
         return cudaLaunchKernelExC(&cfg, fn, args);
     }
     const int max_pos = a.fresh ? a.cap : a.n_pos_fixed;

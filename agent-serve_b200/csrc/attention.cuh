@@ -35,6 +35,7 @@ struct AttnArgs {
                             //    at pos[slot] + m attends over the cache [wstart, pos] as given
     int n_pos_fixed;        // fresh == 0: attend over n_pos_fixed cached positions, q as given
     int* err;
+    long long n_rows;       // hd-element rows addressable from kc / vc (0: n_kv * cap, one slot)
 };
 
 struct PrefillAttnArgs {

@@ -248,6 +248,7 @@ AttnArgs attn_args(tf_model* m, int li) {
     a.n_kv = m->hp.n_kv_head;
     a.hd = m->hd;
     a.n_split = m->n_split;
+    a.n_rows = m->layer_elems / m->hd;
     a.part = m->part;
     a.counters = m->counters;
     a.out = m->attn;
