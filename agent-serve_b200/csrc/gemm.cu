@@ -562,10 +562,13 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                 const int kc = kc0 + u;
                 if (kc < nk && ok) {
                     const int s = kc % WB;
+                    const bool tk = tid == 0 && kc < GM_TR_MAXK;
+                    if (tk) stamp(GM_TR_DQ + 4 * kc);
                     // buffer s was last read by the MMAs of stage kc - WB
                     if (kc >= WB) ok = mbar_wait(&wfree[s], ((kc / WB) - 1) & 1, a.err, ERR_WAIT_EMPTY, abort_flag);
                     if (ok && warp == 0)
                         ok = mbar_wait(&xfull[kc % XS], (kc / XS) & 1, a.err, ERR_WAIT_FULL, abort_flag);
+                    if (tk) stamp(GM_TR_DQ + 4 * kc + 1);
                     ok = __all_sync(0xffffffffu, ok);  // the tensor-memory stores below are warp-wide
                     if (ok) {
                         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -578,7 +581,14 @@ __global__ void __launch_bounds__(GM_TC_THREADS, 1) tf_gemm_q8_tc_kernel(const G
                         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
                         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&wready[s]);
+                        if (lane == 0) {
+                            mbar_arrive(&wready[s]);
+                            if (trc && kc < GM_TR_MAXK) {  // warp 0's arrival; the last arrival and its warp
+                                const unsigned long long t = (unsigned long long)clock64();
+                                if (warp == 0) a.trace[GM_TR_DQ + 4 * kc + 2] = t;
+                                atomicMax(&a.trace[GM_TR_DQ + 4 * kc + 3], (t << 5) | (unsigned long long)warp);
+                            }
+                        }
                     }
                 }
             }
