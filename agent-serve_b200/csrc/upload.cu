@@ -82,6 +82,16 @@ cudaError_t Uploader::copy(void* dst, const void* src, size_t bytes) {
 }
 
 cudaError_t Uploader::copy_rows(void* dst, size_t dpitch, const void* src, size_t width, size_t rows) {
+    if (width == 0 || rows == 0) return cudaSuccess;
+    // one row is staged whole: a row wider than a staging buffer goes row by row through copy()
+    if (width > chunk_) {
+        for (size_t r = 0; r < rows; ++r) {
+            cudaError_t e = copy(static_cast<uint8_t*>(dst) + r * dpitch, static_cast<const uint8_t*>(src) + r * width,
+                                 width);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
     const size_t per = std::max<size_t>(1, chunk_ / width);
     for (size_t r = 0; r < rows; r += per) {
         const size_t n = std::min(per, rows - r);
