@@ -36,7 +36,105 @@ __host__ __device__ __forceinline__ uint32_t gm_kint_off(int row, int k) {
 // ---- activation preparation ----------------------------------------------------------------
 // One CTA per activation row: [embedding lookup ->] [RMSNorm (src/layers.cpp:7-12) ->]
 // power-of-two scale to |x| < 2^14 -> f16 halves.
-__global__ void __launch_bounds__(256) tf_xprep_kernel(const XPrepArgs a) {
+constexpr int XP_THREADS = 256;
+constexpr int XP_REG_CHUNKS = 12;  // float4 chunks a thread holds in registers: rows of K <= 12288
+
+// tf_xprep_kernel with the row in registers (rows read from memory, K <= XP_THREADS * 4 *
+// XP_REG_CHUNKS; xprep_launch picks it): thread t
+// holds float4 chunks t, t + 256, ... of the row, so the RMSNorm's double sum runs in the
+// shared-memory path's order (per thread over its chunks, then warps in order) and every output
+// bit is the same; two CTA barriers instead of four, and no pass through shared memory.  An
+// 8-element chunk of the operand layout is the float4 chunks 2i (even lane) and 2i + 1 (the
+// next lane): the even lane stores its Xh 16 bytes, the odd lane its Xl 16 bytes, each with
+// the other lane's half exchanged by one shuffle pair.
+__global__ void __launch_bounds__(XP_THREADS) tf_xprep_rows_kernel(const XPrepArgs a) {
+    __shared__ double redd[XP_THREADS / 32];
+    __shared__ float redf[XP_THREADS / 32];
+    const int m = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = a.K, nq = K >> 2;
+    // as tf_xprep_kernel: the GEMM may start its set-up now, the reads wait for the writer
+    pdl_trigger();
+    pdl_wait();
+    const float4* xg = reinterpret_cast<const float4*>(a.x + (size_t)m * a.ldx);
+    float4 v[XP_REG_CHUNKS];
+#pragma unroll
+    for (int j = 0; j < XP_REG_CHUNKS; ++j) {
+        const int c = tid + j * XP_THREADS;
+        v[j] = c < nq ? xg[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (a.norm_w) {
+        double ss = 0.0;
+#pragma unroll
+        for (int j = 0; j < XP_REG_CHUNKS; ++j) {
+            if (tid + j * XP_THREADS < nq) {
+                ss = fma((double)v[j].x, (double)v[j].x, ss);
+                ss = fma((double)v[j].y, (double)v[j].y, ss);
+                ss = fma((double)v[j].z, (double)v[j].z, ss);
+                ss = fma((double)v[j].w, (double)v[j].w, ss);
+            }
+        }
+        ss = warp_sum_d(ss);
+        if (lane == 0) redd[warp] = ss;
+        __syncthreads();
+        double tot = 0.0;
+        for (int w = 0; w < XP_THREADS / 32; ++w) tot += redd[w];
+        const float inv = 1.0f / sqrtf((float)(tot / K) + a.eps);
+#pragma unroll
+        for (int j = 0; j < XP_REG_CHUNKS; ++j) {
+            const int c = tid + j * XP_THREADS;
+            if (c < nq) {
+                const float4 w = reinterpret_cast<const float4*>(a.norm_w)[c];
+                v[j].x = __fmul_rn(__fmul_rn(v[j].x, inv), w.x);
+                v[j].y = __fmul_rn(__fmul_rn(v[j].y, inv), w.y);
+                v[j].z = __fmul_rn(__fmul_rn(v[j].z, inv), w.z);
+                v[j].w = __fmul_rn(__fmul_rn(v[j].w, inv), w.w);
+            }
+        }
+    }
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < XP_REG_CHUNKS; ++j)  // chunks past the row are zeros
+        am = fmaxf(fmaxf(am, fmaxf(fabsf(v[j].x), fabsf(v[j].y))), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+    am = warp_max(am);
+    if (lane == 0) redf[warp] = am;
+    __syncthreads();
+    am = 0.f;
+    for (int w = 0; w < XP_THREADS / 32; ++w) am = fmaxf(am, redf[w]);
+    const int be = (int)((__float_as_uint(am) >> 23) & 0xFFu);  // as below
+    int sx = 140 - be;
+    sx = sx > 100 ? 100 : (sx < -100 ? -100 : sx);
+    const float S = ldexpf(1.0f, sx);
+    const bool odd = lane & 1;
+#pragma unroll
+    for (int j = 0; j < XP_REG_CHUNKS; ++j) {
+        if (j * XP_THREADS >= nq) break;  // uniform over the CTA
+        const int c = tid + j * XP_THREADS;
+        const float e[4] = {v[j].x * S, v[j].y * S, v[j].z * S, v[j].w * S};  // exact scaling
+        uint32_t hw[2], lw[2];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+            const __half h0 = __float2half_rn(e[2 * i]), h1 = __float2half_rn(e[2 * i + 1]);
+            const __half l0 = __float2half_rn(e[2 * i] - __half2float(h0));
+            const __half l1 = __float2half_rn(e[2 * i + 1] - __half2float(h1));
+            hw[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            lw[i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        // the even lane takes the odd lane's Xh words, the odd lane the even lane's Xl words
+        const uint32_t s0 = __shfl_xor_sync(0xffffffffu, odd ? hw[0] : lw[0], 1);
+        const uint32_t s1 = __shfl_xor_sync(0xffffffffu, odd ? hw[1] : lw[1], 1);
+        if (c < nq) {
+            const int e0 = 4 * (c & ~1);  // first element of the 8-element chunk
+            const size_t off = (size_t)(e0 >> 6) * a.mp * (GM_BK * 2) + gm_kint_off(m, e0 & 63);
+            if (!odd)
+                *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.xh) + off) = make_uint4(hw[0], hw[1], s0, s1);
+            else
+                *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.xl) + off) = make_uint4(s0, s1, lw[0], lw[1]);
+        }
+    }
+    if (tid == 0) a.sx[m] = sx;
+}
+
+__global__ void __launch_bounds__(XP_THREADS) tf_xprep_kernel(const XPrepArgs a) {
     extern __shared__ __align__(16) float xrow[];  // xpad layout
     __shared__ double redd[8];
     __shared__ float redf[8];
@@ -790,7 +888,9 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 
 cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     if (a.K % GM_BK) return cudaErrorInvalidValue;
-    const size_t smem = (size_t)xpad_len(a.K) * 4;
+    // rows read from memory (no embedding lookup) that fit the registers: the register kernel
+    const bool regs = !a.embd && a.K / 4 <= XP_THREADS * XP_REG_CHUNKS;
+    const size_t smem = regs ? 0 : (size_t)xpad_len(a.K) * 4;
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(tf_xprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
@@ -800,7 +900,7 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     // programmatic dependent launch: the CTAs become resident while the previous kernel drains
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.M);
-    cfg.blockDim = dim3(256);
+    cfg.blockDim = dim3(XP_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -808,7 +908,7 @@ cudaError_t xprep_launch(const XPrepArgs& a, cudaStream_t st) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, tf_xprep_kernel, aa);
+    return cudaLaunchKernelEx(&cfg, regs ? tf_xprep_rows_kernel : tf_xprep_kernel, aa);
 }
 
 int gemm_x_rows(int M) {
