@@ -47,9 +47,30 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int m, int kvh, 
     if (!last_s) return;
     __threadfence();
     const float* pbase = a.part + ((size_t)m * a.n_head + (size_t)kvh * n_rep) * a.n_split * (hd + 2);
+    // with few splits, one round of loads from L2: every split's maximum and sum (shared
+    // memory) and this thread's partial vectors (registers); the arithmetic below runs in the
+    // same order either way
+    constexpr int PO = 4, PS = 4;  // outputs per thread, splits
+    __shared__ float csum[AT_MAX_REP][PS];
+    const bool pre = nsp <= PS && n_rep * hd <= PO * nth;
+    float pv[PO][PS];
+    if (pre) {
+#pragma unroll
+        for (int o = 0; o < PO; ++o) {
+            const int i = tid + o * nth;
+            if (i < n_rep * hd) {
+                const float* pb = pbase + (size_t)(i / hd) * a.n_split * (hd + 2) + 2 + i % hd;
+#pragma unroll
+                for (int s = 0; s < PS; ++s)
+                    if (s < nsp) pv[o][s] = __ldcg(pb + (size_t)s * (hd + 2));
+            }
+        }
+    }
     for (int i = tid; i < n_rep * nsp; i += nth) {
         const int h = i / nsp, s = i % nsp;
-        cw[h][s] = __ldcg(pbase + ((size_t)h * a.n_split + s) * (hd + 2));
+        const float* pp = pbase + ((size_t)h * a.n_split + s) * (hd + 2);
+        cw[h][s] = __ldcg(pp);
+        if (pre) csum[h][s] = __ldcg(pp + 1);
     }
     __syncthreads();
     if (tid < n_rep) {
@@ -58,12 +79,34 @@ __device__ __forceinline__ void attn_combine(const AttnArgs& a, int m, int kvh, 
         float den = 0.f;
         for (int s = 0; s < nsp; ++s) {
             const float w = expf(cw[tid][s] - M);
-            den = fmaf(w, __ldcg(pbase + ((size_t)tid * a.n_split + s) * (hd + 2) + 1), den);
+            den = fmaf(w, pre ? csum[tid][s] : __ldcg(pbase + ((size_t)tid * a.n_split + s) * (hd + 2) + 1), den);
             cw[tid][s] = w;
         }
         cden[tid] = den;
     }
     __syncthreads();
+    if (pre) {
+#pragma unroll
+        for (int o = 0; o < PO; ++o) {
+            const int i = tid + o * nth;
+            if (i < n_rep * hd) {
+                const int h = i / hd, d = i % hd;
+                float num0 = 0.f, num1 = 0.f;
+#pragma unroll
+                for (int s = 0; s < PS; s += 2) {  // the pairs, then the odd last split, as below
+                    if (s + 1 < nsp) {
+                        num0 = fmaf(cw[h][s], pv[o][s], num0);
+                        num1 = fmaf(cw[h][s + 1], pv[o][s + 1], num1);
+                    } else if (s < nsp) {
+                        num0 = fmaf(cw[h][s], pv[o][s], num0);
+                    }
+                }
+                a.out[(size_t)m * a.ld_out + (size_t)(kvh * n_rep + h) * hd + d] = (num0 + num1) / cden[h];
+            }
+        }
+        if (tid == 0) a.counters[(size_t)m * a.n_kv + kvh] = 0u;
+        return;
+    }
     for (int i = tid; i < n_rep * hd; i += nth) {
         const int h = i / hd, d = i % hd;
         const float* pb = pbase + (size_t)h * a.n_split * (hd + 2) + 2 + d;
