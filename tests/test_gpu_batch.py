@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 
 import pyoracle as po
-from tinferno_b200 import gguf, synth
+from tinferno_b200 import gguf, native, synth
 from tinferno_b200.model import Model, RunConfig
 
 pytestmark = pytest.mark.gpu
@@ -129,13 +129,11 @@ def test_chunked_prefill_matches_oracle(ci, n, paths):
     m.close()
 
 
-@pytest.mark.slow
-def test_cfg4_subset_matches_reference(model_cache):
-    """cfg4 at its BASELINE size (Qwen2.5-1.5B shape, 1024-token prompts, 128 greedy steps): 16
-    of the batched benchmark's sequences, the 4 golden ones among them, through prefill_batch
-    and decode_batch (16 rows: the tcgen05 GEMM and the streaming attention).  The golden
-    sequences' greedy ids must equal the reference build's over all 128 steps, and their
-    top-8 logits agree within the north-star 1e-2."""
+def _cfg4_subset(model_cache, kv_type):
+    """The cfg4 golden subset run: 16 of the batched benchmark's sequences (the 4 golden ones
+    first) through prefill_batch and decode_batch with the given cache type.  Returns the
+    golden fixture, the greedy ids [n][16] and, per golden sequence, the top-8 logit error of
+    every decode step."""
     import os
     from conftest import GOLDEN
     cfg = synth.CFG4
@@ -148,18 +146,59 @@ def test_cfg4_subset_matches_reference(model_cache):
     for i in range(len(golden)):
         assert np.array_equal(prompts[i], gold["prompt"][i])
     B, n = len(seqs), gold["tokens"].shape[1]
-    m = Model(path, RunConfig(max_seq=cfg.max_seq, max_batch=B))
+    m = Model(path, RunConfig(max_seq=cfg.max_seq, max_batch=B, kv_type=kv_type))
     tok = m.prefill_batch(list(range(B)), prompts)
     ids = [tok.copy()]
-    err = 0.0
+    errs = [[] for _ in golden]
     for s in range(n - 1):
         tok, lg = m.decode_batch(list(range(B)), tok.tolist(), want_logits=True)
         ids.append(tok.copy())
         for i in range(len(golden)):
-            err = max(err, float(np.abs(lg[i][gold["topi"][i][s + 1]] - gold["topv"][i][s + 1]).max()))
+            errs[i].append(float(np.abs(lg[i][gold["topi"][i][s + 1]] - gold["topv"][i][s + 1]).max()))
     m.close()
-    ids = np.stack(ids)
+    return gold, np.stack(ids), errs
+
+
+@pytest.mark.slow
+def test_cfg4_subset_matches_reference(model_cache):
+    """cfg4 at its BASELINE size (Qwen2.5-1.5B shape, 1024-token prompts, 128 greedy steps): 16
+    of the batched benchmark's sequences, the 4 golden ones among them, through prefill_batch
+    and decode_batch (16 rows: the tcgen05 GEMM and the streaming attention).  The golden
+    sequences' greedy ids must equal the reference build's over all 128 steps, and their
+    top-8 logits agree within the north-star 1e-2."""
+    gold, ids, errs = _cfg4_subset(model_cache, native.TF_KV_F32)
+    golden, n = gold["seqs"].tolist(), gold["tokens"].shape[1]
     for i in range(len(golden)):
         assert ids[:, i].tolist() == gold["tokens"][i].tolist(), f"sequence {golden[i]}"
+    err = max(max(e) for e in errs)
     assert err < 1e-2, err
     print(f"cfg4 subset: {len(golden)} sequences token-exact over {n} ids, top-8 max |diff| {err:.2e}")
+
+
+# opt-in half-precision caches at the cfg4 length (the reference keeps fp32 K/V, so token
+# identity is only promised for fp32): (top-8 logit bound before the first differing id, ids
+# that must agree first).  Measured on a B200: f16 keeps two of the four golden sequences
+# token-exact over all 128 ids and the other two over 43 and 51, top-8 |diff| <= 2.3e-3; bf16
+# differs after 11 to 43 ids with top-8 |diff| up to 1.7e-2, above the north-star 1e-2.
+HALF_KV = {native.TF_KV_F16: (1e-2, 32), native.TF_KV_BF16: (2e-2, 8)}
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("kv", list(HALF_KV), ids=["f16", "bf16"])
+def test_cfg4_subset_half_cache(kv, model_cache):
+    """The cfg4 golden subset with an fp16 / bf16 KV cache: up to the first id that differs
+    from the reference build's, the top-8 logits stay within the type's bound, and at least
+    the stated number of leading ids agree."""
+    tol, min_same = HALF_KV[kv]
+    gold, ids, errs = _cfg4_subset(model_cache, kv)
+    golden, n = gold["seqs"].tolist(), gold["tokens"].shape[1]
+    report = []
+    for i in range(len(golden)):
+        diff = [k for k in range(n) if ids[k, i] != gold["tokens"][i][k]]
+        first = diff[0] if diff else n
+        report.append(first)
+        assert first >= min_same, f"sequence {golden[i]}: ids differ from step {first}"
+        # errs[i][s] is the logits of the step that produced id s + 1
+        before = errs[i][:max(first - 1, 1)]
+        assert max(before) < tol, (golden[i], max(before))
+    print(f"cfg4 subset, {'f16' if kv == native.TF_KV_F16 else 'bf16'} cache: leading identical ids {report} of {n}")
