@@ -399,17 +399,23 @@ __device__ __forceinline__ void gemm_epilogue(const GemmArgs& a, float* tile, in
             }
         return;
     }
+    if (a.epi == EPI_SWIGLU) {  // one (gate, up) row pair per iteration: rows 2j and 2j + 1
+        for (int i = tid; i < (mhi - mlo) * (GM_BN / 2); i += NTH) {
+            const int mm = mlo + i / (GM_BN / 2), j = i % (GM_BN / 2), m = m0 + mm, n = n0 + 2 * j;
+            if (n >= a.N) continue;  // N is even: the up row n + 1 exists with its gate row
+            const float2 gu = *reinterpret_cast<const float2*>(tile + mm * GM_EPI_LD + 2 * j);
+            a.y[(size_t)m * a.ldy + (n >> 1)] = __fmul_rn(__fdiv_rn(gu.x, 1.0f + expf(-gu.x)), gu.y);
+        }
+        return;
+    }
     for (int i = tid; i < (mhi - mlo) * GM_BN; i += NTH) {
         const int mm = mlo + i / GM_BN, nn = i % GM_BN, m = m0 + mm, n = n0 + nn;
         if (n >= a.N) continue;
         const float v = tile[mm * GM_EPI_LD + nn];
         if (a.epi == EPI_STORE) {
             a.y[(size_t)m * a.ldy + n] = v + (a.bias ? a.bias[n] : 0.f);
-        } else if (a.epi == EPI_RESID) {
+        } else {  // EPI_RESID
             a.resid[(size_t)m * a.ldr + n] += v;
-        } else if ((n & 1) == 0) {  // EPI_SWIGLU: rows 2i (gate) and 2i+1 (up)
-            const float gt = v, up = tile[mm * GM_EPI_LD + nn + 1];
-            a.y[(size_t)m * a.ldy + (n >> 1)] = __fmul_rn(__fdiv_rn(gt, 1.0f + expf(-gt)), up);
         }
     }
 }
