@@ -14,8 +14,8 @@ shard: replicas only) and the value is the aggregate tok/s.
              one host->device token copy and one device->host logits copy per step
   roofline   the step's kernel (every launch of the decode step runs it): the bytes a step
              must read (weights + cached K/V) over the CUDA-event time per step, vs
-             MEASURED_PEAKS.json; roofline_lmhead is the same kernel timed alone on the
-             lm_head shape
+             MEASURED_PEAKS.json (frac) and the 8 TB/s specification (frac_of_nominal);
+             roofline_lmhead is the same kernel timed alone on the lm_head shape
   configs    (N = 1) batch-1 prefill + decode of cfg0 / cfg1 / cfg2 at their BASELINE lengths
   batched    cfg4: 256 sequences sharded over the ranks, with the greedy ids of the golden
              subset compared against the reference build's (after the timed region)
@@ -52,6 +52,10 @@ STEP_KERNEL = "tf_gemv_kernel<1, 1> (Q8_0 integer-path GEMV; attention fused int
 STEP_TRAFFIC = 1_323_928_576
 STEP_TRAFFIC_SOURCE = ("ncu dram__bytes_read+write summed over the 65 launches of one step at position 35, "
                        "profiles/decode_step_cfg0_dram.md")
+
+
+# B200 HBM3e bandwidth as specified (8 TB/s), reported beside the measured copy peak
+HBM_NOMINAL_GBS = 8000.0
 
 
 def peaks():
@@ -209,7 +213,8 @@ def run_batched(args, rank, world, local_rank, dist):
             "prefill_tok_s": round(BATCH_SEQS * BATCH_PROMPT / prefill_max, 1),
             "hbm_roofline": {"bytes_per_step_per_gpu": int(step_bytes),
                              "achieved_gbs": round(step_bytes / (ms_max / steps / 1e3) / 1e9, 1),
-                             "frac_of_peak": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / peaks()[0], 4)},
+                             "frac_of_peak": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / peaks()[0], 4),
+                             "frac_of_nominal": round(step_bytes / (ms_max / steps / 1e3) / 1e9 / HBM_NOMINAL_GBS, 4)},
             "parity": parity,
             "path": "tcgen05 GEMM (f16-split, TMEM accumulator) at >= 16 rows per step, split flash-decode attention",
             "e2e": "every step copies S token ids in and S greedy ids out (host)", "cpu_baseline": cpu}
@@ -414,6 +419,7 @@ def run_ours(args, rank, world, local_rank, dist):
         roof = {"bound": "hbm", "kernel": STEP_KERNEL, "scope": "every launch of the decode step (the whole "
                 "step runs on this kernel), timed with CUDA events over the timed region",
                 "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "nominal_peak": HBM_NOMINAL_GBS, "frac_of_nominal": round(ach / HBM_NOMINAL_GBS, 4),
                 "peak_kind": peak_kind, "traffic": STEP_TRAFFIC, "traffic_source": STEP_TRAFFIC_SOURCE,
                 "algorithmic_bytes_per_step": int(step_bytes)}
         line = {"metric": "decode tok/s (batch 1, cfg0 Llama-3.2-1B Q8_0)", "value": round(value, 2), "unit": "tok/s",
